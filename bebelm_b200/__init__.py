@@ -1,0 +1,377 @@
+"""bebelm_b200 — B200 (sm_100a) attention hot path for BebeLM, behind a C-ABI.
+
+Python mirror of the reference's attention interface, calling the in-tree CUDA
+library ``libbebelm_attn.so`` through ctypes:
+
+* :func:`attention_decode` — ``attention_decode`` (src/kernels/attention.rs:17-26)
+* :func:`norm_rope_heads` — ``norm_rope_heads`` (src/model.rs:600-608)
+* :class:`Cache` — the attention part of ``Cache`` (src/cache.rs:9-49) as a
+  device-resident paged window, with ``attn_step`` (src/model.rs:440-451),
+  ``attn_prefill`` (src/model.rs:232-254) and batched decode across caches of
+  one :class:`Pool`.
+
+Host buffers are numpy float32 arrays; device buffers are CUDA torch tensors
+(their data pointers are passed as-is). There is no CPU fallback: if the
+library is missing or no sm_100 device is visible, calls raise.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libbebelm_attn.so")
+
+OK, ERR_INVALID, ERR_CUDA, ERR_OOM, ERR_CAPACITY, ERR_UNSUPPORTED, ERR_TIMEOUT, ERR_NO_DEVICE = 0, -1, -2, -3, -4, -5, -7, -8
+MEM_HOST, MEM_DEVICE = 0, 1
+F32, BF16 = 0, 1
+
+# reference constants (src/config.rs:14-32)
+N_HEADS, N_KV_HEADS, HEAD_DIM, KV_DIM, HIDDEN = 32, 8, 64, 512, 2048
+ROPE_THETA, RMS_EPS = 5_000_000.0, 1e-5
+ATTENTION_LAYERS = (2, 6, 10, 14, 18, 21)
+
+EXPORTS = [
+    "bebelm_abi_version", "bebelm_last_error", "bebelm_device_count", "bebelm_attn_decode_host",
+    "bebelm_norm_rope_heads", "bebelm_kv_pool_create", "bebelm_kv_pool_destroy", "bebelm_kv_pool_free_pages",
+    "bebelm_kv_create", "bebelm_kv_create_in_pool", "bebelm_kv_destroy", "bebelm_kv_clone", "bebelm_kv_clear",
+    "bebelm_kv_len", "bebelm_kv_layer_len", "bebelm_kv_pos", "bebelm_kv_set_pos", "bebelm_kv_evict_front",
+    "bebelm_kv_append", "bebelm_kv_read", "bebelm_attn_step", "bebelm_attn_decode_cached", "bebelm_attn_prefill", "bebelm_attn_decode_batched",
+]
+
+
+class BebelmError(RuntimeError):
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"[{code}] {msg}")
+        self.code = code
+
+
+_lib = None
+
+
+def load_library(path: str = LIB_PATH):
+    """Loads the CUDA library (building it first if it is missing and nvcc exists)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(path):
+        from . import build as _b
+        _b.build()
+    L = C.CDLL(path)
+    vp, sz, i, f = C.c_void_p, C.c_size_t, C.c_int, C.c_float
+    sig = {
+        "bebelm_abi_version": ([], i),
+        "bebelm_last_error": ([C.c_char_p, sz], i),
+        "bebelm_device_count": ([C.POINTER(i)], i),
+        "bebelm_attn_decode_host": ([vp, vp, vp, sz, i, i, i, vp], i),
+        "bebelm_norm_rope_heads": ([vp, sz, i, i, vp, sz, f, f, i, vp], i),
+        "bebelm_kv_pool_create": ([i, i, i, sz, i, i, i, C.POINTER(vp)], i),
+        "bebelm_kv_pool_destroy": ([vp], i),
+        "bebelm_kv_pool_free_pages": ([vp, C.POINTER(sz)], i),
+        "bebelm_kv_create": ([i, i, i, sz, i, i, i, C.POINTER(vp)], i),
+        "bebelm_kv_create_in_pool": ([vp, sz, C.POINTER(vp)], i),
+        "bebelm_kv_destroy": ([vp], i),
+        "bebelm_kv_clone": ([vp, C.POINTER(vp)], i),
+        "bebelm_kv_clear": ([vp], i),
+        "bebelm_kv_len": ([vp, C.POINTER(sz)], i),
+        "bebelm_kv_layer_len": ([vp, i, C.POINTER(sz)], i),
+        "bebelm_kv_pos": ([vp, C.POINTER(sz)], i),
+        "bebelm_kv_set_pos": ([vp, sz], i),
+        "bebelm_kv_evict_front": ([vp, sz], i),
+        "bebelm_kv_append": ([vp, i, vp, vp, sz, i, vp], i),
+        "bebelm_kv_read": ([vp, i, vp, vp, i, vp], i),
+        "bebelm_attn_step": ([vp, i, i, vp, vp, vp, vp, vp, f, f, sz, vp, i, vp], i),
+        "bebelm_attn_decode_cached": ([vp, i, i, vp, vp, i, vp], i),
+        "bebelm_attn_prefill": ([vp, i, i, vp, vp, vp, i, sz, sz, vp, vp, f, f, vp, i, vp], i),
+        "bebelm_attn_decode_batched": ([vp, i, i, i, vp, vp, vp, vp, vp, f, f, vp, vp, i, vp], i),
+    }
+    for name, (args, res) in sig.items():
+        fn = getattr(L, name)
+        fn.argtypes = args
+        fn.restype = res
+    _lib = L
+    return L
+
+
+def last_error() -> str:
+    buf = C.create_string_buffer(1024)
+    load_library().bebelm_last_error(buf, len(buf))
+    return buf.value.decode(errors="replace")
+
+
+def _check(rc: int):
+    if rc != 0:
+        raise BebelmError(rc, last_error())
+
+
+def device_count() -> int:
+    n = C.c_int(0)
+    _check(load_library().bebelm_device_count(C.byref(n)))
+    return n.value
+
+
+# ------------------------------------------------------------ buffer helpers --
+def _is_torch(x) -> bool:
+    return type(x).__module__.startswith("torch")
+
+
+def _buf(x, dtype=np.float32):
+    """Returns (pointer, mem kind, keepalive) for a numpy array or a CUDA tensor."""
+    if _is_torch(x):
+        if not x.is_cuda:
+            x = x.detach().contiguous().numpy()
+        else:
+            if not x.is_contiguous():
+                raise ValueError("device tensors must be contiguous")
+            return C.c_void_p(x.data_ptr()), MEM_DEVICE, x
+    a = np.ascontiguousarray(x, dtype=dtype)
+    return C.c_void_p(a.ctypes.data), MEM_HOST, a
+
+
+def _bufs(*xs, dtype=np.float32):
+    out = [_buf(x, dtype) for x in xs]
+    kinds = {m for _, m, _ in out}
+    if len(kinds) != 1:
+        raise ValueError("mix of host and device buffers in one call")
+    return out, kinds.pop()
+
+
+def _stream_ptr(stream):
+    if stream is None:
+        try:
+            import torch
+            if torch.cuda.is_available():
+                return C.c_void_p(torch.cuda.current_stream().cuda_stream)
+        except Exception:
+            pass
+        return C.c_void_p(0)
+    if hasattr(stream, "cuda_stream"):
+        return C.c_void_p(stream.cuda_stream)
+    return C.c_void_p(int(stream))
+
+
+# ------------------------------------------------------------------ drop-ins --
+def attention_decode(q, k, v, n_ctx: int, n_heads: int, n_kv_heads: int, head_dim: int) -> np.ndarray:
+    """``attention_decode`` (src/kernels/attention.rs:17-26) on the GPU; host float32 in/out."""
+    q = np.ascontiguousarray(q, np.float32).reshape(-1)
+    k = np.ascontiguousarray(k, np.float32).reshape(-1)
+    v = np.ascontiguousarray(v, np.float32).reshape(-1)
+    if q.size != n_heads * head_dim or k.size != n_ctx * n_kv_heads * head_dim or v.size != k.size:
+        raise ValueError("attention_decode: buffer sizes do not match the geometry")
+    out = np.zeros(n_heads * head_dim, np.float32)
+    kp = k.ctypes.data if k.size else None
+    vp = v.ctypes.data if v.size else None
+    _check(load_library().bebelm_attn_decode_host(q.ctypes.data, kp, vp, n_ctx, n_heads, n_kv_heads, head_dim,
+                                                   out.ctypes.data))
+    return out
+
+
+def norm_rope_heads(buf, n_heads: int, head_dim: int, gain, pos: int, theta: float = ROPE_THETA,
+                    eps: float = RMS_EPS, n_tokens: int = 1, stream=None):
+    """``norm_rope_heads`` (src/model.rs:600-608) for n_tokens positions pos, pos+1, ...
+
+    Host input: returns a new normed/roped float32 array. Device tensor: in place, returned."""
+    if _is_torch(buf) and buf.is_cuda:
+        (b, g), mem = _bufs(buf, gain)
+        _check(load_library().bebelm_norm_rope_heads(b[0], n_tokens, n_heads, head_dim, g[0], pos, theta, eps, mem,
+                                                      _stream_ptr(stream)))
+        return buf
+    out = np.array(buf, np.float32, copy=True).reshape(-1)
+    g = np.ascontiguousarray(gain, np.float32)
+    _check(load_library().bebelm_norm_rope_heads(out.ctypes.data, n_tokens, n_heads, head_dim, g.ctypes.data, pos,
+                                                  theta, eps, MEM_HOST, None))
+    return out
+
+
+# --------------------------------------------------------------------- cache --
+class Pool:
+    """A device page pool that several caches (sequences) draw from."""
+
+    def __init__(self, n_layers: int, n_pages: int, n_kv_heads: int = N_KV_HEADS, head_dim: int = HEAD_DIM,
+                 page_tokens: int = 64, device: int = 0):
+        self._h = C.c_void_p()
+        self.n_layers, self.n_kv_heads = n_layers, n_kv_heads
+        _check(load_library().bebelm_kv_pool_create(n_layers, n_kv_heads, head_dim, n_pages, page_tokens, F32, device,
+                                                    C.byref(self._h)))
+
+    def free_pages(self) -> int:
+        n = C.c_size_t()
+        _check(load_library().bebelm_kv_pool_free_pages(self._h, C.byref(n)))
+        return n.value
+
+    def close(self):
+        if self._h:
+            _check(load_library().bebelm_kv_pool_destroy(self._h))
+            self._h = C.c_void_p()
+
+    def __del__(self):
+        try:
+            if self._h:
+                load_library().bebelm_kv_pool_destroy(self._h)
+        except Exception:
+            pass
+
+
+class Cache:
+    """Device replacement of ``Cache`` (src/cache.rs:9-49) for the attention layers.
+
+    ``layer`` indexes the cache's own attention layers (0..n_layers-1); a model
+    maps its absolute attention layers (2, 6, 10, 14, 18, 21) onto these."""
+
+    def __init__(self, n_layers: int = len(ATTENTION_LAYERS), n_kv_heads: int = N_KV_HEADS,
+                 max_context: int = 32768, head_dim: int = HEAD_DIM, device: int = 0, pool: Pool | None = None,
+                 _handle=None):
+        self.n_layers = n_layers if pool is None else pool.n_layers
+        self.n_kv_heads = n_kv_heads if pool is None else pool.n_kv_heads
+        self.head_dim = head_dim
+        self.max_context = max_context
+        self.pool = pool
+        L = load_library()
+        if _handle is not None:
+            self._h = _handle
+        else:
+            self._h = C.c_void_p()
+            if pool is None:
+                _check(L.bebelm_kv_create(n_layers, n_kv_heads, head_dim, max_context, 64, F32, device,
+                                          C.byref(self._h)))
+            else:
+                _check(L.bebelm_kv_create_in_pool(pool._h, max_context, C.byref(self._h)))
+
+    # -- src/cache.rs API -------------------------------------------------
+    def kv_len(self) -> int:
+        n = C.c_size_t()
+        _check(load_library().bebelm_kv_len(self._h, C.byref(n)))
+        return n.value
+
+    def layer_len(self, layer: int) -> int:
+        n = C.c_size_t()
+        _check(load_library().bebelm_kv_layer_len(self._h, layer, C.byref(n)))
+        return n.value
+
+    @property
+    def pos(self) -> int:
+        n = C.c_size_t()
+        _check(load_library().bebelm_kv_pos(self._h, C.byref(n)))
+        return n.value
+
+    @pos.setter
+    def pos(self, p: int):
+        _check(load_library().bebelm_kv_set_pos(self._h, p))
+
+    def evict_front(self, n: int) -> None:
+        _check(load_library().bebelm_kv_evict_front(self._h, n))
+
+    def clone(self) -> "Cache":
+        h = C.c_void_p()
+        _check(load_library().bebelm_kv_clone(self._h, C.byref(h)))
+        return Cache(self.n_layers, self.n_kv_heads, self.max_context, self.head_dim, pool=self.pool, _handle=h)
+
+    def clear(self) -> None:
+        _check(load_library().bebelm_kv_clear(self._h))
+
+    def append(self, layer: int, k, v, stream=None) -> None:
+        """``cache.k[layer].extend_from_slice(k)`` and the same for v."""
+        (kb, vb), mem = _bufs(k, v)
+        t = (kb[2].size if mem == MEM_HOST else kb[2].numel()) // (self.n_kv_heads * self.head_dim)
+        _check(load_library().bebelm_kv_append(self._h, layer, kb[0], vb[0], t, mem, _stream_ptr(stream)))
+
+    def read(self, layer: int):
+        """The window of one layer as host arrays (k, v), each [len, n_kv*64] — what
+        ``cache.k[layer]`` / ``cache.v[layer]`` hold in the reference."""
+        n = self.layer_len(layer)
+        k = np.zeros((n, self.n_kv_heads * self.head_dim), np.float32)
+        v = np.zeros_like(k)
+        if n:
+            _check(load_library().bebelm_kv_read(self._h, layer, k.ctypes.data, v.ctypes.data, MEM_HOST, None))
+        return k, v
+
+    # -- fused ops ----------------------------------------------------------
+    def attn_step(self, layer: int, q, k, v, q_gain, k_gain, pos: int, theta: float = ROPE_THETA,
+                  eps: float = RMS_EPS, out=None, stream=None):
+        """src/model.rs:440-451 (norm+RoPE, append, decode). Returns out [n_heads*64]."""
+        (qb, kb, vb, qg, kg), mem = _bufs(q, k, v, q_gain, k_gain)
+        n_heads = (qb[2].size if mem == MEM_HOST else qb[2].numel()) // self.head_dim
+        if out is None:
+            out = np.zeros(n_heads * self.head_dim, np.float32) if mem == MEM_HOST else qb[2].new_empty(
+                n_heads * self.head_dim, dtype=qb[2].dtype)
+        ob, _, _ = _buf(out)
+        _check(load_library().bebelm_attn_step(self._h, layer, n_heads, qb[0], kb[0], vb[0], qg[0], kg[0], theta, eps,
+                                               pos, ob, mem, _stream_ptr(stream)))
+        return out
+
+    def decode(self, layer: int, q, out=None, stream=None):
+        """``attention_decode`` over the cached window of ``layer`` (no append); q normed+roped."""
+        (qb,), mem = _bufs(q)
+        n_heads = (qb[2].size if mem == MEM_HOST else qb[2].numel()) // self.head_dim
+        if out is None:
+            out = np.zeros(n_heads * self.head_dim, np.float32) if mem == MEM_HOST else qb[2].new_empty(
+                n_heads * self.head_dim)
+        ob, _, _ = _buf(out)
+        _check(load_library().bebelm_attn_decode_cached(self._h, layer, n_heads, qb[0], ob, mem, _stream_ptr(stream)))
+        return out
+
+    def attn_prefill(self, layer: int, q, k, v, q_gain, k_gain, pos0: int, theta: float = ROPE_THETA,
+                     eps: float = RMS_EPS, out=None, stream=None, n_heads: int = N_HEADS):
+        """src/model.rs:232-254 for t tokens. q [t, n_heads*64], k/v [t, n_kv*64] (float32 or bf16
+        tensors). Returns out [t, n_heads*64] float32."""
+        is_dev = _is_torch(q) and q.is_cuda
+        if is_dev:
+            import torch
+            in_dtype = BF16 if q.dtype == torch.bfloat16 else F32
+            t = q.numel() // (n_heads * self.head_dim)
+            if out is None:
+                out = torch.empty((t, n_heads * self.head_dim), dtype=torch.float32, device=q.device)
+            ptrs = [C.c_void_p(x.data_ptr()) for x in (q, k, v, q_gain, k_gain, out)]
+            mem = MEM_DEVICE
+            keep = (q, k, v, q_gain, k_gain, out)
+        else:
+            q = np.ascontiguousarray(q)
+            in_dtype = F32
+            if q.dtype != np.float32:
+                q = q.astype(np.float32)
+            k = np.ascontiguousarray(k, np.float32)
+            v = np.ascontiguousarray(v, np.float32)
+            qg = np.ascontiguousarray(q_gain, np.float32)
+            kg = np.ascontiguousarray(k_gain, np.float32)
+            t = q.size // (n_heads * self.head_dim)
+            out = np.zeros((t, n_heads * self.head_dim), np.float32)
+            keep = (q, k, v, qg, kg, out)
+            ptrs = [C.c_void_p(x.ctypes.data) for x in keep]
+            mem = MEM_HOST
+        _check(load_library().bebelm_attn_prefill(self._h, layer, n_heads, ptrs[0], ptrs[1], ptrs[2], in_dtype, t,
+                                                  pos0, ptrs[3], ptrs[4], theta, eps, ptrs[5], mem,
+                                                  _stream_ptr(stream)))
+        del keep
+        return out
+
+    def close(self):
+        if self._h:
+            _check(load_library().bebelm_kv_destroy(self._h))
+            self._h = C.c_void_p()
+
+    def __del__(self):
+        try:
+            if self._h:
+                load_library().bebelm_kv_destroy(self._h)
+        except Exception:
+            pass
+
+
+def attn_decode_batched(caches, layer: int, q, k, v, q_gain, k_gain, pos, theta: float = ROPE_THETA,
+                        eps: float = RMS_EPS, out=None, stream=None):
+    """One decode token for each cache (all in one :class:`Pool`): q [n, n_heads*64],
+    k/v [n, n_kv*64]. Returns out [n, n_heads*64]."""
+    n = len(caches)
+    arr = (C.c_void_p * n)(*[c._h for c in caches])
+    (qb, kb, vb, qg, kg), mem = _bufs(q, k, v, q_gain, k_gain)
+    numel = qb[2].size if mem == MEM_HOST else qb[2].numel()
+    n_heads = numel // (n * caches[0].head_dim)
+    if out is None:
+        out = np.zeros((n, n_heads * 64), np.float32) if mem == MEM_HOST else qb[2].new_empty((n, n_heads * 64))
+    ob, _, _ = _buf(out)
+    posa = (C.c_size_t * n)(*[int(p) for p in pos])
+    _check(load_library().bebelm_attn_decode_batched(arr, n, layer, n_heads, qb[0], kb[0], vb[0], qg[0], kg[0], theta,
+                                                     eps, posa, ob, mem, _stream_ptr(stream)))
+    return out

@@ -1,0 +1,1016 @@
+// Host runtime behind the C-ABI of include/bebelm_attn.h: page pool and
+// sequence-window bookkeeping (the device replacement of src/cache.rs), host /
+// device staging, and the launch sequences of the fused calls.
+#include <algorithm>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/bebelm_attn.h"
+#include "internal.h"
+
+using namespace bebelm;
+
+// ------------------------------------------------------------------ errors --
+static thread_local std::string g_err;
+
+static int fail(int code, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    g_err = buf;
+    return code;
+}
+
+#define CUDA_TRY(x)                                                                          \
+    do {                                                                                     \
+        cudaError_t e_ = (x);                                                                \
+        if (e_ != cudaSuccess)                                                               \
+            return fail(e_ == cudaErrorMemoryAllocation ? BEBELM_ERR_OOM : BEBELM_ERR_CUDA,  \
+                        "%s failed: %s (%s:%d)", #x, cudaGetErrorString(e_), __FILE__, __LINE__); \
+    } while (0)
+
+#define TRY(x)                 \
+    do {                       \
+        int rc_ = (x);         \
+        if (rc_ != 0) return rc_; \
+    } while (0)
+
+namespace {
+
+struct DeviceGuard {
+    int prev = -1;
+    explicit DeviceGuard(int dev) {
+        cudaGetDevice(&prev);
+        if (prev != dev) cudaSetDevice(dev);
+    }
+    ~DeviceGuard() {
+        int cur = -1;
+        cudaGetDevice(&cur);
+        if (prev >= 0 && cur != prev) cudaSetDevice(prev);
+    }
+};
+
+int check_device(int dev) {
+    int n = 0;
+    cudaError_t e = cudaGetDeviceCount(&n);
+    if (e != cudaSuccess || n == 0)
+        return fail(BEBELM_ERR_NO_DEVICE, "no CUDA device visible (%s)", cudaGetErrorString(e));
+    if (dev < 0 || dev >= n) return fail(BEBELM_ERR_INVALID, "device %d out of range [0,%d)", dev, n);
+    int major = 0;
+    cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+    if (major != 10)
+        return fail(BEBELM_ERR_NO_DEVICE, "device %d is sm_%d0, this library is built for sm_100a", dev, major);
+    return 0;
+}
+
+int current_device(int* dev) {
+    CUDA_TRY(cudaGetDevice(dev));
+    return check_device(*dev);
+}
+
+// Growable device buffer.
+struct DevBuf {
+    void* p = nullptr;
+    size_t bytes = 0;
+    int ensure(size_t need, bool zero = false, cudaStream_t s = 0) {
+        if (need <= bytes) return 0;
+        if (p) {
+            cudaStreamSynchronize(s);
+            cudaFree(p);
+            p = nullptr;
+            bytes = 0;
+        }
+        size_t n = std::max<size_t>(need, 256);
+        CUDA_TRY(cudaMalloc(&p, n));
+        bytes = n;
+        if (zero) CUDA_TRY(cudaMemsetAsync(p, 0, n, s));
+        return 0;
+    }
+    void release() {
+        if (p) cudaFree(p);
+        p = nullptr;
+        bytes = 0;
+    }
+    template <class T> T* as() const { return static_cast<T*>(p); }
+};
+
+// Growable pinned host buffer.
+struct PinBuf {
+    void* p = nullptr;
+    size_t bytes = 0;
+    int ensure(size_t need) {
+        if (need <= bytes) return 0;
+        if (p) cudaFreeHost(p);
+        p = nullptr;
+        bytes = 0;
+        size_t n = std::max<size_t>(need, 4096);
+        CUDA_TRY(cudaHostAlloc(&p, n, cudaHostAllocDefault));
+        bytes = n;
+        return 0;
+    }
+    void release() {
+        if (p) cudaFreeHost(p);
+        p = nullptr;
+        bytes = 0;
+    }
+    template <class T> T* as() const { return static_cast<T*>(p); }
+};
+
+}  // namespace
+
+// -------------------------------------------------------------------- pool --
+struct bebelm_kv_pool {
+    int device = 0, n_layers = 0, n_kv = 0, head_dim = 64, page_tokens = 64, dtype = BEBELM_F32;
+    size_t n_pages = 0, page_floats = 0, block_floats = 0;
+    float* mem = nullptr;
+    std::vector<int> free_list;  // physical pages not in any window
+    int num_sms = 148;
+    int n_seqs = 0;              // live sequences drawing from this pool
+    // scratch shared by every call on this pool's sequences (stream-ordered)
+    DevBuf io, qn, part, counters, seqdesc, bf16, err;
+    PinBuf pin;
+    std::vector<DecodeSeq> h_desc;
+
+    PoolView view(int layer) const {
+        PoolView v;
+        v.base = mem;
+        v.page_floats = page_floats;
+        v.layer_off = (size_t)layer * 2 * block_floats;
+        v.block_floats = block_floats;
+        return v;
+    }
+};
+
+struct bebelm_kv {
+    bebelm_kv_pool* pool = nullptr;
+    bool owns_pool = false;
+    size_t max_context = 0;
+    int cap = 0;                  // ring entries (logical pages held at most)
+    int* d_table = nullptr;       // device copy of the ring
+    std::vector<int> table;       // ring: logical page L -> physical table[L % cap]
+    long long lo = 0, hi = 0;     // allocated logical pages [lo, hi)
+    std::vector<long long> base, len;  // per layer window: slots [base, base+len)
+    size_t pos = 0;
+};
+
+namespace {
+
+int upload_table(bebelm_kv* kv, long long L0, long long L1, cudaStream_t s) {
+    // ring entries of logical pages [L0, L1); pageable source is staged by the
+    // runtime before cudaMemcpyAsync returns, so later host edits cannot race
+    for (long long L = L0; L < L1;) {
+        int i0 = (int)(L % kv->cap);
+        long long n = std::min<long long>(L1 - L, kv->cap - i0);
+        CUDA_TRY(cudaMemcpyAsync(kv->d_table + i0, kv->table.data() + i0, sizeof(int) * n,
+                                 cudaMemcpyHostToDevice, s));
+        L += n;
+    }
+    return 0;
+}
+
+// Make room for t more positions of `layer`; returns the logical slot of the first.
+int reserve(bebelm_kv* kv, int layer, size_t t, long long* slot0, cudaStream_t s) {
+    long long b = kv->base[layer], n = kv->len[layer];
+    if (n == 0 && b < kv->lo * kPageTokens) b = kv->lo * kPageTokens;
+    const long long s0 = b + n, s_end = s0 + (long long)t;
+    const long long need_hi = (s_end + kPageTokens - 1) / kPageTokens;
+    if (need_hi - kv->lo > kv->cap)
+        return fail(BEBELM_ERR_CAPACITY,
+                    "layer %d window would hold %lld positions; this cache holds at most %zu (+%d): "
+                    "evict_front first",
+                    layer, n + (long long)t, kv->max_context, kPageTokens);
+    const long long add = std::max<long long>(0, need_hi - kv->hi);
+    if ((size_t)add > kv->pool->free_list.size())
+        return fail(BEBELM_ERR_OOM, "page pool exhausted: need %lld pages, %zu free", add,
+                    kv->pool->free_list.size());
+    const long long old_hi = kv->hi;
+    for (long long L = kv->hi; L < need_hi; ++L) {
+        kv->table[L % kv->cap] = kv->pool->free_list.back();
+        kv->pool->free_list.pop_back();
+    }
+    if (need_hi > kv->hi) kv->hi = need_hi;
+    if (add) TRY(upload_table(kv, old_hi, kv->hi, s));
+    kv->base[layer] = b;
+    kv->len[layer] = n + (long long)t;
+    *slot0 = s0;
+    return 0;
+}
+
+void release_pages_below(bebelm_kv* kv, long long new_lo) {
+    for (long long L = kv->lo; L < new_lo; ++L) kv->pool->free_list.push_back(kv->table[L % kv->cap]);
+    kv->lo = new_lo;
+}
+
+void recompute_lo(bebelm_kv* kv) {
+    long long new_lo = kv->hi;
+    for (size_t l = 0; l < kv->len.size(); ++l)
+        if (kv->len[l] > 0) new_lo = std::min(new_lo, kv->base[l] / kPageTokens);
+    if (new_lo > kv->lo) release_pages_below(kv, new_lo);
+}
+
+int validate_kv(const bebelm_kv* kv) {
+    if (!kv || !kv->pool) return fail(BEBELM_ERR_INVALID, "null cache handle");
+    return 0;
+}
+
+int validate_layer(const bebelm_kv* kv, int layer) {
+    TRY(validate_kv(kv));
+    if (layer < 0 || layer >= kv->pool->n_layers)
+        return fail(BEBELM_ERR_INVALID, "layer %d out of range [0,%d)", layer, kv->pool->n_layers);
+    return 0;
+}
+
+int pool_create(int n_layers, int n_kv_heads, int head_dim, size_t n_pages, int page_tokens, int dtype,
+                int device, bebelm_kv_pool** out) {
+    if (!out) return fail(BEBELM_ERR_INVALID, "out is null");
+    *out = nullptr;
+    if (n_layers <= 0 || n_kv_heads <= 0 || n_pages == 0)
+        return fail(BEBELM_ERR_INVALID, "n_layers, n_kv_heads and n_pages must be positive");
+    if (head_dim != kHeadDim) return fail(BEBELM_ERR_UNSUPPORTED, "cache head_dim must be 64 (got %d)", head_dim);
+    if (page_tokens != kPageTokens)
+        return fail(BEBELM_ERR_UNSUPPORTED, "page_tokens must be 64 (got %d)", page_tokens);
+    if (dtype != BEBELM_F32) return fail(BEBELM_ERR_UNSUPPORTED, "cache dtype must be BEBELM_F32");
+    if (n_pages > (size_t)INT32_MAX) return fail(BEBELM_ERR_INVALID, "too many pages");
+    TRY(check_device(device));
+    DeviceGuard g(device);
+    auto* P = new bebelm_kv_pool();
+    P->device = device;
+    P->n_layers = n_layers;
+    P->n_kv = n_kv_heads;
+    P->n_pages = n_pages;
+    P->block_floats = (size_t)n_kv_heads * kPageRowFloats;
+    P->page_floats = (size_t)n_layers * 2 * P->block_floats;
+    cudaDeviceGetAttribute(&P->num_sms, cudaDevAttrMultiProcessorCount, device);
+    const size_t bytes = n_pages * P->page_floats * sizeof(float);
+    cudaError_t e = cudaMalloc(&P->mem, bytes);
+    if (e != cudaSuccess) {
+        delete P;
+        return fail(BEBELM_ERR_OOM, "cudaMalloc of %zu bytes for the page pool failed: %s", bytes,
+                    cudaGetErrorString(e));
+    }
+    // zero once so masked rows of a partly filled page are finite
+    e = cudaMemset(P->mem, 0, bytes);
+    if (e == cudaSuccess) {
+        int rc = P->err.ensure(sizeof(int), true);
+        if (rc) {
+            cudaFree(P->mem);
+            delete P;
+            return rc;
+        }
+        e = cudaDeviceSynchronize();
+    }
+    if (e != cudaSuccess) {
+        cudaFree(P->mem);
+        delete P;
+        return fail(BEBELM_ERR_CUDA, "pool initialisation failed: %s", cudaGetErrorString(e));
+    }
+    P->free_list.reserve(n_pages);
+    for (size_t i = n_pages; i-- > 0;) P->free_list.push_back((int)i);
+    *out = P;
+    return 0;
+}
+
+void pool_free(bebelm_kv_pool* P) {
+    DeviceGuard g(P->device);
+    cudaDeviceSynchronize();
+    cudaFree(P->mem);
+    P->io.release();
+    P->qn.release();
+    P->part.release();
+    P->counters.release();
+    P->seqdesc.release();
+    P->bf16.release();
+    P->err.release();
+    P->pin.release();
+    delete P;
+}
+
+int seq_create(bebelm_kv_pool* P, size_t max_context, bool owns, bebelm_kv** out) {
+    if (!out) return fail(BEBELM_ERR_INVALID, "out is null");
+    *out = nullptr;
+    if (max_context == 0) return fail(BEBELM_ERR_INVALID, "max_context must be positive");
+    DeviceGuard g(P->device);
+    auto* kv = new bebelm_kv();
+    kv->pool = P;
+    kv->owns_pool = owns;
+    kv->max_context = max_context;
+    kv->cap = (int)((max_context + kPageTokens - 1) / kPageTokens + 2);
+    kv->table.assign(kv->cap, 0);
+    kv->base.assign(P->n_layers, 0);
+    kv->len.assign(P->n_layers, 0);
+    cudaError_t e = cudaMalloc(&kv->d_table, sizeof(int) * kv->cap);
+    if (e == cudaSuccess) e = cudaMemset(kv->d_table, 0, sizeof(int) * kv->cap);
+    if (e != cudaSuccess) {
+        delete kv;
+        return fail(BEBELM_ERR_OOM, "page table allocation failed: %s", cudaGetErrorString(e));
+    }
+    P->n_seqs++;
+    *out = kv;
+    return 0;
+}
+
+}  // namespace
+
+namespace {
+
+struct Window {
+    const bebelm_kv* kv;
+    long long base;
+    long long len;
+};
+
+void pick_heads_per_cta(int group, int* hpc, int* n_sub) {
+    int h = group % 4 == 0 ? 4 : group % 3 == 0 ? 3 : group % 2 == 0 ? 2 : 1;
+    *hpc = h;
+    *n_sub = group / h;
+}
+
+// Split-K decode of one query per window. q/out: [n_windows][n_heads][64] device.
+int run_decode(bebelm_kv_pool* P, const std::vector<Window>& wins, int layer, int n_heads, const float* d_q,
+               float* d_out, float scale, cudaStream_t s) {
+    const int n = (int)wins.size();
+    if (n == 0) return 0;
+    const int group = n_heads / P->n_kv;
+    int hpc, n_sub;
+    pick_heads_per_cta(group, &hpc, &n_sub);
+    const int NY = P->n_kv * n_sub;
+    long long total_units = 0;
+    std::vector<long long> npages(n);
+    for (int i = 0; i < n; ++i) {
+        const Window& w = wins[i];
+        npages[i] = w.len > 0 ? (w.base + w.len - 1) / kPageTokens - w.base / kPageTokens + 1 : 0;
+        total_units += npages[i] * NY;
+    }
+    const long long target = (long long)P->num_sms * 2;  // two resident CTAs per SM
+    long long per = std::max<long long>(1, (total_units + target - 1) / target);
+    if (n > 1) per = std::min<long long>(per, 8);  // uneven sequences: more, smaller splits
+    P->h_desc.resize(n);
+    int total_splits = 0;
+    for (int i = 0; i < n; ++i) {
+        DecodeSeq& d = P->h_desc[i];
+        d.table = wins[i].kv->d_table;
+        d.cap = wins[i].kv->cap;
+        d.len = (int)wins[i].len;
+        d.base = wins[i].base;
+        d.split0 = total_splits;
+        d.n_splits = (int)std::max<long long>(1, (npages[i] + per - 1) / per);
+        total_splits += d.n_splits;
+    }
+    TRY(P->part.ensure(sizeof(float) * (size_t)total_splits * NY * hpc * (kHeadDim + 2), false, s));
+    TRY(P->counters.ensure(sizeof(unsigned) * (size_t)n * NY, true, s));
+    DecodeArgs a{};
+    if (n == 1) {
+        a.one = P->h_desc[0];
+    } else {
+        TRY(P->seqdesc.ensure(sizeof(DecodeSeq) * n, false, s));
+        CUDA_TRY(cudaMemcpyAsync(P->seqdesc.p, P->h_desc.data(), sizeof(DecodeSeq) * n, cudaMemcpyHostToDevice, s));
+        a.seqs = P->seqdesc.as<DecodeSeq>();
+    }
+    a.n_seqs = n;
+    a.pv = P->view(layer);
+    a.q = d_q;
+    a.out = d_out;
+    a.part_acc = P->part.as<float>();
+    a.part_ml = a.part_acc + (size_t)total_splits * NY * hpc * kHeadDim;
+    a.counters = P->counters.as<unsigned>();
+    a.err = P->err.as<int>();
+    a.n_heads = n_heads;
+    a.n_kv = P->n_kv;
+    a.group = group;
+    a.hpc = hpc;
+    a.n_sub = n_sub;
+    a.pages_per_split = (int)per;
+    a.total_splits = total_splits;
+    a.scale_log2 = scale * 1.4426950408889634f;
+    CUDA_TRY(launch_decode(a, s));
+    return 0;
+}
+
+// Copies host inputs into pinned staging and then into the pool's device io buffer.
+struct Stage {
+    const void* src;
+    size_t bytes;
+    void** dev;  // receives the device address
+};
+
+thread_local size_t g_pin_out_off = 0;  // set by stage_in, read by stage_out (calls are host-synchronous)
+
+int stage_in(bebelm_kv_pool* P, Stage* st, int n, size_t out_bytes, void** d_out, cudaStream_t s) {
+    size_t total = 0;
+    for (int i = 0; i < n; ++i) total += (st[i].bytes + 255) & ~size_t(255);
+    const size_t out_off = total;
+    total += ((out_bytes + 255) & ~size_t(255)) + 256;  // output, then the error word
+    TRY(P->io.ensure(total, false, s));
+    TRY(P->pin.ensure(total));
+    size_t off = 0;
+    for (int i = 0; i < n; ++i) {
+        if (st[i].src && st[i].bytes) std::memcpy(P->pin.as<char>() + off, st[i].src, st[i].bytes);
+        *st[i].dev = st[i].src ? P->io.as<char>() + off : nullptr;
+        off += (st[i].bytes + 255) & ~size_t(255);
+    }
+    if (out_off) CUDA_TRY(cudaMemcpyAsync(P->io.p, P->pin.p, out_off, cudaMemcpyHostToDevice, s));
+    if (d_out) *d_out = P->io.as<char>() + out_off;
+    g_pin_out_off = out_off;
+    return 0;
+}
+
+// Device output back to the caller's host memory through the pinned buffer; also
+// surfaces a device-side timeout recorded by a kernel.
+int stage_out(bebelm_kv_pool* P, const void* d_src, void* h_dst, size_t bytes, cudaStream_t s) {
+    char* pin = P->pin.as<char>() + g_pin_out_off;
+    char* perr = pin + ((bytes + 255) & ~size_t(255));
+    if (bytes) CUDA_TRY(cudaMemcpyAsync(pin, d_src, bytes, cudaMemcpyDeviceToHost, s));
+    CUDA_TRY(cudaMemcpyAsync(perr, P->err.p, sizeof(int), cudaMemcpyDeviceToHost, s));
+    CUDA_TRY(cudaStreamSynchronize(s));
+    int derr = *reinterpret_cast<int*>(perr);
+    if (derr) {
+        cudaMemsetAsync(P->err.p, 0, sizeof(int), s);
+        if (P->counters.p) cudaMemsetAsync(P->counters.p, 0, P->counters.bytes, s);
+        cudaStreamSynchronize(s);
+        return fail(BEBELM_ERR_TIMEOUT, "a device-side wait timed out (code %d); outputs are invalid", derr);
+    }
+    if (bytes) std::memcpy(h_dst, pin, bytes);
+    return 0;
+}
+
+float theta_scale_of(float theta, int head_dim) {
+    // src/kernels/rope.rs:19: freq_base.powf(-2.0 / d as f32), evaluated with the host libm
+    return powf(theta, -2.0f / (float)head_dim);
+}
+
+}  // namespace
+
+namespace {
+
+// Staging for calls that have no pool (the drop-ins): one per device, guarded by a mutex.
+std::mutex g_scratch_mu;
+bebelm_kv_pool* g_scratch[64] = {};
+
+int scratch_pool(int dev, bebelm_kv_pool** out) {
+    if (dev < 0 || dev >= 64) return fail(BEBELM_ERR_INVALID, "device %d unsupported", dev);
+    if (!g_scratch[dev]) {
+        auto* P = new bebelm_kv_pool();
+        P->device = dev;
+        int rc = P->err.ensure(sizeof(int), true);
+        if (rc) {
+            delete P;
+            return rc;
+        }
+        cudaDeviceGetAttribute(&P->num_sms, cudaDevAttrMultiProcessorCount, dev);
+        g_scratch[dev] = P;
+    }
+    *out = g_scratch[dev];
+    return 0;
+}
+
+cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+int check_mem(int mem) {
+    if (mem != BEBELM_MEM_HOST && mem != BEBELM_MEM_DEVICE)
+        return fail(BEBELM_ERR_INVALID, "mem must be BEBELM_MEM_HOST or BEBELM_MEM_DEVICE (got %d)", mem);
+    return 0;
+}
+
+int check_geometry(int n_heads, int n_kv) {
+    if (n_heads <= 0 || n_kv <= 0 || n_heads % n_kv)
+        return fail(BEBELM_ERR_INVALID, "n_heads (%d) must be a positive multiple of n_kv_heads (%d)", n_heads, n_kv);
+    return 0;
+}
+
+}  // namespace
+
+extern "C" {
+
+int bebelm_abi_version(void) { return BEBELM_ABI_VERSION; }
+
+int bebelm_last_error(char* buf, size_t n) {
+    if (!buf || !n) return BEBELM_ERR_INVALID;
+    std::snprintf(buf, n, "%s", g_err.c_str());
+    return 0;
+}
+
+int bebelm_device_count(int* n) {
+    if (!n) return fail(BEBELM_ERR_INVALID, "n is null");
+    *n = 0;
+    int total = 0;
+    if (cudaGetDeviceCount(&total) != cudaSuccess) return 0;
+    for (int d = 0; d < total; ++d) {
+        int major = 0;
+        cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, d);
+        if (major == 10) ++*n;
+    }
+    return 0;
+}
+
+// ------------------------------------------------------------------ pool --
+int bebelm_kv_pool_create(int n_layers, int n_kv_heads, int head_dim, size_t n_pages, int page_tokens, int dtype,
+                          int device, bebelm_kv_pool** out) {
+    return pool_create(n_layers, n_kv_heads, head_dim, n_pages, page_tokens, dtype, device, out);
+}
+
+int bebelm_kv_pool_destroy(bebelm_kv_pool* pool) {
+    if (!pool) return fail(BEBELM_ERR_INVALID, "null pool");
+    if (pool->n_seqs) return fail(BEBELM_ERR_INVALID, "pool still has %d live sequences", pool->n_seqs);
+    pool_free(pool);
+    return 0;
+}
+
+int bebelm_kv_pool_free_pages(const bebelm_kv_pool* pool, size_t* out) {
+    if (!pool || !out) return fail(BEBELM_ERR_INVALID, "null argument");
+    *out = pool->free_list.size();
+    return 0;
+}
+
+// ----------------------------------------------------------------- cache --
+int bebelm_kv_create(int n_layers, int n_kv_heads, int head_dim, size_t max_context, int page_tokens, int dtype,
+                     int device, bebelm_kv** out) {
+    if (!out) return fail(BEBELM_ERR_INVALID, "out is null");
+    *out = nullptr;
+    if (max_context == 0) return fail(BEBELM_ERR_INVALID, "max_context must be positive");
+    const size_t pages = (max_context + kPageTokens - 1) / kPageTokens + 2;
+    bebelm_kv_pool* P = nullptr;
+    TRY(pool_create(n_layers, n_kv_heads, head_dim, pages, page_tokens, dtype, device, &P));
+    int rc = seq_create(P, max_context, true, out);
+    if (rc) pool_free(P);
+    return rc;
+}
+
+int bebelm_kv_create_in_pool(bebelm_kv_pool* pool, size_t max_context, bebelm_kv** out) {
+    if (!pool) return fail(BEBELM_ERR_INVALID, "null pool");
+    return seq_create(pool, max_context, false, out);
+}
+
+int bebelm_kv_destroy(bebelm_kv* kv) {
+    if (!kv) return 0;
+    bebelm_kv_pool* P = kv->pool;
+    {
+        DeviceGuard g(P->device);
+        cudaDeviceSynchronize();  // kernels may still read the pages being returned
+        release_pages_below(kv, kv->hi);
+        cudaFree(kv->d_table);
+    }
+    P->n_seqs--;
+    const bool owns = kv->owns_pool;
+    delete kv;
+    if (owns) pool_free(P);
+    return 0;
+}
+
+int bebelm_kv_clone(const bebelm_kv* src, bebelm_kv** dst) {
+    TRY(validate_kv(src));
+    if (!dst) return fail(BEBELM_ERR_INVALID, "dst is null");
+    *dst = nullptr;
+    bebelm_kv_pool* SP = src->pool;
+    DeviceGuard g(SP->device);
+    bebelm_kv* kv = nullptr;
+    if (src->owns_pool) {
+        TRY(bebelm_kv_create(SP->n_layers, SP->n_kv, kHeadDim, src->max_context, kPageTokens, SP->dtype, SP->device,
+                             &kv));
+    } else {
+        TRY(seq_create(SP, src->max_context, false, &kv));
+    }
+    bebelm_kv_pool* DP = kv->pool;
+    const long long n = src->hi - src->lo;
+    if ((size_t)n > DP->free_list.size()) {
+        bebelm_kv_destroy(kv);
+        return fail(BEBELM_ERR_OOM, "page pool exhausted while cloning (%lld pages needed)", n);
+    }
+    kv->lo = src->lo;
+    kv->hi = src->hi;
+    kv->base = src->base;
+    kv->len = src->len;
+    kv->pos = src->pos;
+    const size_t page_bytes = SP->page_floats * sizeof(float);
+    for (long long L = src->lo; L < src->hi; ++L) {
+        const int phys = DP->free_list.back();
+        DP->free_list.pop_back();
+        kv->table[L % kv->cap] = phys;
+        const int sp = src->table[L % src->cap];
+        cudaError_t e = cudaMemcpyAsync(DP->mem + (size_t)phys * DP->page_floats, SP->mem + (size_t)sp * SP->page_floats,
+                                        page_bytes, cudaMemcpyDeviceToDevice, 0);
+        if (e != cudaSuccess) {
+            bebelm_kv_destroy(kv);
+            return fail(BEBELM_ERR_CUDA, "clone copy failed: %s", cudaGetErrorString(e));
+        }
+    }
+    int rc = upload_table(kv, kv->lo, kv->hi, 0);
+    if (rc == 0 && cudaDeviceSynchronize() != cudaSuccess) rc = fail(BEBELM_ERR_CUDA, "clone sync failed");
+    if (rc) {
+        bebelm_kv_destroy(kv);
+        return rc;
+    }
+    *dst = kv;
+    return 0;
+}
+
+int bebelm_kv_clear(bebelm_kv* kv) {
+    TRY(validate_kv(kv));
+    DeviceGuard g(kv->pool->device);
+    cudaDeviceSynchronize();
+    release_pages_below(kv, kv->hi);
+    kv->lo = kv->hi = 0;
+    std::fill(kv->base.begin(), kv->base.end(), 0);
+    std::fill(kv->len.begin(), kv->len.end(), 0);
+    kv->pos = 0;
+    return 0;
+}
+
+int bebelm_kv_len(const bebelm_kv* kv, size_t* out) {
+    TRY(validate_kv(kv));
+    if (!out) return fail(BEBELM_ERR_INVALID, "out is null");
+    long long m = 0;
+    for (long long l : kv->len) m = std::max(m, l);
+    *out = (size_t)m;
+    return 0;
+}
+
+int bebelm_kv_layer_len(const bebelm_kv* kv, int layer, size_t* out) {
+    TRY(validate_layer(kv, layer));
+    if (!out) return fail(BEBELM_ERR_INVALID, "out is null");
+    *out = (size_t)kv->len[layer];
+    return 0;
+}
+
+int bebelm_kv_pos(const bebelm_kv* kv, size_t* out) {
+    TRY(validate_kv(kv));
+    if (!out) return fail(BEBELM_ERR_INVALID, "out is null");
+    *out = kv->pos;
+    return 0;
+}
+
+int bebelm_kv_set_pos(bebelm_kv* kv, size_t pos) {
+    TRY(validate_kv(kv));
+    kv->pos = pos;
+    return 0;
+}
+
+int bebelm_kv_evict_front(bebelm_kv* kv, size_t n) {
+    TRY(validate_kv(kv));
+    for (size_t l = 0; l < kv->len.size(); ++l) {
+        if (kv->len[l] >= (long long)n) {  // layers shorter than n are left alone (src/cache.rs:43)
+            kv->base[l] += (long long)n;
+            kv->len[l] -= (long long)n;
+        }
+    }
+    recompute_lo(kv);
+    return 0;
+}
+
+int bebelm_kv_append(bebelm_kv* kv, int layer, const float* k, const float* v, size_t t, int mem, void* stream) {
+    TRY(validate_layer(kv, layer));
+    TRY(check_mem(mem));
+    if (t == 0) return 0;
+    if (!k || !v) return fail(BEBELM_ERR_INVALID, "k and v must be non-null");
+    bebelm_kv_pool* P = kv->pool;
+    DeviceGuard g(P->device);
+    cudaStream_t s = as_stream(stream);
+    const size_t row = (size_t)P->n_kv * kHeadDim;
+    const float *dk = k, *dv = v;
+    if (mem == BEBELM_MEM_HOST) {
+        void *pk = nullptr, *pv = nullptr;
+        Stage st[2] = {{k, sizeof(float) * row * t, &pk}, {v, sizeof(float) * row * t, &pv}};
+        TRY(stage_in(P, st, 2, 0, nullptr, s));
+        dk = static_cast<const float*>(pk);
+        dv = static_cast<const float*>(pv);
+    }
+    long long slot0 = 0;
+    TRY(reserve(kv, layer, t, &slot0, s));
+    NormRopeArgs a{};
+    a.k = dk;
+    a.v = dv;
+    a.T = (int)t;
+    a.n_heads = 0;
+    a.n_kv = P->n_kv;
+    a.head_dim = kHeadDim;
+    a.norm_k = 0;
+    a.append = 1;
+    a.pv = P->view(layer);
+    a.table = kv->d_table;
+    a.cap = kv->cap;
+    a.slot0 = slot0;
+    CUDA_TRY(launch_norm_rope(a, s));
+    if (mem == BEBELM_MEM_HOST) CUDA_TRY(cudaStreamSynchronize(s));
+    return 0;
+}
+
+int bebelm_kv_read(const bebelm_kv* kv, int layer, float* k_out, float* v_out, int mem, void* stream) {
+    TRY(validate_layer(kv, layer));
+    TRY(check_mem(mem));
+    bebelm_kv_pool* P = kv->pool;
+    DeviceGuard g(P->device);
+    cudaStream_t s = as_stream(stream);
+    const long long len = kv->len[layer];
+    const size_t bytes = sizeof(float) * (size_t)len * P->n_kv * kHeadDim;
+    if (len == 0) return 0;
+    if (mem == BEBELM_MEM_DEVICE) {
+        CUDA_TRY(launch_kv_gather(P->view(layer), kv->d_table, kv->cap, kv->base[layer], len, P->n_kv, k_out, v_out, s));
+        return 0;
+    }
+    void* dout = nullptr;
+    TRY(stage_in(P, nullptr, 0, 2 * bytes, &dout, s));
+    float* dk = static_cast<float*>(dout);
+    float* dv = dk + bytes / sizeof(float);
+    CUDA_TRY(launch_kv_gather(P->view(layer), kv->d_table, kv->cap, kv->base[layer], len, P->n_kv,
+                              k_out ? dk : nullptr, v_out ? dv : nullptr, s));
+    // stage_out copies one contiguous block: K then V
+    std::vector<float> both;
+    both.resize(2 * bytes / sizeof(float));
+    TRY(stage_out(P, dout, both.data(), 2 * bytes, s));
+    if (k_out) std::memcpy(k_out, both.data(), bytes);
+    if (v_out) std::memcpy(v_out, both.data() + bytes / sizeof(float), bytes);
+    return 0;
+}
+
+}  // extern "C"
+
+extern "C" {
+
+int bebelm_norm_rope_heads(float* buf, size_t n_tokens, int n_heads, int head_dim, const float* gain, size_t pos0,
+                           float theta, float eps, int mem, void* stream) {
+    TRY(check_mem(mem));
+    if (!buf || !gain) return fail(BEBELM_ERR_INVALID, "buf and gain must be non-null");
+    if (n_heads <= 0 || head_dim <= 0 || head_dim > 64 || head_dim % 2)
+        return fail(BEBELM_ERR_UNSUPPORTED, "head_dim must be even and in [2, 64] (got %d), n_heads > 0", head_dim);
+    if (n_tokens == 0) return 0;
+    int dev;
+    TRY(current_device(&dev));
+    cudaStream_t s = as_stream(stream);
+    const size_t n = n_tokens * (size_t)n_heads * head_dim;
+    NormRopeArgs a{};
+    a.T = (int)n_tokens;
+    a.n_heads = n_heads;
+    a.n_kv = 0;
+    a.head_dim = head_dim;
+    a.pos0 = (long long)pos0;
+    a.theta_scale = theta_scale_of(theta, head_dim);
+    a.eps = eps;
+    a.norm_q = 1;
+    if (mem == BEBELM_MEM_DEVICE) {
+        a.q = buf;
+        a.q_gain = gain;
+        a.q_out = buf;
+        CUDA_TRY(launch_norm_rope(a, s));
+        return 0;
+    }
+    std::lock_guard<std::mutex> lk(g_scratch_mu);
+    bebelm_kv_pool* P = nullptr;
+    TRY(scratch_pool(dev, &P));
+    void *dq = nullptr, *dg = nullptr, *dout = nullptr;
+    Stage st[2] = {{buf, sizeof(float) * n, &dq}, {gain, sizeof(float) * head_dim, &dg}};
+    TRY(stage_in(P, st, 2, sizeof(float) * n, &dout, s));
+    a.q = static_cast<const float*>(dq);
+    a.q_gain = static_cast<const float*>(dg);
+    a.q_out = static_cast<float*>(dout);
+    CUDA_TRY(launch_norm_rope(a, s));
+    return stage_out(P, dout, buf, sizeof(float) * n, s);
+}
+
+int bebelm_attn_decode_host(const float* q, const float* k, const float* v, size_t n_ctx, int n_heads, int n_kv_heads,
+                            int head_dim, float* out) {
+    TRY(check_geometry(n_heads, n_kv_heads));
+    if (head_dim <= 0 || head_dim > 64)
+        return fail(BEBELM_ERR_UNSUPPORTED, "head_dim must be in [1, 64] (got %d)", head_dim);
+    if (!q || !out || (n_ctx && (!k || !v))) return fail(BEBELM_ERR_INVALID, "null buffer");
+    const size_t hidden = (size_t)n_heads * head_dim;
+    if (n_ctx == 0) {  // softmax of nothing: the reference leaves zeros
+        std::memset(out, 0, sizeof(float) * hidden);
+        return 0;
+    }
+    int dev;
+    TRY(current_device(&dev));
+    // re-lay out to head_dim 64 (zero padding changes no dot product and no output column)
+    std::vector<float> qp((size_t)n_heads * 64, 0.f), kp, vp;
+    const float *kk = k, *vv = v, *qq = q;
+    if (head_dim != 64) {
+        kp.assign(n_ctx * n_kv_heads * 64, 0.f);
+        vp.assign(n_ctx * n_kv_heads * 64, 0.f);
+        for (size_t r = 0; r < n_ctx * (size_t)n_kv_heads; ++r) {
+            std::memcpy(&kp[r * 64], k + r * head_dim, sizeof(float) * head_dim);
+            std::memcpy(&vp[r * 64], v + r * head_dim, sizeof(float) * head_dim);
+        }
+        for (int h = 0; h < n_heads; ++h) std::memcpy(&qp[(size_t)h * 64], q + (size_t)h * head_dim, sizeof(float) * head_dim);
+        kk = kp.data();
+        vv = vp.data();
+        qq = qp.data();
+    }
+    bebelm_kv* kv = nullptr;
+    TRY(bebelm_kv_create(1, n_kv_heads, 64, n_ctx, kPageTokens, BEBELM_F32, dev, &kv));
+    int rc = bebelm_kv_append(kv, 0, kk, vv, n_ctx, BEBELM_MEM_HOST, nullptr);
+    if (rc == 0) {
+        bebelm_kv_pool* P = kv->pool;
+        void *dq = nullptr, *dout = nullptr;
+        Stage st[1] = {{qq, sizeof(float) * n_heads * 64, &dq}};
+        rc = stage_in(P, st, 1, sizeof(float) * n_heads * 64, &dout, 0);
+        if (rc == 0) {
+            std::vector<Window> w{{kv, kv->base[0], kv->len[0]}};
+            rc = run_decode(P, w, 0, n_heads, static_cast<const float*>(dq), static_cast<float*>(dout),
+                            1.0f / sqrtf((float)head_dim), 0);
+        }
+        if (rc == 0) rc = stage_out(P, dout, qp.data(), sizeof(float) * n_heads * 64, 0);
+        if (rc == 0)
+            for (int h = 0; h < n_heads; ++h)
+                std::memcpy(out + (size_t)h * head_dim, &qp[(size_t)h * 64], sizeof(float) * head_dim);
+    }
+    bebelm_kv_destroy(kv);
+    return rc;
+}
+
+int bebelm_attn_step(bebelm_kv* kv, int layer, int n_heads, const float* q, const float* k, const float* v,
+                     const float* q_gain, const float* k_gain, float theta, float eps, size_t pos, float* out, int mem,
+                     void* stream) {
+    TRY(validate_layer(kv, layer));
+    TRY(check_mem(mem));
+    bebelm_kv_pool* P = kv->pool;
+    TRY(check_geometry(n_heads, P->n_kv));
+    if (!q || !k || !v || !q_gain || !k_gain || !out) return fail(BEBELM_ERR_INVALID, "null buffer");
+    DeviceGuard g(P->device);
+    cudaStream_t s = as_stream(stream);
+    const size_t qn = (size_t)n_heads * kHeadDim, kvn = (size_t)P->n_kv * kHeadDim;
+    const float *dq = q, *dk = k, *dv = v, *dqg = q_gain, *dkg = k_gain;
+    float* dout = out;
+    if (mem == BEBELM_MEM_HOST) {
+        void *a0, *a1, *a2, *a3, *a4, *o;
+        Stage st[5] = {{q, 4 * qn, &a0}, {k, 4 * kvn, &a1}, {v, 4 * kvn, &a2}, {q_gain, 4 * 64, &a3}, {k_gain, 4 * 64, &a4}};
+        TRY(stage_in(P, st, 5, 4 * qn, &o, s));
+        dq = (const float*)a0; dk = (const float*)a1; dv = (const float*)a2;
+        dqg = (const float*)a3; dkg = (const float*)a4; dout = (float*)o;
+    }
+    long long slot0 = 0;
+    TRY(reserve(kv, layer, 1, &slot0, s));
+    TRY(P->qn.ensure(4 * qn, false, s));
+    NormRopeArgs a{};
+    a.q = dq; a.k = dk; a.v = dv; a.q_gain = dqg; a.k_gain = dkg;
+    a.T = 1; a.n_heads = n_heads; a.n_kv = P->n_kv; a.head_dim = kHeadDim;
+    a.pos0 = (long long)pos;
+    a.theta_scale = theta_scale_of(theta, kHeadDim);
+    a.eps = eps;
+    a.norm_q = 1; a.norm_k = 1;
+    a.q_out = P->qn.as<float>();
+    a.append = 1; a.pv = P->view(layer); a.table = kv->d_table; a.cap = kv->cap; a.slot0 = slot0;
+    CUDA_TRY(launch_norm_rope(a, s));
+    std::vector<Window> w{{kv, kv->base[layer], kv->len[layer]}};
+    TRY(run_decode(P, w, layer, n_heads, P->qn.as<float>(), dout, 0.125f, s));
+    if (mem == BEBELM_MEM_HOST) return stage_out(P, dout, out, 4 * qn, s);
+    return 0;
+}
+
+int bebelm_attn_decode_batched(bebelm_kv* const* seqs, int n_seqs, int layer, int n_heads, const float* q,
+                               const float* k, const float* v, const float* q_gain, const float* k_gain, float theta,
+                               float eps, const size_t* pos, float* out, int mem, void* stream) {
+    TRY(check_mem(mem));
+    if (!seqs || n_seqs <= 0 || !pos) return fail(BEBELM_ERR_INVALID, "need n_seqs > 0 sequences and positions");
+    bebelm_kv_pool* P = seqs[0] ? seqs[0]->pool : nullptr;
+    for (int i = 0; i < n_seqs; ++i) {
+        TRY(validate_layer(seqs[i], layer));
+        if (seqs[i]->pool != P) return fail(BEBELM_ERR_INVALID, "batched decode needs all sequences in one pool");
+        for (int j = 0; j < i; ++j)
+            if (seqs[j] == seqs[i]) return fail(BEBELM_ERR_INVALID, "sequence %d appears twice", i);
+    }
+    TRY(check_geometry(n_heads, P->n_kv));
+    if (!q || !k || !v || !q_gain || !k_gain || !out) return fail(BEBELM_ERR_INVALID, "null buffer");
+    DeviceGuard g(P->device);
+    cudaStream_t s = as_stream(stream);
+    const size_t qn = (size_t)n_heads * kHeadDim * n_seqs, kvn = (size_t)P->n_kv * kHeadDim * n_seqs;
+    const float *dq = q, *dk = k, *dv = v, *dqg = q_gain, *dkg = k_gain;
+    float* dout = out;
+    if (mem == BEBELM_MEM_HOST) {
+        void *a0, *a1, *a2, *a3, *a4, *o;
+        Stage st[5] = {{q, 4 * qn, &a0}, {k, 4 * kvn, &a1}, {v, 4 * kvn, &a2}, {q_gain, 4 * 64, &a3}, {k_gain, 4 * 64, &a4}};
+        TRY(stage_in(P, st, 5, 4 * qn, &o, s));
+        dq = (const float*)a0; dk = (const float*)a1; dv = (const float*)a2;
+        dqg = (const float*)a3; dkg = (const float*)a4; dout = (float*)o;
+    }
+    // capacity first for every sequence, so a failure leaves no window changed
+    for (int i = 0; i < n_seqs; ++i) {
+        const bebelm_kv* kv = seqs[i];
+        long long b = kv->base[layer], n = kv->len[layer];
+        if (n == 0 && b < kv->lo * kPageTokens) b = kv->lo * kPageTokens;
+        if ((b + n + 1 + kPageTokens - 1) / kPageTokens - kv->lo > kv->cap)
+            return fail(BEBELM_ERR_CAPACITY, "sequence %d is full: evict_front first", i);
+    }
+    std::vector<AppendTarget> tg(n_seqs);
+    std::vector<Window> w(n_seqs);
+    for (int i = 0; i < n_seqs; ++i) {
+        long long slot = 0;
+        TRY(reserve(seqs[i], layer, 1, &slot, s));
+        tg[i] = {seqs[i]->d_table, seqs[i]->cap, slot, (long long)pos[i]};
+        w[i] = {seqs[i], seqs[i]->base[layer], seqs[i]->len[layer]};
+    }
+    TRY(P->qn.ensure(4 * qn + sizeof(AppendTarget) * n_seqs + 256, false, s));
+    AppendTarget* dtg = reinterpret_cast<AppendTarget*>(P->qn.as<char>() + ((4 * qn + 255) & ~size_t(255)));
+    CUDA_TRY(cudaMemcpyAsync(dtg, tg.data(), sizeof(AppendTarget) * n_seqs, cudaMemcpyHostToDevice, s));
+    NormRopeArgs a{};
+    a.q = dq; a.k = dk; a.v = dv; a.q_gain = dqg; a.k_gain = dkg;
+    a.T = n_seqs; a.n_heads = n_heads; a.n_kv = P->n_kv; a.head_dim = kHeadDim;
+    a.theta_scale = theta_scale_of(theta, kHeadDim);
+    a.eps = eps;
+    a.norm_q = 1; a.norm_k = 1;
+    a.q_out = P->qn.as<float>();
+    a.append = 1; a.pv = P->view(layer); a.targets = dtg;
+    CUDA_TRY(launch_norm_rope(a, s));
+    TRY(run_decode(P, w, layer, n_heads, P->qn.as<float>(), dout, 0.125f, s));
+    if (mem == BEBELM_MEM_HOST) return stage_out(P, dout, out, 4 * qn, s);
+    return 0;
+}
+
+}  // extern "C"
+
+extern "C" {
+
+int bebelm_attn_prefill(bebelm_kv* kv, int layer, int n_heads, const void* q, const void* k, const void* v,
+                        int in_dtype, size_t t, size_t pos0, const float* q_gain, const float* k_gain, float theta,
+                        float eps, float* out, int mem, void* stream) {
+    TRY(validate_layer(kv, layer));
+    TRY(check_mem(mem));
+    bebelm_kv_pool* P = kv->pool;
+    TRY(check_geometry(n_heads, P->n_kv));
+    if (in_dtype != BEBELM_F32 && in_dtype != BEBELM_BF16)
+        return fail(BEBELM_ERR_UNSUPPORTED, "in_dtype must be BEBELM_F32 or BEBELM_BF16");
+    if (t == 0) return 0;
+    if (!q || !k || !v || !q_gain || !k_gain || !out) return fail(BEBELM_ERR_INVALID, "null buffer");
+    if (t > (size_t)INT32_MAX / (size_t)n_heads) return fail(BEBELM_ERR_INVALID, "t too large");
+    DeviceGuard g(P->device);
+    cudaStream_t s = as_stream(stream);
+    const size_t esz = in_dtype == BEBELM_F32 ? 4 : 2;
+    const size_t qn = (size_t)n_heads * kHeadDim * t, kvn = (size_t)P->n_kv * kHeadDim * t;
+    const void *dq = q, *dk = k, *dv = v;
+    const float *dqg = q_gain, *dkg = k_gain;
+    float* dout = out;
+    if (mem == BEBELM_MEM_HOST) {
+        void *a0, *a1, *a2, *a3, *a4, *o;
+        Stage st[5] = {{q, esz * qn, &a0}, {k, esz * kvn, &a1}, {v, esz * kvn, &a2}, {q_gain, 4 * 64, &a3}, {k_gain, 4 * 64, &a4}};
+        TRY(stage_in(P, st, 5, 4 * qn, &o, s));
+        dq = a0; dk = a1; dv = a2;
+        dqg = (const float*)a3; dkg = (const float*)a4; dout = (float*)o;
+    }
+    if (in_dtype == BEBELM_BF16) {
+        TRY(P->bf16.ensure(4 * (qn + 2 * kvn), false, s));
+        float* f = P->bf16.as<float>();
+        CUDA_TRY(launch_bf16_to_f32((const __nv_bfloat16*)dq, f, qn, s));
+        CUDA_TRY(launch_bf16_to_f32((const __nv_bfloat16*)dk, f + qn, kvn, s));
+        CUDA_TRY(launch_bf16_to_f32((const __nv_bfloat16*)dv, f + qn + kvn, kvn, s));
+        dq = f; dk = f + qn; dv = f + qn + kvn;
+    }
+    long long slot0 = 0;
+    TRY(reserve(kv, layer, t, &slot0, s));
+    const long long len_before = kv->len[layer] - (long long)t;
+    TRY(P->qn.ensure(4 * qn, false, s));
+    NormRopeArgs a{};
+    a.q = (const float*)dq; a.k = (const float*)dk; a.v = (const float*)dv; a.q_gain = dqg; a.k_gain = dkg;
+    a.T = (int)t; a.n_heads = n_heads; a.n_kv = P->n_kv; a.head_dim = kHeadDim;
+    a.pos0 = (long long)pos0;
+    a.theta_scale = theta_scale_of(theta, kHeadDim);
+    a.eps = eps;
+    a.norm_q = 1; a.norm_k = 1;
+    a.q_out = P->qn.as<float>();
+    a.append = 1; a.pv = P->view(layer); a.table = kv->d_table; a.cap = kv->cap; a.slot0 = slot0;
+    CUDA_TRY(launch_norm_rope(a, s));
+    // token i sees the window up to and including itself (src/model.rs:240-244)
+    std::vector<Window> w(t);
+    for (size_t i = 0; i < t; ++i) w[i] = {kv, kv->base[layer], len_before + (long long)i + 1};
+    TRY(run_decode(P, w, layer, n_heads, P->qn.as<float>(), dout, 0.125f, s));
+    if (mem == BEBELM_MEM_HOST) return stage_out(P, dout, out, 4 * qn, s);
+    return 0;
+}
+
+}  // extern "C"
+
+extern "C" {
+
+int bebelm_attn_decode_cached(const bebelm_kv* kv, int layer, int n_heads, const float* q, float* out, int mem,
+                              void* stream) {
+    TRY(validate_layer(kv, layer));
+    TRY(check_mem(mem));
+    bebelm_kv_pool* P = kv->pool;
+    TRY(check_geometry(n_heads, P->n_kv));
+    if (!q || !out) return fail(BEBELM_ERR_INVALID, "null buffer");
+    DeviceGuard g(P->device);
+    cudaStream_t s = as_stream(stream);
+    const size_t qn = (size_t)n_heads * kHeadDim;
+    const float* dq = q;
+    float* dout = out;
+    if (mem == BEBELM_MEM_HOST) {
+        void *a0, *o;
+        Stage st[1] = {{q, 4 * qn, &a0}};
+        TRY(stage_in(P, st, 1, 4 * qn, &o, s));
+        dq = (const float*)a0;
+        dout = (float*)o;
+    }
+    if (kv->len[layer] == 0) {
+        CUDA_TRY(cudaMemsetAsync(dout, 0, 4 * qn, s));
+    } else {
+        std::vector<Window> w{{kv, kv->base[layer], kv->len[layer]}};
+        TRY(run_decode(P, w, layer, n_heads, dq, dout, 0.125f, s));
+    }
+    if (mem == BEBELM_MEM_HOST) return stage_out(P, dout, out, 4 * qn, s);
+    return 0;
+}
+
+}  // extern "C"

@@ -1,0 +1,119 @@
+// Internal structures shared by the host runtime (api.cu) and the kernels.
+// Not part of the public ABI (include/bebelm_attn.h is).
+#pragma once
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace bebelm {
+
+constexpr int kHeadDim = 64;     // LFM2.5 head_dim (src/config.rs:20)
+constexpr int kPageTokens = 64;  // positions per KV page
+constexpr int kPageRowFloats = kPageTokens * kHeadDim;  // one kv head of one page: 4096 floats
+
+// Device-side view of the page pool for one layer. A physical page p holds, for
+// every layer l: K[l] then V[l], each [n_kv][64 tokens][64] fp32 (a "block").
+struct PoolView {
+    float* base;          // pool memory
+    size_t page_floats;   // floats per physical page (all layers, K and V)
+    size_t layer_off;     // floats from page start to this layer's K block
+    size_t block_floats;  // floats of one K (or V) block = n_kv * 4096
+};
+
+// A sequence's window for one layer: logical slots [base, base+len) live in
+// logical pages slot/64, mapped through a ring table of `cap` entries.
+struct SeqWindow {
+    const int* table;
+    int cap;
+    int len;
+    long long base;
+};
+
+__host__ __device__ inline size_t slot_offset(const PoolView& pv, const int* table, int cap,
+                                              long long slot, int kvh, int kind) {
+    long long lp = slot >> 6;
+    int phys = table[(int)(lp % cap)];
+    return (size_t)phys * pv.page_floats + pv.layer_off + (size_t)kind * pv.block_floats +
+           (size_t)kvh * kPageRowFloats + (size_t)(slot & 63) * kHeadDim;
+}
+
+// ---- kernel 1: per-head RMSNorm + NEOX RoPE (+ KV append) ------------------
+// Per-token destination when the tokens of one launch belong to different
+// sequences (batched decode): token i goes to slot `slot` of `table` at `pos`.
+struct AppendTarget {
+    const int* table;
+    int cap;
+    long long slot;
+    long long pos;
+};
+
+struct NormRopeArgs {
+    // inputs, token-major: q [T][n_heads][hd], k/v [T][n_kv][hd] (k, v may be null)
+    const float* q;
+    const float* k;
+    const float* v;
+    const float* q_gain;
+    const float* k_gain;
+    int T, n_heads, n_kv, head_dim;
+    long long pos0;
+    float theta_scale;  // powf(theta, -2/head_dim), computed on the host like the reference
+    float eps;
+    int norm_q;         // 1: q heads are normed+roped; 0: q passes through
+    int norm_k;         // 1: k heads are normed+roped; 0: k is appended raw
+    // outputs
+    float* q_out;            // [T][n_heads][hd] or null
+    float* k_out;            // [T][n_kv][hd] contiguous or null
+    __nv_bfloat16* q_bf16;   // optional bf16 copies [T][heads][64] for the prefill MMA
+    __nv_bfloat16* k_bf16;
+    __nv_bfloat16* v_bf16;
+    // optional cache append (head_dim == 64 only)
+    int append;
+    PoolView pv;
+    const int* table;
+    int cap;
+    long long slot0;  // logical slot of token 0
+    const AppendTarget* targets;  // non-null: per-token table/slot/pos instead of the above
+};
+cudaError_t launch_norm_rope(const NormRopeArgs& a, cudaStream_t s);
+
+// Copies a window [base, base+len) of one layer out of the pages, token-major
+// [len][n_kv][64] (either output may be null).
+cudaError_t launch_kv_gather(const PoolView& pv, const int* table, int cap, long long base, long long len,
+                             int n_kv, float* k_out, float* v_out, cudaStream_t s);
+// bf16 -> fp32, n elements.
+cudaError_t launch_bf16_to_f32(const __nv_bfloat16* in, float* out, size_t n, cudaStream_t s);
+
+// ---- kernel 3: split-K decode with fused combine ---------------------------
+struct DecodeSeq {
+    const int* table;
+    int cap;
+    int len;
+    long long base;
+    int split0;    // first global split of this sequence
+    int n_splits;  // splits of this sequence
+};
+
+struct DecodeArgs {
+    const DecodeSeq* seqs;  // device array [n_seqs] (unused when n_seqs == 1)
+    DecodeSeq one;          // the sequence itself when n_seqs == 1 (passed by value)
+    int n_seqs;
+    PoolView pv;
+    const float* q;         // [n_seqs][n_heads][64], normed + roped
+    float* out;             // [n_seqs][n_heads][64]
+    float* part_acc;        // [total_splits][n_kv*n_sub][hpc][64]
+    float* part_ml;         // [total_splits][n_kv*n_sub][hpc][2]
+    unsigned* counters;     // [n_seqs][n_kv*n_sub], zero between launches
+    int* err;               // device error word
+    int n_heads, n_kv, group, hpc, n_sub;
+    int pages_per_split;
+    int total_splits;
+    float scale_log2;       // score scale (1/sqrt(head_dim)) times log2(e)
+};
+cudaError_t launch_decode(const DecodeArgs& a, cudaStream_t s);
+size_t decode_smem_bytes();
+
+// device error codes written to DecodeArgs::err
+constexpr int kErrWaitTimeout = 1;
+
+}  // namespace bebelm

@@ -1,0 +1,217 @@
+// Kernel 1: fused per-head RMSNorm + NEOX RoPE (+ paged KV append).
+//
+// Restates, per head of one position:
+//   rmsnorm   src/kernels/rmsnorm.rs:10-21  (Σx² of f32 squares accumulated in f64,
+//             mean narrowed to f32, scale = 1/sqrtf(mean+eps), out = (x*scale)*g)
+//   rope_neox src/kernels/rope.rs:16-29     (split-half pairs, theta = pos, then
+//             theta *= theta_scale after each pair; accurate sinf/cosf)
+//   glue      src/model.rs:600-608 (norm_rope_heads) and the cache append of
+//             src/model.rs:443-444 / 241-242.
+// Every multiply/add that the reference performs unfused is written with the
+// round-to-nearest intrinsics so the compiler cannot contract it into an FMA;
+// with IEEE division and square root the only rounding differences left are
+// those of sinf/cosf (a few ulp) and the f64 summation order (invisible after
+// narrowing in practice).
+//
+// Mapping: 8 lanes per head (4 heads per warp). Lane `sub` owns pairs
+// 4*sub .. 4*sub+3, i.e. elements x[4sub..4sub+3] and x[half+4sub..+3]; for
+// head_dim 64 these are two float4 loads and two 128-bit stores per lane, so a
+// head row moves as 256 contiguous bytes.
+#include <algorithm>
+
+#include "internal.h"
+
+namespace bebelm {
+namespace {
+
+template <bool HD64>
+__global__ void __launch_bounds__(256) norm_rope_kernel(NormRopeArgs a) {
+    const int lane = threadIdx.x & 31;
+    const int sub = lane & 7;
+    const int nh_all = a.n_heads + a.n_kv;
+    const long long total = (long long)a.T * nh_all;
+    long long item = (long long)blockIdx.x * (blockDim.x >> 3) + (threadIdx.x >> 3);
+    const bool active = item < total;
+    if (!active) item = total - 1;  // keep the 8-lane group converged for the shuffles
+
+    const int hd = HD64 ? 64 : a.head_dim;
+    const int half = hd >> 1;
+    const int tok = (int)(item / nh_all);
+    const int hh = (int)(item % nh_all);
+    const bool is_q = hh < a.n_heads;
+    const int head = is_q ? hh : hh - a.n_heads;
+    const float* src = is_q ? a.q + ((size_t)tok * a.n_heads + head) * hd
+                            : a.k + ((size_t)tok * a.n_kv + head) * hd;
+    const float* gain = is_q ? a.q_gain : a.k_gain;
+    const bool do_norm = is_q ? (a.norm_q != 0) : (a.norm_k != 0);
+
+    float x0[4], x1[4];
+    if (HD64) {
+        float4 u = *reinterpret_cast<const float4*>(src + 4 * sub);
+        float4 w = *reinterpret_cast<const float4*>(src + 32 + 4 * sub);
+        x0[0] = u.x; x0[1] = u.y; x0[2] = u.z; x0[3] = u.w;
+        x1[0] = w.x; x1[1] = w.y; x1[2] = w.z; x1[3] = w.w;
+    } else {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            int i = 4 * sub + e;
+            x0[e] = i < half ? src[i] : 0.f;
+            x1[e] = i < half ? src[i + half] : 0.f;
+        }
+    }
+
+    if (do_norm) {
+        double ss = 0.0;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            ss += (double)__fmul_rn(x0[e], x0[e]);
+            ss += (double)__fmul_rn(x1[e], x1[e]);
+        }
+        ss += __shfl_xor_sync(0xffffffffu, ss, 1);
+        ss += __shfl_xor_sync(0xffffffffu, ss, 2);
+        ss += __shfl_xor_sync(0xffffffffu, ss, 4);
+        const float mean = __double2float_rn(ss / (double)hd);
+        const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, a.eps)));
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            int i = 4 * sub + e;
+            if (HD64 || i < half) {
+                x0[e] = __fmul_rn(__fmul_rn(x0[e], scale), gain[i]);
+                x1[e] = __fmul_rn(__fmul_rn(x1[e], scale), gain[i + half]);
+            }
+        }
+        const long long pos = a.targets ? a.targets[tok].pos : a.pos0 + tok;
+        float theta = __ll2float_rn(pos);
+        for (int t = 0; t < 4 * sub && t < half; ++t) theta = __fmul_rn(theta, a.theta_scale);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            int i = 4 * sub + e;
+            if (HD64 || i < half) {
+                const float sn = sinf(theta), cs = cosf(theta);
+                const float p = x0[e], q = x1[e];
+                x0[e] = __fsub_rn(__fmul_rn(p, cs), __fmul_rn(q, sn));
+                x1[e] = __fadd_rn(__fmul_rn(p, sn), __fmul_rn(q, cs));
+                theta = __fmul_rn(theta, a.theta_scale);
+            }
+        }
+    }
+    if (!active) return;
+
+    float* dst = nullptr;
+    if (is_q) {
+        dst = a.q_out ? a.q_out + ((size_t)tok * a.n_heads + head) * hd : nullptr;
+    } else {
+        dst = a.k_out ? a.k_out + ((size_t)tok * a.n_kv + head) * hd : nullptr;
+    }
+    if (dst) {
+        if (HD64) {
+            *reinterpret_cast<float4*>(dst + 4 * sub) = make_float4(x0[0], x0[1], x0[2], x0[3]);
+            *reinterpret_cast<float4*>(dst + 32 + 4 * sub) = make_float4(x1[0], x1[1], x1[2], x1[3]);
+        } else {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                int i = 4 * sub + e;
+                if (i < half) {
+                    dst[i] = x0[e];
+                    dst[i + half] = x1[e];
+                }
+            }
+        }
+    }
+    if (!HD64) return;
+
+    // bf16 copies for the tensor-core prefill
+    __nv_bfloat16* bdst = is_q ? (a.q_bf16 ? a.q_bf16 + ((size_t)tok * a.n_heads + head) * 64 : nullptr)
+                               : (a.k_bf16 ? a.k_bf16 + ((size_t)tok * a.n_kv + head) * 64 : nullptr);
+    if (bdst) {
+        __nv_bfloat162 b0 = __floats2bfloat162_rn(x0[0], x0[1]), b1 = __floats2bfloat162_rn(x0[2], x0[3]);
+        __nv_bfloat162 b2 = __floats2bfloat162_rn(x1[0], x1[1]), b3 = __floats2bfloat162_rn(x1[2], x1[3]);
+        uint2 lo, hi;
+        lo.x = *reinterpret_cast<uint32_t*>(&b0); lo.y = *reinterpret_cast<uint32_t*>(&b1);
+        hi.x = *reinterpret_cast<uint32_t*>(&b2); hi.y = *reinterpret_cast<uint32_t*>(&b3);
+        *reinterpret_cast<uint2*>(bdst + 4 * sub) = lo;
+        *reinterpret_cast<uint2*>(bdst + 32 + 4 * sub) = hi;
+    }
+    if (is_q) return;
+
+    // V row of the same kv head passes through unchanged
+    const float* vsrc = a.v ? a.v + ((size_t)tok * a.n_kv + head) * 64 : nullptr;
+    float4 v0 = make_float4(0.f, 0.f, 0.f, 0.f), v1 = v0;
+    if (vsrc) {
+        v0 = *reinterpret_cast<const float4*>(vsrc + 4 * sub);
+        v1 = *reinterpret_cast<const float4*>(vsrc + 32 + 4 * sub);
+    }
+    if (a.v_bf16 && vsrc) {
+        __nv_bfloat16* vb = a.v_bf16 + ((size_t)tok * a.n_kv + head) * 64;
+        __nv_bfloat162 b0 = __floats2bfloat162_rn(v0.x, v0.y), b1 = __floats2bfloat162_rn(v0.z, v0.w);
+        __nv_bfloat162 b2 = __floats2bfloat162_rn(v1.x, v1.y), b3 = __floats2bfloat162_rn(v1.z, v1.w);
+        uint2 lo, hi;
+        lo.x = *reinterpret_cast<uint32_t*>(&b0); lo.y = *reinterpret_cast<uint32_t*>(&b1);
+        hi.x = *reinterpret_cast<uint32_t*>(&b2); hi.y = *reinterpret_cast<uint32_t*>(&b3);
+        *reinterpret_cast<uint2*>(vb + 4 * sub) = lo;
+        *reinterpret_cast<uint2*>(vb + 32 + 4 * sub) = hi;
+    }
+    if (a.append) {
+        const int* table = a.targets ? a.targets[tok].table : a.table;
+        const int cap = a.targets ? a.targets[tok].cap : a.cap;
+        const long long slot = a.targets ? a.targets[tok].slot : a.slot0 + tok;
+        float* kd = a.pv.base + slot_offset(a.pv, table, cap, slot, head, 0);
+        float* vd = a.pv.base + slot_offset(a.pv, table, cap, slot, head, 1);
+        *reinterpret_cast<float4*>(kd + 4 * sub) = make_float4(x0[0], x0[1], x0[2], x0[3]);
+        *reinterpret_cast<float4*>(kd + 32 + 4 * sub) = make_float4(x1[0], x1[1], x1[2], x1[3]);
+        *reinterpret_cast<float4*>(vd + 4 * sub) = v0;
+        *reinterpret_cast<float4*>(vd + 32 + 4 * sub) = v1;
+    }
+}
+
+// One warp per (token, kv head) row: 16 lanes x float4 for K, then for V.
+__global__ void __launch_bounds__(256) kv_gather_kernel(PoolView pv, const int* table, int cap, long long base,
+                                                        long long len, int n_kv, float* k_out, float* v_out) {
+    const long long row = (long long)blockIdx.x * 8 + (threadIdx.x >> 5);
+    if (row >= len * n_kv) return;
+    const int lane = threadIdx.x & 31;
+    const long long t = row / n_kv;
+    const int h = (int)(row % n_kv);
+    const int kind = lane >> 4;  // lanes 0-15: K, 16-31: V
+    float* dst = kind ? v_out : k_out;
+    if (!dst) return;
+    const float* src = pv.base + slot_offset(pv, table, cap, base + t, h, kind);
+    const int e = (lane & 15) * 4;
+    *reinterpret_cast<float4*>(dst + (size_t)row * 64 + e) = *reinterpret_cast<const float4*>(src + e);
+}
+
+__global__ void bf16_to_f32_kernel(const __nv_bfloat16* in, float* out, size_t n) {
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+        out[i] = __bfloat162float(in[i]);
+}
+
+}  // namespace
+
+cudaError_t launch_kv_gather(const PoolView& pv, const int* table, int cap, long long base, long long len,
+                             int n_kv, float* k_out, float* v_out, cudaStream_t s) {
+    const long long rows = len * n_kv;
+    if (rows <= 0) return cudaSuccess;
+    kv_gather_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, s>>>(pv, table, cap, base, len, n_kv, k_out, v_out);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_bf16_to_f32(const __nv_bfloat16* in, float* out, size_t n, cudaStream_t s) {
+    if (!n) return cudaSuccess;
+    size_t blocks = std::min<size_t>((n + 255) / 256, 148 * 16);
+    bf16_to_f32_kernel<<<(unsigned)blocks, 256, 0, s>>>(in, out, n);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_norm_rope(const NormRopeArgs& a, cudaStream_t s) {
+    const long long items = (long long)a.T * (a.n_heads + a.n_kv);
+    if (items <= 0) return cudaSuccess;
+    const int heads_per_block = 256 / 8;
+    const long long blocks = (items + heads_per_block - 1) / heads_per_block;
+    if (a.head_dim == 64)
+        norm_rope_kernel<true><<<(unsigned)blocks, 256, 0, s>>>(a);
+    else
+        norm_rope_kernel<false><<<(unsigned)blocks, 256, 0, s>>>(a);
+    return cudaGetLastError();
+}
+
+}  // namespace bebelm

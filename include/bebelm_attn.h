@@ -1,0 +1,170 @@
+/*
+ * bebelm_attn.h — C-ABI of the B200 (sm_100a) attention library for BebeLM.
+ *
+ * Replaces the grouped-query attention hot path of the reference Rust crate
+ * (maximecb/bebelm 0.3.6): the per-head q/k RMSNorm + NEOX RoPE, the KV-cache
+ * append, single-query decode attention, the per-token causal prefill loop, and
+ * the host `Cache` type those read. Each entry point names the reference
+ * interface it stands in for.
+ *
+ * Conventions
+ *  - Every function returns int: 0 on success, a negative BEBELM_ERR_* code on
+ *    failure; bebelm_last_error() returns the message of the calling thread's
+ *    last failure. No C++ exception crosses this boundary.
+ *  - `mem` says where the float buffers of a call live: BEBELM_MEM_HOST (any
+ *    host memory; the call copies through pinned staging and synchronises the
+ *    stream before returning) or BEBELM_MEM_DEVICE (device pointers on the
+ *    handle's GPU; the call only enqueues work on `stream`).
+ *  - `stream` is a cudaStream_t passed as void*; NULL means the legacy default
+ *    stream of the current thread.
+ *  - Handles are opaque. Calls on one handle (or on sequences of one pool) are
+ *    not thread-safe and must be ordered on one stream: they share the pool's
+ *    scratch memory.
+ *  - Geometry: head_dim <= 64 for the drop-ins (padded to 64 internally);
+ *    caches and fused calls take head_dim == 64 and page_tokens == 64.
+ *    n_heads must be a multiple of n_kv_heads (GQA group = n_heads/n_kv_heads).
+ */
+#ifndef BEBELM_ATTN_H
+#define BEBELM_ATTN_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define BEBELM_API __attribute__((visibility("default")))
+#else
+#define BEBELM_API
+#endif
+
+#define BEBELM_ABI_VERSION 1
+
+enum {
+    BEBELM_OK = 0,
+    BEBELM_ERR_INVALID = -1,     /* bad argument, geometry or handle */
+    BEBELM_ERR_CUDA = -2,        /* a CUDA runtime call failed */
+    BEBELM_ERR_OOM = -3,         /* device or pinned allocation failed */
+    BEBELM_ERR_CAPACITY = -4,    /* the window would exceed the cache's capacity */
+    BEBELM_ERR_UNSUPPORTED = -5, /* geometry/dtype this build does not implement */
+    BEBELM_ERR_TIMEOUT = -7,     /* a bounded device-side wait gave up */
+    BEBELM_ERR_NO_DEVICE = -8    /* no CUDA device, or the device is not sm_100 */
+};
+
+enum { BEBELM_MEM_HOST = 0, BEBELM_MEM_DEVICE = 1 };
+enum { BEBELM_F32 = 0, BEBELM_BF16 = 1 };
+
+typedef struct bebelm_kv_pool bebelm_kv_pool; /* device page pool + scratch */
+typedef struct bebelm_kv bebelm_kv;           /* one sequence's KV window */
+
+/* ---------------------------------------------------------------- misc --- */
+BEBELM_API int bebelm_abi_version(void);
+/* Copies the calling thread's last error message (NUL-terminated, truncated to n). */
+BEBELM_API int bebelm_last_error(char* buf, size_t n);
+/* Number of visible sm_100 devices. */
+BEBELM_API int bebelm_device_count(int* n);
+
+/* ------------------------------------------------------------ drop-ins --- */
+/* Replaces `attention_decode(q, k, v, n_ctx, n_heads, n_kv_heads, head_dim, out)`
+ * (src/kernels/attention.rs:17-26). Host buffers: q/out [n_heads*head_dim],
+ * k/v token-major [n_ctx][n_kv_heads][head_dim]. Copies K/V to the current
+ * device each call, so it serves parity tests and one-off calls; the
+ * cache-resident path is bebelm_attn_step. n_ctx == 0 writes zeros. */
+BEBELM_API int bebelm_attn_decode_host(const float* q, const float* k, const float* v, size_t n_ctx,
+                            int n_heads, int n_kv_heads, int head_dim, float* out);
+
+/* Replaces `norm_rope_heads(buf, n_heads, gain, pos)` (src/model.rs:600-608),
+ * i.e. `rmsnorm` (src/kernels/rmsnorm.rs:10-21) then `rope_neox`
+ * (src/kernels/rope.rs:16-29) per head, in place, for n_tokens consecutive
+ * positions pos0, pos0+1, ... buf is [n_tokens][n_heads][head_dim]. head_dim
+ * even and <= 64. The reference fixes theta = 5e6 and eps = 1e-5
+ * (src/config.rs:31-32); both are arguments here. */
+BEBELM_API int bebelm_norm_rope_heads(float* buf, size_t n_tokens, int n_heads, int head_dim,
+                           const float* gain, size_t pos0, float theta, float eps, int mem,
+                           void* stream);
+
+/* ------------------------------------------------------------- KV cache --- */
+/* Device replacement for `Cache` (src/cache.rs:9-49), attention layers only.
+ * Storage is paged: a page holds `page_tokens` (64) positions of K and V for
+ * every attention layer, laid out [layer][K|V][kv_head][token][64] in fp32.
+ * A sequence's window is a ring of pages, so evict_front (the sliding window
+ * of src/agent.rs:471-476) moves an offset and recycles whole pages instead of
+ * moving memory. A window holds at most max_context + page_tokens positions
+ * per layer; beyond that appends fail with BEBELM_ERR_CAPACITY. */
+BEBELM_API int bebelm_kv_pool_create(int n_layers, int n_kv_heads, int head_dim, size_t n_pages,
+                          int page_tokens, int dtype, int device, bebelm_kv_pool** out);
+BEBELM_API int bebelm_kv_pool_destroy(bebelm_kv_pool* pool);
+BEBELM_API int bebelm_kv_pool_free_pages(const bebelm_kv_pool* pool, size_t* out);
+
+/* `Cache::new()` (src/cache.rs:22-29): a sequence with its own private pool. */
+BEBELM_API int bebelm_kv_create(int n_layers, int n_kv_heads, int head_dim, size_t max_context,
+                     int page_tokens, int dtype, int device, bebelm_kv** out);
+/* A sequence drawing pages from a shared pool (batched decode requires this). */
+BEBELM_API int bebelm_kv_create_in_pool(bebelm_kv_pool* pool, size_t max_context, bebelm_kv** out);
+BEBELM_API int bebelm_kv_destroy(bebelm_kv* kv);
+/* `#[derive(Clone)]` on Cache (src/cache.rs:9; Agent fork, src/agent.rs:92):
+ * a deep copy. A private-pool sequence clones into a new private pool; a
+ * shared-pool sequence clones into new pages of the same pool. */
+BEBELM_API int bebelm_kv_clone(const bebelm_kv* src, bebelm_kv** dst);
+/* `Agent::clear` replacing the cache with `Cache::new()` (src/agent.rs:479-483). */
+BEBELM_API int bebelm_kv_clear(bebelm_kv* kv);
+/* `Cache::kv_len` (src/cache.rs:33-35): longest layer window, in positions. */
+BEBELM_API int bebelm_kv_len(const bebelm_kv* kv, size_t* out);
+BEBELM_API int bebelm_kv_layer_len(const bebelm_kv* kv, int layer, size_t* out);
+/* `Cache::pos` (src/cache.rs:18): the next token's absolute position. */
+BEBELM_API int bebelm_kv_pos(const bebelm_kv* kv, size_t* out);
+BEBELM_API int bebelm_kv_set_pos(bebelm_kv* kv, size_t pos);
+/* `Cache::evict_front(n)` (src/cache.rs:40-48): drop the oldest n positions of
+ * every layer holding at least n; pos is not rewound. */
+BEBELM_API int bebelm_kv_evict_front(bebelm_kv* kv, size_t n);
+/* `cache.k[layer].extend_from_slice(k)` + same for v (src/model.rs:443-444,
+ * 241-242): append t positions of already-normed/roped k and raw v,
+ * token-major [t][n_kv_heads][head_dim]. */
+BEBELM_API int bebelm_kv_append(bebelm_kv* kv, int layer, const float* k, const float* v, size_t t,
+                     int mem, void* stream);
+/* Reads layer's window back token-major [len][n_kv_heads][head_dim] (what
+ * `cache.k[layer]` / `cache.v[layer]` hold in the reference). Either pointer
+ * may be NULL. */
+BEBELM_API int bebelm_kv_read(const bebelm_kv* kv, int layer, float* k_out, float* v_out, int mem,
+                   void* stream);
+
+/* ----------------------------------------------------------- fused ops --- */
+/* The middle of `attn_step` (src/model.rs:440-451): q/k norm + RoPE at `pos`,
+ * append k and v to layer's window, single-query GQA attention over the whole
+ * window. q [n_heads*64], k/v [n_kv_heads*64], gains [64], out [n_heads*64].
+ * q is not modified (the reference's in-place q is an internal temporary). */
+BEBELM_API int bebelm_attn_step(bebelm_kv* kv, int layer, int n_heads, const float* q, const float* k,
+                     const float* v, const float* q_gain, const float* k_gain, float theta,
+                     float eps, size_t pos, float* out, int mem, void* stream);
+
+/* `attention_decode` (src/kernels/attention.rs:17-55) over layer's cached
+ * window without appending: q [n_heads*64] already normed and roped (as the
+ * reference's q is when it reaches attention_decode), out [n_heads*64]. This is
+ * the call a Rust `attention_decode` shim makes once K/V live on the device. */
+BEBELM_API int bebelm_attn_decode_cached(const bebelm_kv* kv, int layer, int n_heads, const float* q, float* out,
+                                         int mem, void* stream);
+
+/* The middle of `attn_batch` (src/model.rs:232-254): t tokens at positions
+ * pos0.. are normed/roped, appended, and each attends causally to the window
+ * up to and including itself. q [t][n_heads*64], k/v [t][n_kv_heads*64] in
+ * `in_dtype` (BEBELM_F32 or BEBELM_BF16); out [t][n_heads*64] fp32. The
+ * attention runs on the tensor cores in bf16 with fp32 accumulation. */
+BEBELM_API int bebelm_attn_prefill(bebelm_kv* kv, int layer, int n_heads, const void* q, const void* k,
+                        const void* v, int in_dtype, size_t t, size_t pos0,
+                        const float* q_gain, const float* k_gain, float theta, float eps,
+                        float* out, int mem, void* stream);
+
+/* Batched decode across independent sequences (one Agent each) that share one
+ * pool: for sequence i, the attn_step of its token at pos[i]. q [n][n_heads*64],
+ * k/v [n][n_kv_heads*64], out [n][n_heads*64]; pos is a host array. */
+BEBELM_API int bebelm_attn_decode_batched(bebelm_kv* const* seqs, int n_seqs, int layer, int n_heads,
+                               const float* q, const float* k, const float* v,
+                               const float* q_gain, const float* k_gain, float theta, float eps,
+                               const size_t* pos, float* out, int mem, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* BEBELM_ATTN_H */
