@@ -32,6 +32,7 @@ constexpr int kStages = 3;
 constexpr int kThreads = 128;
 constexpr int kStageBytes = 2 * kPageRowFloats * 4;  // K + V rows of one page, one kv head
 constexpr long long kWaitLimit = 1ll << 22;          // try_wait polls before giving up
+constexpr int kPrefetch = 2;                          // pages prefetched into L2 beyond the ring
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -75,12 +76,18 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, unsigned by
 
 __device__ __forceinline__ float fast_exp2(float x) { return exp2f(x); }
 
+__device__ __forceinline__ void bulk_prefetch_l2(const void* src, unsigned bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
 template <int HPC>
 __global__ void __launch_bounds__(kThreads, 2) decode_kernel(DecodeArgs a) {
     extern __shared__ __align__(128) unsigned char smem[];
     float* stages = reinterpret_cast<float*>(smem);
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes);
     __shared__ float s_m[4][HPC], s_l[4][HPC];
+    __shared__ int s_release[kStages];
+    __shared__ int s_failed;
     __shared__ int s_last;
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -107,24 +114,35 @@ __global__ void __launch_bounds__(kThreads, 2) decode_kernel(DecodeArgs a) {
     if (p1 > last_page + 1) p1 = last_page + 1;
     const int np = p1 > p0 ? (int)(p1 - p0) : 0;
 
-    auto issue = [&](int i) {
-        const int st = i % kStages;
+    auto page_src = [&](int i) -> const float* {
         const long long lp = p0 + i;
         const int phys = S.table[(int)(lp % S.cap)];
-        const float* kp = a.pv.base + (size_t)phys * a.pv.page_floats + a.pv.layer_off +
-                          (size_t)kvh * kPageRowFloats;
-        const float* vp = kp + a.pv.block_floats;
+        return a.pv.base + (size_t)phys * a.pv.page_floats + a.pv.layer_off + (size_t)kvh * kPageRowFloats;
+    };
+    auto issue = [&](int i) {
+        const int st = i % kStages;
+        const float* kp = page_src(i);
         float* dk = stages + (size_t)st * (2 * kPageRowFloats);
         mbar_expect_tx(&full[st], kStageBytes);
         bulk_g2s(dk, kp, kPageRowFloats * 4, &full[st]);
-        bulk_g2s(dk + kPageRowFloats, vp, kPageRowFloats * 4, &full[st]);
+        bulk_g2s(dk + kPageRowFloats, kp + a.pv.block_floats, kPageRowFloats * 4, &full[st]);
+    };
+    auto prefetch = [&](int i) {
+        const float* kp = page_src(i);
+        bulk_prefetch_l2(kp, kPageRowFloats * 4);
+        bulk_prefetch_l2(kp + a.pv.block_floats, kPageRowFloats * 4);
     };
 
     if (tid == 0) {
-        for (int s = 0; s < kStages; ++s) mbar_init(&full[s], 1);
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(&full[s], 1);
+            s_release[s] = 0;
+        }
+        s_failed = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         for (int i = 0; i < kStages && i < np; ++i) issue(i);
+        for (int i = kStages; i < kStages + kPrefetch && i < np; ++i) prefetch(i);
     }
 
     // q slice of this lane, pre-rotated so register index i pairs with chunk c_i
@@ -150,18 +168,16 @@ __global__ void __launch_bounds__(kThreads, 2) decode_kernel(DecodeArgs a) {
     __syncthreads();
 
     const long long win_lo = S.base, win_hi = S.base + S.len;
+    int consumed = 0;  // pages this warp finished (the rest are still owed to the ring)
     for (int i = 0; i < np; ++i) {
         const int st = i % kStages;
-        const bool ok = mbar_wait_bounded(&full[st], (unsigned)((i / kStages) & 1));
-        if (__syncthreads_or(!ok)) {
-            // give up: record, drain our own copies still in flight, return
-            if (tid == 0) {
+        const bool ok = __all_sync(0xffffffffu, mbar_wait_bounded(&full[st], (unsigned)((i / kStages) & 1)));
+        if (!ok) {
+            if (lane == 0) {
                 atomicExch(a.err, kErrWaitTimeout);
-                const int issued = np < i + kStages ? np : i + kStages;
-                for (int k = i; k < issued; ++k)
-                    mbar_wait_bounded(&full[k % kStages], (unsigned)((k / kStages) & 1));
+                atomicExch(&s_failed, 1);
             }
-            return;
+            break;
         }
         const float4* Ks = reinterpret_cast<const float4*>(stages + (size_t)st * (2 * kPageRowFloats));
         const float4* Vs = Ks + kPageRowFloats / 4;
@@ -191,6 +207,23 @@ __global__ void __launch_bounds__(kThreads, 2) decode_kernel(DecodeArgs a) {
                 s[r][h] = valid ? d * a.scale_log2 : -INFINITY;
             }
         }
+        float4 vv[2][4];
+#pragma unroll
+        for (int r = 0; r < 2; ++r)
+#pragma unroll
+            for (int ii = 0; ii < 4; ++ii) vv[r][ii] = Vs[(16 * warp + 8 * r + j) * 16 + c[ii]];
+        // V is in registers: this warp is done with the stage
+        __syncwarp();
+        if (lane == 0) {
+            if (atomicAdd(&s_release[st], 1) == 3) {  // last of the 4 warps refills the stage
+                s_release[st] = 0;
+                if (i + kStages < np) {
+                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                    issue(i + kStages);
+                    if (i + kStages + kPrefetch < np) prefetch(i + kStages + kPrefetch);
+                }
+            }
+        }
         float pr[2][HPC];
 #pragma unroll
         for (int h = 0; h < HPC; ++h) {
@@ -212,34 +245,42 @@ __global__ void __launch_bounds__(kThreads, 2) decode_kernel(DecodeArgs a) {
         }
 #pragma unroll
         for (int r = 0; r < 2; ++r) {
-            const int row = 16 * warp + 8 * r + j;
-            float4 vv[4];
-#pragma unroll
-            for (int ii = 0; ii < 4; ++ii) vv[ii] = Vs[row * 16 + c[ii]];
 #pragma unroll
             for (int h = 0; h < HPC; ++h) {
                 const float w = pr[r][h];
 #pragma unroll
                 for (int ii = 0; ii < 4; ++ii) {
-                    acc[h][4 * ii + 0] = fmaf(w, vv[ii].x, acc[h][4 * ii + 0]);
-                    acc[h][4 * ii + 1] = fmaf(w, vv[ii].y, acc[h][4 * ii + 1]);
-                    acc[h][4 * ii + 2] = fmaf(w, vv[ii].z, acc[h][4 * ii + 2]);
-                    acc[h][4 * ii + 3] = fmaf(w, vv[ii].w, acc[h][4 * ii + 3]);
+                    acc[h][4 * ii + 0] = fmaf(w, vv[r][ii].x, acc[h][4 * ii + 0]);
+                    acc[h][4 * ii + 1] = fmaf(w, vv[r][ii].y, acc[h][4 * ii + 1]);
+                    acc[h][4 * ii + 2] = fmaf(w, vv[r][ii].z, acc[h][4 * ii + 2]);
+                    acc[h][4 * ii + 3] = fmaf(w, vv[r][ii].w, acc[h][4 * ii + 3]);
                 }
             }
         }
-        __syncthreads();  // every warp is done with stage st
-        if (tid == 0 && i + kStages < np) issue(i + kStages);
+        consumed = i + 1;
+    }
+    (void)consumed;
+    __syncthreads();
+    if (s_failed) {
+        // a wait gave up: let our own copies still in flight land (bounded), then leave
+        if (tid == 0) {
+            for (int k = 0; k < kStages && k < np; ++k) {
+                // the newest issue into stage k is the largest page index < np with index % kStages == k
+                const int last = ((np - 1 - k) / kStages) * kStages + k;
+                mbar_wait_bounded(&full[k], (unsigned)((last / kStages) & 1));
+            }
+        }
+        return;
     }
 
-    // ---- merge the 32 row-lanes x 4 warps of this CTA --------------------
+    // ---- merge the 8 row-lanes x 4 warps of this CTA ----------------------
 #pragma unroll
     for (int h = 0; h < HPC; ++h) {
         l[h] += __shfl_xor_sync(0xffffffffu, l[h], 4);
         l[h] += __shfl_xor_sync(0xffffffffu, l[h], 8);
         l[h] += __shfl_xor_sync(0xffffffffu, l[h], 16);
     }
-    float* red = stages;  // [4 warps][8 j][HPC][64]; the ring is idle now
+    float* red = stages;  // [4 warps][8 j][HPC][64]; every copy has landed and been read
 #pragma unroll
     for (int h = 0; h < HPC; ++h) {
         float* dst = red + ((size_t)(warp * 8 + j) * HPC + h) * kHeadDim;
@@ -297,35 +338,60 @@ __global__ void __launch_bounds__(kThreads, 2) decode_kernel(DecodeArgs a) {
     __syncthreads();
     if (!s_last) return;
     __threadfence();
+    const int ns = S.n_splits;
+    // split maxima and sums into shared memory (one load per thread, all in flight at once)
+    float* sm_m = red;                  // [ns][HPC]
+    float* sm_l = red + ns * HPC;       // [ns][HPC]
+    for (int x = tid; x < ns * HPC; x += kThreads) {
+        const size_t pi = ((size_t)(S.split0 + x / HPC) * NY + y) * HPC + (x % HPC);
+        sm_m[x] = __ldcg(a.part_ml + pi * 2);
+        sm_l[x] = __ldcg(a.part_ml + pi * 2 + 1);
+    }
+    __syncthreads();
+    __shared__ float s_L[HPC];
+    if (tid < HPC) {
+        float M = -INFINITY;
+        for (int k = 0; k < ns; ++k) M = fmaxf(M, sm_m[k * HPC + tid]);
+        float L = 0.f;
+        for (int k = 0; k < ns; ++k) {
+            const float f = M == -INFINITY ? 0.f : fast_exp2(sm_m[k * HPC + tid] - M);
+            sm_m[k * HPC + tid] = f;  // now the rescale factor of split k
+            L = fmaf(f, sm_l[k * HPC + tid], L);
+        }
+        s_L[tid] = L;
+    }
+    __syncthreads();
     for (int o = tid; o < HPC * kHeadDim; o += kThreads) {
         const int h = o / kHeadDim, d = o % kHeadDim;
-        float M = -INFINITY;
-        for (int k = 0; k < S.n_splits; ++k) {
-            const size_t pi = ((size_t)(S.split0 + k) * NY + y) * HPC + h;
-            M = fmaxf(M, __ldcg(a.part_ml + pi * 2));
+        float A0 = 0.f, A1 = 0.f, A2 = 0.f, A3 = 0.f;
+        const float* src = a.part_acc + ((size_t)S.split0 * NY + y) * HPC * kHeadDim + (size_t)h * kHeadDim + d;
+        const size_t stride = (size_t)NY * HPC * kHeadDim;
+        int k = 0;
+        for (; k + 4 <= ns; k += 4) {
+            const float x0 = __ldcg(src + (size_t)(k + 0) * stride), x1 = __ldcg(src + (size_t)(k + 1) * stride);
+            const float x2 = __ldcg(src + (size_t)(k + 2) * stride), x3 = __ldcg(src + (size_t)(k + 3) * stride);
+            A0 = fmaf(sm_m[(k + 0) * HPC + h], x0, A0);
+            A1 = fmaf(sm_m[(k + 1) * HPC + h], x1, A1);
+            A2 = fmaf(sm_m[(k + 2) * HPC + h], x2, A2);
+            A3 = fmaf(sm_m[(k + 3) * HPC + h], x3, A3);
         }
-        float A = 0.f, L = 0.f;
-        if (M != -INFINITY) {
-            for (int k = 0; k < S.n_splits; ++k) {
-                const size_t pi = ((size_t)(S.split0 + k) * NY + y) * HPC + h;
-                const float mk = __ldcg(a.part_ml + pi * 2);
-                const float f = fast_exp2(mk - M);
-                A = fmaf(f, __ldcg(a.part_acc + pi * kHeadDim + d), A);
-                L = fmaf(f, __ldcg(a.part_ml + pi * 2 + 1), L);
-            }
-        }
+        for (; k < ns; ++k) A0 = fmaf(sm_m[k * HPC + h], __ldcg(src + (size_t)k * stride), A0);
+        const float A = (A0 + A1) + (A2 + A3);
+        const float L = s_L[h];
         a.out[((size_t)seq * a.n_heads + h0 + h) * kHeadDim + d] = L > 0.f ? A / L : 0.f;
     }
 }
 
 template <int HPC>
 cudaError_t launch_hpc(const DecodeArgs& a, cudaStream_t s) {
-    static bool attr_set = false;  // per process; the attribute is per device function
+    static bool attr_set[64] = {};  // the attribute is per device
     const int smem = (int)decode_smem_bytes();
-    if (!attr_set) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64 || !attr_set[dev]) {
         cudaError_t e = cudaFuncSetAttribute(decode_kernel<HPC>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
         if (e != cudaSuccess) return e;
-        attr_set = true;
+        if (dev >= 0 && dev < 64) attr_set[dev] = true;
     }
     dim3 grid((unsigned)a.total_splits, (unsigned)(a.n_kv * a.n_sub));
     decode_kernel<HPC><<<grid, kThreads, smem, s>>>(a);

@@ -91,8 +91,10 @@ BEBELM_API int bebelm_norm_rope_heads(float* buf, size_t n_tokens, int n_heads, 
  * every attention layer, laid out [layer][K|V][kv_head][token][64] in fp32.
  * A sequence's window is a ring of pages, so evict_front (the sliding window
  * of src/agent.rs:471-476) moves an offset and recycles whole pages instead of
- * moving memory. A window holds at most max_context + page_tokens positions
- * per layer; beyond that appends fail with BEBELM_ERR_CAPACITY. */
+ * moving memory. The ring has ceil(max_context/64) + 2 pages: a window always
+ * fits max_context + page_tokens positions per layer (a page more when it
+ * starts on a page boundary); an append beyond the ring fails with
+ * BEBELM_ERR_CAPACITY and changes nothing. */
 BEBELM_API int bebelm_kv_pool_create(int n_layers, int n_kv_heads, int head_dim, size_t n_pages,
                           int page_tokens, int dtype, int device, bebelm_kv_pool** out);
 BEBELM_API int bebelm_kv_pool_destroy(bebelm_kv_pool* pool);
