@@ -2,6 +2,7 @@
 // sequence-window bookkeeping (the device replacement of src/cache.rs), host /
 // device staging, and the launch sequences of the fused calls.
 #include <algorithm>
+#include <climits>
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
@@ -137,6 +138,14 @@ struct bebelm_kv_pool {
     DevBuf io, qn, part, counters, seqdesc, bf16, err;
     PinBuf pin;
     std::vector<DecodeSeq> h_desc;
+    // cache slots written by the most recent library kernel on this pool: a decode
+    // launched next copies pages below these before its griddepcontrol.wait
+    struct Written {
+        const bebelm_kv* kv;
+        int layer;
+        long long slot_lo;
+    };
+    std::vector<Written> last_writes;
 
     PoolView view(int layer) const {
         PoolView v;
@@ -324,6 +333,19 @@ struct Window {
     const bebelm_kv* kv;
     long long base;
     long long len;
+    long long new_slot;  // appended by this launch (fused step) or -1
+    long long pos;       // RoPE position of the query (fused step)
+};
+
+// Inputs of a fused decode step: raw q (and the appended token's raw k, v), gains.
+struct FusedStep {
+    const float* q_raw;
+    const float* k_new;
+    const float* v_new;
+    const float* q_gain;
+    const float* k_gain;
+    float theta_scale;
+    float eps;
 };
 
 void pick_heads_per_cta(int group, int* hpc, int* n_sub) {
@@ -332,9 +354,17 @@ void pick_heads_per_cta(int group, int* hpc, int* n_sub) {
     *n_sub = group / h;
 }
 
-// Split-K decode of one query per window. q/out: [n_windows][n_heads][64] device.
+long long dep_slot_for(const bebelm_kv_pool* P, const bebelm_kv* kv, int layer) {
+    long long d = LLONG_MAX;
+    for (const auto& w : P->last_writes)
+        if (w.kv == kv && w.layer == layer) d = std::min(d, w.slot_lo);
+    return d;
+}
+
+// Split-K decode of one query per window. out: [n_windows][n_heads][64] device. The
+// query is d_q (normed+roped, [n][n_heads][64]) or, for a fused step, fused->q_raw.
 int run_decode(bebelm_kv_pool* P, const std::vector<Window>& wins, int layer, int n_heads, const float* d_q,
-               float* d_out, float scale, cudaStream_t s) {
+               float* d_out, float scale, const FusedStep* fused, cudaStream_t s) {
     const int n = (int)wins.size();
     if (n == 0) return 0;
     const int group = n_heads / P->n_kv;
@@ -351,6 +381,7 @@ int run_decode(bebelm_kv_pool* P, const std::vector<Window>& wins, int layer, in
     const long long target = (long long)P->num_sms * 2;  // two resident CTAs per SM
     long long per = std::max<long long>(1, (total_units + target - 1) / target);
     if (n > 1) per = std::min<long long>(per, 8);  // uneven sequences: more, smaller splits
+    per = std::min<long long>(per, kDecodeMaxPagesPerSplit);
     P->h_desc.resize(n);
     int total_splits = 0;
     for (int i = 0; i < n; ++i) {
@@ -361,6 +392,9 @@ int run_decode(bebelm_kv_pool* P, const std::vector<Window>& wins, int layer, in
         d.base = wins[i].base;
         d.split0 = total_splits;
         d.n_splits = (int)std::max<long long>(1, (npages[i] + per - 1) / per);
+        d.new_slot = fused ? wins[i].new_slot : -1;
+        d.pos = wins[i].pos;
+        d.dep_slot = dep_slot_for(P, wins[i].kv, layer);
         total_splits += d.n_splits;
     }
     TRY(P->part.ensure(sizeof(float) * (size_t)total_splits * NY * hpc * (kHeadDim + 2), false, s));
@@ -376,6 +410,15 @@ int run_decode(bebelm_kv_pool* P, const std::vector<Window>& wins, int layer, in
     a.n_seqs = n;
     a.pv = P->view(layer);
     a.q = d_q;
+    if (fused) {
+        a.q_raw = fused->q_raw;
+        a.k_new = fused->k_new;
+        a.v_new = fused->v_new;
+        a.q_gain = fused->q_gain;
+        a.k_gain = fused->k_gain;
+        a.theta_scale = fused->theta_scale;
+        a.eps = fused->eps;
+    }
     a.out = d_out;
     a.part_acc = P->part.as<float>();
     a.part_ml = a.part_acc + (size_t)total_splits * NY * hpc * kHeadDim;
@@ -389,7 +432,12 @@ int run_decode(bebelm_kv_pool* P, const std::vector<Window>& wins, int layer, in
     a.pages_per_split = (int)per;
     a.total_splits = total_splits;
     a.scale_log2 = scale * 1.4426950408889634f;
+    a.pdl = 1;
     CUDA_TRY(launch_decode(a, s));
+    P->last_writes.clear();
+    if (fused)
+        for (int i = 0; i < n; ++i)
+            if (wins[i].new_slot >= 0) P->last_writes.push_back({wins[i].kv, layer, wins[i].new_slot});
     return 0;
 }
 
@@ -696,6 +744,7 @@ int bebelm_kv_append(bebelm_kv* kv, int layer, const float* k, const float* v, s
     a.cap = kv->cap;
     a.slot0 = slot0;
     CUDA_TRY(launch_norm_rope(a, s));
+    P->last_writes.assign(1, {kv, layer, slot0});
     if (mem == BEBELM_MEM_HOST) CUDA_TRY(cudaStreamSynchronize(s));
     return 0;
 }
@@ -809,9 +858,9 @@ int bebelm_attn_decode_host(const float* q, const float* k, const float* v, size
         Stage st[1] = {{qq, sizeof(float) * n_heads * 64, &dq}};
         rc = stage_in(P, st, 1, sizeof(float) * n_heads * 64, &dout, 0);
         if (rc == 0) {
-            std::vector<Window> w{{kv, kv->base[0], kv->len[0]}};
+            std::vector<Window> w{{kv, kv->base[0], kv->len[0], -1, 0}};
             rc = run_decode(P, w, 0, n_heads, static_cast<const float*>(dq), static_cast<float*>(dout),
-                            1.0f / sqrtf((float)head_dim), 0);
+                            1.0f / sqrtf((float)head_dim), nullptr, 0);
         }
         if (rc == 0) rc = stage_out(P, dout, qp.data(), sizeof(float) * n_heads * 64, 0);
         if (rc == 0)
@@ -844,19 +893,9 @@ int bebelm_attn_step(bebelm_kv* kv, int layer, int n_heads, const float* q, cons
     }
     long long slot0 = 0;
     TRY(reserve(kv, layer, 1, &slot0, s));
-    TRY(P->qn.ensure(4 * qn, false, s));
-    NormRopeArgs a{};
-    a.q = dq; a.k = dk; a.v = dv; a.q_gain = dqg; a.k_gain = dkg;
-    a.T = 1; a.n_heads = n_heads; a.n_kv = P->n_kv; a.head_dim = kHeadDim;
-    a.pos0 = (long long)pos;
-    a.theta_scale = theta_scale_of(theta, kHeadDim);
-    a.eps = eps;
-    a.norm_q = 1; a.norm_k = 1;
-    a.q_out = P->qn.as<float>();
-    a.append = 1; a.pv = P->view(layer); a.table = kv->d_table; a.cap = kv->cap; a.slot0 = slot0;
-    CUDA_TRY(launch_norm_rope(a, s));
-    std::vector<Window> w{{kv, kv->base[layer], kv->len[layer]}};
-    TRY(run_decode(P, w, layer, n_heads, P->qn.as<float>(), dout, 0.125f, s));
+    const FusedStep fs{dq, dk, dv, dqg, dkg, theta_scale_of(theta, kHeadDim), eps};
+    std::vector<Window> w{{kv, kv->base[layer], kv->len[layer], slot0, (long long)pos}};
+    TRY(run_decode(P, w, layer, n_heads, nullptr, dout, 0.125f, &fs, s));
     if (mem == BEBELM_MEM_HOST) return stage_out(P, dout, out, 4 * qn, s);
     return 0;
 }
@@ -895,27 +934,14 @@ int bebelm_attn_decode_batched(bebelm_kv* const* seqs, int n_seqs, int layer, in
         if ((b + n + 1 + kPageTokens - 1) / kPageTokens - kv->lo > kv->cap)
             return fail(BEBELM_ERR_CAPACITY, "sequence %d is full: evict_front first", i);
     }
-    std::vector<AppendTarget> tg(n_seqs);
     std::vector<Window> w(n_seqs);
     for (int i = 0; i < n_seqs; ++i) {
         long long slot = 0;
         TRY(reserve(seqs[i], layer, 1, &slot, s));
-        tg[i] = {seqs[i]->d_table, seqs[i]->cap, slot, (long long)pos[i]};
-        w[i] = {seqs[i], seqs[i]->base[layer], seqs[i]->len[layer]};
+        w[i] = {seqs[i], seqs[i]->base[layer], seqs[i]->len[layer], slot, (long long)pos[i]};
     }
-    TRY(P->qn.ensure(4 * qn + sizeof(AppendTarget) * n_seqs + 256, false, s));
-    AppendTarget* dtg = reinterpret_cast<AppendTarget*>(P->qn.as<char>() + ((4 * qn + 255) & ~size_t(255)));
-    CUDA_TRY(cudaMemcpyAsync(dtg, tg.data(), sizeof(AppendTarget) * n_seqs, cudaMemcpyHostToDevice, s));
-    NormRopeArgs a{};
-    a.q = dq; a.k = dk; a.v = dv; a.q_gain = dqg; a.k_gain = dkg;
-    a.T = n_seqs; a.n_heads = n_heads; a.n_kv = P->n_kv; a.head_dim = kHeadDim;
-    a.theta_scale = theta_scale_of(theta, kHeadDim);
-    a.eps = eps;
-    a.norm_q = 1; a.norm_k = 1;
-    a.q_out = P->qn.as<float>();
-    a.append = 1; a.pv = P->view(layer); a.targets = dtg;
-    CUDA_TRY(launch_norm_rope(a, s));
-    TRY(run_decode(P, w, layer, n_heads, P->qn.as<float>(), dout, 0.125f, s));
+    const FusedStep fs{dq, dk, dv, dqg, dkg, theta_scale_of(theta, kHeadDim), eps};
+    TRY(run_decode(P, w, layer, n_heads, nullptr, dout, 0.125f, &fs, s));
     if (mem == BEBELM_MEM_HOST) return stage_out(P, dout, out, 4 * qn, s);
     return 0;
 }
@@ -972,10 +998,11 @@ int bebelm_attn_prefill(bebelm_kv* kv, int layer, int n_heads, const void* q, co
     a.q_out = P->qn.as<float>();
     a.append = 1; a.pv = P->view(layer); a.table = kv->d_table; a.cap = kv->cap; a.slot0 = slot0;
     CUDA_TRY(launch_norm_rope(a, s));
+    P->last_writes.assign(1, {kv, layer, slot0});
     // token i sees the window up to and including itself (src/model.rs:240-244)
     std::vector<Window> w(t);
-    for (size_t i = 0; i < t; ++i) w[i] = {kv, kv->base[layer], len_before + (long long)i + 1};
-    TRY(run_decode(P, w, layer, n_heads, P->qn.as<float>(), dout, 0.125f, s));
+    for (size_t i = 0; i < t; ++i) w[i] = {kv, kv->base[layer], len_before + (long long)i + 1, -1, 0};
+    TRY(run_decode(P, w, layer, n_heads, P->qn.as<float>(), dout, 0.125f, nullptr, s));
     if (mem == BEBELM_MEM_HOST) return stage_out(P, dout, out, 4 * qn, s);
     return 0;
 }
@@ -1006,8 +1033,8 @@ int bebelm_attn_decode_cached(const bebelm_kv* kv, int layer, int n_heads, const
     if (kv->len[layer] == 0) {
         CUDA_TRY(cudaMemsetAsync(dout, 0, 4 * qn, s));
     } else {
-        std::vector<Window> w{{kv, kv->base[layer], kv->len[layer]}};
-        TRY(run_decode(P, w, layer, n_heads, dq, dout, 0.125f, s));
+        std::vector<Window> w{{kv, kv->base[layer], kv->len[layer], -1, 0}};
+        TRY(run_decode(P, w, layer, n_heads, dq, dout, 0.125f, nullptr, s));
     }
     if (mem == BEBELM_MEM_HOST) return stage_out(P, dout, out, 4 * qn, s);
     return 0;

@@ -1,5 +1,6 @@
 // Kernel 3: split-K single-query GQA decode over the paged KV cache, with the
-// combine of the splits fused into the last CTA of each (sequence, kv head).
+// combine of the splits fused into the last CTA of each (sequence, kv head),
+// and — for a decode step — the q/k RMSNorm + RoPE and the KV append fused in.
 //
 // Computes, for every query head h of kv head g = h / group (the reference's
 // `attention_decode`, src/kernels/attention.rs:17-55):
@@ -11,11 +12,25 @@
 // (max, sum, acc[64]) per head. The last CTA to finish a (sequence, kv head)
 // merges all partials and writes the output.
 //
+// Fused step (src/model.rs:440-451): with q_raw set, each CTA norms and ropes
+// its own query heads (norm_rope_heads, src/model.rs:600-608, same arithmetic as
+// norm_rope.cu); the CTA whose pages hold the appended slot norms and ropes the
+// new k, stores k and v into the cache, and uses them for that row directly.
+//
 // Data movement: one thread issues 1-D bulk TMA copies (cp.async.bulk) of a
 // page's K rows (16 KB) and V rows (16 KB) for this kv head into a 3-stage
-// shared-memory ring, completed on an mbarrier; 2 CTAs per SM keep ~4 pages
-// (128 KB) in flight per SM. Every wait is bounded: on timeout the CTA records
-// kErrWaitTimeout, drains its own copies (bounded again) and returns.
+// shared-memory ring, completed on an mbarrier, plus L2 prefetches of the next
+// pages. A stage is handed back as soon as all 4 warps hold their rows in
+// registers; the last warp to release it issues the refill, so no CTA-wide
+// barrier sits in the streaming loop. Every wait is bounded: on timeout the CTA
+// records kErrWaitTimeout, lets its own copies land (bounded again) and returns.
+//
+// Programmatic dependent launch: before griddepcontrol.wait a CTA only loads its
+// page-table slice, initialises barriers and starts copies of pages that hold
+// no slot >= dep_slot (the slots the predecessor may still be writing); all
+// inputs and every global store come after the wait. The kernel triggers its
+// dependents when its streaming loop ends, so the next step's prologue overlaps
+// this step's merge.
 //
 // Compute mapping (128 threads, 4 warps): warp w owns rows 16w..16w+15 of each
 // 64-row page; lane = 4*j + p handles rows 16w+j and 16w+8+j and the 16 dims
@@ -28,11 +43,18 @@
 namespace bebelm {
 namespace {
 
-constexpr int kStages = 3;
+#ifndef BEBELM_DECODE_STAGES
+#define BEBELM_DECODE_STAGES 3
+#endif
+#ifndef BEBELM_DECODE_PREFETCH
+#define BEBELM_DECODE_PREFETCH 2
+#endif
+constexpr int kStages = BEBELM_DECODE_STAGES;
 constexpr int kThreads = 128;
 constexpr int kStageBytes = 2 * kPageRowFloats * 4;  // K + V rows of one page, one kv head
 constexpr long long kWaitLimit = 1ll << 22;          // try_wait polls before giving up
-constexpr int kPrefetch = 2;                          // pages prefetched into L2 beyond the ring
+constexpr int kPrefetch = BEBELM_DECODE_PREFETCH;     // pages prefetched into L2 beyond the ring
+constexpr int kMaxPagesPerSplit = kDecodeMaxPagesPerSplit;
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -43,8 +65,7 @@ __device__ __forceinline__ void mbar_init(uint64_t* bar, unsigned count) {
 }
 
 __device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, unsigned bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
-                 "r"(bytes)
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
                  : "memory");
 }
 
@@ -74,10 +95,39 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, unsigned by
         : "memory");
 }
 
-__device__ __forceinline__ float fast_exp2(float x) { return exp2f(x); }
-
 __device__ __forceinline__ void bulk_prefetch_l2(const void* src, unsigned bytes) {
     asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void grid_dep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+__device__ __forceinline__ unsigned atomic_add_acq_rel_gpu(unsigned* p, unsigned v) {
+    unsigned old;
+    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+    return old;
+}
+
+__device__ __forceinline__ float fast_exp2(float x) { return exp2f(x); }
+
+// One head of 64 at `pos`, one warp: lane i returns elements i and i+32 after
+// rmsnorm (f64 sum of f32 squares, IEEE divide/sqrt, unfused products) and NEOX
+// RoPE with the iterative angle — the arithmetic of norm_rope.cu.
+__device__ __forceinline__ void warp_norm_rope64(const float* x, const float* gain, long long pos, float ts,
+                                                 float eps, int lane, float& y0, float& y1) {
+    float a = x[lane], b = x[lane + 32];
+    double ss = (double)__fmul_rn(a, a) + (double)__fmul_rn(b, b);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    const float mean = __double2float_rn(ss / 64.0);
+    const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, eps)));
+    a = __fmul_rn(__fmul_rn(a, scale), gain[lane]);
+    b = __fmul_rn(__fmul_rn(b, scale), gain[lane + 32]);
+    float theta = __ll2float_rn(pos);
+    for (int t = 0; t < lane; ++t) theta = __fmul_rn(theta, ts);
+    const float sn = sinf(theta), cs = cosf(theta);
+    y0 = __fsub_rn(__fmul_rn(a, cs), __fmul_rn(b, sn));
+    y1 = __fadd_rn(__fmul_rn(a, sn), __fmul_rn(b, cs));
 }
 
 template <int HPC>
@@ -87,8 +137,11 @@ __global__ void __launch_bounds__(kThreads, 2) decode_kernel(DecodeArgs a) {
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes);
     __shared__ float s_m[4][HPC], s_l[4][HPC];
     __shared__ int s_release[kStages];
-    __shared__ int s_failed;
-    __shared__ int s_last;
+    __shared__ int s_failed, s_last;
+    __shared__ int s_phys[kMaxPagesPerSplit];
+    __shared__ __align__(16) float s_q[HPC][kHeadDim];
+    __shared__ __align__(16) float s_knew[kHeadDim], s_vnew[kHeadDim];
+    __shared__ float s_L[HPC];
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int j = lane >> 2, p = lane & 3;
@@ -113,11 +166,15 @@ __global__ void __launch_bounds__(kThreads, 2) decode_kernel(DecodeArgs a) {
     long long p1 = p0 + a.pages_per_split;
     if (p1 > last_page + 1) p1 = last_page + 1;
     const int np = p1 > p0 ? (int)(p1 - p0) : 0;
+    // pages [0, n_early) hold no slot the predecessor may still write
+    const long long dep_page = S.dep_slot >> 6;
+    const int n_early = dep_page <= p0 ? 0 : (int)min((long long)np, dep_page - p0);
 
+    // page-table slice (written by the host, never by a kernel)
+    for (int i = tid; i < np; i += kThreads) s_phys[i] = S.table[(int)((p0 + i) % S.cap)];
+    __syncthreads();
     auto page_src = [&](int i) -> const float* {
-        const long long lp = p0 + i;
-        const int phys = S.table[(int)(lp % S.cap)];
-        return a.pv.base + (size_t)phys * a.pv.page_floats + a.pv.layer_off + (size_t)kvh * kPageRowFloats;
+        return a.pv.base + (size_t)s_phys[i] * a.pv.page_floats + a.pv.layer_off + (size_t)kvh * kPageRowFloats;
     };
     auto issue = [&](int i) {
         const int st = i % kStages;
@@ -133,6 +190,7 @@ __global__ void __launch_bounds__(kThreads, 2) decode_kernel(DecodeArgs a) {
         bulk_prefetch_l2(kp + a.pv.block_floats, kPageRowFloats * 4);
     };
 
+    const int n_first = min(kStages, np);
     if (tid == 0) {
         for (int s = 0; s < kStages; ++s) {
             mbar_init(&full[s], 1);
@@ -141,9 +199,54 @@ __global__ void __launch_bounds__(kThreads, 2) decode_kernel(DecodeArgs a) {
         s_failed = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        for (int i = 0; i < kStages && i < np; ++i) issue(i);
-        for (int i = kStages; i < kStages + kPrefetch && i < np; ++i) prefetch(i);
+        for (int i = 0; i < n_first && i < n_early; ++i) issue(i);
+        for (int i = kStages; i < kStages + kPrefetch && i < n_early; ++i) prefetch(i);
     }
+
+    // ---- everything below may read what the predecessor wrote --------------
+    grid_dep_wait();
+    if (tid == 0)
+        for (int i = n_early; i < n_first; ++i) issue(i);
+
+    // this CTA's query heads, normed + roped here for a fused step
+    if (warp < HPC) {
+        const int h = h0 + warp;
+        if (a.q_raw) {
+            float y0, y1;
+            warp_norm_rope64(a.q_raw + ((size_t)seq * a.n_heads + h) * kHeadDim, a.q_gain, S.pos, a.theta_scale,
+                             a.eps, lane, y0, y1);
+            s_q[warp][lane] = y0;
+            s_q[warp][lane + 32] = y1;
+        } else {
+            const float* qs = a.q + ((size_t)seq * a.n_heads + h) * kHeadDim;
+            s_q[warp][lane] = qs[lane];
+            s_q[warp][lane + 32] = qs[lane + 32];
+        }
+    }
+    // the appended token, if its slot is in our pages: norm+rope k, store k and v
+    const bool has_new = S.new_slot >= 0 && (S.new_slot >> 6) >= p0 && (S.new_slot >> 6) < p1 && sub == 0;
+    const bool own_new = S.new_slot >= 0 && (S.new_slot >> 6) >= p0 && (S.new_slot >> 6) < p1;
+    if (own_new && warp == HPC % 4) {
+        const float* kr = a.k_new + ((size_t)seq * a.n_kv + kvh) * kHeadDim;
+        const float* vr = a.v_new + ((size_t)seq * a.n_kv + kvh) * kHeadDim;
+        float y0, y1;
+        warp_norm_rope64(kr, a.k_gain, S.pos, a.theta_scale, a.eps, lane, y0, y1);
+        s_knew[lane] = y0;
+        s_knew[lane + 32] = y1;
+        s_vnew[lane] = vr[lane];
+        s_vnew[lane + 32] = vr[lane + 32];
+        if (has_new) {  // one CTA per kv head writes the cache
+            const int i = (int)((S.new_slot >> 6) - p0);
+            float* kd = a.pv.base + (size_t)s_phys[i] * a.pv.page_floats + a.pv.layer_off +
+                        (size_t)kvh * kPageRowFloats + (size_t)(S.new_slot & 63) * kHeadDim;
+            float* vd = kd + a.pv.block_floats;
+            kd[lane] = y0;
+            kd[lane + 32] = y1;
+            vd[lane] = vr[lane];
+            vd[lane + 32] = vr[lane + 32];
+        }
+    }
+    __syncthreads();
 
     // q slice of this lane, pre-rotated so register index i pairs with chunk c_i
     int c[4];
@@ -151,11 +254,9 @@ __global__ void __launch_bounds__(kThreads, 2) decode_kernel(DecodeArgs a) {
     for (int i = 0; i < 4; ++i) c[i] = (((i + j) & 3) << 2) + p;
     float4 qr[HPC][4];
 #pragma unroll
-    for (int h = 0; h < HPC; ++h) {
-        const float4* q4 = reinterpret_cast<const float4*>(a.q + ((size_t)seq * a.n_heads + h0 + h) * kHeadDim);
+    for (int h = 0; h < HPC; ++h)
 #pragma unroll
-        for (int i = 0; i < 4; ++i) qr[h][i] = q4[c[i]];
-    }
+        for (int i = 0; i < 4; ++i) qr[h][i] = reinterpret_cast<const float4*>(s_q[h])[c[i]];
     float acc[HPC][16];
     float m[HPC], l[HPC];
 #pragma unroll
@@ -165,10 +266,11 @@ __global__ void __launch_bounds__(kThreads, 2) decode_kernel(DecodeArgs a) {
 #pragma unroll
         for (int e = 0; e < 16; ++e) acc[h][e] = 0.f;
     }
-    __syncthreads();
+    if (tid == 0)
+        for (int i = max(n_early, kStages); i < kStages + kPrefetch && i < np; ++i) prefetch(i);
 
     const long long win_lo = S.base, win_hi = S.base + S.len;
-    int consumed = 0;  // pages this warp finished (the rest are still owed to the ring)
+    const long long new_slot = own_new ? S.new_slot : -1;
     for (int i = 0; i < np; ++i) {
         const int st = i % kStages;
         const bool ok = __all_sync(0xffffffffu, mbar_wait_bounded(&full[st], (unsigned)((i / kStages) & 1)));
@@ -182,37 +284,38 @@ __global__ void __launch_bounds__(kThreads, 2) decode_kernel(DecodeArgs a) {
         const float4* Ks = reinterpret_cast<const float4*>(stages + (size_t)st * (2 * kPageRowFloats));
         const float4* Vs = Ks + kPageRowFloats / 4;
         const long long slot0 = (p0 + i) << 6;
-
-        float s[2][HPC];
+#ifdef BEBELM_DECODE_NOCOMPUTE
+        __syncwarp();
+        if (lane == 0 && atomicAdd(&s_release[st], 1) == 3) {
+            s_release[st] = 0;
+            if (i + kStages < np) {
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                issue(i + kStages);
+                if (i + kStages + kPrefetch < np) prefetch(i + kStages + kPrefetch);
+            }
+        }
+        acc[0][0] += Ks[lane].x;
+        continue;
+#endif
+        // both rows of K and V into registers, then hand the stage back at once
+        float4 kk[2][4], vv[2][4];
 #pragma unroll
         for (int r = 0; r < 2; ++r) {
             const int row = 16 * warp + 8 * r + j;
-            const long long slot = slot0 + row;
-            const bool valid = slot >= win_lo && slot < win_hi;
-            float4 kk[4];
-#pragma unroll
-            for (int ii = 0; ii < 4; ++ii) kk[ii] = Ks[row * 16 + c[ii]];
-#pragma unroll
-            for (int h = 0; h < HPC; ++h) {
-                float d = 0.f;
+            if (slot0 + row == new_slot) {  // the appended token: take it from this CTA's own copy
 #pragma unroll
                 for (int ii = 0; ii < 4; ++ii) {
-                    d = fmaf(qr[h][ii].x, kk[ii].x, d);
-                    d = fmaf(qr[h][ii].y, kk[ii].y, d);
-                    d = fmaf(qr[h][ii].z, kk[ii].z, d);
-                    d = fmaf(qr[h][ii].w, kk[ii].w, d);
+                    kk[r][ii] = reinterpret_cast<const float4*>(s_knew)[c[ii]];
+                    vv[r][ii] = reinterpret_cast<const float4*>(s_vnew)[c[ii]];
                 }
-                d += __shfl_xor_sync(0xffffffffu, d, 1);
-                d += __shfl_xor_sync(0xffffffffu, d, 2);
-                s[r][h] = valid ? d * a.scale_log2 : -INFINITY;
+            } else {
+#pragma unroll
+                for (int ii = 0; ii < 4; ++ii) {
+                    kk[r][ii] = Ks[row * 16 + c[ii]];
+                    vv[r][ii] = Vs[row * 16 + c[ii]];
+                }
             }
         }
-        float4 vv[2][4];
-#pragma unroll
-        for (int r = 0; r < 2; ++r)
-#pragma unroll
-            for (int ii = 0; ii < 4; ++ii) vv[r][ii] = Vs[(16 * warp + 8 * r + j) * 16 + c[ii]];
-        // V is in registers: this warp is done with the stage
         __syncwarp();
         if (lane == 0) {
             if (atomicAdd(&s_release[st], 1) == 3) {  // last of the 4 warps refills the stage
@@ -222,6 +325,26 @@ __global__ void __launch_bounds__(kThreads, 2) decode_kernel(DecodeArgs a) {
                     issue(i + kStages);
                     if (i + kStages + kPrefetch < np) prefetch(i + kStages + kPrefetch);
                 }
+            }
+        }
+        float s[2][HPC];
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+            const long long slot = slot0 + 16 * warp + 8 * r + j;
+            const bool valid = slot >= win_lo && slot < win_hi;
+#pragma unroll
+            for (int h = 0; h < HPC; ++h) {
+                float d = 0.f;
+#pragma unroll
+                for (int ii = 0; ii < 4; ++ii) {
+                    d = fmaf(qr[h][ii].x, kk[r][ii].x, d);
+                    d = fmaf(qr[h][ii].y, kk[r][ii].y, d);
+                    d = fmaf(qr[h][ii].z, kk[r][ii].z, d);
+                    d = fmaf(qr[h][ii].w, kk[r][ii].w, d);
+                }
+                d += __shfl_xor_sync(0xffffffffu, d, 1);
+                d += __shfl_xor_sync(0xffffffffu, d, 2);
+                s[r][h] = valid ? d * a.scale_log2 : -INFINITY;
             }
         }
         float pr[2][HPC];
@@ -257,15 +380,14 @@ __global__ void __launch_bounds__(kThreads, 2) decode_kernel(DecodeArgs a) {
                 }
             }
         }
-        consumed = i + 1;
     }
-    (void)consumed;
+    // the next launch may start its prologue now (it writes nothing before its own wait)
+    grid_dep_launch();
     __syncthreads();
     if (s_failed) {
         // a wait gave up: let our own copies still in flight land (bounded), then leave
         if (tid == 0) {
             for (int k = 0; k < kStages && k < np; ++k) {
-                // the newest issue into stage k is the largest page index < np with index % kStages == k
                 const int last = ((np - 1 - k) / kStages) * kStages + k;
                 mbar_wait_bounded(&full[k], (unsigned)((last / kStages) & 1));
             }
@@ -327,58 +449,80 @@ __global__ void __launch_bounds__(kThreads, 2) decode_kernel(DecodeArgs a) {
     if (single) return;
 
     // ---- last CTA of this (sequence, kv head) merges the splits ----------
-    __threadfence();
-    __syncthreads();
+    __syncthreads();  // every partial of this CTA is stored before thread 0 releases it
     if (tid == 0) {
         unsigned* ctr = a.counters + (size_t)seq * NY + y;
-        const unsigned prev = atomicAdd(ctr, 1u);
+        const unsigned prev = atomic_add_acq_rel_gpu(ctr, 1u);
         s_last = (prev == (unsigned)(S.n_splits - 1));
         if (s_last) *ctr = 0u;  // ready for the next launch
     }
     __syncthreads();
     if (!s_last) return;
-    __threadfence();
     const int ns = S.n_splits;
-    // split maxima and sums into shared memory (one load per thread, all in flight at once)
-    float* sm_m = red;                  // [ns][HPC]
-    float* sm_l = red + ns * HPC;       // [ns][HPC]
-    for (int x = tid; x < ns * HPC; x += kThreads) {
-        const size_t pi = ((size_t)(S.split0 + x / HPC) * NY + y) * HPC + (x % HPC);
-        sm_m[x] = __ldcg(a.part_ml + pi * 2);
-        sm_l[x] = __ldcg(a.part_ml + pi * 2 + 1);
+    constexpr int kVec = HPC * kHeadDim / 4;  // float4s per split record
+    constexpr int G = kThreads / kVec;        // thread groups, each a stride of the splits
+    const int ml_stride = (ns * HPC + 3) & ~3;  // keeps sm_acc 16-byte aligned for float4 stores
+    float* sm_m = red;                          // [ns][HPC] split maxima, then rescale factors
+    float* sm_l = red + ml_stride;              // [ns][HPC]
+    float* sm_acc = sm_l + ml_stride;           // [G][HPC*64]
+    const bool active = tid < G * kVec;
+    const int f = tid % kVec, g0 = tid / kVec;
+    const int hh = (f * 4) / kHeadDim;
+    const float4* src = reinterpret_cast<const float4*>(a.part_acc) + ((size_t)S.split0 * NY + y) * kVec + f;
+    const size_t stride = (size_t)NY * kVec;
+    // one round of loads: split maxima/sums and this thread's first 16 partial vectors
+    float4 x[16];
+#pragma unroll
+    for (int u = 0; u < 16; ++u) {
+        const int k = g0 + u * G;
+        x[u] = active && k < ns ? __ldcg(src + (size_t)k * stride) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    for (int t = tid; t < ns * HPC; t += kThreads) {
+        const size_t pi = ((size_t)(S.split0 + t / HPC) * NY + y) * HPC + (t % HPC);
+        sm_m[t] = __ldcg(a.part_ml + pi * 2);
+        sm_l[t] = __ldcg(a.part_ml + pi * 2 + 1);
     }
     __syncthreads();
-    __shared__ float s_L[HPC];
     if (tid < HPC) {
         float M = -INFINITY;
         for (int k = 0; k < ns; ++k) M = fmaxf(M, sm_m[k * HPC + tid]);
         float L = 0.f;
         for (int k = 0; k < ns; ++k) {
-            const float f = M == -INFINITY ? 0.f : fast_exp2(sm_m[k * HPC + tid] - M);
-            sm_m[k * HPC + tid] = f;  // now the rescale factor of split k
-            L = fmaf(f, sm_l[k * HPC + tid], L);
+            const float fk = M == -INFINITY ? 0.f : fast_exp2(sm_m[k * HPC + tid] - M);
+            sm_m[k * HPC + tid] = fk;  // now the rescale factor of split k
+            L = fmaf(fk, sm_l[k * HPC + tid], L);
         }
         s_L[tid] = L;
     }
     __syncthreads();
-    for (int o = tid; o < HPC * kHeadDim; o += kThreads) {
-        const int h = o / kHeadDim, d = o % kHeadDim;
-        float A0 = 0.f, A1 = 0.f, A2 = 0.f, A3 = 0.f;
-        const float* src = a.part_acc + ((size_t)S.split0 * NY + y) * HPC * kHeadDim + (size_t)h * kHeadDim + d;
-        const size_t stride = (size_t)NY * HPC * kHeadDim;
-        int k = 0;
-        for (; k + 4 <= ns; k += 4) {
-            const float x0 = __ldcg(src + (size_t)(k + 0) * stride), x1 = __ldcg(src + (size_t)(k + 1) * stride);
-            const float x2 = __ldcg(src + (size_t)(k + 2) * stride), x3 = __ldcg(src + (size_t)(k + 3) * stride);
-            A0 = fmaf(sm_m[(k + 0) * HPC + h], x0, A0);
-            A1 = fmaf(sm_m[(k + 1) * HPC + h], x1, A1);
-            A2 = fmaf(sm_m[(k + 2) * HPC + h], x2, A2);
-            A3 = fmaf(sm_m[(k + 3) * HPC + h], x3, A3);
+    if (active) {
+        float4 A = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int k0 = g0; k0 < ns; k0 += 16 * G) {
+            if (k0 != g0) {  // more splits than one round holds
+#pragma unroll
+                for (int u = 0; u < 16; ++u) {
+                    const int k = k0 + u * G;
+                    x[u] = k < ns ? __ldcg(src + (size_t)k * stride) : make_float4(0.f, 0.f, 0.f, 0.f);
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < 16; ++u) {
+                const int k = k0 + u * G;
+                const float fk = k < ns ? sm_m[k * HPC + hh] : 0.f;
+                A.x = fmaf(fk, x[u].x, A.x);
+                A.y = fmaf(fk, x[u].y, A.y);
+                A.z = fmaf(fk, x[u].z, A.z);
+                A.w = fmaf(fk, x[u].w, A.w);
+            }
         }
-        for (; k < ns; ++k) A0 = fmaf(sm_m[k * HPC + h], __ldcg(src + (size_t)k * stride), A0);
-        const float A = (A0 + A1) + (A2 + A3);
-        const float L = s_L[h];
-        a.out[((size_t)seq * a.n_heads + h0 + h) * kHeadDim + d] = L > 0.f ? A / L : 0.f;
+        reinterpret_cast<float4*>(sm_acc)[g0 * kVec + f] = A;
+    }
+    __syncthreads();
+    for (int o = tid; o < HPC * kHeadDim; o += kThreads) {
+        float A = 0.f;
+        for (int g = 0; g < G; ++g) A += sm_acc[g * HPC * kHeadDim + o];
+        const float L = s_L[o / kHeadDim];
+        a.out[((size_t)seq * a.n_heads + h0) * kHeadDim + o] = L > 0.f ? A / L : 0.f;
     }
 }
 
@@ -393,9 +537,17 @@ cudaError_t launch_hpc(const DecodeArgs& a, cudaStream_t s) {
         if (e != cudaSuccess) return e;
         if (dev >= 0 && dev < 64) attr_set[dev] = true;
     }
-    dim3 grid((unsigned)a.total_splits, (unsigned)(a.n_kv * a.n_sub));
-    decode_kernel<HPC><<<grid, kThreads, smem, s>>>(a);
-    return cudaGetLastError();
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)a.total_splits, (unsigned)(a.n_kv * a.n_sub));
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = (size_t)smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = a.pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, decode_kernel<HPC>, a);
 }
 
 }  // namespace

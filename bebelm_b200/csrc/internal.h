@@ -84,14 +84,17 @@ cudaError_t launch_kv_gather(const PoolView& pv, const int* table, int cap, long
 // bf16 -> fp32, n elements.
 cudaError_t launch_bf16_to_f32(const __nv_bfloat16* in, float* out, size_t n, cudaStream_t s);
 
-// ---- kernel 3: split-K decode with fused combine ---------------------------
+// ---- kernel 3: split-K decode with fused combine (and fused norm/RoPE/append) --
 struct DecodeSeq {
     const int* table;
     int cap;
-    int len;
-    long long base;
-    int split0;    // first global split of this sequence
-    int n_splits;  // splits of this sequence
+    int len;            // window length, including a token appended by this launch
+    long long base;     // first slot of the window
+    int split0;         // first global split of this sequence
+    int n_splits;       // splits of this sequence
+    long long new_slot; // slot of the token this launch appends, or -1
+    long long pos;      // RoPE position of that token (and of the query)
+    long long dep_slot; // pages holding slots >= dep_slot are read only after griddepcontrol.wait
 };
 
 struct DecodeArgs {
@@ -99,7 +102,15 @@ struct DecodeArgs {
     DecodeSeq one;          // the sequence itself when n_seqs == 1 (passed by value)
     int n_seqs;
     PoolView pv;
-    const float* q;         // [n_seqs][n_heads][64], normed + roped
+    // query: either already normed/roped (q) or raw (q_raw, normed+roped in-kernel)
+    const float* q;         // [n_seqs][n_heads][64]
+    const float* q_raw;     // [n_seqs][n_heads][64] or null
+    // appended token (used when new_slot >= 0): raw k (normed+roped in-kernel) and v
+    const float* k_new;     // [n_seqs][n_kv][64]
+    const float* v_new;     // [n_seqs][n_kv][64]
+    const float* q_gain;
+    const float* k_gain;
+    float theta_scale, eps;
     float* out;             // [n_seqs][n_heads][64]
     float* part_acc;        // [total_splits][n_kv*n_sub][hpc][64]
     float* part_ml;         // [total_splits][n_kv*n_sub][hpc][2]
@@ -109,9 +120,11 @@ struct DecodeArgs {
     int pages_per_split;
     int total_splits;
     float scale_log2;       // score scale (1/sqrt(head_dim)) times log2(e)
+    int pdl;                // launched as a programmatic dependent of the previous kernel
 };
 cudaError_t launch_decode(const DecodeArgs& a, cudaStream_t s);
 size_t decode_smem_bytes();
+constexpr int kDecodeMaxPagesPerSplit = 256;
 
 // device error codes written to DecodeArgs::err
 constexpr int kErrWaitTimeout = 1;
