@@ -38,7 +38,7 @@ EXPORTS = [
     "bebelm_norm_rope_heads", "bebelm_kv_pool_create", "bebelm_kv_pool_destroy", "bebelm_kv_pool_free_pages",
     "bebelm_kv_create", "bebelm_kv_create_in_pool", "bebelm_kv_destroy", "bebelm_kv_clone", "bebelm_kv_clear",
     "bebelm_kv_len", "bebelm_kv_layer_len", "bebelm_kv_pos", "bebelm_kv_set_pos", "bebelm_kv_evict_front",
-    "bebelm_kv_append", "bebelm_kv_read", "bebelm_attn_step", "bebelm_attn_decode_cached", "bebelm_attn_prefill", "bebelm_attn_decode_batched",
+    "bebelm_kv_append", "bebelm_kv_read", "bebelm_attn_step", "bebelm_attn_decode_cached", "bebelm_attn_decode_cached_noalloc", "bebelm_attn_prefill", "bebelm_attn_decode_batched",
 ]
 
 
@@ -84,6 +84,7 @@ def load_library(path: str = LIB_PATH):
         "bebelm_kv_read": ([vp, i, vp, vp, i, vp], i),
         "bebelm_attn_step": ([vp, i, i, vp, vp, vp, vp, vp, f, f, sz, vp, i, vp], i),
         "bebelm_attn_decode_cached": ([vp, i, i, vp, vp, i, vp], i),
+        "bebelm_attn_decode_cached_noalloc": ([vp, i, i, vp, vp, vp], i),
         "bebelm_attn_prefill": ([vp, i, i, vp, vp, vp, i, sz, sz, vp, vp, f, f, vp, i, vp], i),
         "bebelm_attn_decode_batched": ([vp, i, i, i, vp, vp, vp, vp, vp, f, f, vp, vp, i, vp], i),
     }

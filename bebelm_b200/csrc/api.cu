@@ -1041,3 +1041,107 @@ int bebelm_attn_decode_cached(const bebelm_kv* kv, int layer, int n_heads, const
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Decode without any allocation at call time.
+//
+// bebelm_attn_decode_cached keeps its split partials and counters in pool scratch
+// that grows on demand with cudaMalloc. This variant takes them from a fixed
+// file-scope device array instead, for callers that must not allocate device
+// memory while they run (see the header). The array is process-wide: every GPU
+// that loads this library holds kNoAllocScratchFloats floats of it until exit,
+// and every call on a device shares it.
+namespace {
+
+constexpr size_t kNoAllocScratchFloats = (size_t)1 << 19;  // 2 MiB of split partials and counters
+constexpr size_t kNoAllocCounterWords = 1024;              // tail of the array: split counters
+constexpr size_t kNoAllocPartialFloats = kNoAllocScratchFloats - kNoAllocCounterWords - 64;
+
+static __device__ __align__(256) float g_noalloc_scratch[kNoAllocScratchFloats];
+
+std::mutex g_noalloc_mu;
+float* g_noalloc_addr[64] = {};  // device address of g_noalloc_scratch, per device
+
+// Once per device, with that device current: look up the array's device address (the
+// host-side symbol is only a stand-in) and zero the counters and error word.
+int noalloc_scratch(int dev, cudaStream_t s, float** out) {
+    if (dev < 0 || dev >= 64) return fail(BEBELM_ERR_INVALID, "device %d unsupported", dev);
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    if (!g_noalloc_addr[dev]) {
+        float* ptr = nullptr;
+        cudaError_t e = cudaGetSymbolAddress((void**)&ptr, g_noalloc_scratch);
+        if (e != cudaSuccess || !ptr)
+            return fail(BEBELM_ERR_CUDA, "cudaGetSymbolAddress of the no-allocation scratch failed: %s",
+                        cudaGetErrorString(e));
+        e = cudaMemsetAsync(ptr + kNoAllocPartialFloats, 0, sizeof(float) * (kNoAllocCounterWords + 64), s);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+        if (e != cudaSuccess) return fail(BEBELM_ERR_CUDA, "clearing the no-allocation scratch failed: %s", cudaGetErrorString(e));
+        g_noalloc_addr[dev] = ptr;
+    }
+    *out = g_noalloc_addr[dev];
+    return 0;
+}
+
+}  // namespace
+
+extern "C" int bebelm_attn_decode_cached_noalloc(const bebelm_kv* kv, int layer, int n_heads, const float* q,
+                                                 float* out, void* stream) {
+    TRY(validate_layer(kv, layer));
+    bebelm_kv_pool* P = kv->pool;
+    TRY(check_geometry(n_heads, P->n_kv));
+    if (!q || !out) return fail(BEBELM_ERR_INVALID, "null buffer");
+    DeviceGuard g(P->device);
+    cudaStream_t s = as_stream(stream);
+    float* scratch = nullptr;
+    TRY(noalloc_scratch(P->device, s, &scratch));
+    const long long len = kv->len[layer], base = kv->base[layer];
+    if (len == 0) {
+        CUDA_TRY(cudaMemsetAsync(out, 0, sizeof(float) * (size_t)n_heads * kHeadDim, s));
+        return 0;
+    }
+    // the same split plan as run_decode for one window
+    const int group = n_heads / P->n_kv;
+    int hpc, n_sub;
+    pick_heads_per_cta(group, &hpc, &n_sub);
+    const int NY = P->n_kv * n_sub;
+    const long long npages = (base + len - 1) / kPageTokens - base / kPageTokens + 1;
+    const long long target = (long long)P->num_sms * 2;
+    long long per = std::max<long long>(1, (npages * NY + target - 1) / target);
+    per = std::min<long long>(per, kDecodeMaxPagesPerSplit);
+    const long long n_splits = (npages + per - 1) / per;
+    const size_t need = (size_t)n_splits * NY * hpc * (kHeadDim + 2);
+    if (need > kNoAllocPartialFloats || (size_t)NY > kNoAllocCounterWords)
+        return fail(BEBELM_ERR_INVALID,
+                    "window of %lld positions needs %zu scratch floats (%lld splits x %d heads); the no-allocation "
+                    "path holds at most %zu",
+                    len, need, n_splits, NY * hpc, kNoAllocPartialFloats);
+    DecodeArgs a{};
+    a.one.table = kv->d_table;
+    a.one.cap = kv->cap;
+    a.one.len = (int)len;
+    a.one.base = base;
+    a.one.split0 = 0;
+    a.one.n_splits = (int)n_splits;
+    a.one.new_slot = -1;
+    a.one.pos = 0;
+    a.one.dep_slot = dep_slot_for(P, kv, layer);
+    a.n_seqs = 1;
+    a.pv = P->view(layer);
+    a.q = q;
+    a.out = out;
+    a.part_acc = scratch;
+    a.part_ml = scratch + (size_t)n_splits * NY * hpc * kHeadDim;
+    a.counters = reinterpret_cast<unsigned*>(scratch + kNoAllocPartialFloats);
+    a.err = reinterpret_cast<int*>(scratch + kNoAllocPartialFloats + kNoAllocCounterWords);
+    a.n_heads = n_heads;
+    a.n_kv = P->n_kv;
+    a.group = group;
+    a.hpc = hpc;
+    a.n_sub = n_sub;
+    a.pages_per_split = (int)per;
+    a.total_splits = (int)n_splits;
+    a.scale_log2 = 0.125f * 1.4426950408889634f;
+    a.pdl = 1;
+    CUDA_TRY(launch_decode(a, s));
+    return 0;
+}

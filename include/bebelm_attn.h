@@ -148,6 +148,20 @@ BEBELM_API int bebelm_attn_step(bebelm_kv* kv, int layer, int n_heads, const flo
 BEBELM_API int bebelm_attn_decode_cached(const bebelm_kv* kv, int layer, int n_heads, const float* q, float* out,
                                          int mem, void* stream);
 
+/* No counterpart in the reference. bebelm_attn_decode_cached, but allocating
+ * nothing: for callers that cannot call cudaMalloc while they decode — e.g. a
+ * host whose device memory is fully reserved by another allocator, or a token
+ * loop that must not take the device-wide synchronisation cudaMalloc can cause.
+ * The split scratch is a fixed 2 MiB device array inside this library (held by
+ * every GPU that loads it, until exit) instead of the pool's on-demand scratch.
+ * Device pointers only (q normed and roped, [n_heads*64]; out [n_heads*64]).
+ * The first call on a device looks up the array's address and clears its
+ * counters (do that call before any stream capture). A window too large for
+ * the array is rejected with BEBELM_ERR_INVALID. All calls share the array:
+ * calls that overlap on the GPU (different streams, or another thread) race. */
+BEBELM_API int bebelm_attn_decode_cached_noalloc(const bebelm_kv* kv, int layer, int n_heads, const float* q,
+                                                 float* out, void* stream);
+
 /* The middle of `attn_batch` (src/model.rs:232-254): t tokens at positions
  * pos0.. are normed/roped, appended, and each attends causally to the window
  * up to and including itself. q [t][n_heads*64], k/v [t][n_kv_heads*64] in
