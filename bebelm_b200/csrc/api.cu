@@ -135,7 +135,7 @@ struct bebelm_kv_pool {
     int num_sms = 148;
     int n_seqs = 0;              // live sequences drawing from this pool
     // scratch shared by every call on this pool's sequences (stream-ordered)
-    DevBuf io, qn, part, counters, seqdesc, bf16, err;
+    DevBuf io, qn, part, counters, seqdesc, bf16, err, pf;
     PinBuf pin;
     std::vector<DecodeSeq> h_desc;
     // cache slots written by the most recent library kernel on this pool: a decode
@@ -296,6 +296,7 @@ void pool_free(bebelm_kv_pool* P) {
     P->counters.release();
     P->seqdesc.release();
     P->bf16.release();
+    P->pf.release();
     P->err.release();
     P->pin.release();
     delete P;
@@ -987,6 +988,40 @@ int bebelm_attn_prefill(bebelm_kv* kv, int layer, int n_heads, const void* q, co
     long long slot0 = 0;
     TRY(reserve(kv, layer, t, &slot0, s));
     const long long len_before = kv->len[layer] - (long long)t;
+    if (in_dtype == BEBELM_BF16) {
+        // tensor-core path: bf16 q and the bf16 window [prefix | new keys] feed kernel 2
+        const size_t kvrow = (size_t)P->n_kv * kHeadDim;
+        const size_t s_total = (size_t)len_before + t;
+        TRY(P->pf.ensure(2 * (qn + 2 * s_total * kvrow) + 1024, false, s));
+        __nv_bfloat16* qb = P->pf.as<__nv_bfloat16>();
+        __nv_bfloat16* kb = qb + ((qn + 127) & ~size_t(127));
+        __nv_bfloat16* vb = kb + ((s_total * kvrow + 127) & ~size_t(127));
+        if (len_before > 0)
+            CUDA_TRY(launch_kv_gather_bf16(P->view(layer), kv->d_table, kv->cap, kv->base[layer], len_before, P->n_kv,
+                                           kb, vb, s));
+        NormRopeArgs a{};
+        a.q = (const float*)dq; a.k = (const float*)dk; a.v = (const float*)dv; a.q_gain = dqg; a.k_gain = dkg;
+        a.T = (int)t; a.n_heads = n_heads; a.n_kv = P->n_kv; a.head_dim = kHeadDim;
+        a.pos0 = (long long)pos0;
+        a.theta_scale = theta_scale_of(theta, kHeadDim);
+        a.eps = eps;
+        a.norm_q = 1; a.norm_k = 1;
+        a.q_bf16 = qb; a.k_bf16 = kb + (size_t)len_before * kvrow; a.v_bf16 = vb + (size_t)len_before * kvrow;
+        a.append = 1; a.pv = P->view(layer); a.table = kv->d_table; a.cap = kv->cap; a.slot0 = slot0;
+        CUDA_TRY(launch_norm_rope(a, s));
+        P->last_writes.assign(1, {kv, layer, slot0});
+        PrefillArgs pa{};
+        pa.q = qb; pa.k = kb; pa.v = vb; pa.out = dout;
+        pa.t = (int)t; pa.len_before = (int)len_before; pa.n_heads = n_heads; pa.n_kv = P->n_kv;
+        pa.scale_log2 = 0.125f * 1.4426950408889634f;
+        pa.err = P->err.as<int>();
+        cudaError_t e = launch_prefill(pa, s);
+        if (e == cudaErrorInvalidValue) return fail(BEBELM_ERR_CUDA, "building the TMA tensor maps for prefill failed");
+        CUDA_TRY(e);
+        P->last_writes.clear();
+        if (mem == BEBELM_MEM_HOST) return stage_out(P, dout, out, 4 * qn, s);
+        return 0;
+    }
     TRY(P->qn.ensure(4 * qn, false, s));
     NormRopeArgs a{};
     a.q = (const float*)dq; a.k = (const float*)dk; a.v = (const float*)dv; a.q_gain = dqg; a.k_gain = dkg;

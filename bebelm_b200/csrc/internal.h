@@ -126,6 +126,21 @@ cudaError_t launch_decode(const DecodeArgs& a, cudaStream_t s);
 size_t decode_smem_bytes();
 constexpr int kDecodeMaxPagesPerSplit = 256;
 
+// ---- kernel 2: causal prefill on the tensor cores ---------------------------
+struct PrefillArgs {
+    const __nv_bfloat16* q;  // [t][n_heads][64], normed + roped
+    const __nv_bfloat16* k;  // [len_before + t][n_kv][64]: the window, oldest first
+    const __nv_bfloat16* v;  // same
+    float* out;              // [t][n_heads][64]
+    int t, len_before, n_heads, n_kv;
+    float scale_log2;        // score scale times log2(e)
+    int* err;
+};
+cudaError_t launch_prefill(const PrefillArgs& a, cudaStream_t s);
+// Window [base, base+len) of one layer as bf16, token-major [len][n_kv][64].
+cudaError_t launch_kv_gather_bf16(const PoolView& pv, const int* table, int cap, long long base, long long len,
+                                  int n_kv, __nv_bfloat16* k_out, __nv_bfloat16* v_out, cudaStream_t s);
+
 // device error codes written to DecodeArgs::err
 constexpr int kErrWaitTimeout = 1;
 

@@ -180,6 +180,28 @@ __global__ void __launch_bounds__(256) kv_gather_kernel(PoolView pv, const int* 
     *reinterpret_cast<float4*>(dst + (size_t)row * 64 + e) = *reinterpret_cast<const float4*>(src + e);
 }
 
+// One thread per 4 consecutive floats of the [len][n_kv][64] window, K and V.
+__global__ void kv_gather_bf16_kernel(PoolView pv, const int* table, int cap, long long base, long long len, int n_kv,
+                                      __nv_bfloat16* k_out, __nv_bfloat16* v_out) {
+    const long long quads = len * n_kv * 16;
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < quads;
+         i += (long long)gridDim.x * blockDim.x) {
+        const long long row = i >> 4;
+        const int e = (int)(i & 15) * 4;
+        const long long t = row / n_kv;
+        const int h = (int)(row % n_kv);
+        const float4 kf = *reinterpret_cast<const float4*>(pv.base + slot_offset(pv, table, cap, base + t, h, 0) + e);
+        const float4 vf = *reinterpret_cast<const float4*>(pv.base + slot_offset(pv, table, cap, base + t, h, 1) + e);
+        __nv_bfloat162 k0 = __floats2bfloat162_rn(kf.x, kf.y), k1 = __floats2bfloat162_rn(kf.z, kf.w);
+        __nv_bfloat162 v0 = __floats2bfloat162_rn(vf.x, vf.y), v1 = __floats2bfloat162_rn(vf.z, vf.w);
+        uint2 kw, vw;
+        kw.x = *reinterpret_cast<uint32_t*>(&k0); kw.y = *reinterpret_cast<uint32_t*>(&k1);
+        vw.x = *reinterpret_cast<uint32_t*>(&v0); vw.y = *reinterpret_cast<uint32_t*>(&v1);
+        *reinterpret_cast<uint2*>(k_out + row * 64 + e) = kw;
+        *reinterpret_cast<uint2*>(v_out + row * 64 + e) = vw;
+    }
+}
+
 __global__ void bf16_to_f32_kernel(const __nv_bfloat16* in, float* out, size_t n) {
     for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
         out[i] = __bfloat162float(in[i]);
@@ -192,6 +214,15 @@ cudaError_t launch_kv_gather(const PoolView& pv, const int* table, int cap, long
     const long long rows = len * n_kv;
     if (rows <= 0) return cudaSuccess;
     kv_gather_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, s>>>(pv, table, cap, base, len, n_kv, k_out, v_out);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_kv_gather_bf16(const PoolView& pv, const int* table, int cap, long long base, long long len,
+                                  int n_kv, __nv_bfloat16* k_out, __nv_bfloat16* v_out, cudaStream_t s) {
+    const long long quads = len * n_kv * 16;
+    if (quads <= 0) return cudaSuccess;
+    const long long blocks = std::min<long long>((quads + 255) / 256, 148 * 16);
+    kv_gather_bf16_kernel<<<(unsigned)blocks, 256, 0, s>>>(pv, table, cap, base, len, n_kv, k_out, v_out);
     return cudaGetLastError();
 }
 

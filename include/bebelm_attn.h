@@ -165,8 +165,11 @@ BEBELM_API int bebelm_attn_decode_cached_noalloc(const bebelm_kv* kv, int layer,
 /* The middle of `attn_batch` (src/model.rs:232-254): t tokens at positions
  * pos0.. are normed/roped, appended, and each attends causally to the window
  * up to and including itself. q [t][n_heads*64], k/v [t][n_kv_heads*64] in
- * `in_dtype` (BEBELM_F32 or BEBELM_BF16); out [t][n_heads*64] fp32. The
- * attention runs on the tensor cores in bf16 with fp32 accumulation. */
+ * `in_dtype` (BEBELM_F32 or BEBELM_BF16); out [t][n_heads*64] fp32. The cache
+ * always stores the fp32 normed/roped k and raw v. BEBELM_BF16 inputs run the
+ * attention on the tensor cores (tcgen05, bf16 operands, fp32 accumulation,
+ * within 2e-2 relative of the reference); BEBELM_F32 inputs keep the reference's
+ * fp32 arithmetic on the CUDA cores (within 1e-3 absolute). */
 BEBELM_API int bebelm_attn_prefill(bebelm_kv* kv, int layer, int n_heads, const void* q, const void* k,
                         const void* v, int in_dtype, size_t t, size_t pos0,
                         const float* q_gain, const float* k_gain, float theta, float eps,

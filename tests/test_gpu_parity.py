@@ -307,3 +307,63 @@ def test_config2_prefill_2048():
     got = dev.attn_prefill(0, q, k, v, qg, kg, 0, theta=1e6)
     want, _, _, _, _ = oracle.attn_batch(q, k, v, 0, qg, kg, 1e6, 1e-5, H, KVH, D, n_threads=oracle.max_threads())
     assert np.abs(got - want).max() <= DECODE_ATOL
+
+
+# ------------------------------------------------ tensor-core prefill (bf16) --
+PREFILL_REL = 2e-2  # bf16 operands, fp32 accumulation: max |err| / max |want|
+
+
+def _bf16_round(x):
+    torch = pytest.importorskip("torch")
+    return torch.from_numpy(np.ascontiguousarray(x)).to(torch.bfloat16).float().numpy()
+
+
+def _prefill_bf16(dev_cache, q, k, v, qg, kg, pos0, theta):
+    torch = pytest.importorskip("torch")
+    tq, tk, tv = (torch.from_numpy(np.ascontiguousarray(x)).cuda().to(torch.bfloat16) for x in (q, k, v))
+    tqg, tkg = torch.from_numpy(qg).cuda(), torch.from_numpy(kg).cuda()
+    out = dev_cache.attn_prefill(0, tq, tk, tv, tqg, tkg, pos0, theta=theta)
+    torch.cuda.synchronize()
+    return out.cpu().numpy()
+
+
+@pytest.mark.parametrize("t", [128, 300, 1000])
+def test_tensor_core_prefill_matches_oracle(t):
+    qg, kg = gains(61)
+    q, k, v = (_bf16_round(oracle.normal(s, shp)) for s, shp in ((1, (t, HID)), (2, (t, KVD)), (3, (t, KVD))))
+    dev = bb.Cache(n_layers=1, max_context=4096)
+    got = _prefill_bf16(dev, q, k, v, qg, kg, 0, 1e6)
+    want = oracle.attn_batch(q, k, v, 0, qg, kg, 1e6, 1e-5, H, KVH, D, n_threads=oracle.max_threads())[0]
+    rel = np.abs(got - want).max() / np.abs(want).max()
+    assert rel <= PREFILL_REL, rel
+    # the cache holds the fp32 normed/roped keys and raw values either way
+    kd, vd = dev.read(0)
+    ck = oracle.attn_batch(q, k, v, 0, qg, kg, 1e6, 1e-5, H, KVH, D)[1]
+    assert np.abs(kd - ck).max() <= ROPE_ATOL and np.array_equal(vd, v)
+
+
+def test_tensor_core_prefill_on_a_cached_prefix():
+    """A chunk after 333 cached positions (not a multiple of the 128-key tile), after eviction."""
+    qg, kg = gains(71)
+    dev = bb.Cache(n_layers=1, max_context=4096)
+    pk, pv = oracle.normal(5, (400, KVD)), oracle.normal(6, (400, KVD))
+    dev.append(0, pk, pv)
+    dev.evict_front(67)
+    t = 257
+    q, k, v = (_bf16_round(oracle.normal(s, shp)) for s, shp in ((7, (t, HID)), (8, (t, KVD)), (9, (t, KVD))))
+    got = _prefill_bf16(dev, q, k, v, qg, kg, 400, 5e6)
+    want = oracle.attn_batch(q, k, v, 400, qg, kg, 5e6, 1e-5, H, KVH, D, pk[67:], pv[67:],
+                             n_threads=oracle.max_threads())[0]
+    rel = np.abs(got - want).max() / np.abs(want).max()
+    assert rel <= PREFILL_REL, rel
+
+
+def test_config2_tensor_core_prefill_2048():
+    t = 2048
+    qg, kg = gains(81)
+    q, k, v = (_bf16_round(oracle.normal(s, shp)) for s, shp in ((11, (t, HID)), (12, (t, KVD)), (13, (t, KVD))))
+    dev = bb.Cache(n_layers=1, max_context=t)
+    got = _prefill_bf16(dev, q, k, v, qg, kg, 0, 1e6)
+    want = oracle.attn_batch(q, k, v, 0, qg, kg, 1e6, 1e-5, H, KVH, D, n_threads=oracle.max_threads())[0]
+    rel = np.abs(got - want).max() / np.abs(want).max()
+    assert rel <= PREFILL_REL, rel
