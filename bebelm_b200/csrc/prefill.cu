@@ -14,10 +14,12 @@
 //     TMEM columns [0,128) and commits to an mbarrier.
 //   * Every thread loads its S row from TMEM (tcgen05.ld 32x32b), applies the
 //     causal mask and the online softmax in fp32 (exp2 with log2e folded into
-//     the scale), and writes P in bf16 to shared memory in the 128-byte-swizzled
-//     K-major layout the MMA reads.
-//   * Thread 0 issues O_tile = P V as 8 tcgen05.mma (N=64, K=16, V read
-//     MN-major) into TMEM columns [128,192); each thread folds its row into the
+//     the scale), and writes P in bf16 back into TMEM over its S columns
+//     (tcgen05.st), where the next MMA reads it as the A operand.
+//   * Thread 0 issues O_tile = P V as 8 tcgen05.mma (A = P from TMEM, N=64,
+//     K=16, V read MN-major from shared memory) into TMEM columns [128,192);
+//     80 KB of shared memory and 256 TMEM columns let 2 CTAs share an SM, so
+//     one CTA's softmax overlaps the other's MMAs. Each thread folds its row into the
 //     fp32 output held in registers with the running rescale.
 // Tiles entirely above the diagonal are never visited. Every mbarrier wait is
 // bounded: on timeout the CTA records kErrWaitTimeout, waits (bounded) for its
@@ -30,19 +32,9 @@
 namespace bebelm {
 namespace {
 
-constexpr int kThreads = 128;
 constexpr int kTileQ = 128, kTileK = 128;
 constexpr int kTileBytes = kTileQ * kHeadDim * 2;  // 16 KB: 128 rows x 128 B
-constexpr int kTmemCols = 256;                     // S: [0,128), O tile: [128,192)
 constexpr long long kWaitLimit = 1ll << 22;
-
-// shared memory map (offsets from a 1024-byte aligned base)
-constexpr int kOffQ = 0;
-constexpr int kOffK = kOffQ + kTileBytes;           // 2 buffers
-constexpr int kOffV = kOffK + 2 * kTileBytes;       // 2 buffers
-constexpr int kOffP = kOffV + 2 * kTileBytes;       // 2 blocks of 64 keys
-constexpr int kOffBar = kOffP + 2 * kTileBytes;
-constexpr int kSmemBytes = kOffBar + 64 + 1024;     // barriers + alignment slack
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -66,6 +58,33 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, unsigned parity)
         if (ok) return true;
     }
     return false;
+}
+// Same bound, but polling with test_wait: the issuing thread never sleeps, so it reacts to
+// a completed phase at once (one thread spins; the other 31 lanes of its warp are parked).
+__device__ __forceinline__ bool mbar_spin_bounded(uint32_t bar, unsigned parity) {
+    for (long long it = 0; it < 64 * kWaitLimit; ++it) {
+        uint32_t ok;
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+            "selp.u32 %0, 1, 0, p;\n\t}"
+            : "=r"(ok)
+            : "r"(bar), "r"(parity)
+            : "memory");
+        if (ok) return true;
+    }
+    return false;
+}
+__device__ __forceinline__ bool mbar_test(uint32_t bar, unsigned parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
 }
 __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, int c0, int c1, int c2,
                                             uint32_t bar) {
@@ -121,168 +140,358 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
     for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// 32 lanes x 64 consecutive columns into 64 registers, wait included (see tmem_ld32).
+__device__ __forceinline__ void tmem_ld64(uint32_t taddr, float* v) {
+    uint32_t r[64];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x64.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32, %33, %34, %35, "
+        "%36, %37, %38, %39, %40, %41, %42, %43, %44, %45, %46, %47, %48, %49, %50, %51, %52, %53, %54, %55, %56, "
+        "%57, %58, %59, %60, %61, %62, %63}, [%64];\n\t"
+        "tcgen05.wait::ld.sync.aligned;"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31]),
+          "=r"(r[32]), "=r"(r[33]), "=r"(r[34]), "=r"(r[35]), "=r"(r[36]), "=r"(r[37]), "=r"(r[38]), "=r"(r[39]),
+          "=r"(r[40]), "=r"(r[41]), "=r"(r[42]), "=r"(r[43]), "=r"(r[44]), "=r"(r[45]), "=r"(r[46]), "=r"(r[47]),
+          "=r"(r[48]), "=r"(r[49]), "=r"(r[50]), "=r"(r[51]), "=r"(r[52]), "=r"(r[53]), "=r"(r[54]), "=r"(r[55]),
+          "=r"(r[56]), "=r"(r[57]), "=r"(r[58]), "=r"(r[59]), "=r"(r[60]), "=r"(r[61]), "=r"(r[62]), "=r"(r[63])
+        : "r"(taddr));
+#pragma unroll
+    for (int i = 0; i < 64; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// 32 lanes x 32 consecutive 32-bit TMEM columns from 32 registers per thread.
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t* r) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr),
+        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+        "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]),
+        "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]),
+        "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+        : "memory");
+}
+__device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// O_tile += P V with A (= P) read from TMEM.
+__device__ __forceinline__ void mma_bf16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b, uint32_t idesc,
+                                            uint32_t acc) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(b), "r"(idesc), "r"(acc)
+        : "memory");
+}
+
+__device__ __forceinline__ float ex2(float x) {  // 2^x on the MUFU unit; -inf gives 0
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
 __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
     __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
     return *reinterpret_cast<uint32_t*>(&h);
 }
 
-__global__ void __launch_bounds__(kThreads, 1)
+#ifdef BEBELM_PREFILL_TRACE
+__device__ long long g_trace[16 * 2 * 64];  // [event][tile][j] = clock64, CTA (0,0) only
+#define TRACE(ev, j, X)                                                           \
+    do {                                                                          \
+        if (blockIdx.x == 0 && blockIdx.y == 0 && (j) < 64)                       \
+            g_trace[((ev) * 2 + (X)) * 64 + (j)] = clock64();                     \
+    } while (0)
+#else
+#define TRACE(ev, j, X) \
+    do {                \
+    } while (0)
+#endif
+
+// ---- roles: warps 0-3 softmax for tile A, 4-7 softmax for tile B, 8 TMA, 9 MMA ----
+constexpr int kWarps = 10;
+constexpr int kCtaThreads = kWarps * 32;
+constexpr int kStages = 3;                              // K/V ring depth
+constexpr float kRescaleSlack = 8.0f;                   // log2 headroom before O is rescaled
+// shared memory map v2 (offsets from a 1024-byte aligned base)
+constexpr int kOff2Q = 0;                               // Q_A, Q_B
+constexpr int kOff2K = 2 * kTileBytes;                  // kStages K tiles
+constexpr int kOff2V = kOff2K + kStages * kTileBytes;   // kStages V tiles
+constexpr int kOff2Bar = kOff2V + kStages * kTileBytes;
+// barriers (8 bytes each)
+constexpr int kBarQ = 0, kBarK = 1, kBarV = kBarK + kStages, kBarEmpty = kBarV + kStages,
+              kBarS = kBarEmpty + kStages, kBarP = kBarS + 2, kBarO = kBarP + 2, kBarC = kBarO + 2,
+              kNumBars = kBarC + 2;
+constexpr int kSmem2Bytes = kOff2Bar + 8 * kNumBars + 1024;
+constexpr int kTmem2Cols = 512;  // S_A [0,128) S_B [128,256) P_A [256,320) P_B [320,384) O_A [384,448) O_B [448,512)
+constexpr int kColP = 256, kColO = 384;
+
+__global__ void __launch_bounds__(kCtaThreads, 1)
     prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                    const __grid_constant__ CUtensorMap tm_v, PrefillArgs a) {
     extern __shared__ unsigned char smem_raw[];
     unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const uint32_t sbase = smem_u32(smem);
-    const uint32_t bar_q = sbase + kOffBar, bar_kv0 = bar_q + 8, bar_s = bar_q + 24, bar_o = bar_q + 32;
+    auto bar = [&](int i) -> uint32_t { return sbase + kOff2Bar + 8 * i; };
     __shared__ uint32_t s_tmem;
     __shared__ int s_fail;
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int n_qt = (a.t + kTileQ - 1) / kTileQ;
-    const int qt = n_qt - 1 - (int)blockIdx.x;  // longest rows first
-    const int h = blockIdx.y, kvh = h / (a.n_heads / a.n_kv);
-    const int q0 = qt * kTileQ;
-    const int q_last = min(q0 + kTileQ, a.t) - 1;
-    const int n_kt = (a.len_before + q_last) / kTileK + 1;
+    const int n_pairs = (n_qt + 1) / 2;
+    // grid (heads, pairs): all heads' longest tile pairs are scheduled before any shorter one
+    const int pair = n_pairs - 1 - (int)blockIdx.y;
+    const int h = blockIdx.x, kvh = h / (a.n_heads / a.n_kv);
+    // tile X in {0 (A), 1 (B)} covers queries [q0_X, q0_X + 128)
+    auto n_kt_of = [&](int X) -> int {
+        const int q0 = (2 * pair + X) * kTileQ;
+        if (q0 >= a.t) return 0;
+        return (a.len_before + min(q0 + kTileQ, a.t) - 1) / kTileK + 1;
+    };
+    const int nkt[2] = {n_kt_of(0), n_kt_of(1)};
+    const int nkt_max = max(nkt[0], nkt[1]);
 
     if (warp == 0) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&s_tmem)),
-                     "r"(kTmemCols));
+                     "r"(kTmem2Cols));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
     }
     if (tid == 0) {
         s_fail = 0;
-        for (int i = 0; i < 5; ++i) mbar_init(bar_q + 8 * i, 1);
+        for (int i = 0; i < kNumBars; ++i) mbar_init(bar(i), (i >= kBarP && i < kBarP + 2) || (i >= kBarC && i < kBarC + 2) ? 128 : 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        mbar_expect_tx(bar_q, kTileBytes);
-        tma_load_3d(sbase + kOffQ, &tm_q, 0, h, q0, bar_q);
-        for (int i = 0; i < 2 && i < n_kt; ++i) {
-            mbar_expect_tx(bar_kv0 + 8 * i, 2 * kTileBytes);
-            tma_load_3d(sbase + kOffK + i * kTileBytes, &tm_k, 0, kvh, i * kTileK, bar_kv0 + 8 * i);
-            tma_load_3d(sbase + kOffV + i * kTileBytes, &tm_v, 0, kvh, i * kTileK, bar_kv0 + 8 * i);
-        }
     }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = s_tmem;
-    const uint32_t t_row = tmem + ((uint32_t)(32 * warp) << 16);  // this warp's TMEM lanes
 
-    const int row = 32 * warp + lane;
-    const int qi = q0 + row;
-    const long long key_lim = (long long)a.len_before + qi;  // last key this row may see
-    float o[kHeadDim];
-#pragma unroll
-    for (int d = 0; d < kHeadDim; ++d) o[d] = 0.f;
-    float m = -INFINITY, l = 0.f;
-    constexpr uint32_t kIdescS = instr_desc(kTileK, false), kIdescO = instr_desc(kHeadDim, true);
-    bool failed = false;
-    int kt = 0;
-    for (; kt < n_kt; ++kt) {
-        const int b = kt & 1;
-        // ---- S = Q K^T ------------------------------------------------------
-        if (tid == 0) {
-            bool ok = (kt > 0 || mbar_wait_bounded(bar_q, 0)) && mbar_wait_bounded(bar_kv0 + 8 * b, (kt >> 1) & 1);
-            if (ok) {
-                tc_fence_after();
-                const uint32_t qa = sbase + kOffQ, ka = sbase + kOffK + b * kTileBytes;
-#pragma unroll
-                for (int k = 0; k < kHeadDim / 16; ++k)
-                    mma_bf16(tmem, smem_desc(qa + 32 * k, 16, 1024), smem_desc(ka + 32 * k, 16, 1024), kIdescS, k > 0);
-                mma_commit(bar_s);
-            } else {
-                s_fail = 1;
+    if (warp == 8) {
+        // ---------------- TMA producer ----------------
+        if (lane == 0) {
+            mbar_expect_tx(bar(kBarQ), 2 * kTileBytes);
+            tma_load_3d(sbase + kOff2Q, &tm_q, 0, h, (2 * pair) * kTileQ, bar(kBarQ));
+            tma_load_3d(sbase + kOff2Q + kTileBytes, &tm_q, 0, h, (2 * pair + 1) * kTileQ, bar(kBarQ));
+            for (int j = 0; j < nkt_max; ++j) {
+                const int st = j % kStages;
+                if (j >= kStages && !mbar_wait_bounded(bar(kBarEmpty + st), ((j / kStages) - 1) & 1)) {
+                    s_fail = 1;
+                    break;
+                }
+                TRACE(5, j, 0);
+                mbar_expect_tx(bar(kBarK + st), kTileBytes);
+                tma_load_3d(sbase + kOff2K + st * kTileBytes, &tm_k, 0, kvh, j * kTileK, bar(kBarK + st));
+                mbar_expect_tx(bar(kBarV + st), kTileBytes);
+                tma_load_3d(sbase + kOff2V + st * kTileBytes, &tm_v, 0, kvh, j * kTileK, bar(kBarV + st));
             }
         }
-        const bool ok_s = mbar_wait_bounded(bar_s, kt & 1);
-        if (__syncthreads_or(!ok_s || s_fail)) {
-            failed = true;
-            break;
-        }
-        tc_fence_after();
-        // ---- online softmax on this thread's row -----------------------------
-        float s[kTileK];
+    } else if (warp == 9) {
+        // ---------------- MMA issuer ----------------
+        // A polling scheduler over both query tiles: S_X(j) = Q_X K(j)^T as soon as K(j) is
+        // in and softmax has read S_X(j-1); O_X += P_X(j) V(j) as soon as V(j) and P_X(j) are
+        // in. Either kind may go first, so one tile waiting for its softmax never holds back
+        // the other tile's MMAs. No barrier can run two phases ahead of these tests: S_X(j)
+        // needs S_X(j-1) read, and softmax writes P_X(j) only after PV_X(j-1) completed.
+        if (lane == 0) {
+            constexpr uint32_t kIdescS = instr_desc(kTileK, false), kIdescO = instr_desc(kHeadDim, true);
+            const uint64_t dq0 = smem_desc(sbase + kOff2Q, 16, 1024), dq1 = smem_desc(sbase + kOff2Q + kTileBytes, 16, 1024);
+            bool ok = mbar_spin_bounded(bar(kBarQ), 0);
+            int nS[2] = {0, 0}, nPV[2] = {0, 0}, n_free = 0;
+            long long idle = 0;
+            while (ok && (nPV[0] < nkt[0] || nPV[1] < nkt[1])) {
+                bool progress = false;
 #pragma unroll
-        for (int c = 0; c < kTileK; c += 32) tmem_ld32(t_row + c, s + c);
-        const long long k0 = (long long)kt * kTileK;
-        float mx = m;
+                for (int X = 0; X < 2; ++X) {
+                    const int js = nS[X];
+                    if (js < nkt[X] && mbar_test(bar(kBarK + js % kStages), (js / kStages) & 1) &&
+                        (js == 0 || mbar_test(bar(kBarC + X), (js - 1) & 1))) {
+                        tc_fence_after();
+                        const uint64_t dq = X ? dq1 : dq0;
+                        const uint64_t dk = smem_desc(sbase + kOff2K + (js % kStages) * kTileBytes, 16, 1024);
 #pragma unroll
-        for (int c = 0; c < kTileK; ++c) {
-            s[c] = (k0 + c <= key_lim) ? s[c] * a.scale_log2 : -INFINITY;
-            mx = fmaxf(mx, s[c]);
-        }
-        const float alpha = exp2f(m - mx);  // m = -inf gives 0
-        m = mx;
-        float psum = 0.f;
-        unsigned char* pbase = smem + kOffP;
+                        for (int k = 0; k < kHeadDim / 16; ++k)  // 16 dims: +32 B in both operands
+                            mma_bf16(tmem + 128 * X, dq + (uint64_t)(2 * k), dk + (uint64_t)(2 * k), kIdescS, k > 0);
+                        mma_commit(bar(kBarS + X));
+                        TRACE(2, js, X);
+                        ++nS[X];
+                        progress = true;
+                    }
+                    const int jp = nPV[X];
+                    if (jp < nS[X] && mbar_test(bar(kBarV + jp % kStages), (jp / kStages) & 1) &&
+                        mbar_test(bar(kBarP + X), jp & 1)) {
+                        tc_fence_after();
+                        const uint64_t dv = smem_desc(sbase + kOff2V + (jp % kStages) * kTileBytes, kTileBytes, 1024);
 #pragma unroll
-        for (int c = 0; c < kTileK; c += 8) {
-            float p[8];
-#pragma unroll
-            for (int e = 0; e < 8; ++e) {
-                p[e] = exp2f(s[c + e] - mx);
-                psum += p[e];
+                        for (int k = 0; k < kTileK / 16; ++k)  // 16 keys: +8 TMEM columns of P, +2048 B of V
+                            mma_bf16_ts(tmem + kColO + 64 * X, tmem + kColP + 64 * X + 8 * k, dv + (uint64_t)(128 * k),
+                                        kIdescO, (jp > 0 || k > 0));
+                        mma_commit(bar(kBarO + X));
+                        TRACE(1, jp, X);
+                        ++nPV[X];
+                        progress = true;
+                    }
+                }
+                // a K/V stage is free once every PV that reads it has been issued (the commit
+                // fires when they complete)
+                while (n_free < nkt_max && (nPV[0] > n_free || nkt[0] <= n_free) &&
+                       (nPV[1] > n_free || nkt[1] <= n_free)) {
+                    mma_commit(bar(kBarEmpty + n_free % kStages));
+                    ++n_free;
+                }
+                if (progress) {
+                    idle = 0;
+                } else if (++idle > 64 * kWaitLimit) {
+                    ok = false;
+                }
             }
-            uint4 w = make_uint4(pack_bf16(p[0], p[1]), pack_bf16(p[2], p[3]), pack_bf16(p[4], p[5]),
-                                 pack_bf16(p[6], p[7]));
-            const int blk = c >> 6, chunk = (c & 63) >> 3;
-            *reinterpret_cast<uint4*>(pbase + blk * kTileBytes + row * 128 + ((chunk ^ (row & 7)) << 4)) = w;
+            if (!ok) s_fail = 1;
         }
-        l = l * alpha + psum;
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        tc_fence_before();
-        __syncthreads();
-        // ---- O_tile = P V ----------------------------------------------------
-        if (tid == 0) {
+    } else if (warp < 8) {
+        // ---------------- softmax warpgroups ----------------
+        const int X = warp >> 2;               // tile
+        const int row = 32 * (warp & 3) + lane;  // TMEM lane
+        const int qi = (2 * pair + X) * kTileQ + row;
+        const long long key_lim = (long long)a.len_before + qi;
+        const uint32_t t_s = tmem + ((uint32_t)(32 * (warp & 3)) << 16) + 128 * X;
+        const uint32_t t_p = tmem + ((uint32_t)(32 * (warp & 3)) << 16) + kColP + 64 * X;
+        const uint32_t t_o = tmem + ((uint32_t)(32 * (warp & 3)) << 16) + kColO + 64 * X;
+        float m_used = -INFINITY, l = 0.f;
+        bool ok = true;
+        for (int j = 0; j < nkt[X]; ++j) {
+            ok = __all_sync(0xffffffffu, mbar_wait_bounded(bar(kBarS + X), j & 1));
+            if (!ok) break;
+            if ((warp & 3) == 0 && lane == 0) TRACE(3, j, X);
             tc_fence_after();
-            const uint32_t pa = sbase + kOffP, va = sbase + kOffV + b * kTileBytes;
+            const long long k0 = (long long)j * kTileK;
+            const bool diag = k0 + kTileK - 1 > (long long)a.len_before + (2 * pair + X) * kTileQ;
+            // keys of this tile this row may see: columns [0, lim] (all of them off the diagonal)
+            const long long lim_ll = key_lim - k0;
+            const int lim = diag ? (lim_ll < kTileK - 1 ? (int)lim_ll : kTileK - 1) : kTileK - 1;
+            // pass 1: row max, 64 columns at a time, 8 independent chains
+            float mxv[8];
 #pragma unroll
-            for (int k = 0; k < kTileK / 16; ++k)
-                mma_bf16(tmem + 128, smem_desc(pa + (k >> 2) * kTileBytes + 32 * (k & 3), 16, 1024),
-                         smem_desc(va + 2048 * k, kTileBytes, 1024), kIdescO, k > 0);
-            mma_commit(bar_o);
-        }
-        const bool ok_o = mbar_wait_bounded(bar_o, kt & 1);
-        if (__syncthreads_or(!ok_o)) {
-            failed = true;
-            break;
-        }
-        tc_fence_after();
-        float pv[kHeadDim];
-        tmem_ld32(t_row + 128, pv);
-        tmem_ld32(t_row + 160, pv + 32);
+            for (int e = 0; e < 8; ++e) mxv[e] = -INFINITY;
 #pragma unroll
-        for (int d = 0; d < kHeadDim; ++d) o[d] = fmaf(o[d], alpha, pv[d]);
-        tc_fence_before();
-        __syncthreads();  // S, P and this K/V buffer are free again
-        if (tid == 0 && kt + 2 < n_kt) {
-            mbar_expect_tx(bar_kv0 + 8 * b, 2 * kTileBytes);
-            tma_load_3d(sbase + kOffK + b * kTileBytes, &tm_k, 0, kvh, (kt + 2) * kTileK, bar_kv0 + 8 * b);
-            tma_load_3d(sbase + kOffV + b * kTileBytes, &tm_v, 0, kvh, (kt + 2) * kTileK, bar_kv0 + 8 * b);
+            for (int c = 0; c < kTileK; c += 64) {
+                float v[64];
+                if ((warp & 3) == 0 && lane == 0 && c == 0) TRACE(9, j, X);
+                tmem_ld64(t_s + c, v);
+                if ((warp & 3) == 0 && lane == 0 && c == 0) TRACE(10, j, X);
+                if (diag) {
+#pragma unroll
+                    for (int e = 0; e < 64; ++e)
+                        if (c + e <= lim) mxv[e & 7] = fmaxf(mxv[e & 7], v[e]);
+                } else {
+#pragma unroll
+                    for (int e = 0; e < 64; ++e) mxv[e & 7] = fmaxf(mxv[e & 7], v[e]);
+                }
+            }
+            if ((warp & 3) == 0 && lane == 0) TRACE(6, j, X);
+            const float mx = fmaxf(fmaxf(fmaxf(mxv[0], mxv[1]), fmaxf(mxv[2], mxv[3])),
+                                   fmaxf(fmaxf(mxv[4], mxv[5]), fmaxf(mxv[6], mxv[7]))) * a.scale_log2;
+            // lazy rescale: move the reference max only when a score would exceed it by 2^8
+            const bool bump = mx > m_used + kRescaleSlack;
+            const float m_new = bump ? mx : m_used;
+            const float f = ex2(m_used - m_new);  // 1 without a bump, 0 on the first tile
+            l *= f;
+            m_used = m_new;
+            const float neg_m = -m_used;
+            // pass 2: P = 2^(s - m) in bf16 (two keys per 32-bit column)
+            float ps[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) ps[e] = 0.f;
+            uint32_t w[64];
+#pragma unroll
+            for (int c = 0; c < kTileK; c += 64) {
+                float v[64];
+                tmem_ld64(t_s + c, v);
+                if (c + 64 == kTileK) {  // S_X(j) fully read: the next S may overwrite it
+                    tc_fence_before();
+                    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar(kBarC + X)) : "memory");
+                }
+                if (diag) {
+#pragma unroll
+                    for (int e = 0; e < 32; ++e) {
+                        const float p0 = c + 2 * e <= lim ? ex2(fmaf(v[2 * e], a.scale_log2, neg_m)) : 0.f;
+                        const float p1 = c + 2 * e + 1 <= lim ? ex2(fmaf(v[2 * e + 1], a.scale_log2, neg_m)) : 0.f;
+                        ps[e & 7] += p0 + p1;
+                        w[c / 2 + e] = pack_bf16(p0, p1);
+                    }
+                } else {
+#pragma unroll
+                    for (int e = 0; e < 32; ++e) {
+                        const float p0 = ex2(fmaf(v[2 * e], a.scale_log2, neg_m));
+                        const float p1 = ex2(fmaf(v[2 * e + 1], a.scale_log2, neg_m));
+                        ps[e & 7] += p0 + p1;
+                        w[c / 2 + e] = pack_bf16(p0, p1);
+                    }
+                }
+            }
+            // P_X and O_X are read by PV(j-1): wait for it before writing either (S(j) no
+            // longer implies it, since S(j) is issued before PV(j-1))
+            if (j > 0) {
+                ok = __all_sync(0xffffffffu, mbar_wait_bounded(bar(kBarO + X), (j - 1) & 1));
+                if (!ok) break;
+                tc_fence_after();
+            }
+            tmem_st32(t_p, w);
+            tmem_st32(t_p + 32, w + 32);
+            const float psum = ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
+            if ((warp & 3) == 0 && lane == 0) TRACE(7, j, X);
+            if (__any_sync(0xffffffffu, bump && j > 0)) {
+                // PV(j-1) has completed (waited above) and PV(j) waits for this thread: O_X is stable
+#pragma unroll
+                for (int half = 0; half < 2; ++half) {
+                    float o[32];
+                    uint32_t w[32];
+                    tmem_ld32(t_o + 32 * half, o);
+#pragma unroll
+                    for (int e = 0; e < 32; ++e) w[e] = __float_as_uint(o[e] * f);
+                    tmem_st32(t_o + 32 * half, w);
+                }
+            }
+            l += psum;
+            tmem_st_wait();
+            if ((warp & 3) == 0 && lane == 0) TRACE(8, j, X);
+            tc_fence_before();
+            asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar(kBarP + X)) : "memory");
+            if ((warp & 3) == 0 && lane == 0) TRACE(4, j, X);
+        }
+        // epilogue: wait for the last PV, normalise, store
+        if (ok && nkt[X] > 0) ok = __all_sync(0xffffffffu, mbar_wait_bounded(bar(kBarO + X), (nkt[X] - 1) & 1));
+        if (!ok) {
+            s_fail = 1;
+        } else if (nkt[X] > 0) {
+            tc_fence_after();
+            float o[kHeadDim];
+            tmem_ld32(t_o, o);
+            tmem_ld32(t_o + 32, o + 32);
+            if (qi < a.t) {
+                const float inv = l > 0.f ? 1.f / l : 0.f;
+                float4* dst = reinterpret_cast<float4*>(a.out + ((size_t)qi * a.n_heads + h) * kHeadDim);
+#pragma unroll
+                for (int d = 0; d < kHeadDim; d += 4)
+                    dst[d / 4] = make_float4(o[d] * inv, o[d + 1] * inv, o[d + 2] * inv, o[d + 3] * inv);
+            }
         }
     }
 
-    if (failed) {
-        if (tid == 0) {
-            atomicExch(a.err, kErrWaitTimeout);
-            // let whatever this CTA started land before its memory goes away
-            mbar_wait_bounded(bar_q, 0);
-            for (int k = kt; k < kt + 2 && k < n_kt; ++k) mbar_wait_bounded(bar_kv0 + 8 * (k & 1), (k >> 1) & 1);
-            mbar_wait_bounded(bar_s, kt & 1);
-            mbar_wait_bounded(bar_o, kt & 1);
-        }
-    } else if (qi < a.t) {
-        const float inv = l > 0.f ? 1.f / l : 0.f;
-        float4* dst = reinterpret_cast<float4*>(a.out + ((size_t)qi * a.n_heads + h) * kHeadDim);
-#pragma unroll
-        for (int d = 0; d < kHeadDim; d += 4)
-            dst[d / 4] = make_float4(o[d] * inv, o[d + 1] * inv, o[d + 2] * inv, o[d + 3] * inv);
-    }
     tc_fence_before();
     __syncthreads();
+    if (s_fail && tid == 0) {
+        atomicExch(a.err, kErrWaitTimeout);
+        // let copies and MMAs this CTA started land (bounded) before its memory goes away
+        for (int st = 0; st < kStages; ++st) {
+            mbar_wait_bounded(bar(kBarK + st), 0);
+            mbar_wait_bounded(bar(kBarV + st), 0);
+        }
+        for (int X = 0; X < 2; ++X) mbar_wait_bounded(bar(kBarO + X), 0);
+    }
     if (warp == 0) {
         tc_fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmem2Cols));
     }
 }
 
@@ -325,12 +534,13 @@ cudaError_t launch_prefill(const PrefillArgs& a, cudaStream_t s) {
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 0 || dev >= 64 || !attr_set[dev]) {
-        cudaError_t e = cudaFuncSetAttribute(prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+        cudaError_t e = cudaFuncSetAttribute(prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem2Bytes);
         if (e != cudaSuccess) return e;
         if (dev >= 0 && dev < 64) attr_set[dev] = true;
     }
-    dim3 grid((unsigned)((a.t + kTileQ - 1) / kTileQ), (unsigned)a.n_heads);
-    prefill_kernel<<<grid, kThreads, kSmemBytes, s>>>(mq, mk, mv, a);
+    const int n_qt = (a.t + kTileQ - 1) / kTileQ;
+    dim3 grid((unsigned)a.n_heads, (unsigned)((n_qt + 1) / 2));
+    prefill_kernel<<<grid, kCtaThreads, kSmem2Bytes, s>>>(mq, mk, mv, a);
     return cudaGetLastError();
 }
 
