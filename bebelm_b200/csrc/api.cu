@@ -135,7 +135,7 @@ struct bebelm_kv_pool {
     int num_sms = 148;
     int n_seqs = 0;              // live sequences drawing from this pool
     // scratch shared by every call on this pool's sequences (stream-ordered)
-    DevBuf io, qn, part, counters, seqdesc, bf16, err, pf;
+    DevBuf io, qn, part, counters, seqdesc, err, pf;
     PinBuf pin;
     std::vector<DecodeSeq> h_desc;
     // cache slots written by the most recent library kernel on this pool: a decode
@@ -295,7 +295,6 @@ void pool_free(bebelm_kv_pool* P) {
     P->part.release();
     P->counters.release();
     P->seqdesc.release();
-    P->bf16.release();
     P->pf.release();
     P->err.release();
     P->pin.release();
@@ -977,14 +976,6 @@ int bebelm_attn_prefill(bebelm_kv* kv, int layer, int n_heads, const void* q, co
         dq = a0; dk = a1; dv = a2;
         dqg = (const float*)a3; dkg = (const float*)a4; dout = (float*)o;
     }
-    if (in_dtype == BEBELM_BF16) {
-        TRY(P->bf16.ensure(4 * (qn + 2 * kvn), false, s));
-        float* f = P->bf16.as<float>();
-        CUDA_TRY(launch_bf16_to_f32((const __nv_bfloat16*)dq, f, qn, s));
-        CUDA_TRY(launch_bf16_to_f32((const __nv_bfloat16*)dk, f + qn, kvn, s));
-        CUDA_TRY(launch_bf16_to_f32((const __nv_bfloat16*)dv, f + qn + kvn, kvn, s));
-        dq = f; dk = f + qn; dv = f + qn + kvn;
-    }
     long long slot0 = 0;
     TRY(reserve(kv, layer, t, &slot0, s));
     const long long len_before = kv->len[layer] - (long long)t;
@@ -996,6 +987,14 @@ int bebelm_attn_prefill(bebelm_kv* kv, int layer, int n_heads, const void* q, co
         __nv_bfloat16* qb = P->pf.as<__nv_bfloat16>();
         __nv_bfloat16* kb = qb + ((qn + 127) & ~size_t(127));
         __nv_bfloat16* vb = kb + ((s_total * kvrow + 127) & ~size_t(127));
+        // descriptors first, so the two kernels below go out back to back
+        PrefillArgs pa{};
+        pa.q = qb; pa.k = kb; pa.v = vb; pa.out = dout;
+        pa.t = (int)t; pa.len_before = (int)len_before; pa.n_heads = n_heads; pa.n_kv = P->n_kv;
+        pa.scale_log2 = 0.125f * 1.4426950408889634f;
+        pa.err = P->err.as<int>();
+        PrefillMaps maps;
+        if (!prefill_make_maps(pa, &maps)) return fail(BEBELM_ERR_CUDA, "building the TMA tensor maps for prefill failed");
         if (len_before > 0)
             CUDA_TRY(launch_kv_gather_bf16(P->view(layer), kv->d_table, kv->cap, kv->base[layer], len_before, P->n_kv,
                                            kb, vb, s));
@@ -1008,16 +1007,10 @@ int bebelm_attn_prefill(bebelm_kv* kv, int layer, int n_heads, const void* q, co
         a.norm_q = 1; a.norm_k = 1;
         a.q_bf16 = qb; a.k_bf16 = kb + (size_t)len_before * kvrow; a.v_bf16 = vb + (size_t)len_before * kvrow;
         a.append = 1; a.pv = P->view(layer); a.table = kv->d_table; a.cap = kv->cap; a.slot0 = slot0;
+        a.in_bf16 = 1;  // norm + RoPE read the bf16 inputs directly
         CUDA_TRY(launch_norm_rope(a, s));
         P->last_writes.assign(1, {kv, layer, slot0});
-        PrefillArgs pa{};
-        pa.q = qb; pa.k = kb; pa.v = vb; pa.out = dout;
-        pa.t = (int)t; pa.len_before = (int)len_before; pa.n_heads = n_heads; pa.n_kv = P->n_kv;
-        pa.scale_log2 = 0.125f * 1.4426950408889634f;
-        pa.err = P->err.as<int>();
-        cudaError_t e = launch_prefill(pa, s);
-        if (e == cudaErrorInvalidValue) return fail(BEBELM_ERR_CUDA, "building the TMA tensor maps for prefill failed");
-        CUDA_TRY(e);
+        CUDA_TRY(launch_prefill(pa, maps, s));
         P->last_writes.clear();
         if (mem == BEBELM_MEM_HOST) return stage_out(P, dout, out, 4 * qn, s);
         return 0;

@@ -74,6 +74,7 @@ struct NormRopeArgs {
     int cap;
     long long slot0;  // logical slot of token 0
     const AppendTarget* targets;  // non-null: per-token table/slot/pos instead of the above
+    int in_bf16;                  // q, k, v hold bf16 (head_dim 64 only)
 };
 cudaError_t launch_norm_rope(const NormRopeArgs& a, cudaStream_t s);
 
@@ -81,8 +82,6 @@ cudaError_t launch_norm_rope(const NormRopeArgs& a, cudaStream_t s);
 // [len][n_kv][64] (either output may be null).
 cudaError_t launch_kv_gather(const PoolView& pv, const int* table, int cap, long long base, long long len,
                              int n_kv, float* k_out, float* v_out, cudaStream_t s);
-// bf16 -> fp32, n elements.
-cudaError_t launch_bf16_to_f32(const __nv_bfloat16* in, float* out, size_t n, cudaStream_t s);
 
 // ---- kernel 3: split-K decode with fused combine (and fused norm/RoPE/append) --
 struct DecodeSeq {
@@ -136,7 +135,12 @@ struct PrefillArgs {
     float scale_log2;        // score scale times log2(e)
     int* err;
 };
-cudaError_t launch_prefill(const PrefillArgs& a, cudaStream_t s);
+// TMA descriptors of q, k, v (opaque 128-byte CUtensorMap objects).
+struct alignas(64) PrefillMaps {
+    unsigned char q[128], k[128], v[128];
+};
+bool prefill_make_maps(const PrefillArgs& a, PrefillMaps* m);  // host only; false on failure
+cudaError_t launch_prefill(const PrefillArgs& a, const PrefillMaps& m, cudaStream_t s);
 // Window [base, base+len) of one layer as bf16, token-major [len][n_kv][64].
 cudaError_t launch_kv_gather_bf16(const PoolView& pv, const int* table, int cap, long long base, long long len,
                                   int n_kv, __nv_bfloat16* k_out, __nv_bfloat16* v_out, cudaStream_t s);

@@ -24,6 +24,15 @@
 namespace bebelm {
 namespace {
 
+__device__ __forceinline__ void load_bf16x4(const __nv_bfloat16* p, float* out) {
+    const uint2 u = *reinterpret_cast<const uint2*>(p);
+    const __nv_bfloat162 a = *reinterpret_cast<const __nv_bfloat162*>(&u.x), b = *reinterpret_cast<const __nv_bfloat162*>(&u.y);
+    out[0] = __low2float(a);
+    out[1] = __high2float(a);
+    out[2] = __low2float(b);
+    out[3] = __high2float(b);
+}
+
 template <bool HD64>
 __global__ void __launch_bounds__(256) norm_rope_kernel(NormRopeArgs a) {
     const int lane = threadIdx.x & 31;
@@ -37,16 +46,42 @@ __global__ void __launch_bounds__(256) norm_rope_kernel(NormRopeArgs a) {
     const int hd = HD64 ? 64 : a.head_dim;
     const int half = hd >> 1;
     const int tok = (int)(item / nh_all);
+
+    // RoPE angles depend only on (position, pair): every head of a token shares them, so the
+    // block builds cos/sin once per token it touches (at most 32 tokens: 32 items per block),
+    // with the reference's iterative angle, theta = pos * scale^i by repeated multiplication
+    __shared__ float s_cos[32][32], s_sin[32][32];
+    const long long item0 = (long long)blockIdx.x * (blockDim.x >> 3);
+    const int tok0 = (int)(item0 / nh_all);
+    if (a.norm_q || a.norm_k) {
+        const long long item_last = min(total - 1, item0 + (blockDim.x >> 3) - 1);
+        const int ntok = (int)(item_last / nh_all) - tok0 + 1;
+        for (int idx = threadIdx.x; idx < ntok * half; idx += blockDim.x) {
+            const int t = idx / half, i = idx % half;
+            const long long pos = a.targets ? a.targets[tok0 + t].pos : a.pos0 + tok0 + t;
+            float theta = __ll2float_rn(pos);
+            for (int r = 0; r < i; ++r) theta = __fmul_rn(theta, a.theta_scale);
+            s_cos[t][i] = cosf(theta);
+            s_sin[t][i] = sinf(theta);
+        }
+        __syncthreads();
+    }
     const int hh = (int)(item % nh_all);
     const bool is_q = hh < a.n_heads;
     const int head = is_q ? hh : hh - a.n_heads;
-    const float* src = is_q ? a.q + ((size_t)tok * a.n_heads + head) * hd
-                            : a.k + ((size_t)tok * a.n_kv + head) * hd;
+    const size_t src_elem = is_q ? ((size_t)tok * a.n_heads + head) * hd : ((size_t)tok * a.n_kv + head) * hd;
+    const float* src = a.in_bf16 ? reinterpret_cast<const float*>(
+                                       reinterpret_cast<const __nv_bfloat16*>(is_q ? a.q : a.k) + src_elem)
+                                 : (is_q ? a.q : a.k) + src_elem;
     const float* gain = is_q ? a.q_gain : a.k_gain;
     const bool do_norm = is_q ? (a.norm_q != 0) : (a.norm_k != 0);
 
     float x0[4], x1[4];
-    if (HD64) {
+    if (HD64 && a.in_bf16) {
+        const __nv_bfloat16* bsrc = reinterpret_cast<const __nv_bfloat16*>(src);
+        load_bf16x4(bsrc + 4 * sub, x0);
+        load_bf16x4(bsrc + 32 + 4 * sub, x1);
+    } else if (HD64) {
         float4 u = *reinterpret_cast<const float4*>(src + 4 * sub);
         float4 w = *reinterpret_cast<const float4*>(src + 32 + 4 * sub);
         x0[0] = u.x; x0[1] = u.y; x0[2] = u.z; x0[3] = u.w;
@@ -80,18 +115,14 @@ __global__ void __launch_bounds__(256) norm_rope_kernel(NormRopeArgs a) {
                 x1[e] = __fmul_rn(__fmul_rn(x1[e], scale), gain[i + half]);
             }
         }
-        const long long pos = a.targets ? a.targets[tok].pos : a.pos0 + tok;
-        float theta = __ll2float_rn(pos);
-        for (int t = 0; t < 4 * sub && t < half; ++t) theta = __fmul_rn(theta, a.theta_scale);
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
             int i = 4 * sub + e;
             if (HD64 || i < half) {
-                const float sn = sinf(theta), cs = cosf(theta);
+                const float sn = s_sin[tok - tok0][i], cs = s_cos[tok - tok0][i];
                 const float p = x0[e], q = x1[e];
                 x0[e] = __fsub_rn(__fmul_rn(p, cs), __fmul_rn(q, sn));
                 x1[e] = __fadd_rn(__fmul_rn(p, sn), __fmul_rn(q, cs));
-                theta = __fmul_rn(theta, a.theta_scale);
             }
         }
     }
@@ -135,9 +166,19 @@ __global__ void __launch_bounds__(256) norm_rope_kernel(NormRopeArgs a) {
     if (is_q) return;
 
     // V row of the same kv head passes through unchanged
-    const float* vsrc = a.v ? a.v + ((size_t)tok * a.n_kv + head) * 64 : nullptr;
+    const size_t v_elem = ((size_t)tok * a.n_kv + head) * 64;
+    const float* vsrc = !a.v ? nullptr
+                        : a.in_bf16 ? reinterpret_cast<const float*>(reinterpret_cast<const __nv_bfloat16*>(a.v) + v_elem)
+                                    : a.v + v_elem;
     float4 v0 = make_float4(0.f, 0.f, 0.f, 0.f), v1 = v0;
-    if (vsrc) {
+    if (vsrc && a.in_bf16) {
+        const __nv_bfloat16* bv = reinterpret_cast<const __nv_bfloat16*>(vsrc);
+        float t0[4], t1[4];
+        load_bf16x4(bv + 4 * sub, t0);
+        load_bf16x4(bv + 32 + 4 * sub, t1);
+        v0 = make_float4(t0[0], t0[1], t0[2], t0[3]);
+        v1 = make_float4(t1[0], t1[1], t1[2], t1[3]);
+    } else if (vsrc) {
         v0 = *reinterpret_cast<const float4*>(vsrc + 4 * sub);
         v1 = *reinterpret_cast<const float4*>(vsrc + 32 + 4 * sub);
     }
@@ -202,10 +243,6 @@ __global__ void kv_gather_bf16_kernel(PoolView pv, const int* table, int cap, lo
     }
 }
 
-__global__ void bf16_to_f32_kernel(const __nv_bfloat16* in, float* out, size_t n) {
-    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
-        out[i] = __bfloat162float(in[i]);
-}
 
 }  // namespace
 
@@ -223,13 +260,6 @@ cudaError_t launch_kv_gather_bf16(const PoolView& pv, const int* table, int cap,
     if (quads <= 0) return cudaSuccess;
     const long long blocks = std::min<long long>((quads + 255) / 256, 148 * 16);
     kv_gather_bf16_kernel<<<(unsigned)blocks, 256, 0, s>>>(pv, table, cap, base, len, n_kv, k_out, v_out);
-    return cudaGetLastError();
-}
-
-cudaError_t launch_bf16_to_f32(const __nv_bfloat16* in, float* out, size_t n, cudaStream_t s) {
-    if (!n) return cudaSuccess;
-    size_t blocks = std::min<size_t>((n + 255) / 256, 148 * 16);
-    bf16_to_f32_kernel<<<(unsigned)blocks, 256, 0, s>>>(in, out, n);
     return cudaGetLastError();
 }
 

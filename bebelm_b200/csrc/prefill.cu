@@ -523,13 +523,16 @@ bool make_map(CUtensorMap* m, const void* base, int heads, long long rows) {
 
 }  // namespace
 
-cudaError_t launch_prefill(const PrefillArgs& a, cudaStream_t s) {
-    if (a.t <= 0) return cudaSuccess;
-    CUtensorMap mq, mk, mv;
+bool prefill_make_maps(const PrefillArgs& a, PrefillMaps* m) {
     const long long s_total = (long long)a.len_before + a.t;
-    if (!make_map(&mq, a.q, a.n_heads, a.t) || !make_map(&mk, a.k, a.n_kv, s_total) ||
-        !make_map(&mv, a.v, a.n_kv, s_total))
-        return cudaErrorInvalidValue;
+    static_assert(sizeof(CUtensorMap) == sizeof(m->q), "tensor map size");
+    return make_map(reinterpret_cast<CUtensorMap*>(m->q), a.q, a.n_heads, a.t) &&
+           make_map(reinterpret_cast<CUtensorMap*>(m->k), a.k, a.n_kv, s_total) &&
+           make_map(reinterpret_cast<CUtensorMap*>(m->v), a.v, a.n_kv, s_total);
+}
+
+cudaError_t launch_prefill(const PrefillArgs& a, const PrefillMaps& m, cudaStream_t s) {
+    if (a.t <= 0) return cudaSuccess;
     static bool attr_set[64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
@@ -540,7 +543,9 @@ cudaError_t launch_prefill(const PrefillArgs& a, cudaStream_t s) {
     }
     const int n_qt = (a.t + kTileQ - 1) / kTileQ;
     dim3 grid((unsigned)a.n_heads, (unsigned)((n_qt + 1) / 2));
-    prefill_kernel<<<grid, kCtaThreads, kSmem2Bytes, s>>>(mq, mk, mv, a);
+    prefill_kernel<<<grid, kCtaThreads, kSmem2Bytes, s>>>(*reinterpret_cast<const CUtensorMap*>(m.q),
+                                                           *reinterpret_cast<const CUtensorMap*>(m.k),
+                                                           *reinterpret_cast<const CUtensorMap*>(m.v), a);
     return cudaGetLastError();
 }
 
