@@ -1,0 +1,102 @@
+"""Multi-GPU layouts of the attention path (one process per GPU, torch.distributed).
+
+* :class:`KVHeadSharded` — KV-head sharding. Rank r of N owns kv heads
+  [8r/N, 8(r+1)/N) and their query heads [32r/N, 32(r+1)/N) for every attention
+  layer; its cache holds only those heads, so each rank reads 1/N of the KV bytes.
+  After the local fused step (or prefill) the head outputs are all-gathered over
+  NCCL; rank order is head order, so the gathered buffer is the full
+  [n_heads*64] (or [t, n_heads*64]) output of ``attn_step`` / ``attn_batch``
+  (src/model.rs:440-451, 232-254).
+* :func:`assign_sequences` — per-sequence sharding for independent Agent
+  sequences: longest-processing-time assignment of sequences to ranks by KV
+  length. No collective is needed; each rank runs batched decode on its share.
+
+The per-rank cache defaults to :class:`bebelm_b200.Cache` on the current CUDA
+device; ``cache_factory`` lets a test substitute another implementation of the
+same methods (e.g. a CPU reference) to check the sharding and gather logic on
+gloo ranks.
+"""
+from __future__ import annotations
+
+import heapq
+
+import torch
+import torch.distributed as dist
+
+from . import HEAD_DIM, N_HEADS, N_KV_HEADS, RMS_EPS, ROPE_THETA, Cache
+
+
+def assign_sequences(lengths, world: int):
+    """Longest-processing-time assignment: sequence indices per rank, balancing the summed
+    KV lengths (the bytes each rank's decode reads)."""
+    heap = [(0, r) for r in range(world)]
+    out = [[] for _ in range(world)]
+    for i in sorted(range(len(lengths)), key=lambda i: -int(lengths[i])):
+        load, r = heapq.heappop(heap)
+        out[r].append(i)
+        heapq.heappush(heap, (load + int(lengths[i]), r))
+    return [sorted(x) for x in out]
+
+
+class KVHeadSharded:
+    """One rank's share of a KV-head-sharded attention stack."""
+
+    def __init__(self, n_layers: int, max_context: int, n_heads: int = N_HEADS, n_kv_heads: int = N_KV_HEADS,
+                 group=None, cache_factory=None):
+        self.group = group
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        if n_kv_heads % self.world or n_heads % n_kv_heads:
+            raise ValueError(f"{n_kv_heads} kv heads cannot be split over {self.world} ranks")
+        self.n_heads, self.n_kv = n_heads, n_kv_heads
+        self.kv_per = n_kv_heads // self.world
+        self.h_per = n_heads // self.world
+        self.h0, self.kv0 = self.rank * self.h_per, self.rank * self.kv_per
+        if cache_factory is None:
+            dev = torch.cuda.current_device()
+            self.cache = Cache(n_layers=n_layers, n_kv_heads=self.kv_per, max_context=max_context, device=dev)
+        else:
+            self.cache = cache_factory(n_layers, self.kv_per, max_context)
+
+    # -- slicing ---------------------------------------------------------------
+    def _heads(self, x, per, first, t=None):
+        if t is None:
+            return x.reshape(-1, HEAD_DIM)[first:first + per].reshape(-1).contiguous()
+        return x.reshape(t, -1, HEAD_DIM)[:, first:first + per].reshape(t, -1).contiguous()
+
+    def _gather(self, local):
+        if self.world == 1:
+            return local
+        local = local.contiguous()
+        flat = local.new_empty(self.world * local.numel())  # concatenated in rank order
+        dist.all_gather_into_tensor(flat, local.reshape(-1), group=self.group)
+        return flat.view((self.world,) + tuple(local.shape))
+
+    # -- the reference operator ------------------------------------------------
+    def attn_step(self, layer: int, q, k, v, q_gain, k_gain, pos: int, theta: float = ROPE_THETA,
+                  eps: float = RMS_EPS):
+        """q [n_heads*64], k/v [n_kv*64] (replicated on every rank) -> full out [n_heads*64]."""
+        out = self.cache.attn_step(layer, self._heads(q, self.h_per, self.h0), self._heads(k, self.kv_per, self.kv0),
+                                   self._heads(v, self.kv_per, self.kv0), q_gain, k_gain, pos=pos, theta=theta, eps=eps)
+        return self._gather(out).reshape(-1)
+
+    def attn_prefill(self, layer: int, q, k, v, q_gain, k_gain, pos0: int, theta: float = ROPE_THETA,
+                     eps: float = RMS_EPS):
+        """q [t, n_heads*64], k/v [t, n_kv*64] -> full out [t, n_heads*64]."""
+        t = q.shape[0]
+        out = self.cache.attn_prefill(layer, self._heads(q, self.h_per, self.h0, t),
+                                      self._heads(k, self.kv_per, self.kv0, t), self._heads(v, self.kv_per, self.kv0, t),
+                                      q_gain, k_gain, pos0, theta=theta, eps=eps, n_heads=self.h_per)
+        full = self._gather(out)  # [world, t, h_per*64]
+        if self.world == 1:
+            return full
+        return full.permute(1, 0, 2).reshape(t, -1)
+
+    def evict_front(self, n: int):
+        self.cache.evict_front(n)
+
+    def kv_len(self) -> int:
+        return self.cache.kv_len()
+
+    def clear(self):
+        self.cache.clear()

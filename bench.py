@@ -279,6 +279,10 @@ def run_ours(args):
         prefill = {"config2_2048": bench_prefill(bb, torch, dev, stream, bf16_peak, peak_kind, 2048, 6),
                    "config5_8192_one_layer": bench_prefill(bb, torch, dev, stream, bf16_peak, peak_kind, 8192, 2)}
 
+    cfg4 = None if args.no_cfg4 else bench_config4(bb, torch, dev, stream, world, rank)
+    hbm_peak_, bf16_peak_, _ = peaks()
+    cfg5 = None if args.no_cfg5 else bench_config5(bb, torch, dev, stream, world, rank, bf16_peak_)
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         import oracle
@@ -312,6 +316,8 @@ def run_ours(args):
             "clocks": clk,
             "cpu_baseline": cpu,
             "prefill": prefill,
+            "config4": cfg4,
+            "config5": cfg5,
         }
         print(json.dumps(line), flush=True)
     barrier(world)
@@ -368,6 +374,95 @@ def bench_prefill(bb, torch, dev, stream, bf16_peak, peak_kind, T=2048, reps=6):
                          "frac": round(tf / bf16_peak, 4), "peak_kind": peak_kind}}
 
 
+def bench_config4(bb, torch, dev, stream, world, rank, steps=128):
+    """Config 4: 64 independent sequences, KV lengths U[1024, 16384] by seed, one decode token
+    each per step, sequences LPT-sharded over the ranks (no collective)."""
+    import numpy as np
+    from bebelm_b200.sharded import assign_sequences
+    lengths = np.random.default_rng(4).integers(1024, 16385, size=64)
+    mine = assign_sequences(lengths, world)[rank]
+    pages = sum(int(lengths[i]) // 64 + (steps + 64) // 64 + 3 for i in mine)
+    pool = bb.Pool(n_layers=1, n_pages=pages, device=dev.index)
+    caches = [bb.Cache(max_context=int(lengths[i]) + steps + 64, pool=pool) for i in mine]
+    g = torch.Generator(device=dev)
+    g.manual_seed(40 + rank)
+    for c, i in zip(caches, mine):
+        for c0 in range(0, int(lengths[i]), 8192):
+            n = min(8192, int(lengths[i]) - c0)
+            c.append(0, torch.randn((n, KVD), generator=g, device=dev), torch.randn((n, KVD), generator=g, device=dev))
+    n = len(mine)
+    Q = torch.randn((steps + 3, n, HID), generator=g, device=dev)
+    K = torch.randn((steps + 3, n, KVD), generator=g, device=dev)
+    V = torch.randn((steps + 3, n, KVD), generator=g, device=dev)
+    qg = 1 + 0.02 * torch.randn(D, generator=g, device=dev)
+    kg = 1 + 0.02 * torch.randn(D, generator=g, device=dev)
+    out = torch.empty((n, HID), device=dev)
+    pos = [int(lengths[i]) for i in mine]
+    for i in range(3):
+        bb.attn_decode_batched(caches, 0, Q[i], K[i], V[i], qg, kg, pos, theta=THETA, out=out, stream=stream)
+        pos = [p + 1 for p in pos]
+    barrier(world)
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for i in range(3, steps + 3):
+        bb.attn_decode_batched(caches, 0, Q[i], K[i], V[i], qg, kg, pos, theta=THETA, out=out, stream=stream)
+        pos = [p + 1 for p in pos]
+    b.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    ms = max_over_ranks(a.elapsed_time(b), world, dev)
+    total = sum(bytes_per_step(int(l) + 3 + s + 1) for l in lengths for s in range(steps))
+    for c in caches:
+        c.close()
+    pool.close()
+    return {"workload": "config4: 64 sequences, KV lengths U[1024,16384] (seed 4), 128 decode steps, 64-token pages",
+            "value": round(total / (ms * 1e-3) / 1e9, 1), "unit": "GB/s",
+            "tok_per_s": round(64 * steps / (ms * 1e-3), 1), "ms_per_step": round(ms / steps, 4),
+            "parallelism": f"per-sequence x{world} (LPT by KV length), no collective"}
+
+
+def bench_config5(bb, torch, dev, stream, world, rank, bf16_peak, T=8192, steps=512):
+    """Config 5: the 6 attention layers of the stack, KV heads sharded over the ranks with an NCCL
+    all-gather of head outputs: causal prefill of T bf16 tokens, then `steps` decode steps."""
+    from bebelm_b200.sharded import KVHeadSharded
+    L = 6
+    sh = KVHeadSharded(n_layers=L, max_context=T + steps + 64)
+    g = torch.Generator(device=dev)
+    g.manual_seed(50)  # identical activations on every rank (replicated projections)
+    q = torch.randn((T, HID), generator=g, device=dev).to(torch.bfloat16)
+    k = torch.randn((T, KVD), generator=g, device=dev).to(torch.bfloat16)
+    v = torch.randn((T, KVD), generator=g, device=dev).to(torch.bfloat16)
+    qg = 1 + 0.02 * torch.randn(D, generator=g, device=dev)
+    kg = 1 + 0.02 * torch.randn(D, generator=g, device=dev)
+    Qd = torch.randn((steps, HID), generator=g, device=dev)
+    Kd = torch.randn((steps, KVD), generator=g, device=dev)
+    Vd = torch.randn((steps, KVD), generator=g, device=dev)
+    barrier(world)
+    torch.cuda.synchronize()
+    e = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+    e[0].record(stream)
+    for layer in range(L):
+        sh.attn_prefill(layer, q, k, v, qg, kg, 0, theta=THETA)
+    e[1].record(stream)
+    for s in range(steps):
+        for layer in range(L):
+            sh.attn_step(layer, Qd[s], Kd[s], Vd[s], qg, kg, pos=T + s, theta=THETA)
+    e[2].record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    pre_ms = max_over_ranks(e[0].elapsed_time(e[1]), world, dev)
+    dec_ms = max_over_ranks(e[1].elapsed_time(e[2]), world, dev)
+    sh.cache.close()
+    flops = L * 4096.0 * T * (T + 1)
+    tf = flops / (pre_ms * 1e-3) / 1e12
+    return {"workload": f"config5: 6 GQA layers, causal prefill of {T} bf16 tokens then {steps} decode steps",
+            "prefill_ms": round(pre_ms, 3), "prefill_tflops": round(tf, 1),
+            "prefill_frac_of_bf16_peak_per_gpu": round(tf / world / bf16_peak, 4),
+            "decode_ms_per_step": round(dec_ms / steps, 4), "decode_tok_per_s": round(steps / (dec_ms * 1e-3), 1),
+            "parallelism": f"kv heads / {world} per GPU, NCCL all-gather of head outputs per layer"}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -376,6 +471,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-prefill", action="store_true")
+    ap.add_argument("--no-cfg4", action="store_true")
+    ap.add_argument("--no-cfg5", action="store_true")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
