@@ -60,8 +60,10 @@ class KVHeadSharded:
 
     # -- slicing ---------------------------------------------------------------
     def _heads(self, x, per, first, t=None):
-        if t is None:
-            return x.reshape(-1, HEAD_DIM)[first:first + per].reshape(-1).contiguous()
+        if self.world == 1:
+            return x
+        if t is None:  # consecutive heads of one token: a contiguous view
+            return x.reshape(-1)[first * HEAD_DIM:(first + per) * HEAD_DIM]
         return x.reshape(t, -1, HEAD_DIM)[:, first:first + per].reshape(t, -1).contiguous()
 
     def _gather(self, local):
