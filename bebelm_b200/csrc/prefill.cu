@@ -192,6 +192,39 @@ __device__ __forceinline__ float ex2(float x) {  // 2^x on the MUFU unit; -inf g
     return y;
 }
 
+#ifndef BEBELM_PF_POLY
+#define BEBELM_PF_POLY 0  // of every 8 key pairs, how many take 2^x on the FMA pipe
+#endif
+
+// 2^x on the FMA pipe instead of the MUFU unit, so the two units can share the softmax's
+// exponentials. x is clamped to >= -125 (2^-125 is zero for every later use) and split as
+// x = j + f, with j = round(x) from the 1.5*2^23 rounding constant and f in [-1/2, 1/2].
+// 2^f is a degree-3 polynomial, fitted here by least squares to minimise the relative
+// error on that interval: max 7.5e-5, far below the bf16 rounding of P. Then 2^j is added
+// to the exponent field.
+__device__ __forceinline__ float exp2_poly(float x) {
+    x = fmaxf(x, -125.0f);
+    const float t = x + 12582912.0f;
+    const float jf = t - 12582912.0f;
+    const float f = x - jf;
+    float p = fmaf(0.05517161265f, f, 0.24261112511f);
+    p = fmaf(p, f, 0.69326096773f);
+    p = fmaf(p, f, 0.99992805719f);
+    return __uint_as_float(__float_as_uint(p) + (__float_as_uint(t) << 23));
+}
+
+#ifndef BEBELM_PF_ALU_PACK
+#define BEBELM_PF_ALU_PACK 0
+#endif
+// Two non-negative finite floats to a bf16 pair, round to nearest even, on the integer ALU
+// (low half = a). Keeps the conversion off the unit that also computes the exponentials.
+__device__ __forceinline__ uint32_t pack_bf16_alu(float a, float b) {
+    uint32_t ua = __float_as_uint(a), ub = __float_as_uint(b);
+    ua += 0x7FFFu + ((ua >> 16) & 1u);
+    ub += 0x7FFFu + ((ub >> 16) & 1u);
+    return __byte_perm(ua, ub, 0x7632);
+}
+
 __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
     __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
     return *reinterpret_cast<uint32_t*>(&h);
@@ -213,8 +246,14 @@ __device__ long long g_trace[16 * 2 * 64];  // [event][tile][j] = clock64, CTA (
 // ---- roles: warps 0-3 softmax for tile A, 4-7 softmax for tile B, 8 TMA, 9 MMA ----
 constexpr int kWarps = 10;
 constexpr int kCtaThreads = kWarps * 32;
-constexpr int kStages = 3;                              // K/V ring depth
-constexpr float kRescaleSlack = 8.0f;                   // log2 headroom before O is rescaled
+#ifndef BEBELM_PF_STAGES
+#define BEBELM_PF_STAGES 3
+#endif
+constexpr int kStages = BEBELM_PF_STAGES;               // K/V ring depth
+constexpr float kRescaleSlack = 8.0f;
+#ifndef BEBELM_PF_SLEEP_NS
+#define BEBELM_PF_SLEEP_NS 64
+#endif                   // log2 headroom before O is rescaled
 // shared memory map v2 (offsets from a 1024-byte aligned base)
 constexpr int kOff2Q = 0;                               // Q_A, Q_B
 constexpr int kOff2K = 2 * kTileBytes;                  // kStages K tiles
@@ -305,6 +344,7 @@ __global__ void __launch_bounds__(kCtaThreads, 1)
 #pragma unroll
                 for (int X = 0; X < 2; ++X) {
                     const int js = nS[X];
+                    if (js < nkt[X] && mbar_test(bar(kBarK + js % kStages), (js / kStages) & 1)) TRACE(12, js, X);
                     if (js < nkt[X] && mbar_test(bar(kBarK + js % kStages), (js / kStages) & 1) &&
                         (js == 0 || mbar_test(bar(kBarC + X), (js - 1) & 1))) {
                         tc_fence_after();
@@ -342,8 +382,10 @@ __global__ void __launch_bounds__(kCtaThreads, 1)
                 }
                 if (progress) {
                     idle = 0;
-                } else if (++idle > 64 * kWaitLimit) {
+                } else if (++idle > kWaitLimit) {
                     ok = false;
+                } else {
+                    __nanosleep(BEBELM_PF_SLEEP_NS);  // leave the issue slots to the softmax warps
                 }
             }
             if (!ok) s_fail = 1;
@@ -369,36 +411,12 @@ __global__ void __launch_bounds__(kCtaThreads, 1)
             // keys of this tile this row may see: columns [0, lim] (all of them off the diagonal)
             const long long lim_ll = key_lim - k0;
             const int lim = diag ? (lim_ll < kTileK - 1 ? (int)lim_ll : kTileK - 1) : kTileK - 1;
-            // pass 1: row max, 64 columns at a time, 8 independent chains
-            float mxv[8];
-#pragma unroll
-            for (int e = 0; e < 8; ++e) mxv[e] = -INFINITY;
-#pragma unroll
-            for (int c = 0; c < kTileK; c += 64) {
-                float v[64];
-                if ((warp & 3) == 0 && lane == 0 && c == 0) TRACE(9, j, X);
-                tmem_ld64(t_s + c, v);
-                if ((warp & 3) == 0 && lane == 0 && c == 0) TRACE(10, j, X);
-                if (diag) {
-#pragma unroll
-                    for (int e = 0; e < 64; ++e)
-                        if (c + e <= lim) mxv[e & 7] = fmaxf(mxv[e & 7], v[e]);
-                } else {
-#pragma unroll
-                    for (int e = 0; e < 64; ++e) mxv[e & 7] = fmaxf(mxv[e & 7], v[e]);
-                }
-            }
-            if ((warp & 3) == 0 && lane == 0) TRACE(6, j, X);
-            const float mx = fmaxf(fmaxf(fmaxf(mxv[0], mxv[1]), fmaxf(mxv[2], mxv[3])),
-                                   fmaxf(fmaxf(mxv[4], mxv[5]), fmaxf(mxv[6], mxv[7]))) * a.scale_log2;
-            // lazy rescale: move the reference max only when a score would exceed it by 2^8
-            const bool bump = mx > m_used + kRescaleSlack;
-            const float m_new = bump ? mx : m_used;
-            const float f = ex2(m_used - m_new);  // 1 without a bump, 0 on the first tile
-            l *= f;
-            m_used = m_new;
-            const float neg_m = -m_used;
-            // pass 2: P = 2^(s - m) in bf16 (two keys per 32-bit column)
+            // One pass over S, 64 columns at a time. The reference max m_used moves only when a
+            // chunk's max exceeds it by 2^8 (lazy rescale); if the second chunk moves it, the
+            // first chunk's P (still in registers) and the running sum are rescaled here and O
+            // after the P store. S is read from TMEM exactly once.
+            float fo = 1.f;  // factor O must take for this tile
+            bool bump = false;
             float ps[8];
 #pragma unroll
             for (int e = 0; e < 8; ++e) ps[e] = 0.f;
@@ -410,7 +428,38 @@ __global__ void __launch_bounds__(kCtaThreads, 1)
                 if (c + 64 == kTileK) {  // S_X(j) fully read: the next S may overwrite it
                     tc_fence_before();
                     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar(kBarC + X)) : "memory");
+                    if ((warp & 3) == 0 && lane == 0) TRACE(11, j, X);
                 }
+                float mxv[8];
+#pragma unroll
+                for (int e = 0; e < 8; ++e) mxv[e] = -INFINITY;
+                if (diag) {
+#pragma unroll
+                    for (int e = 0; e < 64; ++e)
+                        if (c + e <= lim) mxv[e & 7] = fmaxf(mxv[e & 7], v[e]);
+                } else {
+#pragma unroll
+                    for (int e = 0; e < 64; ++e) mxv[e & 7] = fmaxf(mxv[e & 7], v[e]);
+                }
+                const float mc = fmaxf(fmaxf(fmaxf(mxv[0], mxv[1]), fmaxf(mxv[2], mxv[3])),
+                                       fmaxf(fmaxf(mxv[4], mxv[5]), fmaxf(mxv[6], mxv[7]))) * a.scale_log2;
+                if (mc > m_used + kRescaleSlack) {
+                    const float f = ex2(m_used - mc);  // 0 while nothing has been seen
+                    l *= f;
+                    fo *= f;
+                    bump = true;
+                    if (c > 0) {  // rescale the first chunk's P (bf16 pairs) and its partial sums
+#pragma unroll
+                        for (int e = 0; e < 32; ++e) {
+                            __nv_bfloat162 h = *reinterpret_cast<__nv_bfloat162*>(&w[e]);
+                            w[e] = pack_bf16(__low2float(h) * f, __high2float(h) * f);
+                        }
+#pragma unroll
+                        for (int e = 0; e < 8; ++e) ps[e] *= f;
+                    }
+                    m_used = mc;
+                }
+                const float neg_m = -m_used;
                 if (diag) {
 #pragma unroll
                     for (int e = 0; e < 32; ++e) {
@@ -422,13 +471,17 @@ __global__ void __launch_bounds__(kCtaThreads, 1)
                 } else {
 #pragma unroll
                     for (int e = 0; e < 32; ++e) {
-                        const float p0 = ex2(fmaf(v[2 * e], a.scale_log2, neg_m));
-                        const float p1 = ex2(fmaf(v[2 * e + 1], a.scale_log2, neg_m));
+                        const float x0 = fmaf(v[2 * e], a.scale_log2, neg_m), x1 = fmaf(v[2 * e + 1], a.scale_log2, neg_m);
+                        const bool poly = (e & 7) < BEBELM_PF_POLY;
+                        const float p0 = poly ? exp2_poly(x0) : ex2(x0);
+                        const float p1 = poly ? exp2_poly(x1) : ex2(x1);
                         ps[e & 7] += p0 + p1;
-                        w[c / 2 + e] = pack_bf16(p0, p1);
+                        w[c / 2 + e] = BEBELM_PF_ALU_PACK ? pack_bf16_alu(p0, p1) : pack_bf16(p0, p1);
                     }
                 }
             }
+            const float f = fo;
+            if ((warp & 3) == 0 && lane == 0) TRACE(7, j, X);
             // P_X and O_X are read by PV(j-1): wait for it before writing either (S(j) no
             // longer implies it, since S(j) is issued before PV(j-1))
             if (j > 0) {
@@ -439,7 +492,6 @@ __global__ void __launch_bounds__(kCtaThreads, 1)
             tmem_st32(t_p, w);
             tmem_st32(t_p + 32, w + 32);
             const float psum = ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
-            if ((warp & 3) == 0 && lane == 0) TRACE(7, j, X);
             if (__any_sync(0xffffffffu, bump && j > 0)) {
                 // PV(j-1) has completed (waited above) and PV(j) waits for this thread: O_X is stable
 #pragma unroll
