@@ -126,6 +126,45 @@ struct PinBuf {
 
 }  // namespace
 
+// Small host-to-device uploads (page-table entries, sequence descriptors) go through a
+// ring of pinned slots: a copy from pinned memory is truly asynchronous, whereas one from
+// pageable memory is staged by the runtime and can hold the host to the GPU's pace. A slot
+// is reused only after the event recorded behind its last copy has completed.
+struct UploadRing {
+    static constexpr int kSlots = 16;
+    static constexpr size_t kSlotBytes = 64 * 1024;
+    char* pin = nullptr;
+    cudaEvent_t done[kSlots] = {};
+    int next = 0;
+
+    // Enqueues a copy of `bytes` from src to the device address dst on stream s.
+    cudaError_t copy(void* dst, const void* src, size_t bytes, cudaStream_t s) {
+        if (bytes > kSlotBytes) return cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, s);
+        if (!pin) {
+            cudaError_t e = cudaHostAlloc(reinterpret_cast<void**>(&pin), kSlots * kSlotBytes, cudaHostAllocDefault);
+            if (e != cudaSuccess) return e;
+            for (int i = 0; i < kSlots; ++i) {
+                e = cudaEventCreateWithFlags(&done[i], cudaEventDisableTiming);
+                if (e != cudaSuccess) return e;
+            }
+        }
+        const int i = next;
+        next = (next + 1) % kSlots;
+        cudaError_t e = cudaEventSynchronize(done[i]);  // the slot's previous copy has been read
+        if (e != cudaSuccess) return e;
+        std::memcpy(pin + (size_t)i * kSlotBytes, src, bytes);
+        e = cudaMemcpyAsync(dst, pin + (size_t)i * kSlotBytes, bytes, cudaMemcpyHostToDevice, s);
+        if (e != cudaSuccess) return e;
+        return cudaEventRecord(done[i], s);
+    }
+    void release() {
+        for (int i = 0; i < kSlots; ++i)
+            if (done[i]) cudaEventDestroy(done[i]);
+        if (pin) cudaFreeHost(pin);
+        pin = nullptr;
+    }
+};
+
 // -------------------------------------------------------------------- pool --
 struct bebelm_kv_pool {
     int device = 0, n_layers = 0, n_kv = 0, head_dim = 64, page_tokens = 64, dtype = BEBELM_F32;
@@ -137,6 +176,7 @@ struct bebelm_kv_pool {
     // scratch shared by every call on this pool's sequences (stream-ordered)
     DevBuf io, qn, part, counters, seqdesc, err, pf;
     PinBuf pin;
+    UploadRing uploads;
     std::vector<DecodeSeq> h_desc;
     // cache slots written by the most recent library kernel on this pool: a decode
     // launched next copies pages below these before its griddepcontrol.wait
@@ -172,13 +212,12 @@ struct bebelm_kv {
 namespace {
 
 int upload_table(bebelm_kv* kv, long long L0, long long L1, cudaStream_t s) {
-    // ring entries of logical pages [L0, L1); pageable source is staged by the
-    // runtime before cudaMemcpyAsync returns, so later host edits cannot race
+    // ring entries of logical pages [L0, L1), copied through the pool's pinned upload ring
+    // (the bytes are captured when the copy is enqueued, so later host edits cannot race)
     for (long long L = L0; L < L1;) {
         int i0 = (int)(L % kv->cap);
         long long n = std::min<long long>(L1 - L, kv->cap - i0);
-        CUDA_TRY(cudaMemcpyAsync(kv->d_table + i0, kv->table.data() + i0, sizeof(int) * n,
-                                 cudaMemcpyHostToDevice, s));
+        CUDA_TRY(kv->pool->uploads.copy(kv->d_table + i0, kv->table.data() + i0, sizeof(int) * n, s));
         L += n;
     }
     return 0;
@@ -289,6 +328,7 @@ int pool_create(int n_layers, int n_kv_heads, int head_dim, size_t n_pages, int 
 void pool_free(bebelm_kv_pool* P) {
     DeviceGuard g(P->device);
     cudaDeviceSynchronize();
+    P->uploads.release();
     cudaFree(P->mem);
     P->io.release();
     P->qn.release();
@@ -404,7 +444,7 @@ int run_decode(bebelm_kv_pool* P, const std::vector<Window>& wins, int layer, in
         a.one = P->h_desc[0];
     } else {
         TRY(P->seqdesc.ensure(sizeof(DecodeSeq) * n, false, s));
-        CUDA_TRY(cudaMemcpyAsync(P->seqdesc.p, P->h_desc.data(), sizeof(DecodeSeq) * n, cudaMemcpyHostToDevice, s));
+        CUDA_TRY(P->uploads.copy(P->seqdesc.p, P->h_desc.data(), sizeof(DecodeSeq) * n, s));
         a.seqs = P->seqdesc.as<DecodeSeq>();
     }
     a.n_seqs = n;

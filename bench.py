@@ -411,7 +411,11 @@ def bench_config4(bb, torch, dev, stream, world, rank, steps=128):
     b.record(stream)
     torch.cuda.synchronize()
     barrier(world)
-    ms = max_over_ranks(a.elapsed_time(b), world, dev)
+    ms_local = a.elapsed_time(b)
+    if os.environ.get("BEBELM_BENCH_VERBOSE"):
+        print(f"config4 rank {rank}: {len(mine)} seqs, {sum(int(lengths[i]) for i in mine)} positions, "
+              f"{ms_local / steps:.4f} ms/step", file=sys.stderr, flush=True)
+    ms = max_over_ranks(ms_local, world, dev)
     total = sum(bytes_per_step(int(l) + 3 + s + 1) for l in lengths for s in range(steps))
     for c in caches:
         c.close()
