@@ -348,6 +348,7 @@ __global__ void __launch_bounds__(kCtaThreads, 1)
                     if (js < nkt[X] && mbar_test(bar(kBarK + js % kStages), (js / kStages) & 1) &&
                         (js == 0 || mbar_test(bar(kBarC + X), (js - 1) & 1))) {
                         tc_fence_after();
+                        TRACE(14, js, X);
                         const uint64_t dq = X ? dq1 : dq0;
                         const uint64_t dk = smem_desc(sbase + kOff2K + (js % kStages) * kTileBytes, 16, 1024);
 #pragma unroll
@@ -362,6 +363,7 @@ __global__ void __launch_bounds__(kCtaThreads, 1)
                     if (jp < nS[X] && mbar_test(bar(kBarV + jp % kStages), (jp / kStages) & 1) &&
                         mbar_test(bar(kBarP + X), jp & 1)) {
                         tc_fence_after();
+                        TRACE(13, jp, X);
                         const uint64_t dv = smem_desc(sbase + kOff2V + (jp % kStages) * kTileBytes, kTileBytes, 1024);
 #pragma unroll
                         for (int k = 0; k < kTileK / 16; ++k)  // 16 keys: +8 TMEM columns of P, +2048 B of V
