@@ -191,11 +191,11 @@ class Pool:
     """A device page pool that several caches (sequences) draw from."""
 
     def __init__(self, n_layers: int, n_pages: int, n_kv_heads: int = N_KV_HEADS, head_dim: int = HEAD_DIM,
-                 page_tokens: int = 64, device: int = 0):
+                 page_tokens: int = 64, device: int = 0, kv_dtype: int = F32):
         self._h = C.c_void_p()
         self.n_layers, self.n_kv_heads = n_layers, n_kv_heads
-        _check(load_library().bebelm_kv_pool_create(n_layers, n_kv_heads, head_dim, n_pages, page_tokens, F32, device,
-                                                    C.byref(self._h)))
+        _check(load_library().bebelm_kv_pool_create(n_layers, n_kv_heads, head_dim, n_pages, page_tokens, kv_dtype,
+                                                    device, C.byref(self._h)))
 
     def free_pages(self) -> int:
         n = C.c_size_t()
@@ -223,19 +223,22 @@ class Cache:
 
     def __init__(self, n_layers: int = len(ATTENTION_LAYERS), n_kv_heads: int = N_KV_HEADS,
                  max_context: int = 32768, head_dim: int = HEAD_DIM, device: int = 0, pool: Pool | None = None,
-                 _handle=None):
+                 kv_dtype: int = F32, _handle=None):
+        """kv_dtype F32 keeps the reference's fp32 history; BF16 halves the bytes every decode
+        step reads (K/V rounded to bf16 when appended)."""
         self.n_layers = n_layers if pool is None else pool.n_layers
         self.n_kv_heads = n_kv_heads if pool is None else pool.n_kv_heads
         self.head_dim = head_dim
         self.max_context = max_context
         self.pool = pool
+        self.kv_dtype = kv_dtype
         L = load_library()
         if _handle is not None:
             self._h = _handle
         else:
             self._h = C.c_void_p()
             if pool is None:
-                _check(L.bebelm_kv_create(n_layers, n_kv_heads, head_dim, max_context, 64, F32, device,
+                _check(L.bebelm_kv_create(n_layers, n_kv_heads, head_dim, max_context, 64, kv_dtype, device,
                                           C.byref(self._h)))
             else:
                 _check(L.bebelm_kv_create_in_pool(pool._h, max_context, C.byref(self._h)))
@@ -267,7 +270,8 @@ class Cache:
     def clone(self) -> "Cache":
         h = C.c_void_p()
         _check(load_library().bebelm_kv_clone(self._h, C.byref(h)))
-        return Cache(self.n_layers, self.n_kv_heads, self.max_context, self.head_dim, pool=self.pool, _handle=h)
+        return Cache(self.n_layers, self.n_kv_heads, self.max_context, self.head_dim, pool=self.pool,
+                     kv_dtype=self.kv_dtype, _handle=h)
 
     def clear(self) -> None:
         _check(load_library().bebelm_kv_clear(self._h))

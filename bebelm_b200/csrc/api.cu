@@ -168,8 +168,8 @@ struct UploadRing {
 // -------------------------------------------------------------------- pool --
 struct bebelm_kv_pool {
     int device = 0, n_layers = 0, n_kv = 0, head_dim = 64, page_tokens = 64, dtype = BEBELM_F32;
-    size_t n_pages = 0, page_floats = 0, block_floats = 0;
-    float* mem = nullptr;
+    size_t n_pages = 0, page_bytes = 0, block_bytes = 0;
+    char* mem = nullptr;
     std::vector<int> free_list;  // physical pages not in any window
     int num_sms = 148;
     int n_seqs = 0;              // live sequences drawing from this pool
@@ -190,9 +190,10 @@ struct bebelm_kv_pool {
     PoolView view(int layer) const {
         PoolView v;
         v.base = mem;
-        v.page_floats = page_floats;
-        v.layer_off = (size_t)layer * 2 * block_floats;
-        v.block_floats = block_floats;
+        v.page_bytes = page_bytes;
+        v.layer_off = (size_t)layer * 2 * block_bytes;
+        v.block_bytes = block_bytes;
+        v.bf16 = dtype == BEBELM_BF16;
         return v;
     }
 };
@@ -284,7 +285,8 @@ int pool_create(int n_layers, int n_kv_heads, int head_dim, size_t n_pages, int 
     if (head_dim != kHeadDim) return fail(BEBELM_ERR_UNSUPPORTED, "cache head_dim must be 64 (got %d)", head_dim);
     if (page_tokens != kPageTokens)
         return fail(BEBELM_ERR_UNSUPPORTED, "page_tokens must be 64 (got %d)", page_tokens);
-    if (dtype != BEBELM_F32) return fail(BEBELM_ERR_UNSUPPORTED, "cache dtype must be BEBELM_F32");
+    if (dtype != BEBELM_F32 && dtype != BEBELM_BF16)
+        return fail(BEBELM_ERR_UNSUPPORTED, "cache dtype must be BEBELM_F32 or BEBELM_BF16");
     if (n_pages > (size_t)INT32_MAX) return fail(BEBELM_ERR_INVALID, "too many pages");
     TRY(check_device(device));
     DeviceGuard g(device);
@@ -293,10 +295,11 @@ int pool_create(int n_layers, int n_kv_heads, int head_dim, size_t n_pages, int 
     P->n_layers = n_layers;
     P->n_kv = n_kv_heads;
     P->n_pages = n_pages;
-    P->block_floats = (size_t)n_kv_heads * kPageRowFloats;
-    P->page_floats = (size_t)n_layers * 2 * P->block_floats;
+    P->dtype = dtype;
+    P->block_bytes = (size_t)n_kv_heads * kPageRowFloats * (dtype == BEBELM_BF16 ? 2 : 4);
+    P->page_bytes = (size_t)n_layers * 2 * P->block_bytes;
     cudaDeviceGetAttribute(&P->num_sms, cudaDevAttrMultiProcessorCount, device);
-    const size_t bytes = n_pages * P->page_floats * sizeof(float);
+    const size_t bytes = n_pages * P->page_bytes;
     cudaError_t e = cudaMalloc(&P->mem, bytes);
     if (e != cudaSuccess) {
         delete P;
@@ -675,13 +678,13 @@ int bebelm_kv_clone(const bebelm_kv* src, bebelm_kv** dst) {
     kv->base = src->base;
     kv->len = src->len;
     kv->pos = src->pos;
-    const size_t page_bytes = SP->page_floats * sizeof(float);
+    const size_t page_bytes = SP->page_bytes;
     for (long long L = src->lo; L < src->hi; ++L) {
         const int phys = DP->free_list.back();
         DP->free_list.pop_back();
         kv->table[L % kv->cap] = phys;
         const int sp = src->table[L % src->cap];
-        cudaError_t e = cudaMemcpyAsync(DP->mem + (size_t)phys * DP->page_floats, SP->mem + (size_t)sp * SP->page_floats,
+        cudaError_t e = cudaMemcpyAsync(DP->mem + (size_t)phys * DP->page_bytes, SP->mem + (size_t)sp * SP->page_bytes,
                                         page_bytes, cudaMemcpyDeviceToDevice, 0);
         if (e != cudaSuccess) {
             bebelm_kv_destroy(kv);

@@ -51,7 +51,7 @@ namespace {
 #endif
 constexpr int kStages = BEBELM_DECODE_STAGES;
 constexpr int kThreads = 128;
-constexpr int kStageBytes = 2 * kPageRowFloats * 4;  // K + V rows of one page, one kv head
+constexpr int kRingBytes = kStages * 2 * kPageRowFloats * 4;  // the shared-memory ring: 3 fp32 pages of K + V
 constexpr long long kWaitLimit = 1ll << 22;          // try_wait polls before giving up
 constexpr int kPrefetch = BEBELM_DECODE_PREFETCH;     // pages prefetched into L2 beyond the ring
 constexpr int kMaxPagesPerSplit = kDecodeMaxPagesPerSplit;
@@ -130,13 +130,18 @@ __device__ __forceinline__ void warp_norm_rope64(const float* x, const float* ga
     y1 = __fadd_rn(__fmul_rn(a, sn), __fmul_rn(b, cs));
 }
 
-template <int HPC>
+template <int HPC, bool BF>
 __global__ void __launch_bounds__(kThreads, 2) decode_kernel(DecodeArgs a) {
+    // BF: the cache holds bf16 (half the bytes per page row, twice the stages in the same ring)
+    constexpr int ES = BF ? 2 : 4;
+    constexpr int ROWB = kPageRowFloats * ES;  // one kv head of one page
+    constexpr int SB = 2 * ROWB;               // a stage: its K rows and V rows
+    constexpr int NST = kRingBytes / SB;
     extern __shared__ __align__(128) unsigned char smem[];
-    float* stages = reinterpret_cast<float*>(smem);
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes);
+    unsigned char* stages = smem;
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + kRingBytes);
     __shared__ float s_m[4][HPC], s_l[4][HPC];
-    __shared__ int s_release[kStages];
+    __shared__ int s_release[NST];
     __shared__ int s_failed, s_last;
     __shared__ int s_phys[kMaxPagesPerSplit];
     __shared__ __align__(16) float s_q[HPC][kHeadDim];
@@ -173,26 +178,26 @@ __global__ void __launch_bounds__(kThreads, 2) decode_kernel(DecodeArgs a) {
     // page-table slice (written by the host, never by a kernel)
     for (int i = tid; i < np; i += kThreads) s_phys[i] = S.table[(int)((p0 + i) % S.cap)];
     __syncthreads();
-    auto page_src = [&](int i) -> const float* {
-        return a.pv.base + (size_t)s_phys[i] * a.pv.page_floats + a.pv.layer_off + (size_t)kvh * kPageRowFloats;
+    auto page_src = [&](int i) -> const char* {
+        return a.pv.base + (size_t)s_phys[i] * a.pv.page_bytes + a.pv.layer_off + (size_t)kvh * ROWB;
     };
     auto issue = [&](int i) {
-        const int st = i % kStages;
-        const float* kp = page_src(i);
-        float* dk = stages + (size_t)st * (2 * kPageRowFloats);
-        mbar_expect_tx(&full[st], kStageBytes);
-        bulk_g2s(dk, kp, kPageRowFloats * 4, &full[st]);
-        bulk_g2s(dk + kPageRowFloats, kp + a.pv.block_floats, kPageRowFloats * 4, &full[st]);
+        const int st = i % NST;
+        const char* kp = page_src(i);
+        unsigned char* dk = stages + (size_t)st * SB;
+        mbar_expect_tx(&full[st], SB);
+        bulk_g2s(dk, kp, ROWB, &full[st]);
+        bulk_g2s(dk + ROWB, kp + a.pv.block_bytes, ROWB, &full[st]);
     };
     auto prefetch = [&](int i) {
-        const float* kp = page_src(i);
-        bulk_prefetch_l2(kp, kPageRowFloats * 4);
-        bulk_prefetch_l2(kp + a.pv.block_floats, kPageRowFloats * 4);
+        const char* kp = page_src(i);
+        bulk_prefetch_l2(kp, ROWB);
+        bulk_prefetch_l2(kp + a.pv.block_bytes, ROWB);
     };
 
-    const int n_first = min(kStages, np);
+    const int n_first = min(NST, np);
     if (tid == 0) {
-        for (int s = 0; s < kStages; ++s) {
+        for (int s = 0; s < NST; ++s) {
             mbar_init(&full[s], 1);
             s_release[s] = 0;
         }
@@ -200,7 +205,7 @@ __global__ void __launch_bounds__(kThreads, 2) decode_kernel(DecodeArgs a) {
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         for (int i = 0; i < n_first && i < n_early; ++i) issue(i);
-        for (int i = kStages; i < kStages + kPrefetch && i < n_early; ++i) prefetch(i);
+        for (int i = NST; i < NST + kPrefetch && i < n_early; ++i) prefetch(i);
     }
 
     // ---- everything below may read what the predecessor wrote --------------
@@ -231,19 +236,33 @@ __global__ void __launch_bounds__(kThreads, 2) decode_kernel(DecodeArgs a) {
         const float* vr = a.v_new + ((size_t)seq * a.n_kv + kvh) * kHeadDim;
         float y0, y1;
         warp_norm_rope64(kr, a.k_gain, S.pos, a.theta_scale, a.eps, lane, y0, y1);
+        float w0 = vr[lane], w1 = vr[lane + 32];
+        if (BF) {  // this step uses exactly what the cache will hold
+            y0 = __bfloat162float(__float2bfloat16_rn(y0));
+            y1 = __bfloat162float(__float2bfloat16_rn(y1));
+            w0 = __bfloat162float(__float2bfloat16_rn(w0));
+            w1 = __bfloat162float(__float2bfloat16_rn(w1));
+        }
         s_knew[lane] = y0;
         s_knew[lane + 32] = y1;
-        s_vnew[lane] = vr[lane];
-        s_vnew[lane + 32] = vr[lane + 32];
+        s_vnew[lane] = w0;
+        s_vnew[lane + 32] = w1;
         if (has_new) {  // one CTA per kv head writes the cache
             const int i = (int)((S.new_slot >> 6) - p0);
-            float* kd = a.pv.base + (size_t)s_phys[i] * a.pv.page_floats + a.pv.layer_off +
-                        (size_t)kvh * kPageRowFloats + (size_t)(S.new_slot & 63) * kHeadDim;
-            float* vd = kd + a.pv.block_floats;
-            kd[lane] = y0;
-            kd[lane + 32] = y1;
-            vd[lane] = vr[lane];
-            vd[lane + 32] = vr[lane + 32];
+            char* kd = a.pv.base + (size_t)s_phys[i] * a.pv.page_bytes + a.pv.layer_off + (size_t)kvh * ROWB +
+                       (size_t)(S.new_slot & 63) * kHeadDim * ES;
+            char* vd = kd + a.pv.block_bytes;
+            if (BF) {
+                reinterpret_cast<__nv_bfloat16*>(kd)[lane] = __float2bfloat16_rn(y0);
+                reinterpret_cast<__nv_bfloat16*>(kd)[lane + 32] = __float2bfloat16_rn(y1);
+                reinterpret_cast<__nv_bfloat16*>(vd)[lane] = __float2bfloat16_rn(w0);
+                reinterpret_cast<__nv_bfloat16*>(vd)[lane + 32] = __float2bfloat16_rn(w1);
+            } else {
+                reinterpret_cast<float*>(kd)[lane] = y0;
+                reinterpret_cast<float*>(kd)[lane + 32] = y1;
+                reinterpret_cast<float*>(vd)[lane] = w0;
+                reinterpret_cast<float*>(vd)[lane + 32] = w1;
+            }
         }
     }
     __syncthreads();
@@ -267,13 +286,13 @@ __global__ void __launch_bounds__(kThreads, 2) decode_kernel(DecodeArgs a) {
         for (int e = 0; e < 16; ++e) acc[h][e] = 0.f;
     }
     if (tid == 0)
-        for (int i = max(n_early, kStages); i < kStages + kPrefetch && i < np; ++i) prefetch(i);
+        for (int i = max(n_early, NST); i < NST + kPrefetch && i < np; ++i) prefetch(i);
 
     const long long win_lo = S.base, win_hi = S.base + S.len;
     const long long new_slot = own_new ? S.new_slot : -1;
     for (int i = 0; i < np; ++i) {
-        const int st = i % kStages;
-        const bool ok = __all_sync(0xffffffffu, mbar_wait_bounded(&full[st], (unsigned)((i / kStages) & 1)));
+        const int st = i % NST;
+        const bool ok = __all_sync(0xffffffffu, mbar_wait_bounded(&full[st], (unsigned)((i / NST) & 1)));
         if (!ok) {
             if (lane == 0) {
                 atomicExch(a.err, kErrWaitTimeout);
@@ -281,20 +300,29 @@ __global__ void __launch_bounds__(kThreads, 2) decode_kernel(DecodeArgs a) {
             }
             break;
         }
-        const float4* Ks = reinterpret_cast<const float4*>(stages + (size_t)st * (2 * kPageRowFloats));
-        const float4* Vs = Ks + kPageRowFloats / 4;
+        // 4 elements of chunk c of row r, as floats (16 B of fp32 or 8 B of bf16)
+        const unsigned char* Kst = stages + (size_t)st * SB;
+        const unsigned char* Vst = Kst + ROWB;
+        auto ld4 = [&](const unsigned char* base, int idx) -> float4 {
+            if (BF) {
+                const uint2 u = reinterpret_cast<const uint2*>(base)[idx];
+                return make_float4(__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xffff0000u),
+                                   __uint_as_float(u.y << 16), __uint_as_float(u.y & 0xffff0000u));
+            }
+            return reinterpret_cast<const float4*>(base)[idx];
+        };
         const long long slot0 = (p0 + i) << 6;
 #ifdef BEBELM_DECODE_NOCOMPUTE
         __syncwarp();
         if (lane == 0 && atomicAdd(&s_release[st], 1) == 3) {
             s_release[st] = 0;
-            if (i + kStages < np) {
+            if (i + NST < np) {
                 asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-                issue(i + kStages);
-                if (i + kStages + kPrefetch < np) prefetch(i + kStages + kPrefetch);
+                issue(i + NST);
+                if (i + NST + kPrefetch < np) prefetch(i + NST + kPrefetch);
             }
         }
-        acc[0][0] += Ks[lane].x;
+        acc[0][0] += ld4(Kst, lane).x;
         continue;
 #endif
         // both rows of K and V into registers, then hand the stage back at once
@@ -311,8 +339,8 @@ __global__ void __launch_bounds__(kThreads, 2) decode_kernel(DecodeArgs a) {
             } else {
 #pragma unroll
                 for (int ii = 0; ii < 4; ++ii) {
-                    kk[r][ii] = Ks[row * 16 + c[ii]];
-                    vv[r][ii] = Vs[row * 16 + c[ii]];
+                    kk[r][ii] = ld4(Kst, row * 16 + c[ii]);
+                    vv[r][ii] = ld4(Vst, row * 16 + c[ii]);
                 }
             }
         }
@@ -320,10 +348,10 @@ __global__ void __launch_bounds__(kThreads, 2) decode_kernel(DecodeArgs a) {
         if (lane == 0) {
             if (atomicAdd(&s_release[st], 1) == 3) {  // last of the 4 warps refills the stage
                 s_release[st] = 0;
-                if (i + kStages < np) {
+                if (i + NST < np) {
                     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-                    issue(i + kStages);
-                    if (i + kStages + kPrefetch < np) prefetch(i + kStages + kPrefetch);
+                    issue(i + NST);
+                    if (i + NST + kPrefetch < np) prefetch(i + NST + kPrefetch);
                 }
             }
         }
@@ -387,9 +415,9 @@ __global__ void __launch_bounds__(kThreads, 2) decode_kernel(DecodeArgs a) {
     if (s_failed) {
         // a wait gave up: let our own copies still in flight land (bounded), then leave
         if (tid == 0) {
-            for (int k = 0; k < kStages && k < np; ++k) {
-                const int last = ((np - 1 - k) / kStages) * kStages + k;
-                mbar_wait_bounded(&full[k], (unsigned)((last / kStages) & 1));
+            for (int k = 0; k < NST && k < np; ++k) {
+                const int last = ((np - 1 - k) / NST) * NST + k;
+                mbar_wait_bounded(&full[k], (unsigned)((last / NST) & 1));
             }
         }
         return;
@@ -402,7 +430,7 @@ __global__ void __launch_bounds__(kThreads, 2) decode_kernel(DecodeArgs a) {
         l[h] += __shfl_xor_sync(0xffffffffu, l[h], 8);
         l[h] += __shfl_xor_sync(0xffffffffu, l[h], 16);
     }
-    float* red = stages;  // [4 warps][8 j][HPC][64]; every copy has landed and been read
+    float* red = reinterpret_cast<float*>(stages);  // [4 warps][8 j][HPC][64]; every copy has landed and been read
 #pragma unroll
     for (int h = 0; h < HPC; ++h) {
         float* dst = red + ((size_t)(warp * 8 + j) * HPC + h) * kHeadDim;
@@ -526,14 +554,14 @@ __global__ void __launch_bounds__(kThreads, 2) decode_kernel(DecodeArgs a) {
     }
 }
 
-template <int HPC>
+template <int HPC, bool BF>
 cudaError_t launch_hpc(const DecodeArgs& a, cudaStream_t s) {
     static bool attr_set[64] = {};  // the attribute is per device
     const int smem = (int)decode_smem_bytes();
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 0 || dev >= 64 || !attr_set[dev]) {
-        cudaError_t e = cudaFuncSetAttribute(decode_kernel<HPC>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        cudaError_t e = cudaFuncSetAttribute(decode_kernel<HPC, BF>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
         if (e != cudaSuccess) return e;
         if (dev >= 0 && dev < 64) attr_set[dev] = true;
     }
@@ -547,20 +575,20 @@ cudaError_t launch_hpc(const DecodeArgs& a, cudaStream_t s) {
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = a.pdl ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, decode_kernel<HPC>, a);
+    return cudaLaunchKernelEx(&cfg, decode_kernel<HPC, BF>, a);
 }
 
 }  // namespace
 
-size_t decode_smem_bytes() { return (size_t)kStages * kStageBytes + kStages * sizeof(uint64_t); }
+size_t decode_smem_bytes() { return (size_t)kRingBytes + 2 * kStages * sizeof(uint64_t); }
 
 cudaError_t launch_decode(const DecodeArgs& a, cudaStream_t s) {
     if (a.total_splits <= 0) return cudaSuccess;
     switch (a.hpc) {
-        case 1: return launch_hpc<1>(a, s);
-        case 2: return launch_hpc<2>(a, s);
-        case 3: return launch_hpc<3>(a, s);
-        case 4: return launch_hpc<4>(a, s);
+        case 1: return a.pv.bf16 ? launch_hpc<1, true>(a, s) : launch_hpc<1, false>(a, s);
+        case 2: return a.pv.bf16 ? launch_hpc<2, true>(a, s) : launch_hpc<2, false>(a, s);
+        case 3: return a.pv.bf16 ? launch_hpc<3, true>(a, s) : launch_hpc<3, false>(a, s);
+        case 4: return a.pv.bf16 ? launch_hpc<4, true>(a, s) : launch_hpc<4, false>(a, s);
         default: return cudaErrorInvalidValue;
     }
 }

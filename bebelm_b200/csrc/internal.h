@@ -12,13 +12,15 @@ constexpr int kHeadDim = 64;     // LFM2.5 head_dim (src/config.rs:20)
 constexpr int kPageTokens = 64;  // positions per KV page
 constexpr int kPageRowFloats = kPageTokens * kHeadDim;  // one kv head of one page: 4096 floats
 
-// Device-side view of the page pool for one layer. A physical page p holds, for
-// every layer l: K[l] then V[l], each [n_kv][64 tokens][64] fp32 (a "block").
+// Device-side view of the page pool for one layer. A physical page p holds, for every
+// layer l: K[l] then V[l], each a "block" [n_kv][64 tokens][64] of fp32 or bf16 elements.
+// All offsets are in bytes.
 struct PoolView {
-    float* base;          // pool memory
-    size_t page_floats;   // floats per physical page (all layers, K and V)
-    size_t layer_off;     // floats from page start to this layer's K block
-    size_t block_floats;  // floats of one K (or V) block = n_kv * 4096
+    char* base;           // pool memory
+    size_t page_bytes;    // one physical page (all layers, K and V)
+    size_t layer_off;     // page start to this layer's K block
+    size_t block_bytes;   // one K (or V) block = n_kv rows of a page
+    int bf16;             // elements are bf16 (else fp32)
 };
 
 // A sequence's window for one layer: logical slots [base, base+len) live in
@@ -30,13 +32,41 @@ struct SeqWindow {
     long long base;
 };
 
-__host__ __device__ inline size_t slot_offset(const PoolView& pv, const int* table, int cap,
-                                              long long slot, int kvh, int kind) {
-    long long lp = slot >> 6;
-    int phys = table[(int)(lp % cap)];
-    return (size_t)phys * pv.page_floats + pv.layer_off + (size_t)kind * pv.block_floats +
-           (size_t)kvh * kPageRowFloats + (size_t)(slot & 63) * kHeadDim;
+// Bytes of one kv head of one page (64 tokens x 64 elements).
+__host__ __device__ inline size_t row_bytes(const PoolView& pv) { return (size_t)kPageRowFloats * (pv.bf16 ? 2 : 4); }
+
+// Byte offset of (slot, kv head, K or V) in the pool.
+__host__ __device__ inline size_t slot_offset(const PoolView& pv, const int* table, int cap, long long slot, int kvh,
+                                              int kind) {
+    const long long lp = slot >> 6;
+    const int phys = table[(int)(lp % cap)];
+    return (size_t)phys * pv.page_bytes + pv.layer_off + (size_t)kind * pv.block_bytes + (size_t)kvh * row_bytes(pv) +
+           (size_t)(slot & 63) * kHeadDim * (pv.bf16 ? 2 : 4);
 }
+
+#ifdef __CUDACC__
+// Four consecutive elements (e..e+3) of the row at byte offset `off`, as floats.
+__device__ __forceinline__ float4 kv_load4(const PoolView& pv, size_t off, int e) {
+    if (pv.bf16) {
+        const uint2 u = *reinterpret_cast<const uint2*>(pv.base + off + 2 * (size_t)e);
+        return make_float4(__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xffff0000u), __uint_as_float(u.y << 16),
+                           __uint_as_float(u.y & 0xffff0000u));
+    }
+    return *reinterpret_cast<const float4*>(pv.base + off + 4 * (size_t)e);
+}
+// Stores four floats at elements e..e+3 (rounded to nearest-even bf16 in a bf16 pool).
+__device__ __forceinline__ void kv_store4(const PoolView& pv, size_t off, int e, float4 v) {
+    if (pv.bf16) {
+        __nv_bfloat162 a = __floats2bfloat162_rn(v.x, v.y), b = __floats2bfloat162_rn(v.z, v.w);
+        uint2 u;
+        u.x = *reinterpret_cast<uint32_t*>(&a);
+        u.y = *reinterpret_cast<uint32_t*>(&b);
+        *reinterpret_cast<uint2*>(pv.base + off + 2 * (size_t)e) = u;
+    } else {
+        *reinterpret_cast<float4*>(pv.base + off + 4 * (size_t)e) = v;
+    }
+}
+#endif
 
 // ---- kernel 1: per-head RMSNorm + NEOX RoPE (+ KV append) ------------------
 // Per-token destination when the tokens of one launch belong to different

@@ -196,12 +196,12 @@ __global__ void __launch_bounds__(256) norm_rope_kernel(NormRopeArgs a) {
         const int* table = a.targets ? a.targets[tok].table : a.table;
         const int cap = a.targets ? a.targets[tok].cap : a.cap;
         const long long slot = a.targets ? a.targets[tok].slot : a.slot0 + tok;
-        float* kd = a.pv.base + slot_offset(a.pv, table, cap, slot, head, 0);
-        float* vd = a.pv.base + slot_offset(a.pv, table, cap, slot, head, 1);
-        *reinterpret_cast<float4*>(kd + 4 * sub) = make_float4(x0[0], x0[1], x0[2], x0[3]);
-        *reinterpret_cast<float4*>(kd + 32 + 4 * sub) = make_float4(x1[0], x1[1], x1[2], x1[3]);
-        *reinterpret_cast<float4*>(vd + 4 * sub) = v0;
-        *reinterpret_cast<float4*>(vd + 32 + 4 * sub) = v1;
+        const size_t kd = slot_offset(a.pv, table, cap, slot, head, 0);
+        const size_t vd = slot_offset(a.pv, table, cap, slot, head, 1);
+        kv_store4(a.pv, kd, 4 * sub, make_float4(x0[0], x0[1], x0[2], x0[3]));
+        kv_store4(a.pv, kd, 32 + 4 * sub, make_float4(x1[0], x1[1], x1[2], x1[3]));
+        kv_store4(a.pv, vd, 4 * sub, v0);
+        kv_store4(a.pv, vd, 32 + 4 * sub, v1);
     }
 }
 
@@ -216,9 +216,9 @@ __global__ void __launch_bounds__(256) kv_gather_kernel(PoolView pv, const int* 
     const int kind = lane >> 4;  // lanes 0-15: K, 16-31: V
     float* dst = kind ? v_out : k_out;
     if (!dst) return;
-    const float* src = pv.base + slot_offset(pv, table, cap, base + t, h, kind);
+    const size_t src = slot_offset(pv, table, cap, base + t, h, kind);
     const int e = (lane & 15) * 4;
-    *reinterpret_cast<float4*>(dst + (size_t)row * 64 + e) = *reinterpret_cast<const float4*>(src + e);
+    *reinterpret_cast<float4*>(dst + (size_t)row * 64 + e) = kv_load4(pv, src, e);
 }
 
 // One thread per 4 consecutive floats of the [len][n_kv][64] window, K and V.
@@ -231,8 +231,8 @@ __global__ void kv_gather_bf16_kernel(PoolView pv, const int* table, int cap, lo
         const int e = (int)(i & 15) * 4;
         const long long t = row / n_kv;
         const int h = (int)(row % n_kv);
-        const float4 kf = *reinterpret_cast<const float4*>(pv.base + slot_offset(pv, table, cap, base + t, h, 0) + e);
-        const float4 vf = *reinterpret_cast<const float4*>(pv.base + slot_offset(pv, table, cap, base + t, h, 1) + e);
+        const float4 kf = kv_load4(pv, slot_offset(pv, table, cap, base + t, h, 0), e);
+        const float4 vf = kv_load4(pv, slot_offset(pv, table, cap, base + t, h, 1), e);
         __nv_bfloat162 k0 = __floats2bfloat162_rn(kf.x, kf.y), k1 = __floats2bfloat162_rn(kf.z, kf.w);
         __nv_bfloat162 v0 = __floats2bfloat162_rn(vf.x, vf.y), v1 = __floats2bfloat162_rn(vf.z, vf.w);
         uint2 kw, vw;

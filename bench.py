@@ -279,6 +279,7 @@ def run_ours(args):
         prefill = {"config2_2048": bench_prefill(bb, torch, dev, stream, bf16_peak, peak_kind, 2048, 6),
                    "config5_8192_one_layer": bench_prefill(bb, torch, dev, stream, bf16_peak, peak_kind, 8192, 2)}
 
+    c3bf = bench_config3_bf16(bb, torch, dev, stream, world, args.steps)
     cfg4 = None if args.no_cfg4 else bench_config4(bb, torch, dev, stream, world, rank)
     hbm_peak_, bf16_peak_, _ = peaks()
     cfg5 = None if args.no_cfg5 else bench_config5(bb, torch, dev, stream, world, rank, bf16_peak_)
@@ -316,6 +317,7 @@ def run_ours(args):
             "clocks": clk,
             "cpu_baseline": cpu,
             "prefill": prefill,
+            "config3_bf16_kv": c3bf,
             "config4": cfg4,
             "config5": cfg5,
         }
@@ -372,6 +374,41 @@ def bench_prefill(bb, torch, dev, stream, bf16_peak, peak_kind, T=2048, reps=6):
             "ms": round(ms, 4), "value": round(tf, 3), "unit": "TFLOP/s",
             "roofline": {"bound": "tensor", "achieved": round(tf, 3), "peak": bf16_peak, "unit": "TFLOP/s",
                          "frac": round(tf / bf16_peak, 4), "peak_kind": peak_kind}}
+
+
+def bench_config3_bf16(bb, torch, dev, stream, world, steps):
+    """Config 3 with the bf16 KV cache: same step, half the bytes per position."""
+    cache = bb.Cache(n_layers=1, max_context=CTX, device=dev.index, kv_dtype=bb.BF16)
+    g = torch.Generator(device=dev)
+    g.manual_seed(31)
+    for c0 in range(0, CTX, 4096):
+        cache.append(0, torch.randn((4096, KVD), generator=g, device=dev), torch.randn((4096, KVD), generator=g, device=dev))
+    n = steps + 5
+    Q = torch.randn((n, HID), generator=g, device=dev)
+    K = torch.randn((n, KVD), generator=g, device=dev)
+    V = torch.randn((n, KVD), generator=g, device=dev)
+    qg = 1 + 0.02 * torch.randn(D, generator=g, device=dev)
+    kg = 1 + 0.02 * torch.randn(D, generator=g, device=dev)
+    out = torch.empty((n, HID), device=dev)
+    for i in range(5):
+        cache.attn_step(0, Q[i], K[i], V[i], qg, kg, pos=CTX + i, theta=THETA, out=out[i], stream=stream)
+        cache.evict_front(1)
+    barrier(world)
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for i in range(5, n):
+        cache.attn_step(0, Q[i], K[i], V[i], qg, kg, pos=CTX + i, theta=THETA, out=out[i], stream=stream)
+        cache.evict_front(1)
+    b.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    ms = max_over_ranks(a.elapsed_time(b), world, dev)
+    cache.close()
+    per_step = 2 * (CTX + 1) * KVD * 2
+    return {"workload": "config3 with a bf16 KV cache (K/V rounded to bf16 on append, attention in fp32)",
+            "value": round(per_step * steps * world / (ms * 1e-3) / 1e9, 1), "unit": "GB/s (bf16 bytes)",
+            "tok_per_s": round(steps * world / (ms * 1e-3), 1), "ms_per_step": round(ms / steps, 5)}
 
 
 def bench_config4(bb, torch, dev, stream, world, rank, steps=128):

@@ -88,7 +88,10 @@ BEBELM_API int bebelm_norm_rope_heads(float* buf, size_t n_tokens, int n_heads, 
 /* ------------------------------------------------------------- KV cache --- */
 /* Device replacement for `Cache` (src/cache.rs:9-49), attention layers only.
  * Storage is paged: a page holds `page_tokens` (64) positions of K and V for
- * every attention layer, laid out [layer][K|V][kv_head][token][64] in fp32.
+ * every attention layer, laid out [layer][K|V][kv_head][token][64]. dtype
+ * BEBELM_F32 keeps the reference's fp32 history; BEBELM_BF16 stores K and V
+ * rounded to bf16 (nearest even) when appended, halving the bytes each decode
+ * step reads, with attention still computed in fp32.
  * A sequence's window is a ring of pages, so evict_front (the sliding window
  * of src/agent.rs:471-476) moves an offset and recycles whole pages instead of
  * moving memory. The ring has ceil(max_context/64) + 2 pages: a window always

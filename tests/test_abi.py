@@ -45,7 +45,7 @@ def test_argument_validation_without_device():
     L = bb.load_library()
     assert L.bebelm_kv_create(6, 8, 32, 1024, 64, 0, 0, C.byref(C.c_void_p())) == bb.ERR_UNSUPPORTED
     assert L.bebelm_kv_create(6, 8, 64, 1024, 32, 0, 0, C.byref(C.c_void_p())) == bb.ERR_UNSUPPORTED
-    assert L.bebelm_kv_create(6, 8, 64, 1024, 64, 1, 0, C.byref(C.c_void_p())) == bb.ERR_UNSUPPORTED
+    assert L.bebelm_kv_create(6, 8, 64, 1024, 64, 7, 0, C.byref(C.c_void_p())) == bb.ERR_UNSUPPORTED  # unknown dtype
     assert L.bebelm_kv_len(None, C.byref(C.c_size_t())) == bb.ERR_INVALID
     assert L.bebelm_attn_decode_host(None, None, None, 1, 3, 2, 64, None) == bb.ERR_INVALID
     buf = C.create_string_buffer(64)

@@ -367,3 +367,76 @@ def test_config2_tensor_core_prefill_2048():
     want = oracle.attn_batch(q, k, v, 0, qg, kg, 1e6, 1e-5, H, KVH, D, n_threads=oracle.max_threads())[0]
     rel = np.abs(got - want).max() / np.abs(want).max()
     assert rel <= PREFILL_REL, rel
+
+
+# ------------------------------------------------------------ bf16 KV cache --
+def _bf16(x):
+    torch = pytest.importorskip("torch")
+    return torch.from_numpy(np.ascontiguousarray(x, np.float32)).to(torch.bfloat16).float().numpy()
+
+
+def test_bf16_cache_decode_matches_oracle_on_the_same_values():
+    """Over bf16-exact K/V the bf16 cache must give what the fp32 reference arithmetic gives."""
+    n = 3000
+    dev = bb.Cache(n_layers=2, max_context=4096, kv_dtype=bb.BF16)
+    k, v = _bf16(oracle.normal(1, (n, KVD))), _bf16(oracle.normal(2, (n, KVD)))
+    dev.append(1, k, v)
+    dev.evict_front(129)
+    kd, vd = dev.read(1)
+    assert np.array_equal(kd, k[129:]) and np.array_equal(vd, v[129:])
+    torch = pytest.importorskip("torch")
+    q = oracle.normal(3, (HID,))
+    got = dev.decode(1, torch.from_numpy(q).cuda()).cpu().numpy()
+    want = oracle.attention_decode(q, k[129:], v[129:], n - 129, H, KVH, D)
+    assert np.abs(got - want).max() <= 1e-5
+
+
+def _ref_step_bf16(ref, q, k, v, qg, kg, pos):
+    """attn_step on the oracle, with the appended k and v rounded to bf16 as the bf16 cache stores them."""
+    qn = oracle.norm_rope_heads(q, H, D, qg, pos, 1e6, 1e-5)
+    kn = _bf16(oracle.norm_rope_heads(k, KVH, D, kg, pos, 1e6, 1e-5))
+    ref.append(0, kn, _bf16(v))
+    return oracle.attention_decode(qn, ref.k[0], ref.v[0], ref.k[0].shape[0], H, KVH, D)
+
+
+def test_bf16_cache_fused_step_and_batched():
+    qg, kg = gains(91)
+    dev = bb.Cache(n_layers=1, max_context=2048, kv_dtype=bb.BF16)
+    ref = oracle.Cache(1, KVD)
+    k0, v0 = _bf16(oracle.normal(4, (700, KVD))), _bf16(oracle.normal(5, (700, KVD)))
+    dev.append(0, k0, v0)
+    ref.append(0, k0, v0)
+    for step in range(3):
+        q, k, v = oracle.normal(10 + step, (HID,)), oracle.normal(20 + step, (KVD,)), oracle.normal(30 + step, (KVD,))
+        got = dev.attn_step(0, q, k, v, qg, kg, pos=700 + step, theta=1e6)
+        want = _ref_step_bf16(ref, q, k, v, qg, kg, 700 + step)
+        assert np.abs(got - want).max() <= 1e-4, step
+    kd, vd = dev.read(0)
+    # the appended k may differ by one bf16 ulp where sinf/cosf ulps move it across a rounding boundary
+    assert np.abs(kd - ref.k[0]).max() <= 2e-2 and np.array_equal(vd, ref.v[0])
+    pool = bb.Pool(n_layers=1, n_pages=100, kv_dtype=bb.BF16)
+    lens = [5, 130, 1000]
+    devs = [bb.Cache(max_context=2048, pool=pool, kv_dtype=bb.BF16) for _ in lens]
+    refs = [oracle.Cache(1, KVD) for _ in lens]
+    for i, n in enumerate(lens):
+        kk, vv = _bf16(oracle.normal(40 + i, (n, KVD))), _bf16(oracle.normal(50 + i, (n, KVD)))
+        devs[i].append(0, kk, vv)
+        refs[i].append(0, kk, vv)
+    q, k, v = oracle.normal(6, (3, HID)), oracle.normal(7, (3, KVD)), oracle.normal(8, (3, KVD))
+    got = bb.attn_decode_batched(devs, 0, q, k, v, qg, kg, [n for n in lens], theta=1e6)
+    for i in range(3):
+        want = _ref_step_bf16(refs[i], q[i], k[i], v[i], qg, kg, lens[i])
+        assert np.abs(got[i] - want).max() <= 1e-4, i
+
+
+def test_bf16_cache_tensor_core_prefill():
+    qg, kg = gains(95)
+    dev = bb.Cache(n_layers=1, max_context=4096, kv_dtype=bb.BF16)
+    pk, pv = _bf16(oracle.normal(5, (300, KVD))), _bf16(oracle.normal(6, (300, KVD)))
+    dev.append(0, pk, pv)
+    t = 400
+    q, k, v = (_bf16_round(oracle.normal(s, shp)) for s, shp in ((7, (t, HID)), (8, (t, KVD)), (9, (t, KVD))))
+    got = _prefill_bf16(dev, q, k, v, qg, kg, 300, 1e6)
+    want = oracle.attn_batch(q, k, v, 300, qg, kg, 1e6, 1e-5, H, KVH, D, pk, pv, n_threads=oracle.max_threads())[0]
+    rel = np.abs(got - want).max() / np.abs(want).max()
+    assert rel <= PREFILL_REL, rel
