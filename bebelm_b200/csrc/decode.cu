@@ -110,6 +110,26 @@ __device__ __forceinline__ unsigned atomic_add_acq_rel_gpu(unsigned* p, unsigned
 
 __device__ __forceinline__ float fast_exp2(float x) { return exp2f(x); }
 
+// (c0, c1) += (a0, a1) * (b0, b1). PACKED: one f32x2 FMA instruction (two fp32 FMAs, each
+// rounded once), which pays where the loop is short of issue slots (the bf16 cache moves half
+// the bytes per FMA); otherwise two scalar FMAs.
+template <bool PACKED>
+__device__ __forceinline__ void fma2(float& c0, float& c1, float a0, float a1, float b0, float b1) {
+    if (PACKED) {
+        asm("{\n\t.reg .b64 a, b, c;\n\t"
+        "mov.b64 a, {%2, %3};\n\t"
+        "mov.b64 b, {%4, %5};\n\t"
+        "mov.b64 c, {%0, %1};\n\t"
+        "fma.rn.f32x2 c, a, b, c;\n\t"
+        "mov.b64 {%0, %1}, c;\n\t}"
+        : "+f"(c0), "+f"(c1)
+        : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
+    } else {
+        c0 = fmaf(a0, b0, c0);
+        c1 = fmaf(a1, b1, c1);
+    }
+}
+
 // One head of 64 at `pos`, one warp: lane i returns elements i and i+32 after
 // rmsnorm (f64 sum of f32 squares, IEEE divide/sqrt, unfused products) and NEOX
 // RoPE with the iterative angle — the arithmetic of norm_rope.cu.
@@ -362,14 +382,13 @@ __global__ void __launch_bounds__(kThreads, 2) decode_kernel(DecodeArgs a) {
             const bool valid = slot >= win_lo && slot < win_hi;
 #pragma unroll
             for (int h = 0; h < HPC; ++h) {
-                float d = 0.f;
+                float d0 = 0.f, d1 = 0.f;  // even and odd dims, summed at the end
 #pragma unroll
                 for (int ii = 0; ii < 4; ++ii) {
-                    d = fmaf(qr[h][ii].x, kk[r][ii].x, d);
-                    d = fmaf(qr[h][ii].y, kk[r][ii].y, d);
-                    d = fmaf(qr[h][ii].z, kk[r][ii].z, d);
-                    d = fmaf(qr[h][ii].w, kk[r][ii].w, d);
+                    fma2<BF>(d0, d1, qr[h][ii].x, qr[h][ii].y, kk[r][ii].x, kk[r][ii].y);
+                    fma2<BF>(d0, d1, qr[h][ii].z, qr[h][ii].w, kk[r][ii].z, kk[r][ii].w);
                 }
+                float d = d0 + d1;
                 d += __shfl_xor_sync(0xffffffffu, d, 1);
                 d += __shfl_xor_sync(0xffffffffu, d, 2);
                 s[r][h] = valid ? d * a.scale_log2 : -INFINITY;
@@ -401,10 +420,8 @@ __global__ void __launch_bounds__(kThreads, 2) decode_kernel(DecodeArgs a) {
                 const float w = pr[r][h];
 #pragma unroll
                 for (int ii = 0; ii < 4; ++ii) {
-                    acc[h][4 * ii + 0] = fmaf(w, vv[r][ii].x, acc[h][4 * ii + 0]);
-                    acc[h][4 * ii + 1] = fmaf(w, vv[r][ii].y, acc[h][4 * ii + 1]);
-                    acc[h][4 * ii + 2] = fmaf(w, vv[r][ii].z, acc[h][4 * ii + 2]);
-                    acc[h][4 * ii + 3] = fmaf(w, vv[r][ii].w, acc[h][4 * ii + 3]);
+                    fma2<BF>(acc[h][4 * ii + 0], acc[h][4 * ii + 1], w, w, vv[r][ii].x, vv[r][ii].y);
+                    fma2<BF>(acc[h][4 * ii + 2], acc[h][4 * ii + 3], w, w, vv[r][ii].z, vv[r][ii].w);
                 }
             }
         }
