@@ -39,7 +39,10 @@ EXPORTS = [
     "bebelm_kv_create", "bebelm_kv_create_in_pool", "bebelm_kv_destroy", "bebelm_kv_clone", "bebelm_kv_clear",
     "bebelm_kv_len", "bebelm_kv_layer_len", "bebelm_kv_pos", "bebelm_kv_set_pos", "bebelm_kv_evict_front",
     "bebelm_kv_append", "bebelm_kv_read", "bebelm_attn_step", "bebelm_attn_decode_cached", "bebelm_attn_decode_cached_noalloc", "bebelm_attn_prefill", "bebelm_attn_decode_batched",
+    "bebelm_kv_check", "bebelm_peer_group_create", "bebelm_peer_group_connect", "bebelm_peer_group_destroy",
+    "bebelm_attn_step_allgather",
 ]
+IPC_HANDLE_BYTES = 64
 
 
 class BebelmError(RuntimeError):
@@ -87,6 +90,11 @@ def load_library(path: str = LIB_PATH):
         "bebelm_attn_decode_cached_noalloc": ([vp, i, i, vp, vp, vp], i),
         "bebelm_attn_prefill": ([vp, i, i, vp, vp, vp, i, sz, sz, vp, vp, f, f, vp, i, vp], i),
         "bebelm_attn_decode_batched": ([vp, i, i, i, vp, vp, vp, vp, vp, f, f, vp, vp, i, vp], i),
+        "bebelm_kv_check": ([vp, vp], i),
+        "bebelm_peer_group_create": ([i, i, i, sz, vp, C.POINTER(vp)], i),
+        "bebelm_peer_group_connect": ([vp, vp], i),
+        "bebelm_peer_group_destroy": ([vp], i),
+        "bebelm_attn_step_allgather": ([vp, vp, i, i, vp, vp, vp, vp, vp, f, f, sz, vp, i, vp], i),
     }
     for name, (args, res) in sig.items():
         fn = getattr(L, name)
@@ -306,6 +314,25 @@ class Cache:
                                                pos, ob, mem, _stream_ptr(stream)))
         return out
 
+    def attn_step_allgather(self, group: "PeerGroup", layer: int, q, k, v, q_gain, k_gain, pos: int,
+                            theta: float = ROPE_THETA, eps: float = RMS_EPS, out=None, stream=None):
+        """:meth:`attn_step` on this rank's heads with the all-gather fused into the decode
+        kernel (peer stores over NVLink). q/k/v are this rank's slices; returns the full
+        [world * n_heads * 64] output in rank order."""
+        (qb, kb, vb, qg, kg), mem = _bufs(q, k, v, q_gain, k_gain)
+        n_heads = (qb[2].size if mem == MEM_HOST else qb[2].numel()) // self.head_dim
+        n_out = group.world * n_heads * self.head_dim
+        if out is None:
+            out = np.zeros(n_out, np.float32) if mem == MEM_HOST else qb[2].new_empty(n_out, dtype=qb[2].dtype)
+        ob, _, _ = _buf(out)
+        _check(load_library().bebelm_attn_step_allgather(self._h, group._h, layer, n_heads, qb[0], kb[0], vb[0], qg[0],
+                                                         kg[0], theta, eps, pos, ob, mem, _stream_ptr(stream)))
+        return out
+
+    def check(self, stream=None) -> None:
+        """Synchronises and raises if a bounded device-side wait gave up (device-memory calls)."""
+        _check(load_library().bebelm_kv_check(self._h, _stream_ptr(stream)))
+
     def decode(self, layer: int, q, out=None, stream=None):
         """``attention_decode`` over the cached window of ``layer`` (no append); q normed+roped."""
         (qb,), mem = _bufs(q)
@@ -362,6 +389,32 @@ class Cache:
                 load_library().bebelm_kv_destroy(self._h)
         except Exception:
             pass
+
+
+class PeerGroup:
+    """Landing zones for the fused decode + all-gather of KV-head sharding (one per rank).
+
+    Collective protocol: construct on every rank, exchange :attr:`handle` (bytes), then call
+    :meth:`connect` with all ranks' handles in rank order. ``slice_floats`` = n_heads*64 of
+    one rank. Close collectively (host barrier first)."""
+
+    def __init__(self, world: int, rank: int, slice_floats: int, device: int = 0):
+        self.world, self.rank, self.slice = world, rank, slice_floats
+        self._h = C.c_void_p()
+        buf = C.create_string_buffer(IPC_HANDLE_BYTES)
+        _check(load_library().bebelm_peer_group_create(device, world, rank, slice_floats, buf, C.byref(self._h)))
+        self.handle = buf.raw
+
+    def connect(self, handles) -> None:
+        if len(handles) != self.world or any(len(h) != IPC_HANDLE_BYTES for h in handles):
+            raise ValueError(f"need {self.world} handles of {IPC_HANDLE_BYTES} bytes")
+        blob = C.create_string_buffer(b"".join(handles), IPC_HANDLE_BYTES * self.world)
+        _check(load_library().bebelm_peer_group_connect(self._h, blob))
+
+    def close(self) -> None:
+        if self._h:
+            load_library().bebelm_peer_group_destroy(self._h)
+            self._h = C.c_void_p()
 
 
 def attn_decode_batched(caches, layer: int, q, k, v, q_gain, k_gain, pos, theta: float = ROPE_THETA,

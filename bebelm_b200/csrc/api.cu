@@ -406,8 +406,16 @@ long long dep_slot_for(const bebelm_kv_pool* P, const bebelm_kv* kv, int layer) 
 
 // Split-K decode of one query per window. out: [n_windows][n_heads][64] device. The
 // query is d_q (normed+roped, [n][n_heads][64]) or, for a fused step, fused->q_raw.
+// Where a fused all-gather sends the final outputs (one window only): every rank's landing zone.
+struct PeerTarget {
+    float* const* bufs;
+    unsigned long long* const* flags;
+    int world, rank;
+    size_t off;
+};
+
 int run_decode(bebelm_kv_pool* P, const std::vector<Window>& wins, int layer, int n_heads, const float* d_q,
-               float* d_out, float scale, const FusedStep* fused, cudaStream_t s) {
+               float* d_out, float scale, const FusedStep* fused, cudaStream_t s, const PeerTarget* peer = nullptr) {
     const int n = (int)wins.size();
     if (n == 0) return 0;
     const int group = n_heads / P->n_kv;
@@ -476,6 +484,13 @@ int run_decode(bebelm_kv_pool* P, const std::vector<Window>& wins, int layer, in
     a.total_splits = total_splits;
     a.scale_log2 = scale * 1.4426950408889634f;
     a.pdl = 1;
+    if (peer) {
+        a.peer_bufs = peer->bufs;
+        a.peer_flags = peer->flags;
+        a.peer_world = peer->world;
+        a.peer_rank = peer->rank;
+        a.peer_off = peer->off;
+    }
     CUDA_TRY(launch_decode(a, s));
     P->last_writes.clear();
     if (fused)
@@ -1216,3 +1231,166 @@ extern "C" int bebelm_attn_decode_cached_noalloc(const bebelm_kv* kv, int layer,
     CUDA_TRY(launch_decode(a, s));
     return 0;
 }
+
+// ---------------------------------------------------------------------------
+// Fused KV-head-sharded step: decode + all-gather over peer memory (NVLink stores).
+//
+// Each rank owns a landing zone allocated with cudaMalloc and exported by CUDA IPC:
+//   [flags: world x u64, padded to 256 B][parity 0: world x slice floats][parity 1: ...]
+// flags[r] counts the output-writing CTAs of source rank r over all steps; step e (1-based)
+// is complete on this rank once every flags[r] >= e * writers. Parity e&1 alternates so a
+// rank may run one step ahead of a peer that is still copying out the previous step: a
+// writer of step e+2 has already waited for every rank's step e+1 signals, which each rank
+// issues only after (stream order) its own copy-out of step e.
+// ---------------------------------------------------------------------------
+constexpr int kMaxPeers = 32;  // flags fit the 256-byte header
+
+struct bebelm_peer_group {
+    int device = -1, world = 0, rank = 0;
+    size_t slice = 0;  // floats per rank per parity
+    char* zone = nullptr;
+    char* peer_base[kMaxPeers] = {};  // opened IPC mappings (own entry: zone)
+    DevBuf tables;                    // float* bufs[world], then u64* flags[world]
+    unsigned long long epoch = 0;
+    bool connected = false;
+    size_t zone_bytes() const { return 256 + 2 * (size_t)world * slice * sizeof(float); }
+    float* const* d_bufs() const { return tables.as<float* const>(); }
+    unsigned long long* const* d_flags() const {
+        return reinterpret_cast<unsigned long long* const*>(tables.as<char>() + sizeof(void*) * world);
+    }
+};
+
+extern "C" {
+
+int bebelm_kv_check(const bebelm_kv* kv, void* stream) {
+    if (!kv) return fail(BEBELM_ERR_INVALID, "null handle");
+    bebelm_kv_pool* P = kv->pool;
+    DeviceGuard dg(P->device);
+    cudaStream_t s = as_stream(stream);
+    int derr = 0;
+    CUDA_TRY(cudaMemcpyAsync(&derr, P->err.p, sizeof(int), cudaMemcpyDeviceToHost, s));
+    CUDA_TRY(cudaStreamSynchronize(s));
+    if (derr) {
+        cudaMemsetAsync(P->err.p, 0, sizeof(int), s);
+        if (P->counters.p) cudaMemsetAsync(P->counters.p, 0, P->counters.bytes, s);
+        cudaStreamSynchronize(s);
+        return fail(BEBELM_ERR_TIMEOUT, "a device-side wait timed out (code %d); outputs are invalid", derr);
+    }
+    return 0;
+}
+
+int bebelm_peer_group_create(int device, int world, int rank, size_t slice_floats, void* handle_out,
+                             bebelm_peer_group** out) {
+    if (!out || !handle_out) return fail(BEBELM_ERR_INVALID, "null argument");
+    *out = nullptr;
+    if (world < 1 || world > kMaxPeers || rank < 0 || rank >= world)
+        return fail(BEBELM_ERR_INVALID, "rank %d / world %d out of range (world <= %d)", rank, world, kMaxPeers);
+    if (slice_floats == 0 || slice_floats % 64)
+        return fail(BEBELM_ERR_INVALID, "slice_floats (%zu) must be a positive multiple of 64", slice_floats);
+    int n_dev = 0;
+    CUDA_TRY(cudaGetDeviceCount(&n_dev));
+    if (device < 0 || device >= n_dev) return fail(BEBELM_ERR_INVALID, "device %d not present", device);
+    DeviceGuard dg(device);
+    auto* g = new bebelm_peer_group();
+    g->device = device;
+    g->world = world;
+    g->rank = rank;
+    g->slice = slice_floats;
+    cudaError_t e = cudaMalloc(&g->zone, g->zone_bytes());
+    if (e == cudaSuccess) e = cudaMemset(g->zone, 0, g->zone_bytes());
+    if (e == cudaSuccess) e = cudaIpcGetMemHandle(static_cast<cudaIpcMemHandle_t*>(handle_out), g->zone);
+    if (e != cudaSuccess) {
+        if (g->zone) cudaFree(g->zone);
+        delete g;
+        return fail(BEBELM_ERR_CUDA, "peer zone: %s", cudaGetErrorString(e));
+    }
+    g->peer_base[rank] = g->zone;
+    *out = g;
+    return 0;
+}
+
+int bebelm_peer_group_connect(bebelm_peer_group* g, const void* handles) {
+    if (!g || !handles) return fail(BEBELM_ERR_INVALID, "null argument");
+    if (g->connected) return fail(BEBELM_ERR_INVALID, "peer group already connected");
+    DeviceGuard dg(g->device);
+    const auto* h = static_cast<const cudaIpcMemHandle_t*>(handles);
+    for (int r = 0; r < g->world; ++r) {
+        if (r == g->rank) continue;
+        void* p = nullptr;
+        cudaError_t e = cudaIpcOpenMemHandle(&p, h[r], cudaIpcMemLazyEnablePeerAccess);
+        if (e != cudaSuccess) {
+            for (int q = 0; q < r; ++q)
+                if (q != g->rank && g->peer_base[q]) cudaIpcCloseMemHandle(g->peer_base[q]), g->peer_base[q] = nullptr;
+            return fail(BEBELM_ERR_CUDA, "opening rank %d's zone: %s", r, cudaGetErrorString(e));
+        }
+        g->peer_base[r] = static_cast<char*>(p);
+    }
+    std::vector<void*> tab(2 * (size_t)g->world);
+    for (int r = 0; r < g->world; ++r) {
+        tab[r] = g->peer_base[r] + 256;
+        tab[g->world + r] = g->peer_base[r];
+    }
+    TRY(g->tables.ensure(sizeof(void*) * tab.size()));
+    CUDA_TRY(cudaMemcpy(g->tables.p, tab.data(), sizeof(void*) * tab.size(), cudaMemcpyHostToDevice));
+    g->connected = true;
+    return 0;
+}
+
+int bebelm_peer_group_destroy(bebelm_peer_group* g) {
+    if (!g) return 0;
+    DeviceGuard dg(g->device);
+    cudaDeviceSynchronize();
+    for (int r = 0; r < g->world; ++r)
+        if (r != g->rank && g->peer_base[r]) cudaIpcCloseMemHandle(g->peer_base[r]);
+    g->tables.release();
+    if (g->zone) cudaFree(g->zone);
+    delete g;
+    return 0;
+}
+
+int bebelm_attn_step_allgather(bebelm_kv* kv, bebelm_peer_group* g, int layer, int n_heads, const float* q,
+                               const float* k, const float* v, const float* q_gain, const float* k_gain, float theta,
+                               float eps, size_t pos, float* out, int mem, void* stream) {
+    TRY(validate_layer(kv, layer));
+    TRY(check_mem(mem));
+    if (!g || !g->connected) return fail(BEBELM_ERR_INVALID, "peer group missing or not connected");
+    bebelm_kv_pool* P = kv->pool;
+    TRY(check_geometry(n_heads, P->n_kv));
+    if (P->device != g->device) return fail(BEBELM_ERR_INVALID, "cache and peer group are on different devices");
+    const size_t qn = (size_t)n_heads * kHeadDim, kvn = (size_t)P->n_kv * kHeadDim;
+    if (qn != g->slice)
+        return fail(BEBELM_ERR_INVALID, "n_heads*64 (%zu) differs from the group's slice (%zu)", qn, g->slice);
+    if (!q || !k || !v || !q_gain || !k_gain || !out) return fail(BEBELM_ERR_INVALID, "null buffer");
+    DeviceGuard dg(P->device);
+    cudaStream_t s = as_stream(stream);
+    const size_t full = (size_t)g->world * qn;
+    const float *dq = q, *dk = k, *dv = v, *dqg = q_gain, *dkg = k_gain;
+    float* dout = out;
+    if (mem == BEBELM_MEM_HOST) {
+        void *a0, *a1, *a2, *a3, *a4, *o;
+        Stage st[5] = {{q, 4 * qn, &a0}, {k, 4 * kvn, &a1}, {v, 4 * kvn, &a2}, {q_gain, 4 * 64, &a3}, {k_gain, 4 * 64, &a4}};
+        TRY(stage_in(P, st, 5, 4 * full, &o, s));
+        dq = (const float*)a0; dk = (const float*)a1; dv = (const float*)a2;
+        dqg = (const float*)a3; dkg = (const float*)a4; dout = (float*)o;
+    }
+    long long slot0 = 0;
+    TRY(reserve(kv, layer, 1, &slot0, s));
+    const FusedStep fs{dq, dk, dv, dqg, dkg, theta_scale_of(theta, kHeadDim), eps};
+    std::vector<Window> w{{kv, kv->base[layer], kv->len[layer], slot0, (long long)pos}};
+    const unsigned long long e = g->epoch + 1;
+    const size_t par_off = (size_t)(e & 1) * g->world * g->slice;
+    const PeerTarget pt{g->d_bufs(), g->d_flags(), g->world, g->rank, par_off};
+    TRY(run_decode(P, w, layer, n_heads, nullptr, dout, 0.125f, &fs, s, &pt));
+    g->epoch = e;
+    // output-writing CTAs per rank: one per (kv head, head subgroup); every rank has the same shape
+    int hpc, n_sub;
+    pick_heads_per_cta(n_heads / P->n_kv, &hpc, &n_sub);
+    const unsigned long long writers = (unsigned long long)P->n_kv * n_sub;
+    const float* land = reinterpret_cast<const float*>(g->zone + 256) + par_off;
+    CUDA_TRY(launch_peer_wait(reinterpret_cast<const unsigned long long*>(g->zone), g->world, e * writers, land, dout,
+                              full, P->err.as<int>(), s));
+    if (mem == BEBELM_MEM_HOST) return stage_out(P, dout, out, 4 * full, s);
+    return 0;
+}
+
+}  // extern "C"

@@ -130,6 +130,31 @@ __device__ __forceinline__ void fma2(float& c0, float& c1, float a0, float a1, f
     }
 }
 
+// Final output element `idx` (head*64 + d) of sequence `seq`: to `out`, or, for the fused
+// all-gather, to this rank's slice of every rank's landing zone (NVLink stores to peers).
+__device__ __forceinline__ void emit_out(const DecodeArgs& a, int seq, size_t idx, float v) {
+    if (a.peer_world > 0) {
+        const size_t off = a.peer_off + (size_t)a.peer_rank * a.n_heads * kHeadDim + idx;
+        for (int w = 0; w < a.peer_world; ++w) a.peer_bufs[w][off] = v;
+    } else {
+        a.out[(size_t)seq * a.n_heads * kHeadDim + idx] = v;
+    }
+}
+
+// After a CTA has emitted its outputs to the landing zones: make them visible system-wide,
+// then count this CTA once on every rank's flag for this source rank (release, system scope).
+__device__ __forceinline__ void signal_peers(const DecodeArgs& a) {
+    if (a.peer_world <= 0) return;
+    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int w = 0; w < a.peer_world; ++w) {
+            unsigned long long* f = a.peer_flags[w] + a.peer_rank;
+            asm volatile("red.release.sys.global.add.u64 [%0], %1;" ::"l"(f), "l"(1ull) : "memory");
+        }
+    }
+}
+
 // One head of 64 at `pos`, one warp: lane i returns elements i and i+32 after
 // rmsnorm (f64 sum of f32 squares, IEEE divide/sqrt, unfused products) and NEOX
 // RoPE with the iterative angle — the arithmetic of norm_rope.cu.
@@ -481,7 +506,7 @@ __global__ void __launch_bounds__(kThreads, 2) decode_kernel(DecodeArgs a) {
             }
         }
         if (single) {
-            a.out[((size_t)seq * a.n_heads + h0 + h) * kHeadDim + d] = L > 0.f ? A / L : 0.f;
+            emit_out(a, seq, (size_t)(h0 + h) * kHeadDim + d, L > 0.f ? A / L : 0.f);
         } else {
             const size_t pi = ((size_t)gsplit * NY + y) * HPC + h;
             a.part_acc[pi * kHeadDim + d] = A;
@@ -491,7 +516,10 @@ __global__ void __launch_bounds__(kThreads, 2) decode_kernel(DecodeArgs a) {
             }
         }
     }
-    if (single) return;
+    if (single) {
+        signal_peers(a);
+        return;
+    }
 
     // ---- last CTA of this (sequence, kv head) merges the splits ----------
     __syncthreads();  // every partial of this CTA is stored before thread 0 releases it
@@ -567,8 +595,9 @@ __global__ void __launch_bounds__(kThreads, 2) decode_kernel(DecodeArgs a) {
         float A = 0.f;
         for (int g = 0; g < G; ++g) A += sm_acc[g * HPC * kHeadDim + o];
         const float L = s_L[o / kHeadDim];
-        a.out[((size_t)seq * a.n_heads + h0) * kHeadDim + o] = L > 0.f ? A / L : 0.f;
+        emit_out(a, seq, (size_t)h0 * kHeadDim + o, L > 0.f ? A / L : 0.f);
     }
+    signal_peers(a);
 }
 
 template <int HPC, bool BF>
@@ -595,7 +624,39 @@ cudaError_t launch_hpc(const DecodeArgs& a, cudaStream_t s) {
     return cudaLaunchKernelEx(&cfg, decode_kernel<HPC, BF>, a);
 }
 
+__global__ void peer_wait_kernel(const unsigned long long* flags, int world, unsigned long long expected,
+                                 const float* src, float* dst, size_t n, int* err) {
+    __shared__ int s_ok;
+    if (threadIdx.x == 0) s_ok = 1;
+    __syncthreads();
+    if ((int)threadIdx.x < world) {
+        bool ok = false;
+        for (long long it = 0; it < kWaitLimit; ++it) {
+            unsigned long long v;
+            asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(flags + threadIdx.x) : "memory");
+            if (v >= expected) {
+                ok = true;
+                break;
+            }
+            __nanosleep(128);
+        }
+        if (!ok) {
+            atomicExch(&s_ok, 0);
+            atomicExch(err, kErrWaitTimeout);
+        }
+    }
+    __syncthreads();
+    if (!s_ok) return;
+    for (size_t i = threadIdx.x; i < n; i += blockDim.x) dst[i] = __ldcv(src + i);  // written by peers
+}
+
 }  // namespace
+
+cudaError_t launch_peer_wait(const unsigned long long* flags, int world, unsigned long long expected, const float* src,
+                             float* dst, size_t n, int* err, cudaStream_t s) {
+    peer_wait_kernel<<<1, 256, 0, s>>>(flags, world, expected, src, dst, n, err);
+    return cudaGetLastError();
+}
 
 size_t decode_smem_bytes() { return (size_t)kRingBytes + 2 * kStages * sizeof(uint64_t); }
 

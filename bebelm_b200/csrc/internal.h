@@ -150,7 +150,18 @@ struct DecodeArgs {
     int total_splits;
     float scale_log2;       // score scale (1/sqrt(head_dim)) times log2(e)
     int pdl;                // launched as a programmatic dependent of the previous kernel
+    // fused all-gather (KV-head sharding): when peer_world > 0 the final output of sequence 0
+    // goes to every rank's landing zone instead of `out`, at [peer_off + peer_rank*n_heads*64 +
+    // head*64 + d], and each writing CTA then bumps peer_flags[w][peer_rank] on every rank w
+    float* const* peer_bufs;
+    unsigned long long* const* peer_flags;
+    int peer_world, peer_rank;
+    size_t peer_off;
 };
+// Waits (bounded) until flags[r] >= expected for every source rank r, then copies n floats of
+// the gathered landing buffer to dst. On timeout it records kErrWaitTimeout and copies nothing.
+cudaError_t launch_peer_wait(const unsigned long long* flags, int world, unsigned long long expected, const float* src,
+                             float* dst, size_t n, int* err, cudaStream_t s);
 cudaError_t launch_decode(const DecodeArgs& a, cudaStream_t s);
 size_t decode_smem_bytes();
 constexpr int kDecodeMaxPagesPerSplit = 256;

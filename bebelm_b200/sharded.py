@@ -3,8 +3,11 @@
 * :class:`KVHeadSharded` — KV-head sharding. Rank r of N owns kv heads
   [8r/N, 8(r+1)/N) and their query heads [32r/N, 32(r+1)/N) for every attention
   layer; its cache holds only those heads, so each rank reads 1/N of the KV bytes.
-  After the local fused step (or prefill) the head outputs are all-gathered over
-  NCCL; rank order is head order, so the gathered buffer is the full
+  After the local prefill the head outputs are all-gathered over NCCL; a decode
+  step instead gathers inside its kernel (``fused_gather``): the CTAs that finish
+  each head store it into every rank's landing zone over NVLink and raise a flag
+  there (:class:`bebelm_b200.PeerGroup`). Rank order is head order, so the
+  gathered buffer is the full
   [n_heads*64] (or [t, n_heads*64]) output of ``attn_step`` / ``attn_batch``
   (src/model.rs:440-451, 232-254).
 * :func:`assign_sequences` — per-sequence sharding for independent Agent
@@ -23,7 +26,7 @@ import heapq
 import torch
 import torch.distributed as dist
 
-from . import HEAD_DIM, N_HEADS, N_KV_HEADS, RMS_EPS, ROPE_THETA, Cache
+from . import HEAD_DIM, N_HEADS, N_KV_HEADS, RMS_EPS, ROPE_THETA, Cache, PeerGroup
 
 
 def assign_sequences(lengths, world: int):
@@ -42,7 +45,9 @@ class KVHeadSharded:
     """One rank's share of a KV-head-sharded attention stack."""
 
     def __init__(self, n_layers: int, max_context: int, n_heads: int = N_HEADS, n_kv_heads: int = N_KV_HEADS,
-                 group=None, cache_factory=None):
+                 group=None, cache_factory=None, fused_gather: bool | None = None):
+        """fused_gather: gather decode outputs inside the decode kernel over peer memory
+        (default: on for the CUDA cache with more than one rank); off uses NCCL."""
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
@@ -57,6 +62,15 @@ class KVHeadSharded:
             self.cache = Cache(n_layers=n_layers, n_kv_heads=self.kv_per, max_context=max_context, device=dev)
         else:
             self.cache = cache_factory(n_layers, self.kv_per, max_context)
+        if fused_gather is None:
+            fused_gather = cache_factory is None and self.world > 1
+        self.peers = None
+        if fused_gather:
+            self.peers = PeerGroup(self.world, self.rank, self.h_per * HEAD_DIM, device=torch.cuda.current_device())
+            handles = [None] * self.world
+            dist.all_gather_object(handles, self.peers.handle, group=self.group)
+            self.peers.connect(handles)
+            dist.barrier(group=self.group)
 
     # -- slicing ---------------------------------------------------------------
     def _heads(self, x, per, first, t=None):
@@ -78,6 +92,11 @@ class KVHeadSharded:
     def attn_step(self, layer: int, q, k, v, q_gain, k_gain, pos: int, theta: float = ROPE_THETA,
                   eps: float = RMS_EPS):
         """q [n_heads*64], k/v [n_kv*64] (replicated on every rank) -> full out [n_heads*64]."""
+        if self.peers is not None:
+            return self.cache.attn_step_allgather(self.peers, layer, self._heads(q, self.h_per, self.h0),
+                                                  self._heads(k, self.kv_per, self.kv0),
+                                                  self._heads(v, self.kv_per, self.kv0), q_gain, k_gain, pos=pos,
+                                                  theta=theta, eps=eps)
         out = self.cache.attn_step(layer, self._heads(q, self.h_per, self.h0), self._heads(k, self.kv_per, self.kv0),
                                    self._heads(v, self.kv_per, self.kv0), q_gain, k_gain, pos=pos, theta=theta, eps=eps)
         return self._gather(out).reshape(-1)
@@ -102,3 +121,11 @@ class KVHeadSharded:
 
     def clear(self):
         self.cache.clear()
+
+    def close(self):
+        """Collective: every rank's steps are done before any landing zone is freed."""
+        if self.peers is not None:
+            torch.cuda.synchronize()
+            dist.barrier(group=self.group)
+            self.peers.close()
+            self.peers = None

@@ -464,11 +464,12 @@ def bench_config4(bb, torch, dev, stream, world, rank, steps=128):
 
 
 def bench_config5(bb, torch, dev, stream, world, rank, bf16_peak, T=8192, steps=512):
-    """Config 5: the 6 attention layers of the stack, KV heads sharded over the ranks with an NCCL
-    all-gather of head outputs: causal prefill of T bf16 tokens, then `steps` decode steps."""
+    """Config 5: the 6 attention layers of the stack, KV heads sharded over the ranks: causal
+    prefill of T bf16 tokens (NCCL all-gather of head outputs), then `steps` decode steps whose
+    all-gather is fused into the decode kernel (peer stores over NVLink). With more than one
+    rank the decode is also timed with an NCCL all-gather instead, for comparison."""
     from bebelm_b200.sharded import KVHeadSharded
     L = 6
-    sh = KVHeadSharded(n_layers=L, max_context=T + steps + 64)
     g = torch.Generator(device=dev)
     g.manual_seed(50)  # identical activations on every rank (replicated projections)
     q = torch.randn((T, HID), generator=g, device=dev).to(torch.bfloat16)
@@ -479,35 +480,48 @@ def bench_config5(bb, torch, dev, stream, world, rank, bf16_peak, T=8192, steps=
     Qd = torch.randn((steps, HID), generator=g, device=dev)
     Kd = torch.randn((steps, KVD), generator=g, device=dev)
     Vd = torch.randn((steps, KVD), generator=g, device=dev)
-    # untimed warm-up of every call and collective the timed region makes
-    for layer in range(L):
-        sh.attn_prefill(layer, q, k, v, qg, kg, 0, theta=THETA)
-        for s in range(3):
-            sh.attn_step(layer, Qd[s], Kd[s], Vd[s], qg, kg, pos=T + s, theta=THETA)
-    sh.clear()
-    barrier(world)
-    torch.cuda.synchronize()
-    e = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
-    e[0].record(stream)
-    for layer in range(L):
-        sh.attn_prefill(layer, q, k, v, qg, kg, 0, theta=THETA)
-    e[1].record(stream)
-    for s in range(steps):
+
+    def run(fused):
+        sh = KVHeadSharded(n_layers=L, max_context=T + steps + 64, fused_gather=fused)
+        # untimed warm-up of every call and collective the timed region makes
         for layer in range(L):
-            sh.attn_step(layer, Qd[s], Kd[s], Vd[s], qg, kg, pos=T + s, theta=THETA)
-    e[2].record(stream)
-    torch.cuda.synchronize()
-    barrier(world)
-    pre_ms = max_over_ranks(e[0].elapsed_time(e[1]), world, dev)
-    dec_ms = max_over_ranks(e[1].elapsed_time(e[2]), world, dev)
-    sh.cache.close()
+            sh.attn_prefill(layer, q, k, v, qg, kg, 0, theta=THETA)
+            for s in range(3):
+                sh.attn_step(layer, Qd[s], Kd[s], Vd[s], qg, kg, pos=T + s, theta=THETA)
+        sh.clear()
+        barrier(world)
+        torch.cuda.synchronize()
+        e = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+        e[0].record(stream)
+        for layer in range(L):
+            sh.attn_prefill(layer, q, k, v, qg, kg, 0, theta=THETA)
+        e[1].record(stream)
+        for s in range(steps):
+            for layer in range(L):
+                sh.attn_step(layer, Qd[s], Kd[s], Vd[s], qg, kg, pos=T + s, theta=THETA)
+        e[2].record(stream)
+        torch.cuda.synchronize()
+        barrier(world)
+        pre = max_over_ranks(e[0].elapsed_time(e[1]), world, dev)
+        dec = max_over_ranks(e[1].elapsed_time(e[2]), world, dev)
+        sh.close()
+        sh.cache.close()
+        return pre, dec
+
+    pre_ms, dec_ms = run(None)
     flops = L * 4096.0 * T * (T + 1)
     tf = flops / (pre_ms * 1e-3) / 1e12
-    return {"workload": f"config5: 6 GQA layers, causal prefill of {T} bf16 tokens then {steps} decode steps",
-            "prefill_ms": round(pre_ms, 3), "prefill_tflops": round(tf, 1),
-            "prefill_frac_of_bf16_peak_per_gpu": round(tf / world / bf16_peak, 4),
-            "decode_ms_per_step": round(dec_ms / steps, 4), "decode_tok_per_s": round(steps / (dec_ms * 1e-3), 1),
-            "parallelism": f"kv heads / {world} per GPU, NCCL all-gather of head outputs per layer"}
+    out = {"workload": f"config5: 6 GQA layers, causal prefill of {T} bf16 tokens then {steps} decode steps",
+           "prefill_ms": round(pre_ms, 3), "prefill_tflops": round(tf, 1),
+           "prefill_frac_of_bf16_peak_per_gpu": round(tf / world / bf16_peak, 4),
+           "decode_ms_per_step": round(dec_ms / steps, 4), "decode_tok_per_s": round(steps / (dec_ms * 1e-3), 1),
+           "parallelism": (f"kv heads / {world} per GPU; prefill: NCCL all-gather of head outputs; decode: "
+                           "all-gather fused into the decode kernel (NVLink peer stores + flags)") if world > 1
+           else "one GPU, all heads"}
+    if world > 1:
+        _, dec_nccl = run(False)
+        out["decode_ms_per_step_nccl_gather"] = round(dec_nccl / steps, 4)
+    return out
 
 
 def main():

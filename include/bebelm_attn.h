@@ -186,6 +186,45 @@ BEBELM_API int bebelm_attn_decode_batched(bebelm_kv* const* seqs, int n_seqs, in
                                const float* q_gain, const float* k_gain, float theta, float eps,
                                const size_t* pos, float* out, int mem, void* stream);
 
+/* Synchronises `stream` and reports whether a bounded device-side wait of any
+ * call on kv's pool gave up since the last check (BEBELM_ERR_TIMEOUT; the flag
+ * is then cleared). Host-memory calls check this themselves; device-memory
+ * calls only enqueue work, so their callers check here. */
+BEBELM_API int bebelm_kv_check(const bebelm_kv* kv, void* stream);
+
+/* ------------------------------------------- multi-GPU (KV-head sharding) --- */
+/* Fused decode + all-gather for KV-head sharding over NVLink, one process per
+ * GPU. The reference runs every head on one CPU (src/model.rs:440-451); here
+ * rank r of `world` holds kv heads [r*n_kv, (r+1)*n_kv) of the model and their
+ * query heads, and the full [world * n_heads * 64] output of the step lands
+ * on every rank without a separate collective: the kernel's output-writing
+ * CTAs store their heads straight into every rank's landing zone (peer
+ * stores over NVLink) and raise a per-source flag there; a one-block kernel
+ * then waits (bounded) for all ranks' flags and copies the zone out.
+ *
+ * Setup is collective: every rank calls bebelm_peer_group_create (which
+ * allocates its zone and writes a BEBELM_IPC_HANDLE_BYTES handle), the caller
+ * exchanges the handles (e.g. an all_gather over torch.distributed), then every
+ * rank calls bebelm_peer_group_connect with all `world` handles in rank order.
+ * slice_floats is one rank's output, n_heads*64. Steps must be called by all
+ * ranks in the same order with the same geometry and window lengths; a rank
+ * that stops calling makes its peers' next step fail with BEBELM_ERR_TIMEOUT
+ * (seen by bebelm_kv_check, or at once for host-memory calls). Destroy is
+ * collective too: barrier on the host after the last step, then destroy. */
+#define BEBELM_IPC_HANDLE_BYTES 64
+typedef struct bebelm_peer_group bebelm_peer_group;
+BEBELM_API int bebelm_peer_group_create(int device, int world, int rank, size_t slice_floats,
+                                        void* handle_out, bebelm_peer_group** out);
+BEBELM_API int bebelm_peer_group_connect(bebelm_peer_group* g, const void* handles);
+BEBELM_API int bebelm_peer_group_destroy(bebelm_peer_group* g);
+/* bebelm_attn_step on this rank's heads, gathered: q [n_heads*64] and k/v
+ * [n_kv_heads*64] are this rank's slices, out [world*n_heads*64] is the full
+ * output in rank (= head) order. */
+BEBELM_API int bebelm_attn_step_allgather(bebelm_kv* kv, bebelm_peer_group* g, int layer, int n_heads,
+                                          const float* q, const float* k, const float* v,
+                                          const float* q_gain, const float* k_gain, float theta,
+                                          float eps, size_t pos, float* out, int mem, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

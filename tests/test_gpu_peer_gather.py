@@ -1,0 +1,124 @@
+"""Fused decode + all-gather over peer memory (KV-head sharding), through the C-ABI.
+
+* world 1 (any GPU box): the landing-zone path — output CTAs store into the zone and raise
+  the flag, the wait kernel copies the zone out — must give exactly the plain fused step.
+* world 2 (needs 2 GPUs, one process each): every rank's gathered output must match the
+  unsharded oracle (src/model.rs:440-451 over all 32 heads) within the decode tolerance,
+  and be identical on both ranks. Then rank 1 skips a step between steps (no kernel in
+  flight) and rank 0's bounded wait must report BEBELM_ERR_TIMEOUT instead of hanging.
+"""
+import multiprocessing as mp
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+
+import bebelm_b200 as bb
+import oracle
+
+pytestmark = pytest.mark.gpu
+
+H, KVH, D = 32, 8, 64
+THETA, EPS = 5e6, 1e-5
+
+
+def _inputs(seed, t):
+    g = torch.Generator().manual_seed(seed)
+    return (torch.randn((t, H * D), generator=g), torch.randn((t, KVH * D), generator=g),
+            torch.randn((t, KVH * D), generator=g), 1 + 0.02 * torch.randn(D, generator=g),
+            1 + 0.02 * torch.randn(D, generator=g))
+
+
+def test_world1_zone_path_equals_fused_step():
+    qq, kk, vv, qg, kg = [x.numpy() for x in _inputs(11, 1300)]
+    a = bb.Cache(n_layers=2, max_context=2048)
+    a.attn_prefill(1, qq[:1280], kk[:1280], vv[:1280], qg, kg, 0, theta=THETA)
+    b = a.clone()
+    g = bb.PeerGroup(1, 0, H * D, device=0)
+    g.connect([g.handle])
+    try:
+        for i in range(12):  # both parities several times, host and device buffers
+            p = 1280 + i
+            want = a.attn_step(1, qq[p], kk[p], vv[p], qg, kg, pos=p, theta=THETA)
+            if i % 2:
+                got = b.attn_step_allgather(g, 1, qq[p], kk[p], vv[p], qg, kg, pos=p, theta=THETA)
+            else:
+                dev = [torch.from_numpy(x).cuda() for x in (qq[p], kk[p], vv[p], qg, kg)]
+                got = b.attn_step_allgather(g, 1, *dev, pos=p, theta=THETA).cpu().numpy()
+                b.check()
+            np.testing.assert_array_equal(got, want)
+    finally:
+        torch.cuda.synchronize()
+        g.close()
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, q):
+    try:
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+        torch.cuda.set_device(rank)
+        torch.distributed.init_process_group("nccl", rank=rank, world_size=world,
+                                             device_id=torch.device("cuda", rank))
+        from bebelm_b200.sharded import KVHeadSharded
+        sh = KVHeadSharded(n_layers=2, max_context=4096)
+        assert sh.peers is not None
+        qq, kk, vv, qg, kg = [x.cuda() for x in _inputs(7, 3000 + 10)]
+        sh.attn_prefill(1, qq[:3000], kk[:3000], vv[:3000], qg, kg, 0)
+        outs = []
+        for i in range(10):
+            p = 3000 + i
+            outs.append(sh.attn_step(1, qq[p], kk[p], vv[p], qg, kg, pos=p).cpu().numpy())
+        sh.cache.check()
+        # rank 1 leaves between steps; rank 0's next step must time out, not hang
+        status = None
+        if rank == 0:
+            h = [x.cpu().numpy() for x in (qq[0], kk[0], vv[0])]
+            try:
+                sh.cache.attn_step_allgather(sh.peers, 1, h[0][:H // world * D], h[1][:KVH // world * D],
+                                             h[2][:KVH // world * D], qg.cpu().numpy(), kg.cpu().numpy(), pos=3010)
+                status = 0
+            except bb.BebelmError as e:
+                status = e.code
+        sh.close()
+        q.put((rank, np.stack(outs), status))
+        torch.distributed.destroy_process_group()
+    except Exception as e:  # surface the failure to the parent
+        import traceback
+        q.put((rank, traceback.format_exc(), None))
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_world2_fused_gather_matches_oracle_and_times_out_cleanly():
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = {}
+    for _ in range(world):
+        r, outs, status = q.get(timeout=600)
+        res[r] = (outs, status)
+    for p in procs:
+        p.join(timeout=120)
+    for r in range(world):
+        assert not isinstance(res[r][0], str), res[r][0]
+
+    qq, kk, vv, qg, kg = [x.numpy() for x in _inputs(7, 3010)]
+    ref = oracle.Cache(2, KVH * D)
+    _, ref.k[1], ref.v[1], _, _ = oracle.attn_batch(qq[:3000], kk[:3000], vv[:3000], 0, qg, kg, THETA, EPS, H, KVH, D,
+                                                    None, None, n_threads=oracle.max_threads())
+    for i in range(10):
+        p = 3000 + i
+        want = ref.attn_step(1, qq[p], kk[p], vv[p], qg, kg, THETA, EPS, H, KVH, D, pos=p)
+        np.testing.assert_allclose(res[0][0][i], want, atol=1e-3, rtol=0)
+    np.testing.assert_array_equal(res[0][0], res[1][0])
+    assert res[0][1] == bb.ERR_TIMEOUT, res[0][1]
