@@ -6,24 +6,26 @@
 // is appended), out[i, h] = Σ_{j <= len_before+i} softmax_j(q_i·k_j * scale) v_j
 // with bf16 operands and fp32 accumulation, as a flash-attention loop.
 //
-// One CTA per (128-query tile, query head); 128 threads = 4 warps, warp w owns
-// TMEM lanes / query rows 32w..32w+31.
-//   * TMA (cp.async.bulk.tensor, 128-byte swizzle) brings the Q tile once and
-//     K/V tiles of 128 keys into a 2-deep ring.
-//   * Thread 0 issues S = Q Kᵀ as 4 tcgen05.mma (M=128, N=128, K=16) into
-//     TMEM columns [0,128) and commits to an mbarrier.
-//   * Every thread loads its S row from TMEM (tcgen05.ld 32x32b), applies the
-//     causal mask and the online softmax in fp32 (exp2 with log2e folded into
-//     the scale), and writes P in bf16 back into TMEM over its S columns
-//     (tcgen05.st), where the next MMA reads it as the A operand.
-//   * Thread 0 issues O_tile = P V as 8 tcgen05.mma (A = P from TMEM, N=64,
-//     K=16, V read MN-major from shared memory) into TMEM columns [128,192);
-//     80 KB of shared memory and 256 TMEM columns let 2 CTAs share an SM, so
-//     one CTA's softmax overlaps the other's MMAs. Each thread folds its row into the
-//     fp32 output held in registers with the running rescale.
-// Tiles entirely above the diagonal are never visited. Every mbarrier wait is
-// bounded: on timeout the CTA records kErrWaitTimeout, waits (bounded) for its
-// own copies and MMAs, frees its TMEM and returns.
+// One CTA per (query head, pair of 128-query tiles), one CTA per SM (512 TMEM columns),
+// 10 warps in fixed roles:
+//   * warp 1 (TMA): the two Q tiles once, then K/V tiles of 128 keys into a 3-stage ring
+//     (cp.async.bulk.tensor, 128-byte swizzle, mbarrier complete_tx).
+//   * warp 0 (MMA, one elected lane): S_X = Q_X K^T (4 x tcgen05.mma M=128 N=128 K=16, both
+//     operands from shared memory) into TMEM and O_X += P_X V (8 x tcgen05.mma N=64, P read
+//     from TMEM, V MN-major from shared memory), for both tiles X, by a polling scheduler
+//     that issues whichever is ready. It is the CTA's oldest warp, so the warp scheduler it
+//     shares with two softmax warps serves it first.
+//   * warps 2-5 / 6-9 (softmax, one TMEM lane = one query row per thread): read S once in
+//     64-column chunks, causal mask on the diagonal tile only, online softmax in the exp2
+//     domain with a lazy reference max (O and the running sum are rescaled only when a
+//     chunk's max exceeds it by 2^8), P to TMEM as bf16, O rescaled in TMEM when needed.
+//     Exponentials: the MUFU ex2 for 7 of every 8 pairs of scores, a degree-3 polynomial on
+//     the FMA pipe for the 8th, since the MUFU (16 per clock per SM) is the unit that bounds
+//     a head_dim-64 tile; packed f32x2 FMAs/adds and a three-input max keep the other
+//     instructions from crowding its issue slots.
+// Tiles entirely above the diagonal are never visited; the longest tile pairs are scheduled
+// first. Every mbarrier wait is bounded: on timeout the CTA records kErrWaitTimeout, waits
+// (bounded) for its own copies and MMAs, frees its TMEM and returns.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -193,24 +195,39 @@ __device__ __forceinline__ float ex2(float x) {  // 2^x on the MUFU unit; -inf g
 }
 
 #ifndef BEBELM_PF_POLY
-#define BEBELM_PF_POLY 0  // of every 8 key pairs, how many take 2^x on the FMA pipe
+#define BEBELM_PF_POLY 2  // of every 16 key pairs, how many take 2^x on the FMA pipe
 #endif
 
-// 2^x on the FMA pipe instead of the MUFU unit, so the two units can share the softmax's
-// exponentials. x is clamped to >= -125 (2^-125 is zero for every later use) and split as
-// x = j + f, with j = round(x) from the 1.5*2^23 rounding constant and f in [-1/2, 1/2].
-// 2^f is a degree-3 polynomial, fitted here by least squares to minimise the relative
-// error on that interval: max 7.5e-5, far below the bf16 rounding of P. Then 2^j is added
-// to the exponent field.
-__device__ __forceinline__ float exp2_poly(float x) {
-    x = fmaxf(x, -125.0f);
-    const float t = x + 12582912.0f;
-    const float jf = t - 12582912.0f;
-    const float f = x - jf;
-    float p = fmaf(0.05517161265f, f, 0.24261112511f);
-    p = fmaf(p, f, 0.69326096773f);
-    p = fmaf(p, f, 0.99992805719f);
-    return __uint_as_float(__float_as_uint(p) + (__float_as_uint(t) << 23));
+// 2^x for two values on the FMA pipe instead of the MUFU unit, so the two units share the
+// softmax's exponentials. x is clamped to >= -125 (2^-125 is zero for every later use) and
+// split as x = j + f, with j = round(x) from the 1.5*2^23 rounding constant and f in
+// [-1/2, 1/2]. 2^f is a degree-3 polynomial, fitted here by least squares to minimise the
+// relative error on that interval: max 7.5e-5, far below the bf16 rounding of P. 2^j enters
+// the exponent field through one integer multiply-add. Arithmetic is packed f32x2.
+__device__ __forceinline__ void exp2_poly2(float& y0, float& y1, float x0, float x1) {
+    x0 = fmaxf(x0, -125.0f);
+    x1 = fmaxf(x1, -125.0f);
+    uint32_t t0, t1, p0, p1;
+    asm("{\n\t.reg .b64 x, t, j, f, p, m, c;\n\t"
+        "mov.b64 x, {%4, %5};\n\t"
+        "mov.b64 m, {%6, %6};\n\t"
+        "add.rn.f32x2 t, x, m;\n\t"
+        "sub.rn.f32x2 j, t, m;\n\t"
+        "sub.rn.f32x2 f, x, j;\n\t"
+        "mov.b64 p, {%7, %7};\n\t"
+        "mov.b64 c, {%8, %8};\n\t"
+        "fma.rn.f32x2 p, p, f, c;\n\t"
+        "mov.b64 c, {%9, %9};\n\t"
+        "fma.rn.f32x2 p, p, f, c;\n\t"
+        "mov.b64 c, {%10, %10};\n\t"
+        "fma.rn.f32x2 p, p, f, c;\n\t"
+        "mov.b64 {%0, %1}, t;\n\t"
+        "mov.b64 {%2, %3}, p;\n\t}"
+        : "=r"(t0), "=r"(t1), "=r"(p0), "=r"(p1)
+        : "f"(x0), "f"(x1), "f"(12582912.0f), "f"(0.05517161265f), "f"(0.24261112511f), "f"(0.69326096773f),
+          "f"(0.99992805719f));
+    y0 = __uint_as_float(t0 * (1u << 23) + p0);
+    y1 = __uint_as_float(t1 * (1u << 23) + p1);
 }
 
 #ifndef BEBELM_PF_ALU_PACK
@@ -225,6 +242,34 @@ __device__ __forceinline__ uint32_t pack_bf16_alu(float a, float b) {
     return __byte_perm(ua, ub, 0x7632);
 }
 
+// max(a, b, c) in one instruction (sm_100)
+__device__ __forceinline__ float max3(float a, float b, float c) {
+    float r;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+    return r;
+}
+// (x0, x1) = (v0, v1) * s + (c, c): one packed f32x2 FMA, each lane rounded once as fmaf
+__device__ __forceinline__ void ffma2_sc(float& x0, float& x1, float v0, float v1, float s, float c) {
+    asm("{\n\t.reg .b64 a, b, c;\n\t"
+        "mov.b64 a, {%2, %3};\n\t"
+        "mov.b64 b, {%4, %4};\n\t"
+        "mov.b64 c, {%5, %5};\n\t"
+        "fma.rn.f32x2 c, a, b, c;\n\t"
+        "mov.b64 {%0, %1}, c;\n\t}"
+        : "=f"(x0), "=f"(x1)
+        : "f"(v0), "f"(v1), "f"(s), "f"(c));
+}
+// (a0, a1) += (b0, b1): one packed f32x2 add
+__device__ __forceinline__ void fadd2(float& a0, float& a1, float b0, float b1) {
+    asm("{\n\t.reg .b64 a, b;\n\t"
+        "mov.b64 a, {%0, %1};\n\t"
+        "mov.b64 b, {%2, %3};\n\t"
+        "add.rn.f32x2 a, a, b;\n\t"
+        "mov.b64 {%0, %1}, a;\n\t}"
+        : "+f"(a0), "+f"(a1)
+        : "f"(b0), "f"(b1));
+}
+
 __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
     __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
     return *reinterpret_cast<uint32_t*>(&h);
@@ -237,14 +282,38 @@ __device__ long long g_trace[16 * 2 * 64];  // [event][tile][j] = clock64, CTA (
         if (blockIdx.x == 0 && blockIdx.y == 0 && (j) < 64)                       \
             g_trace[((ev) * 2 + (X)) * 64 + (j)] = clock64();                     \
     } while (0)
+// first time / last of several threads, for events more than one site or warp records
+#define TRACE_FIRST(ev, j, X)                                                         \
+    do {                                                                              \
+        if (blockIdx.x == 0 && blockIdx.y == 0 && (j) < 64 && !g_trace[((ev) * 2 + (X)) * 64 + (j)]) \
+            g_trace[((ev) * 2 + (X)) * 64 + (j)] = clock64();                         \
+    } while (0)
+#define TRACE_MAX(ev, j, X)                                                           \
+    do {                                                                              \
+        if (blockIdx.x == 0 && blockIdx.y == 0 && (j) < 64)                           \
+            atomicMax(&g_trace[((ev) * 2 + (X)) * 64 + (j)], (long long)clock64());   \
+    } while (0)
 #else
+#define TRACE_FIRST(ev, j, X) \
+    do {                      \
+    } while (0)
+#define TRACE_MAX(ev, j, X) \
+    do {                    \
+    } while (0)
 #define TRACE(ev, j, X) \
     do {                \
     } while (0)
 #endif
 
-// ---- roles: warps 0-3 softmax for tile A, 4-7 softmax for tile B, 8 TMA, 9 MMA ----
+// ---- roles: warp 0 MMA, 1 TMA, 2-5 softmax for tile A, 6-9 softmax for tile B ----
+// The MMA issuer is the CTA's oldest warp: a warp scheduler favours older warps, so the
+// issuer (which shares its scheduler with two exponential-bound softmax warps) gets its
+// slots as soon as it is ready instead of waiting for both softmax warps to stall.
+#ifdef BEBELM_PREFILL_TRACE
+constexpr int kWarps = 11;  // + a watcher warp that records when each K/V tile lands
+#else
 constexpr int kWarps = 10;
+#endif
 constexpr int kCtaThreads = kWarps * 32;
 #ifndef BEBELM_PF_STAGES
 #define BEBELM_PF_STAGES 3
@@ -307,7 +376,7 @@ __global__ void __launch_bounds__(kCtaThreads, 1)
     tc_fence_after();
     const uint32_t tmem = s_tmem;
 
-    if (warp == 8) {
+    if (warp == 1) {
         // ---------------- TMA producer ----------------
         if (lane == 0) {
             mbar_expect_tx(bar(kBarQ), 2 * kTileBytes);
@@ -326,7 +395,7 @@ __global__ void __launch_bounds__(kCtaThreads, 1)
                 tma_load_3d(sbase + kOff2V + st * kTileBytes, &tm_v, 0, kvh, j * kTileK, bar(kBarV + st));
             }
         }
-    } else if (warp == 9) {
+    } else if (warp == 0) {
         // ---------------- MMA issuer ----------------
         // A polling scheduler over both query tiles: S_X(j) = Q_X K(j)^T as soon as K(j) is
         // in and softmax has read S_X(j-1); O_X += P_X(j) V(j) as soon as V(j) and P_X(j) are
@@ -344,7 +413,7 @@ __global__ void __launch_bounds__(kCtaThreads, 1)
 #pragma unroll
                 for (int X = 0; X < 2; ++X) {
                     const int js = nS[X];
-                    if (js < nkt[X] && mbar_test(bar(kBarK + js % kStages), (js / kStages) & 1)) TRACE(12, js, X);
+                    if (js < nkt[X] && mbar_test(bar(kBarK + js % kStages), (js / kStages) & 1)) TRACE_FIRST(12, js, X);
                     if (js < nkt[X] && mbar_test(bar(kBarK + js % kStages), (js / kStages) & 1) &&
                         (js == 0 || mbar_test(bar(kBarC + X), (js - 1) & 1))) {
                         tc_fence_after();
@@ -386,15 +455,27 @@ __global__ void __launch_bounds__(kCtaThreads, 1)
                     idle = 0;
                 } else if (++idle > kWaitLimit) {
                     ok = false;
-                } else {
+                } else if (BEBELM_PF_SLEEP_NS > 0) {
                     __nanosleep(BEBELM_PF_SLEEP_NS);  // leave the issue slots to the softmax warps
                 }
             }
             if (!ok) s_fail = 1;
         }
-    } else if (warp < 8) {
+#ifdef BEBELM_PREFILL_TRACE
+    } else if (warp == 10) {
+        if (lane == 0)
+            for (int j = 0; j < nkt_max && j < 64; ++j) {
+                mbar_wait_bounded(bar(kBarK + j % kStages), (j / kStages) & 1);
+                TRACE(15, j, 0);
+                mbar_wait_bounded(bar(kBarV + j % kStages), (j / kStages) & 1);
+                TRACE(15, j, 1);
+            }
+#endif
+    } else if (warp >= 2 && warp < 10) {
         // ---------------- softmax warpgroups ----------------
-        const int X = warp >> 2;               // tile
+        // warp w may reach TMEM lanes 32*(w%4) .. +31 only, so each group of four
+        // consecutive warps covers the 128 lanes of its tile
+        const int X = (warp - 2) >> 2;         // tile
         const int row = 32 * (warp & 3) + lane;  // TMEM lane
         const int qi = (2 * pair + X) * kTileQ + row;
         const long long key_lim = (long long)a.len_before + qi;
@@ -422,15 +503,16 @@ __global__ void __launch_bounds__(kCtaThreads, 1)
             float ps[8];
 #pragma unroll
             for (int e = 0; e < 8; ++e) ps[e] = 0.f;
-            uint32_t w[64];
+            uint32_t w[64];  // P of the tile, bf16 pairs
 #pragma unroll
             for (int c = 0; c < kTileK; c += 64) {
+                const int wo = c / 2;
                 float v[64];
                 tmem_ld64(t_s + c, v);
                 if (c + 64 == kTileK) {  // S_X(j) fully read: the next S may overwrite it
                     tc_fence_before();
                     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar(kBarC + X)) : "memory");
-                    if ((warp & 3) == 0 && lane == 0) TRACE(11, j, X);
+                    if (lane == 0) TRACE_MAX(11, j, X);
                 }
                 float mxv[8];
 #pragma unroll
@@ -439,9 +521,9 @@ __global__ void __launch_bounds__(kCtaThreads, 1)
 #pragma unroll
                     for (int e = 0; e < 64; ++e)
                         if (c + e <= lim) mxv[e & 7] = fmaxf(mxv[e & 7], v[e]);
-                } else {
+                } else {  // three-input max: half an instruction per score
 #pragma unroll
-                    for (int e = 0; e < 64; ++e) mxv[e & 7] = fmaxf(mxv[e & 7], v[e]);
+                    for (int e = 0; e < 64; e += 2) mxv[(e >> 1) & 7] = max3(mxv[(e >> 1) & 7], v[e], v[e + 1]);
                 }
                 const float mc = fmaxf(fmaxf(fmaxf(mxv[0], mxv[1]), fmaxf(mxv[2], mxv[3])),
                                        fmaxf(fmaxf(mxv[4], mxv[5]), fmaxf(mxv[6], mxv[7]))) * a.scale_log2;
@@ -468,17 +550,22 @@ __global__ void __launch_bounds__(kCtaThreads, 1)
                         const float p0 = c + 2 * e <= lim ? ex2(fmaf(v[2 * e], a.scale_log2, neg_m)) : 0.f;
                         const float p1 = c + 2 * e + 1 <= lim ? ex2(fmaf(v[2 * e + 1], a.scale_log2, neg_m)) : 0.f;
                         ps[e & 7] += p0 + p1;
-                        w[c / 2 + e] = pack_bf16(p0, p1);
+                        w[wo + e] = pack_bf16(p0, p1);
                     }
                 } else {
 #pragma unroll
-                    for (int e = 0; e < 32; ++e) {
-                        const float x0 = fmaf(v[2 * e], a.scale_log2, neg_m), x1 = fmaf(v[2 * e + 1], a.scale_log2, neg_m);
-                        const bool poly = (e & 7) < BEBELM_PF_POLY;
-                        const float p0 = poly ? exp2_poly(x0) : ex2(x0);
-                        const float p1 = poly ? exp2_poly(x1) : ex2(x1);
-                        ps[e & 7] += p0 + p1;
-                        w[c / 2 + e] = BEBELM_PF_ALU_PACK ? pack_bf16_alu(p0, p1) : pack_bf16(p0, p1);
+                    for (int e = 0; e < 32; ++e) {  // packed f32x2 FMA and add: the MUFU gets more of the issue slots
+                        float x0, x1;
+                        ffma2_sc(x0, x1, v[2 * e], v[2 * e + 1], a.scale_log2, neg_m);
+                        float p0, p1;
+                        if (((c / 2 + e) & 15) < BEBELM_PF_POLY) {
+                            exp2_poly2(p0, p1, x0, x1);
+                        } else {
+                            p0 = ex2(x0);
+                            p1 = ex2(x1);
+                        }
+                        fadd2(ps[2 * (e & 3)], ps[2 * (e & 3) + 1], p0, p1);
+                        w[wo + e] = BEBELM_PF_ALU_PACK ? pack_bf16_alu(p0, p1) : pack_bf16(p0, p1);
                     }
                 }
             }
