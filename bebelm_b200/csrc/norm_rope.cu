@@ -47,25 +47,6 @@ __global__ void __launch_bounds__(256) norm_rope_kernel(NormRopeArgs a) {
     const int half = hd >> 1;
     const int tok = (int)(item / nh_all);
 
-    // RoPE angles depend only on (position, pair): every head of a token shares them, so the
-    // block builds cos/sin once per token it touches (at most 32 tokens: 32 items per block),
-    // with the reference's iterative angle, theta = pos * scale^i by repeated multiplication
-    __shared__ float s_cos[32][32], s_sin[32][32];
-    const long long item0 = (long long)blockIdx.x * (blockDim.x >> 3);
-    const int tok0 = (int)(item0 / nh_all);
-    if (a.norm_q || a.norm_k) {
-        const long long item_last = min(total - 1, item0 + (blockDim.x >> 3) - 1);
-        const int ntok = (int)(item_last / nh_all) - tok0 + 1;
-        for (int idx = threadIdx.x; idx < ntok * half; idx += blockDim.x) {
-            const int t = idx / half, i = idx % half;
-            const long long pos = a.targets ? a.targets[tok0 + t].pos : a.pos0 + tok0 + t;
-            float theta = __ll2float_rn(pos);
-            for (int r = 0; r < i; ++r) theta = __fmul_rn(theta, a.theta_scale);
-            s_cos[t][i] = cosf(theta);
-            s_sin[t][i] = sinf(theta);
-        }
-        __syncthreads();
-    }
     const int hh = (int)(item % nh_all);
     const bool is_q = hh < a.n_heads;
     const int head = is_q ? hh : hh - a.n_heads;
@@ -95,6 +76,43 @@ __global__ void __launch_bounds__(256) norm_rope_kernel(NormRopeArgs a) {
         }
     }
 
+    // V row of the same kv head passes through unchanged (loaded now, stored at the end)
+    const size_t v_elem = ((size_t)tok * a.n_kv + head) * 64;
+    const float* vsrc = !HD64 || is_q || !a.v ? nullptr
+                        : a.in_bf16 ? reinterpret_cast<const float*>(reinterpret_cast<const __nv_bfloat16*>(a.v) + v_elem)
+                                    : a.v + v_elem;
+    float4 v0 = make_float4(0.f, 0.f, 0.f, 0.f), v1 = v0;
+    if (vsrc && a.in_bf16) {
+        const __nv_bfloat16* bv = reinterpret_cast<const __nv_bfloat16*>(vsrc);
+        float t0[4], t1[4];
+        load_bf16x4(bv + 4 * sub, t0);
+        load_bf16x4(bv + 32 + 4 * sub, t1);
+        v0 = make_float4(t0[0], t0[1], t0[2], t0[3]);
+        v1 = make_float4(t1[0], t1[1], t1[2], t1[3]);
+    } else if (vsrc) {
+        v0 = *reinterpret_cast<const float4*>(vsrc + 4 * sub);
+        v1 = *reinterpret_cast<const float4*>(vsrc + 32 + 4 * sub);
+    }
+    // RoPE angles depend only on (position, pair): every head of a token shares them, so the
+    // block builds cos/sin once per token it touches (at most 32 tokens: 32 items per block),
+    // with the reference's iterative angle, theta = pos * scale^i by repeated multiplication.
+    // It does so after issuing its loads, so their latency overlaps the table.
+    __shared__ float s_cos[32][32], s_sin[32][32];
+    const long long item0 = (long long)blockIdx.x * (blockDim.x >> 3);
+    const int tok0 = (int)(item0 / nh_all);
+    if (a.norm_q || a.norm_k) {
+        const long long item_last = min(total - 1, item0 + (blockDim.x >> 3) - 1);
+        const int ntok = (int)(item_last / nh_all) - tok0 + 1;
+        for (int idx = threadIdx.x; idx < ntok * half; idx += blockDim.x) {
+            const int t = idx / half, i = idx % half;
+            const long long pos = a.targets ? a.targets[tok0 + t].pos : a.pos0 + tok0 + t;
+            float theta = __ll2float_rn(pos);
+            for (int r = 0; r < i; ++r) theta = __fmul_rn(theta, a.theta_scale);
+            s_cos[t][i] = cosf(theta);
+            s_sin[t][i] = sinf(theta);
+        }
+        __syncthreads();
+    }
     if (do_norm) {
         double ss = 0.0;
 #pragma unroll
@@ -165,23 +183,6 @@ __global__ void __launch_bounds__(256) norm_rope_kernel(NormRopeArgs a) {
     }
     if (is_q) return;
 
-    // V row of the same kv head passes through unchanged
-    const size_t v_elem = ((size_t)tok * a.n_kv + head) * 64;
-    const float* vsrc = !a.v ? nullptr
-                        : a.in_bf16 ? reinterpret_cast<const float*>(reinterpret_cast<const __nv_bfloat16*>(a.v) + v_elem)
-                                    : a.v + v_elem;
-    float4 v0 = make_float4(0.f, 0.f, 0.f, 0.f), v1 = v0;
-    if (vsrc && a.in_bf16) {
-        const __nv_bfloat16* bv = reinterpret_cast<const __nv_bfloat16*>(vsrc);
-        float t0[4], t1[4];
-        load_bf16x4(bv + 4 * sub, t0);
-        load_bf16x4(bv + 32 + 4 * sub, t1);
-        v0 = make_float4(t0[0], t0[1], t0[2], t0[3]);
-        v1 = make_float4(t1[0], t1[1], t1[2], t1[3]);
-    } else if (vsrc) {
-        v0 = *reinterpret_cast<const float4*>(vsrc + 4 * sub);
-        v1 = *reinterpret_cast<const float4*>(vsrc + 32 + 4 * sub);
-    }
     if (a.v_bf16 && vsrc) {
         __nv_bfloat16* vb = a.v_bf16 + ((size_t)tok * a.n_kv + head) * 64;
         __nv_bfloat162 b0 = __floats2bfloat162_rn(v0.x, v0.y), b1 = __floats2bfloat162_rn(v0.z, v0.w);
