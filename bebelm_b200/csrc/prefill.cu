@@ -7,14 +7,14 @@
 // with bf16 operands and fp32 accumulation, as a flash-attention loop.
 //
 // One CTA per (query head, pair of 128-query tiles), one CTA per SM (512 TMEM columns),
-// 10 warps in fixed roles:
+// 11 warps in fixed roles:
 //   * warp 1 (TMA): the two Q tiles once, then K/V tiles of 128 keys into a 3-stage ring
 //     (cp.async.bulk.tensor, 128-byte swizzle, mbarrier complete_tx).
-//   * warp 0 (MMA, one elected lane): S_X = Q_X K^T (4 x tcgen05.mma M=128 N=128 K=16, both
-//     operands from shared memory) into TMEM and O_X += P_X V (8 x tcgen05.mma N=64, P read
-//     from TMEM, V MN-major from shared memory), for both tiles X, by a polling scheduler
-//     that issues whichever is ready. It is the CTA's oldest warp, so the warp scheduler it
-//     shares with two softmax warps serves it first.
+//   * warps 0 and 10 (MMA, one lane each, one per query tile X): S_X = Q_X K^T (4 x
+//     tcgen05.mma M=128 N=128 K=16, both operands from shared memory) into TMEM and
+//     O_X += P_X V (8 x tcgen05.mma N=64, P read from TMEM, V MN-major from shared memory).
+//     MMA issue blocks while the tensor pipe's short queue is full, so each tile has its own
+//     issuer and neither waits behind the other's issue.
 //   * warps 2-5 / 6-9 (softmax, one TMEM lane = one query row per thread): read S once in
 //     64-column chunks, causal mask on the diagonal tile only, online softmax in the exp2
 //     domain with a lazy reference max (O and the running sum are rescaled only when a
@@ -309,10 +309,15 @@ __device__ long long g_trace[16 * 2 * 64];  // [event][tile][j] = clock64, CTA (
 // The MMA issuer is the CTA's oldest warp: a warp scheduler favours older warps, so the
 // issuer (which shares its scheduler with two exponential-bound softmax warps) gets its
 // slots as soon as it is ready instead of waiting for both softmax warps to stall.
+#ifndef BEBELM_PF_MMA2
+#define BEBELM_PF_MMA2 1  // one MMA issuer warp per query tile (warps 0 and 10) instead of one for both
+#endif
+constexpr int kWarpMmaB = 10;  // the second issuer when BEBELM_PF_MMA2
 #ifdef BEBELM_PREFILL_TRACE
-constexpr int kWarps = 11;  // + a watcher warp that records when each K/V tile lands
+constexpr int kWarpWatch = 10 + BEBELM_PF_MMA2;
+constexpr int kWarps = 11 + BEBELM_PF_MMA2;  // + a watcher warp that records when each K/V tile lands
 #else
-constexpr int kWarps = 10;
+constexpr int kWarps = 10 + BEBELM_PF_MMA2;
 #endif
 constexpr int kCtaThreads = kWarps * 32;
 #ifndef BEBELM_PF_STAGES
@@ -368,7 +373,10 @@ __global__ void __launch_bounds__(kCtaThreads, 1)
     }
     if (tid == 0) {
         s_fail = 0;
-        for (int i = 0; i < kNumBars; ++i) mbar_init(bar(i), (i >= kBarP && i < kBarP + 2) || (i >= kBarC && i < kBarC + 2) ? 128 : 1);
+        for (int i = 0; i < kNumBars; ++i)
+            mbar_init(bar(i), (i >= kBarP && i < kBarP + 2) || (i >= kBarC && i < kBarC + 2) ? 128
+                              : (BEBELM_PF_MMA2 && i >= kBarEmpty && i < kBarEmpty + kStages) ? 2
+                                                                                             : 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     tc_fence_before();
@@ -395,7 +403,59 @@ __global__ void __launch_bounds__(kCtaThreads, 1)
                 tma_load_3d(sbase + kOff2V + st * kTileBytes, &tm_v, 0, kvh, j * kTileK, bar(kBarV + st));
             }
         }
-    } else if (warp == 0) {
+    } else if (BEBELM_PF_MMA2 && (warp == 0 || warp == kWarpMmaB)) {
+        // ---------------- MMA issuers, one per query tile ----------------
+        // tcgen05.mma issue blocks while the tensor pipe's short queue is full, so one thread
+        // serving both tiles spends its time inside issue and reaches the other tile's ready
+        // work late. Here each tile has its own issuer, in the tile's natural order with
+        // blocking waits: S(j+1) once K(j+1) is in and softmax has read S(j), then O += P(j) V(j)
+        // once P(j) is written. Each issuer commits once per K/V stage to the stage's
+        // "empty" barrier (count 2), also for stages past its own last tile.
+        if (lane == 0) {
+            const int X = warp == 0 ? 0 : 1;
+            constexpr uint32_t kIdescS = instr_desc(kTileK, false), kIdescO = instr_desc(kHeadDim, true);
+            const uint64_t dq = smem_desc(sbase + kOff2Q + X * kTileBytes, 16, 1024);
+            bool ok = mbar_wait_bounded(bar(kBarQ), 0);
+            auto issue_s = [&](int j) -> bool {
+                if (!mbar_wait_bounded(bar(kBarK + j % kStages), (j / kStages) & 1)) return false;
+                if (j > 0 && !mbar_wait_bounded(bar(kBarC + X), (j - 1) & 1)) return false;
+                tc_fence_after();
+                TRACE(14, j, X);
+                const uint64_t dk = smem_desc(sbase + kOff2K + (j % kStages) * kTileBytes, 16, 1024);
+#pragma unroll
+                for (int k = 0; k < kHeadDim / 16; ++k)  // 16 dims: +32 B in both operands
+                    mma_bf16(tmem + 128 * X, dq + (uint64_t)(2 * k), dk + (uint64_t)(2 * k), kIdescS, k > 0);
+                mma_commit(bar(kBarS + X));
+                TRACE(2, j, X);
+                return true;
+            };
+            auto issue_pv = [&](int j) -> bool {
+                if (!mbar_wait_bounded(bar(kBarV + j % kStages), (j / kStages) & 1)) return false;
+                if (!mbar_wait_bounded(bar(kBarP + X), j & 1)) return false;
+                tc_fence_after();
+                TRACE(13, j, X);
+                const uint64_t dv = smem_desc(sbase + kOff2V + (j % kStages) * kTileBytes, kTileBytes, 1024);
+#pragma unroll
+                for (int k = 0; k < kTileK / 16; ++k)  // 16 keys: +8 TMEM columns of P, +2048 B of V
+                    mma_bf16_ts(tmem + kColO + 64 * X, tmem + kColP + 64 * X + 8 * k, dv + (uint64_t)(128 * k),
+                                kIdescO, (j > 0 || k > 0));
+                mma_commit(bar(kBarO + X));
+                TRACE(1, j, X);
+                return true;
+            };
+            if (ok && nkt[X] > 0) ok = issue_s(0);
+            for (int j = 0; ok && j < nkt_max; ++j) {
+                if (j + 1 < nkt[X]) ok = issue_s(j + 1);
+                if (ok && j < nkt[X]) ok = issue_pv(j);
+                // Past its own last tile, an issuer first waits for use j of the stage to be
+                // loaded: the load follows the completion of use j - kStages, so this issuer's
+                // arrival cannot count towards an earlier use the other issuer still reads.
+                if (ok && j >= nkt[X]) ok = mbar_wait_bounded(bar(kBarK + j % kStages), (j / kStages) & 1);
+                if (ok) mma_commit(bar(kBarEmpty + j % kStages));  // fires once this issuer's MMAs so far complete
+            }
+            if (!ok) s_fail = 1;
+        }
+    } else if (!BEBELM_PF_MMA2 && warp == 0) {
         // ---------------- MMA issuer ----------------
         // A polling scheduler over both query tiles: S_X(j) = Q_X K(j)^T as soon as K(j) is
         // in and softmax has read S_X(j-1); O_X += P_X(j) V(j) as soon as V(j) and P_X(j) are
@@ -413,7 +473,6 @@ __global__ void __launch_bounds__(kCtaThreads, 1)
 #pragma unroll
                 for (int X = 0; X < 2; ++X) {
                     const int js = nS[X];
-                    if (js < nkt[X] && mbar_test(bar(kBarK + js % kStages), (js / kStages) & 1)) TRACE_FIRST(12, js, X);
                     if (js < nkt[X] && mbar_test(bar(kBarK + js % kStages), (js / kStages) & 1) &&
                         (js == 0 || mbar_test(bar(kBarC + X), (js - 1) & 1))) {
                         tc_fence_after();
@@ -462,7 +521,7 @@ __global__ void __launch_bounds__(kCtaThreads, 1)
             if (!ok) s_fail = 1;
         }
 #ifdef BEBELM_PREFILL_TRACE
-    } else if (warp == 10) {
+    } else if (warp == kWarpWatch) {
         if (lane == 0)
             for (int j = 0; j < nkt_max && j < 64; ++j) {
                 mbar_wait_bounded(bar(kBarK + j % kStages), (j / kStages) & 1);
