@@ -61,33 +61,6 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, unsigned parity)
     }
     return false;
 }
-// Same bound, but polling with test_wait: the issuing thread never sleeps, so it reacts to
-// a completed phase at once (one thread spins; the other 31 lanes of its warp are parked).
-__device__ __forceinline__ bool mbar_spin_bounded(uint32_t bar, unsigned parity) {
-    for (long long it = 0; it < 64 * kWaitLimit; ++it) {
-        uint32_t ok;
-        asm volatile(
-            "{\n\t.reg .pred p;\n\t"
-            "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-            "selp.u32 %0, 1, 0, p;\n\t}"
-            : "=r"(ok)
-            : "r"(bar), "r"(parity)
-            : "memory");
-        if (ok) return true;
-    }
-    return false;
-}
-__device__ __forceinline__ bool mbar_test(uint32_t bar, unsigned parity) {
-    uint32_t ok;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(ok)
-        : "r"(bar), "r"(parity)
-        : "memory");
-    return ok != 0;
-}
 __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, int c0, int c1, int c2,
                                             uint32_t bar) {
     asm volatile(
@@ -305,19 +278,13 @@ __device__ long long g_trace[16 * 2 * 64];  // [event][tile][j] = clock64, CTA (
     } while (0)
 #endif
 
-// ---- roles: warp 0 MMA, 1 TMA, 2-5 softmax for tile A, 6-9 softmax for tile B ----
-// The MMA issuer is the CTA's oldest warp: a warp scheduler favours older warps, so the
-// issuer (which shares its scheduler with two exponential-bound softmax warps) gets its
-// slots as soon as it is ready instead of waiting for both softmax warps to stall.
-#ifndef BEBELM_PF_MMA2
-#define BEBELM_PF_MMA2 1  // one MMA issuer warp per query tile (warps 0 and 10) instead of one for both
-#endif
-constexpr int kWarpMmaB = 10;  // the second issuer when BEBELM_PF_MMA2
+// ---- roles: warps 0 / 10 MMA for tile A / B, 1 TMA, 2-5 softmax for tile A, 6-9 for tile B ----
+constexpr int kWarpMmaB = 10;  // issuer of the second query tile (the first is warp 0)
 #ifdef BEBELM_PREFILL_TRACE
-constexpr int kWarpWatch = 10 + BEBELM_PF_MMA2;
-constexpr int kWarps = 11 + BEBELM_PF_MMA2;  // + a watcher warp that records when each K/V tile lands
+constexpr int kWarpWatch = 11;
+constexpr int kWarps = 12;  // + a watcher warp that records when each K/V tile lands
 #else
-constexpr int kWarps = 10 + BEBELM_PF_MMA2;
+constexpr int kWarps = 11;
 #endif
 constexpr int kCtaThreads = kWarps * 32;
 #ifndef BEBELM_PF_STAGES
@@ -325,9 +292,7 @@ constexpr int kCtaThreads = kWarps * 32;
 #endif
 constexpr int kStages = BEBELM_PF_STAGES;               // K/V ring depth
 constexpr float kRescaleSlack = 8.0f;
-#ifndef BEBELM_PF_SLEEP_NS
-#define BEBELM_PF_SLEEP_NS 64
-#endif                   // log2 headroom before O is rescaled
+                   // log2 headroom before O is rescaled
 // shared memory map v2 (offsets from a 1024-byte aligned base)
 constexpr int kOff2Q = 0;                               // Q_A, Q_B
 constexpr int kOff2K = 2 * kTileBytes;                  // kStages K tiles
@@ -375,7 +340,7 @@ __global__ void __launch_bounds__(kCtaThreads, 1)
         s_fail = 0;
         for (int i = 0; i < kNumBars; ++i)
             mbar_init(bar(i), (i >= kBarP && i < kBarP + 2) || (i >= kBarC && i < kBarC + 2) ? 128
-                              : (BEBELM_PF_MMA2 && i >= kBarEmpty && i < kBarEmpty + kStages) ? 2
+                              : (i >= kBarEmpty && i < kBarEmpty + kStages) ? 2
                                                                                              : 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -403,7 +368,7 @@ __global__ void __launch_bounds__(kCtaThreads, 1)
                 tma_load_3d(sbase + kOff2V + st * kTileBytes, &tm_v, 0, kvh, j * kTileK, bar(kBarV + st));
             }
         }
-    } else if (BEBELM_PF_MMA2 && (warp == 0 || warp == kWarpMmaB)) {
+    } else if (warp == 0 || warp == kWarpMmaB) {
         // ---------------- MMA issuers, one per query tile ----------------
         // tcgen05.mma issue blocks while the tensor pipe's short queue is full, so one thread
         // serving both tiles spends its time inside issue and reaches the other tile's ready
@@ -452,71 +417,6 @@ __global__ void __launch_bounds__(kCtaThreads, 1)
                 // arrival cannot count towards an earlier use the other issuer still reads.
                 if (ok && j >= nkt[X]) ok = mbar_wait_bounded(bar(kBarK + j % kStages), (j / kStages) & 1);
                 if (ok) mma_commit(bar(kBarEmpty + j % kStages));  // fires once this issuer's MMAs so far complete
-            }
-            if (!ok) s_fail = 1;
-        }
-    } else if (!BEBELM_PF_MMA2 && warp == 0) {
-        // ---------------- MMA issuer ----------------
-        // A polling scheduler over both query tiles: S_X(j) = Q_X K(j)^T as soon as K(j) is
-        // in and softmax has read S_X(j-1); O_X += P_X(j) V(j) as soon as V(j) and P_X(j) are
-        // in. Either kind may go first, so one tile waiting for its softmax never holds back
-        // the other tile's MMAs. No barrier can run two phases ahead of these tests: S_X(j)
-        // needs S_X(j-1) read, and softmax writes P_X(j) only after PV_X(j-1) completed.
-        if (lane == 0) {
-            constexpr uint32_t kIdescS = instr_desc(kTileK, false), kIdescO = instr_desc(kHeadDim, true);
-            const uint64_t dq0 = smem_desc(sbase + kOff2Q, 16, 1024), dq1 = smem_desc(sbase + kOff2Q + kTileBytes, 16, 1024);
-            bool ok = mbar_spin_bounded(bar(kBarQ), 0);
-            int nS[2] = {0, 0}, nPV[2] = {0, 0}, n_free = 0;
-            long long idle = 0;
-            while (ok && (nPV[0] < nkt[0] || nPV[1] < nkt[1])) {
-                bool progress = false;
-#pragma unroll
-                for (int X = 0; X < 2; ++X) {
-                    const int js = nS[X];
-                    if (js < nkt[X] && mbar_test(bar(kBarK + js % kStages), (js / kStages) & 1) &&
-                        (js == 0 || mbar_test(bar(kBarC + X), (js - 1) & 1))) {
-                        tc_fence_after();
-                        TRACE(14, js, X);
-                        const uint64_t dq = X ? dq1 : dq0;
-                        const uint64_t dk = smem_desc(sbase + kOff2K + (js % kStages) * kTileBytes, 16, 1024);
-#pragma unroll
-                        for (int k = 0; k < kHeadDim / 16; ++k)  // 16 dims: +32 B in both operands
-                            mma_bf16(tmem + 128 * X, dq + (uint64_t)(2 * k), dk + (uint64_t)(2 * k), kIdescS, k > 0);
-                        mma_commit(bar(kBarS + X));
-                        TRACE(2, js, X);
-                        ++nS[X];
-                        progress = true;
-                    }
-                    const int jp = nPV[X];
-                    if (jp < nS[X] && mbar_test(bar(kBarV + jp % kStages), (jp / kStages) & 1) &&
-                        mbar_test(bar(kBarP + X), jp & 1)) {
-                        tc_fence_after();
-                        TRACE(13, jp, X);
-                        const uint64_t dv = smem_desc(sbase + kOff2V + (jp % kStages) * kTileBytes, kTileBytes, 1024);
-#pragma unroll
-                        for (int k = 0; k < kTileK / 16; ++k)  // 16 keys: +8 TMEM columns of P, +2048 B of V
-                            mma_bf16_ts(tmem + kColO + 64 * X, tmem + kColP + 64 * X + 8 * k, dv + (uint64_t)(128 * k),
-                                        kIdescO, (jp > 0 || k > 0));
-                        mma_commit(bar(kBarO + X));
-                        TRACE(1, jp, X);
-                        ++nPV[X];
-                        progress = true;
-                    }
-                }
-                // a K/V stage is free once every PV that reads it has been issued (the commit
-                // fires when they complete)
-                while (n_free < nkt_max && (nPV[0] > n_free || nkt[0] <= n_free) &&
-                       (nPV[1] > n_free || nkt[1] <= n_free)) {
-                    mma_commit(bar(kBarEmpty + n_free % kStages));
-                    ++n_free;
-                }
-                if (progress) {
-                    idle = 0;
-                } else if (++idle > kWaitLimit) {
-                    ok = false;
-                } else if (BEBELM_PF_SLEEP_NS > 0) {
-                    __nanosleep(BEBELM_PF_SLEEP_NS);  // leave the issue slots to the softmax warps
-                }
             }
             if (!ok) s_fail = 1;
         }
