@@ -134,9 +134,9 @@ def _buf(x, dtype=np.float32):
         else:
             if not x.is_contiguous():
                 raise ValueError("device tensors must be contiguous")
-            return C.c_void_p(x.data_ptr()), MEM_DEVICE, x
+            return x.data_ptr(), MEM_DEVICE, x
     a = np.ascontiguousarray(x, dtype=dtype)
-    return C.c_void_p(a.ctypes.data), MEM_HOST, a
+    return a.ctypes.data, MEM_HOST, a
 
 
 def _bufs(*xs, dtype=np.float32):
@@ -147,15 +147,24 @@ def _bufs(*xs, dtype=np.float32):
     return out, kinds.pop()
 
 
-def _stream_ptr(stream):
+_torch = None
+
+
+def _stream_ptr(stream, mem=MEM_DEVICE):
+    """The cudaStream_t for a call. Host-memory calls synchronise before returning, so they
+    run on the legacy default stream (NULL) unless one is given; device-memory calls default
+    to torch's current stream."""
+    global _torch
     if stream is None:
-        try:
-            import torch
-            if torch.cuda.is_available():
-                return C.c_void_p(torch.cuda.current_stream().cuda_stream)
-        except Exception:
-            pass
-        return C.c_void_p(0)
+        if mem == MEM_HOST:
+            return None
+        if _torch is None:
+            try:
+                import torch
+                _torch = torch if torch.cuda.is_available() else False
+            except Exception:
+                _torch = False
+        return C.c_void_p(_torch.cuda.current_stream().cuda_stream) if _torch else None
     if hasattr(stream, "cuda_stream"):
         return C.c_void_p(stream.cuda_stream)
     return C.c_void_p(int(stream))
@@ -185,7 +194,7 @@ def norm_rope_heads(buf, n_heads: int, head_dim: int, gain, pos: int, theta: flo
     if _is_torch(buf) and buf.is_cuda:
         (b, g), mem = _bufs(buf, gain)
         _check(load_library().bebelm_norm_rope_heads(b[0], n_tokens, n_heads, head_dim, g[0], pos, theta, eps, mem,
-                                                      _stream_ptr(stream)))
+                                                      _stream_ptr(stream, mem)))
         return buf
     out = np.array(buf, np.float32, copy=True).reshape(-1)
     g = np.ascontiguousarray(gain, np.float32)
@@ -288,7 +297,7 @@ class Cache:
         """``cache.k[layer].extend_from_slice(k)`` and the same for v."""
         (kb, vb), mem = _bufs(k, v)
         t = (kb[2].size if mem == MEM_HOST else kb[2].numel()) // (self.n_kv_heads * self.head_dim)
-        _check(load_library().bebelm_kv_append(self._h, layer, kb[0], vb[0], t, mem, _stream_ptr(stream)))
+        _check(load_library().bebelm_kv_append(self._h, layer, kb[0], vb[0], t, mem, _stream_ptr(stream, mem)))
 
     def read(self, layer: int):
         """The window of one layer as host arrays (k, v), each [len, n_kv*64] — what
@@ -311,7 +320,7 @@ class Cache:
                 n_heads * self.head_dim, dtype=qb[2].dtype)
         ob, _, _ = _buf(out)
         _check(load_library().bebelm_attn_step(self._h, layer, n_heads, qb[0], kb[0], vb[0], qg[0], kg[0], theta, eps,
-                                               pos, ob, mem, _stream_ptr(stream)))
+                                               pos, ob, mem, _stream_ptr(stream, mem)))
         return out
 
     def attn_step_allgather(self, group: "PeerGroup", layer: int, q, k, v, q_gain, k_gain, pos: int,
@@ -326,7 +335,7 @@ class Cache:
             out = np.zeros(n_out, np.float32) if mem == MEM_HOST else qb[2].new_empty(n_out, dtype=qb[2].dtype)
         ob, _, _ = _buf(out)
         _check(load_library().bebelm_attn_step_allgather(self._h, group._h, layer, n_heads, qb[0], kb[0], vb[0], qg[0],
-                                                         kg[0], theta, eps, pos, ob, mem, _stream_ptr(stream)))
+                                                         kg[0], theta, eps, pos, ob, mem, _stream_ptr(stream, mem)))
         return out
 
     def check(self, stream=None) -> None:
@@ -341,7 +350,7 @@ class Cache:
             out = np.zeros(n_heads * self.head_dim, np.float32) if mem == MEM_HOST else qb[2].new_empty(
                 n_heads * self.head_dim)
         ob, _, _ = _buf(out)
-        _check(load_library().bebelm_attn_decode_cached(self._h, layer, n_heads, qb[0], ob, mem, _stream_ptr(stream)))
+        _check(load_library().bebelm_attn_decode_cached(self._h, layer, n_heads, qb[0], ob, mem, _stream_ptr(stream, mem)))
         return out
 
     def attn_prefill(self, layer: int, q, k, v, q_gain, k_gain, pos0: int, theta: float = ROPE_THETA,
@@ -374,7 +383,7 @@ class Cache:
             mem = MEM_HOST
         _check(load_library().bebelm_attn_prefill(self._h, layer, n_heads, ptrs[0], ptrs[1], ptrs[2], in_dtype, t,
                                                   pos0, ptrs[3], ptrs[4], theta, eps, ptrs[5], mem,
-                                                  _stream_ptr(stream)))
+                                                  _stream_ptr(stream, mem)))
         del keep
         return out
 
@@ -431,5 +440,5 @@ def attn_decode_batched(caches, layer: int, q, k, v, q_gain, k_gain, pos, theta:
     ob, _, _ = _buf(out)
     posa = (C.c_size_t * n)(*[int(p) for p in pos])
     _check(load_library().bebelm_attn_decode_batched(arr, n, layer, n_heads, qb[0], kb[0], vb[0], qg[0], kg[0], theta,
-                                                     eps, posa, ob, mem, _stream_ptr(stream)))
+                                                     eps, posa, ob, mem, _stream_ptr(stream, mem)))
     return out

@@ -102,26 +102,54 @@ struct DevBuf {
     template <class T> T* as() const { return static_cast<T*>(p); }
 };
 
-// Growable pinned host buffer.
+// Growable pinned host buffer, also mapped into the device's address space (d): a kernel
+// may store a small result straight into it instead of the host copying it back.
 struct PinBuf {
     void* p = nullptr;
+    void* d = nullptr;
     size_t bytes = 0;
     int ensure(size_t need) {
         if (need <= bytes) return 0;
         if (p) cudaFreeHost(p);
-        p = nullptr;
+        p = d = nullptr;
         bytes = 0;
         size_t n = std::max<size_t>(need, 4096);
-        CUDA_TRY(cudaHostAlloc(&p, n, cudaHostAllocDefault));
+        CUDA_TRY(cudaHostAlloc(&p, n, cudaHostAllocMapped | cudaHostAllocPortable));
         bytes = n;
+        CUDA_TRY(cudaHostGetDevicePointer(&d, p, 0));
         return 0;
     }
     void release() {
         if (p) cudaFreeHost(p);
-        p = nullptr;
+        p = d = nullptr;
         bytes = 0;
     }
     template <class T> T* as() const { return static_cast<T*>(p); }
+};
+
+// A pool's error word: pinned host memory mapped into the device. A kernel whose bounded
+// wait gives up stores its code there (a plain store); the host reads it after
+// synchronising, without a copy.
+struct ErrWord {
+    int* h = nullptr;  // host address
+    int* d = nullptr;  // device address of the same word
+    int ensure() {
+        if (h) return 0;
+        void* p = nullptr;
+        CUDA_TRY(cudaHostAlloc(&p, 64, cudaHostAllocMapped | cudaHostAllocPortable));
+        h = static_cast<int*>(p);
+        *h = 0;
+        void* dp = nullptr;
+        CUDA_TRY(cudaHostGetDevicePointer(&dp, p, 0));
+        d = static_cast<int*>(dp);
+        return 0;
+    }
+    int read() const { return *reinterpret_cast<volatile int*>(h); }
+    void clear() { *reinterpret_cast<volatile int*>(h) = 0; }
+    void release() {
+        if (h) cudaFreeHost(h);
+        h = d = nullptr;
+    }
 };
 
 }  // namespace
@@ -174,7 +202,8 @@ struct bebelm_kv_pool {
     int num_sms = 148;
     int n_seqs = 0;              // live sequences drawing from this pool
     // scratch shared by every call on this pool's sequences (stream-ordered)
-    DevBuf io, qn, part, counters, seqdesc, err, pf;
+    DevBuf io, qn, part, counters, seqdesc, pf;
+    ErrWord err;
     PinBuf pin;
     UploadRing uploads;
     std::vector<DecodeSeq> h_desc;
@@ -309,7 +338,7 @@ int pool_create(int n_layers, int n_kv_heads, int head_dim, size_t n_pages, int 
     // zero once so masked rows of a partly filled page are finite
     e = cudaMemset(P->mem, 0, bytes);
     if (e == cudaSuccess) {
-        int rc = P->err.ensure(sizeof(int), true);
+        int rc = P->err.ensure();
         if (rc) {
             cudaFree(P->mem);
             delete P;
@@ -474,7 +503,7 @@ int run_decode(bebelm_kv_pool* P, const std::vector<Window>& wins, int layer, in
     a.part_acc = P->part.as<float>();
     a.part_ml = a.part_acc + (size_t)total_splits * NY * hpc * kHeadDim;
     a.counters = P->counters.as<unsigned>();
-    a.err = P->err.as<int>();
+    a.err = P->err.d;
     a.n_heads = n_heads;
     a.n_kv = P->n_kv;
     a.group = group;
@@ -506,13 +535,18 @@ struct Stage {
     void** dev;  // receives the device address
 };
 
-thread_local size_t g_pin_out_off = 0;  // set by stage_in, read by stage_out (calls are host-synchronous)
+thread_local size_t g_pin_out_off = 0;   // set by stage_in, read by stage_out (calls are host-synchronous)
+thread_local bool g_pin_out_direct = false;  // the output was stored straight into the pinned buffer
+
+// Outputs up to this size are stored by the kernel straight into the mapped pinned buffer
+// (over the host link, as the copy back would go); larger ones are copied back once.
+constexpr size_t kDirectOutBytes = 64 * 1024;
 
 int stage_in(bebelm_kv_pool* P, Stage* st, int n, size_t out_bytes, void** d_out, cudaStream_t s) {
     size_t total = 0;
     for (int i = 0; i < n; ++i) total += (st[i].bytes + 255) & ~size_t(255);
     const size_t out_off = total;
-    total += ((out_bytes + 255) & ~size_t(255)) + 256;  // output, then the error word
+    total += ((out_bytes + 255) & ~size_t(255)) + 256;
     TRY(P->io.ensure(total, false, s));
     TRY(P->pin.ensure(total));
     size_t off = 0;
@@ -522,22 +556,22 @@ int stage_in(bebelm_kv_pool* P, Stage* st, int n, size_t out_bytes, void** d_out
         off += (st[i].bytes + 255) & ~size_t(255);
     }
     if (out_off) CUDA_TRY(cudaMemcpyAsync(P->io.p, P->pin.p, out_off, cudaMemcpyHostToDevice, s));
-    if (d_out) *d_out = P->io.as<char>() + out_off;
+    g_pin_out_direct = out_bytes <= kDirectOutBytes;
+    if (d_out) *d_out = (g_pin_out_direct ? static_cast<char*>(P->pin.d) : P->io.as<char>()) + out_off;
     g_pin_out_off = out_off;
     return 0;
 }
 
-// Device output back to the caller's host memory through the pinned buffer; also
-// surfaces a device-side timeout recorded by a kernel.
+// Waits for the call's work, surfaces a device-side timeout recorded by a kernel, and
+// delivers the output to the caller's host memory (from the pinned buffer, after copying
+// it there unless the kernel stored it there directly).
 int stage_out(bebelm_kv_pool* P, const void* d_src, void* h_dst, size_t bytes, cudaStream_t s) {
     char* pin = P->pin.as<char>() + g_pin_out_off;
-    char* perr = pin + ((bytes + 255) & ~size_t(255));
-    if (bytes) CUDA_TRY(cudaMemcpyAsync(pin, d_src, bytes, cudaMemcpyDeviceToHost, s));
-    CUDA_TRY(cudaMemcpyAsync(perr, P->err.p, sizeof(int), cudaMemcpyDeviceToHost, s));
+    if (bytes && !g_pin_out_direct) CUDA_TRY(cudaMemcpyAsync(pin, d_src, bytes, cudaMemcpyDeviceToHost, s));
     CUDA_TRY(cudaStreamSynchronize(s));
-    int derr = *reinterpret_cast<int*>(perr);
+    const int derr = P->err.read();
     if (derr) {
-        cudaMemsetAsync(P->err.p, 0, sizeof(int), s);
+        P->err.clear();
         if (P->counters.p) cudaMemsetAsync(P->counters.p, 0, P->counters.bytes, s);
         cudaStreamSynchronize(s);
         return fail(BEBELM_ERR_TIMEOUT, "a device-side wait timed out (code %d); outputs are invalid", derr);
@@ -564,7 +598,7 @@ int scratch_pool(int dev, bebelm_kv_pool** out) {
     if (!g_scratch[dev]) {
         auto* P = new bebelm_kv_pool();
         P->device = dev;
-        int rc = P->err.ensure(sizeof(int), true);
+        int rc = P->err.ensure();
         if (rc) {
             delete P;
             return rc;
@@ -1050,7 +1084,7 @@ int bebelm_attn_prefill(bebelm_kv* kv, int layer, int n_heads, const void* q, co
         pa.q = qb; pa.k = kb; pa.v = vb; pa.out = dout;
         pa.t = (int)t; pa.len_before = (int)len_before; pa.n_heads = n_heads; pa.n_kv = P->n_kv;
         pa.scale_log2 = 0.125f * 1.4426950408889634f;
-        pa.err = P->err.as<int>();
+        pa.err = P->err.d;
         PrefillMaps maps;
         if (!prefill_make_maps(pa, &maps)) return fail(BEBELM_ERR_CUDA, "building the TMA tensor maps for prefill failed");
         if (len_before > 0)
@@ -1267,11 +1301,10 @@ int bebelm_kv_check(const bebelm_kv* kv, void* stream) {
     bebelm_kv_pool* P = kv->pool;
     DeviceGuard dg(P->device);
     cudaStream_t s = as_stream(stream);
-    int derr = 0;
-    CUDA_TRY(cudaMemcpyAsync(&derr, P->err.p, sizeof(int), cudaMemcpyDeviceToHost, s));
     CUDA_TRY(cudaStreamSynchronize(s));
+    const int derr = P->err.read();
     if (derr) {
-        cudaMemsetAsync(P->err.p, 0, sizeof(int), s);
+        P->err.clear();
         if (P->counters.p) cudaMemsetAsync(P->counters.p, 0, P->counters.bytes, s);
         cudaStreamSynchronize(s);
         return fail(BEBELM_ERR_TIMEOUT, "a device-side wait timed out (code %d); outputs are invalid", derr);
@@ -1388,7 +1421,7 @@ int bebelm_attn_step_allgather(bebelm_kv* kv, bebelm_peer_group* g, int layer, i
     const unsigned long long writers = (unsigned long long)P->n_kv * n_sub;
     const float* land = reinterpret_cast<const float*>(g->zone + 256) + par_off;
     CUDA_TRY(launch_peer_wait(reinterpret_cast<const unsigned long long*>(g->zone), g->world, e * writers, land, dout,
-                              full, P->err.as<int>(), s));
+                              full, P->err.d, s));
     if (mem == BEBELM_MEM_HOST) return stage_out(P, dout, out, 4 * full, s);
     return 0;
 }

@@ -340,7 +340,7 @@ __global__ void __launch_bounds__(kThreads, 2) decode_kernel(DecodeArgs a) {
         const bool ok = __all_sync(0xffffffffu, mbar_wait_bounded(&full[st], (unsigned)((i / NST) & 1)));
         if (!ok) {
             if (lane == 0) {
-                atomicExch(a.err, kErrWaitTimeout);
+                *reinterpret_cast<volatile int*>(a.err) = kErrWaitTimeout;
                 atomicExch(&s_failed, 1);
             }
             break;
@@ -642,7 +642,7 @@ __global__ void peer_wait_kernel(const unsigned long long* flags, int world, uns
         }
         if (!ok) {
             atomicExch(&s_ok, 0);
-            atomicExch(err, kErrWaitTimeout);
+            *reinterpret_cast<volatile int*>(err) = kErrWaitTimeout;
         }
     }
     __syncthreads();

@@ -144,7 +144,7 @@ struct DecodeArgs {
     float* part_acc;        // [total_splits][n_kv*n_sub][hpc][64]
     float* part_ml;         // [total_splits][n_kv*n_sub][hpc][2]
     unsigned* counters;     // [n_seqs][n_kv*n_sub], zero between launches
-    int* err;               // device error word
+    int* err;               // error word (device-visible; a timed-out wait stores its code)
     int n_heads, n_kv, group, hpc, n_sub;
     int pages_per_split;
     int total_splits;

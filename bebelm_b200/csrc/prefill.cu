@@ -581,7 +581,7 @@ __global__ void __launch_bounds__(kCtaThreads, 1)
     tc_fence_before();
     __syncthreads();
     if (s_fail && tid == 0) {
-        atomicExch(a.err, kErrWaitTimeout);
+        *reinterpret_cast<volatile int*>(a.err) = kErrWaitTimeout;
         // let copies and MMAs this CTA started land (bounded) before its memory goes away
         for (int st = 0; st < kStages; ++st) {
             mbar_wait_bounded(bar(kBarK + st), 0);

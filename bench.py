@@ -252,7 +252,9 @@ def run_ours(args):
     isolated = bytes_per_step(CTX) / (kern_ms * 1e-3) / 1e9
     traffic = load_profile_traffic()
 
-    # -- end to end through the public API with host buffers (H2D/D2H inside each call)
+    # -- end to end through the C-ABI with host buffers: the call a Rust caller makes per step
+    #    (bebelm_attn_step with mem = HOST: inputs copied in and the output back inside the
+    #    call, which returns once the output is in the caller's memory) plus evict_front
     e2e_steps = min(args.steps, 128)
     rs = np.random.default_rng(99 + rank)
     hq = rs.standard_normal((e2e_steps, HID), dtype=np.float32)
@@ -260,16 +262,24 @@ def run_ours(args):
     hv = rs.standard_normal((e2e_steps, KVD), dtype=np.float32)
     hqg, hkg = qg.cpu().numpy(), kg.cpu().numpy()
     hout = np.zeros(HID, np.float32)
-    cache.attn_step(0, hq[0], hk[0], hv[0], hqg, hkg, pos=pos[0], theta=THETA, out=hout)
-    cache.evict_front(1)
-    pos[0] += 1
+    lib = bb.load_library()
+    qp, kp, vp, gqp, gkp, op = (x.ctypes.data for x in (hq, hk, hv, hqg, hkg, hout))
+
+    def e2e_step(i):
+        rc = lib.bebelm_attn_step(cache._h, 0, H, qp + 4 * HID * i, kp + 4 * KVD * i, vp + 4 * KVD * i, gqp, gkp,
+                                  THETA, 1e-5, pos[0], op, bb.MEM_HOST, None)
+        if rc == 0:
+            rc = lib.bebelm_kv_evict_front(cache._h, 1)
+        if rc != 0:
+            raise bb.BebelmError(rc, bb.last_error())
+        pos[0] += 1
+
+    e2e_step(0)
     barrier(world)
     torch.cuda.synchronize()
     t0 = time.perf_counter()
     for i in range(e2e_steps):
-        cache.attn_step(0, hq[i], hk[i], hv[i], hqg, hkg, pos=pos[0], theta=THETA, out=hout)
-        cache.evict_front(1)
-        pos[0] += 1
+        e2e_step(i)
     e2e_s = max_over_ranks(time.perf_counter() - t0, world, dev)
     e2e_value = bytes_per_step(CTX + 1) * e2e_steps * world / e2e_s / 1e9
 
