@@ -40,7 +40,8 @@ EXPORTS = [
     "bebelm_kv_len", "bebelm_kv_layer_len", "bebelm_kv_pos", "bebelm_kv_set_pos", "bebelm_kv_evict_front",
     "bebelm_kv_append", "bebelm_kv_read", "bebelm_attn_step", "bebelm_attn_decode_cached", "bebelm_attn_decode_cached_noalloc", "bebelm_attn_prefill", "bebelm_attn_decode_batched",
     "bebelm_kv_check", "bebelm_peer_group_create", "bebelm_peer_group_connect", "bebelm_peer_group_destroy",
-    "bebelm_attn_step_allgather",
+    "bebelm_attn_step_allgather", "bebelm_step_plan_create", "bebelm_step_plan_launch", "bebelm_step_plan_steps",
+    "bebelm_step_plan_finish",
 ]
 IPC_HANDLE_BYTES = 64
 
@@ -95,6 +96,10 @@ def load_library(path: str = LIB_PATH):
         "bebelm_peer_group_connect": ([vp, vp], i),
         "bebelm_peer_group_destroy": ([vp], i),
         "bebelm_attn_step_allgather": ([vp, vp, i, i, vp, vp, vp, vp, vp, f, f, sz, vp, i, vp], i),
+        "bebelm_step_plan_create": ([vp, i, i, sz, C.POINTER(vp)], i),
+        "bebelm_step_plan_launch": ([vp, vp, vp, vp, vp, vp, f, f, vp, vp], i),
+        "bebelm_step_plan_steps": ([vp, C.POINTER(C.c_ulonglong), vp], i),
+        "bebelm_step_plan_finish": ([vp, vp], i),
     }
     for name, (args, res) in sig.items():
         fn = getattr(L, name)
@@ -342,6 +347,10 @@ class Cache:
         """Synchronises and raises if a bounded device-side wait gave up (device-memory calls)."""
         _check(load_library().bebelm_kv_check(self._h, _stream_ptr(stream)))
 
+    def step_plan(self, layer: int, n_heads: int = N_HEADS, window: int = 0) -> "StepPlan":
+        """A device-driven decode step for ``layer`` (see :class:`StepPlan`)."""
+        return StepPlan(self, layer, n_heads, window)
+
     def decode(self, layer: int, q, out=None, stream=None):
         """``attention_decode`` over the cached window of ``layer`` (no append); q normed+roped."""
         (qb,), mem = _bufs(q)
@@ -398,6 +407,40 @@ class Cache:
                 load_library().bebelm_kv_destroy(self._h)
         except Exception:
             pass
+
+
+class StepPlan:
+    """Device-driven decode steps of one cache layer, for CUDA-graph capture.
+
+    Each :meth:`launch` is the ``attn_step`` of the next token (position ``cache.pos + n`` for
+    the n-th launch), with the window sliding once it holds ``window`` positions; the launch
+    does no host work that depends on the step, so ``torch.cuda.graph`` can capture it and
+    replays advance the sequence. Device tensors only. :meth:`finish` writes the steps back
+    into the cache; until then other calls on the cache are refused."""
+
+    def __init__(self, cache: "Cache", layer: int, n_heads: int = N_HEADS, window: int = 0):
+        self.cache, self.layer, self.n_heads = cache, layer, n_heads
+        self._h = C.c_void_p()
+        _check(load_library().bebelm_step_plan_create(cache._h, layer, n_heads, window, C.byref(self._h)))
+
+    def launch(self, q, k, v, q_gain, k_gain, out, theta: float = ROPE_THETA, eps: float = RMS_EPS, stream=None):
+        for x in (q, k, v, q_gain, k_gain, out):
+            if not (_is_torch(x) and x.is_cuda and x.is_contiguous()):
+                raise ValueError("step plans take contiguous CUDA tensors")
+        _check(load_library().bebelm_step_plan_launch(self._h, q.data_ptr(), k.data_ptr(), v.data_ptr(),
+                                                      q_gain.data_ptr(), k_gain.data_ptr(), theta, eps,
+                                                      out.data_ptr(), _stream_ptr(stream)))
+        return out
+
+    def steps(self, stream=None) -> int:
+        n = C.c_ulonglong()
+        _check(load_library().bebelm_step_plan_steps(self._h, C.byref(n), _stream_ptr(stream)))
+        return n.value
+
+    def finish(self, stream=None) -> None:
+        if self._h:
+            h, self._h = self._h, C.c_void_p()
+            _check(load_library().bebelm_step_plan_finish(h, _stream_ptr(stream)))
 
 
 class PeerGroup:

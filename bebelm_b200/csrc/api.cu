@@ -206,6 +206,8 @@ struct bebelm_kv_pool {
     ErrWord err;
     PinBuf pin;
     UploadRing uploads;
+    const void* last_plan = nullptr;  // the step plan of the last decode launch, if it was one
+    unsigned long long last_capture = 0;  // the stream capture that launch was recorded in (0: none)
     std::vector<DecodeSeq> h_desc;
     // cache slots written by the most recent library kernel on this pool: a decode
     // launched next copies pages below these before its griddepcontrol.wait
@@ -237,6 +239,7 @@ struct bebelm_kv {
     long long lo = 0, hi = 0;     // allocated logical pages [lo, hi)
     std::vector<long long> base, len;  // per layer window: slots [base, base+len)
     size_t pos = 0;
+    int plans = 0;                // open step plans: the device owns the window state meanwhile
 };
 
 namespace {
@@ -295,6 +298,8 @@ void recompute_lo(bebelm_kv* kv) {
 
 int validate_kv(const bebelm_kv* kv) {
     if (!kv || !kv->pool) return fail(BEBELM_ERR_INVALID, "null cache handle");
+    if (kv->plans > 0)
+        return fail(BEBELM_ERR_INVALID, "the cache has %d open step plan(s): finish them first", kv->plans);
     return 0;
 }
 
@@ -521,6 +526,7 @@ int run_decode(bebelm_kv_pool* P, const std::vector<Window>& wins, int layer, in
         a.peer_off = peer->off;
     }
     CUDA_TRY(launch_decode(a, s));
+    P->last_plan = nullptr;
     P->last_writes.clear();
     if (fused)
         for (int i = 0; i < n; ++i)
@@ -689,6 +695,8 @@ int bebelm_kv_create_in_pool(bebelm_kv_pool* pool, size_t max_context, bebelm_kv
 
 int bebelm_kv_destroy(bebelm_kv* kv) {
     if (!kv) return 0;
+    if (kv->plans > 0)
+        return fail(BEBELM_ERR_INVALID, "the cache has %d open step plan(s): finish them first", kv->plans);
     bebelm_kv_pool* P = kv->pool;
     {
         DeviceGuard g(P->device);
@@ -1424,6 +1432,203 @@ int bebelm_attn_step_allgather(bebelm_kv* kv, bebelm_peer_group* g, int layer, i
                               full, P->err.d, s));
     if (mem == BEBELM_MEM_HOST) return stage_out(P, dout, out, 4 * full, s);
     return 0;
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Step plans: device-driven decode steps for CUDA-graph capture.
+//
+// A plan fixes everything a decode step's launch needs except the window, which the kernel
+// derives from a step counter in device memory (StepState) and the plan's starting point:
+// step n appends slot slot0 + n at position pos0 + n and attends to the last
+// min(len0 + n + 1, window) slots. Creating a plan assigns a physical page to every entry
+// of the sequence's page ring, so no later step needs the host: the window (at most
+// ceil(window/64) + 1 pages) always fits the ring (ceil(max_context/64) + 2 entries). The
+// split plan and the grid are sized for the largest window; CTAs past the current window
+// contribute empty partials. Finishing folds the steps taken back into the host state.
+// ---------------------------------------------------------------------------
+struct bebelm_step_plan {
+    bebelm_kv* kv = nullptr;
+    int layer = 0, n_heads = 0;
+    long long slot0 = 0, pos0 = 0, len0 = 0, window = 0;
+    int n_splits = 0, per = 0, hpc = 0, n_sub = 0;
+    DevBuf state, part, counters;  // StepState, split partials, combine counters
+};
+
+extern "C" {
+
+int bebelm_step_plan_create(bebelm_kv* kv, int layer, int n_heads, size_t window, bebelm_step_plan** out) {
+    if (!out) return fail(BEBELM_ERR_INVALID, "out is null");
+    *out = nullptr;
+    if (!kv || !kv->pool) return fail(BEBELM_ERR_INVALID, "null cache handle");
+    if (layer < 0 || layer >= kv->pool->n_layers)
+        return fail(BEBELM_ERR_INVALID, "layer %d out of range [0,%d)", layer, kv->pool->n_layers);
+    bebelm_kv_pool* P = kv->pool;
+    TRY(check_geometry(n_heads, P->n_kv));
+    if (window == 0) window = kv->max_context;
+    if (window > kv->max_context)
+        return fail(BEBELM_ERR_INVALID, "window %zu exceeds the cache's max_context %zu", window, kv->max_context);
+    if (kv->len[layer] > (long long)window)
+        return fail(BEBELM_ERR_INVALID, "layer %d holds %lld positions, more than the window %zu", layer,
+                    kv->len[layer], window);
+    // every other non-empty layer must share this window (the model appends to all layers in
+    // lockstep); a window lagging behind could be overwritten once this one wraps the ring
+    for (size_t l = 0; l < kv->len.size(); ++l)
+        if ((int)l != layer && kv->len[l] > 0 && (kv->len[l] != kv->len[layer] || kv->base[l] != kv->base[layer]))
+            return fail(BEBELM_ERR_INVALID, "layer %zu's window differs from layer %d's; step plans need equal windows",
+                        l, layer);
+    DeviceGuard g(P->device);
+    cudaStream_t s = 0;
+    // give every ring entry a physical page
+    if (kv->hi - kv->lo < kv->cap) {
+        const long long add = kv->lo + kv->cap - kv->hi;
+        if ((size_t)add > P->free_list.size())
+            return fail(BEBELM_ERR_OOM, "page pool exhausted: a step plan needs %lld more pages, %zu free", add,
+                        P->free_list.size());
+        const long long old_hi = kv->hi;
+        for (long long L = kv->hi; L < kv->lo + kv->cap; ++L) {
+            kv->table[L % kv->cap] = P->free_list.back();
+            P->free_list.pop_back();
+        }
+        kv->hi = kv->lo + kv->cap;
+        TRY(upload_table(kv, old_hi, kv->hi, s));
+    }
+    auto* pl = new bebelm_step_plan();
+    pl->kv = kv;
+    pl->layer = layer;
+    pl->n_heads = n_heads;
+    long long b = kv->base[layer], n = kv->len[layer];
+    if (n == 0 && b < kv->lo * kPageTokens) b = kv->lo * kPageTokens;
+    pl->slot0 = b + n;
+    pl->pos0 = (long long)kv->pos;
+    pl->len0 = n;
+    pl->window = (long long)window;
+    // split plan for the largest window: the pages [base, base + window) can span
+    const int group = n_heads / P->n_kv;
+    pick_heads_per_cta(group, &pl->hpc, &pl->n_sub);
+    const int NY = P->n_kv * pl->n_sub;
+    const long long max_pages = (pl->window + kPageTokens - 1) / kPageTokens + 1;
+    const long long target = (long long)P->num_sms * 2;  // two resident CTAs per SM, as run_decode
+    long long per = std::max<long long>(1, (max_pages * NY + target - 1) / target);
+    per = std::min<long long>(per, kDecodeMaxPagesPerSplit);
+    pl->per = (int)per;
+    pl->n_splits = (int)((max_pages + per - 1) / per);
+    int rc = pl->state.ensure(sizeof(StepState), true, s);
+    if (!rc) rc = pl->part.ensure(sizeof(float) * (size_t)pl->n_splits * NY * pl->hpc * (kHeadDim + 2), false, s);
+    if (!rc) rc = pl->counters.ensure(sizeof(unsigned) * (size_t)NY, true, s);
+    if (!rc && cudaStreamSynchronize(s) != cudaSuccess) rc = fail(BEBELM_ERR_CUDA, "step plan initialisation failed");
+    if (rc) {
+        pl->state.release();
+        pl->part.release();
+        pl->counters.release();
+        delete pl;
+        return rc;
+    }
+    kv->plans++;
+    *out = pl;
+    return 0;
+}
+
+int bebelm_step_plan_launch(bebelm_step_plan* pl, const float* q, const float* k, const float* v,
+                            const float* q_gain, const float* k_gain, float theta, float eps, float* out,
+                            void* stream) {
+    if (!pl || !pl->kv) return fail(BEBELM_ERR_INVALID, "null step plan");
+    if (!q || !k || !v || !q_gain || !k_gain || !out) return fail(BEBELM_ERR_INVALID, "null buffer");
+    bebelm_kv* kv = pl->kv;
+    bebelm_kv_pool* P = kv->pool;
+    DeviceGuard g(P->device);
+    const int NY = P->n_kv * pl->n_sub;
+    DecodeArgs a{};
+    a.one.table = kv->d_table;
+    a.one.cap = kv->cap;
+    a.one.split0 = 0;
+    a.one.n_splits = pl->n_splits;
+    a.one.dep_slot = -1;
+    a.n_seqs = 1;
+    a.pv = P->view(pl->layer);
+    a.q_raw = q;
+    a.k_new = k;
+    a.v_new = v;
+    a.q_gain = q_gain;
+    a.k_gain = k_gain;
+    a.theta_scale = theta_scale_of(theta, kHeadDim);
+    a.eps = eps;
+    a.out = out;
+    a.part_acc = pl->part.as<float>();
+    a.part_ml = a.part_acc + (size_t)pl->n_splits * NY * pl->hpc * kHeadDim;
+    a.counters = pl->counters.as<unsigned>();
+    a.err = P->err.d;
+    a.n_heads = pl->n_heads;
+    a.n_kv = P->n_kv;
+    a.group = pl->n_heads / P->n_kv;
+    a.hpc = pl->hpc;
+    a.n_sub = pl->n_sub;
+    a.pages_per_split = pl->per;
+    a.total_splits = pl->n_splits;
+    a.scale_log2 = 0.125f * 1.4426950408889634f;
+    a.pdl = 1;
+    a.step = pl->state.as<StepState>();
+    a.step_slot0 = pl->slot0;
+    a.step_pos0 = pl->pos0;
+    a.step_len0 = pl->len0;
+    a.step_window = pl->window;
+    // Early reads need the previous decode launch to be another plan's, in the same stream
+    // capture (or both uncaptured): a graph's first node must not rely on what preceded the
+    // capture, since replays follow the graph's own last node.
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    unsigned long long cap_id = 0;
+    CUDA_TRY(cudaStreamGetCaptureInfo(as_stream(stream), &cs, &cap_id));
+    if (cs != cudaStreamCaptureStatusActive) cap_id = 0;
+    a.step_prewait = P->last_plan != nullptr && P->last_plan != pl && P->last_capture == cap_id;
+    CUDA_TRY(launch_decode(a, as_stream(stream)));
+    P->last_plan = pl;
+    P->last_capture = cap_id;
+    return 0;
+}
+
+int bebelm_step_plan_steps(const bebelm_step_plan* pl, unsigned long long* n, void* stream) {
+    if (!pl || !pl->kv || !n) return fail(BEBELM_ERR_INVALID, "null argument");
+    DeviceGuard g(pl->kv->pool->device);
+    cudaStream_t s = as_stream(stream);
+    StepState st{};
+    CUDA_TRY(cudaMemcpyAsync(&st, pl->state.p, sizeof(st), cudaMemcpyDeviceToHost, s));
+    CUDA_TRY(cudaStreamSynchronize(s));
+    *n = st.n;
+    if (pl->kv->pool->err.read())
+        return fail(BEBELM_ERR_TIMEOUT, "a device-side wait timed out; the plan's outputs are invalid");
+    return 0;
+}
+
+int bebelm_step_plan_finish(bebelm_step_plan* pl, void* stream) {
+    if (!pl || !pl->kv) return fail(BEBELM_ERR_INVALID, "null step plan");
+    unsigned long long n = 0;
+    const int rc = bebelm_step_plan_steps(pl, &n, stream);
+    bebelm_kv* kv = pl->kv;
+    if (rc == 0) {
+        const long long end = pl->slot0 + (long long)n;  // one past the last appended slot
+        const long long len = std::min(pl->len0 + (long long)n, pl->window);
+        kv->base[pl->layer] = end - len;
+        kv->len[pl->layer] = len;
+        kv->pos = (size_t)(pl->pos0 + (long long)n);
+        // the ring's pages now stand for the logical pages from the oldest live one on
+        long long lo = LLONG_MAX;
+        for (size_t l = 0; l < kv->len.size(); ++l)
+            if (kv->len[l] > 0) lo = std::min(lo, kv->base[l] / kPageTokens);
+        if (lo != LLONG_MAX && lo > kv->lo) {
+            kv->lo = lo;
+            kv->hi = lo + kv->cap;
+        }
+    }
+    {
+        DeviceGuard g(kv->pool->device);
+        pl->state.release();
+        pl->part.release();
+        pl->counters.release();
+    }
+    kv->plans--;
+    delete pl;
+    return rc;
 }
 
 }  // extern "C"

@@ -155,6 +155,18 @@ __device__ __forceinline__ void signal_peers(const DecodeArgs& a) {
     }
 }
 
+// Step plans: every CTA counts itself done once it has used the step counter; the last CTA
+// of the grid advances the counter for the next step (which reads it after its
+// griddepcontrol.wait, i.e. after this grid has completed).
+__device__ __forceinline__ void step_done(const DecodeArgs& a) {
+    if (!a.step || threadIdx.x != 0) return;
+    const unsigned total = gridDim.x * gridDim.y;
+    if (atomicAdd(&a.step->done, 1u) == total - 1) {
+        a.step->done = 0u;
+        a.step->n += 1ull;
+    }
+}
+
 // One head of 64 at `pos`, one warp: lane i returns elements i and i+32 after
 // rmsnorm (f64 sum of f32 squares, IEEE divide/sqrt, unfused products) and NEOX
 // RoPE with the iterative angle — the arithmetic of norm_rope.cu.
@@ -208,7 +220,20 @@ __global__ void __launch_bounds__(kThreads, 2) decode_kernel(DecodeArgs a) {
         if (a.seqs[mid].split0 <= gsplit) lo = mid; else hi = mid - 1;
     }
     const int seq = lo;
-    const DecodeSeq S = a.n_seqs == 1 ? a.one : a.seqs[seq];
+    DecodeSeq S = a.n_seqs == 1 ? a.one : a.seqs[seq];
+    if (a.step) {
+        // device-driven step: the window follows from the steps already taken, which this
+        // plan's previous step counted when it finished. Unless that step is known to be
+        // complete already (step_prewait), the counter is read after the wait and no page is
+        // copied before it; otherwise nothing the predecessor writes is in this layer's window.
+        if (!a.step_prewait) grid_dep_wait();
+        const long long n = (long long)*reinterpret_cast<volatile unsigned long long*>(&a.step->n);
+        S.new_slot = a.step_slot0 + n;
+        S.pos = a.step_pos0 + n;
+        S.len = a.step_len0 + n + 1 < a.step_window ? a.step_len0 + n + 1 : a.step_window;
+        S.base = S.new_slot + 1 - S.len;
+        S.dep_slot = a.step_prewait ? LLONG_MAX : -1;
+    }
     const int split = gsplit - S.split0;
     const long long first_page = S.base >> 6;
     const long long last_page = S.len > 0 ? (S.base + S.len - 1) >> 6 : first_page - 1;
@@ -462,6 +487,7 @@ __global__ void __launch_bounds__(kThreads, 2) decode_kernel(DecodeArgs a) {
                 mbar_wait_bounded(&full[k], (unsigned)((last / NST) & 1));
             }
         }
+        step_done(a);
         return;
     }
 
@@ -518,6 +544,7 @@ __global__ void __launch_bounds__(kThreads, 2) decode_kernel(DecodeArgs a) {
     }
     if (single) {
         signal_peers(a);
+        step_done(a);
         return;
     }
 
@@ -530,7 +557,10 @@ __global__ void __launch_bounds__(kThreads, 2) decode_kernel(DecodeArgs a) {
         if (s_last) *ctr = 0u;  // ready for the next launch
     }
     __syncthreads();
-    if (!s_last) return;
+    if (!s_last) {
+        step_done(a);
+        return;
+    }
     const int ns = S.n_splits;
     constexpr int kVec = HPC * kHeadDim / 4;  // float4s per split record
     constexpr int G = kThreads / kVec;        // thread groups, each a stride of the splits
@@ -598,6 +628,7 @@ __global__ void __launch_bounds__(kThreads, 2) decode_kernel(DecodeArgs a) {
         emit_out(a, seq, (size_t)h0 * kHeadDim + o, L > 0.f ? A / L : 0.f);
     }
     signal_peers(a);
+    step_done(a);
 }
 
 template <int HPC, bool BF>

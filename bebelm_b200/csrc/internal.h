@@ -126,6 +126,16 @@ struct DecodeSeq {
     long long dep_slot; // pages holding slots >= dep_slot are read only after griddepcontrol.wait
 };
 
+// Device-driven decode (step plans): step n of a plan appends slot slot0 + n at RoPE position
+// pos0 + n and attends to the window that ends there (at most `window` positions). n lives
+// in device memory; the last CTA of step n's grid advances it, so the launch arguments are
+// the same for every step and the launch can be captured in a CUDA graph.
+struct StepState {
+    unsigned long long n;  // steps completed
+    unsigned done;         // CTAs of the running step that have finished (reset by the last)
+    unsigned pad;
+};
+
 struct DecodeArgs {
     const DecodeSeq* seqs;  // device array [n_seqs] (unused when n_seqs == 1)
     DecodeSeq one;          // the sequence itself when n_seqs == 1 (passed by value)
@@ -157,6 +167,14 @@ struct DecodeArgs {
     unsigned long long* const* peer_flags;
     int peer_world, peer_rank;
     size_t peer_off;
+    // step plan (one sequence): non-null step makes the window of `one` follow the counter
+    StepState* step;
+    long long step_slot0, step_pos0, step_len0, step_window;
+    // the launch before this one was not this plan's: its previous step is at least two
+    // launches back, hence complete when this grid starts (each decode grid triggers its
+    // dependents only after its own griddepcontrol.wait), so the counter and every page may
+    // be read before the wait
+    int step_prewait;
 };
 // Waits (bounded) until flags[r] >= expected for every source rank r, then copies n floats of
 // the gathered landing buffer to dst. On timeout it records kErrWaitTimeout and copies nothing.

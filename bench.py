@@ -531,6 +531,36 @@ def bench_config5(bb, torch, dev, stream, world, rank, bf16_peak, T=8192, steps=
     if world > 1:
         _, dec_nccl = run(False)
         out["decode_ms_per_step_nccl_gather"] = round(dec_nccl / steps, 4)
+    else:
+        # the same decode as one CUDA graph: step plans (device-driven window state) for the 6
+        # layers, all `steps` steps x 6 layers captured once (each node reads its own step's
+        # inputs) and replayed, so no host work sits between the kernels
+        from bebelm_b200 import Cache
+        c = Cache(n_layers=L, max_context=T + steps + 64)
+        for layer in range(L):
+            c.attn_prefill(layer, q, k, v, qg, kg, 0, theta=THETA)
+        c.pos = T
+        plans = [c.step_plan(layer) for layer in range(L)]
+        o = torch.empty((steps, L, HID), device=dev)
+        graph, cap = torch.cuda.CUDAGraph(), torch.cuda.Stream()
+        torch.cuda.synchronize()
+        with torch.cuda.graph(graph, stream=cap):
+            for s_ in range(steps):
+                for layer in range(L):
+                    plans[layer].launch(Qd[s_], Kd[s_], Vd[s_], qg, kg, o[s_, layer], theta=THETA)
+        graph.replay()  # warm-up: steps tokens
+        torch.cuda.synchronize()
+        e = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+        e[0].record(stream)
+        graph.replay()  # the next steps tokens
+        e[1].record(stream)
+        torch.cuda.synchronize()
+        g_ms = e[0].elapsed_time(e[1])
+        for p_ in plans:
+            p_.finish()
+        c.close()
+        out["decode_graph"] = {"ms_per_step": round(g_ms / steps, 4), "tok_per_s": round(steps / (g_ms * 1e-3), 1),
+                               "how": "step plans, one CUDA graph of all steps x 6 layers"}
     return out
 
 

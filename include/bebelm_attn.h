@@ -192,6 +192,34 @@ BEBELM_API int bebelm_attn_decode_batched(bebelm_kv* const* seqs, int n_seqs, in
  * calls only enqueue work, so their callers check here. */
 BEBELM_API int bebelm_kv_check(const bebelm_kv* kv, void* stream);
 
+/* ---------------------------------------------------- step plans (graphs) --- */
+/* No counterpart in the reference. Device-driven decode steps, for a token loop captured
+ * once in a CUDA graph and replayed: the host work of bebelm_attn_step (slot bookkeeping,
+ * split plan, page assignment) is done once when the plan is created, and the kernel keeps
+ * the window state itself. Step n of a plan (n = 0, 1, ... counted on the device) is the
+ * attn_step of a token at RoPE position pos + n, where pos is the cache's pos when the plan
+ * was created (bebelm_kv_set_pos): its k/v are appended after the layer's window and it
+ * attends to the last min(len + n + 1, window) positions (len = the layer's window length at
+ * creation), i.e. the window slides by one position per step once full, as the Agent's
+ * trim_context does (src/agent.rs:466-476). window 0 means max_context.
+ *  - create: gives every entry of the sequence's page ring a physical page (so no step needs
+ *    the host), and fails if another non-empty layer's window differs from this layer's
+ *    (the model steps all layers in lockstep: one plan per layer, each launched per token).
+ *  - launch: device pointers only (q [n_heads*64], k/v [n_kv_heads*64], gains [64], out
+ *    [n_heads*64]); allocates, copies and synchronises nothing, so it may be captured. Each
+ *    launch is one step; steps of one plan must run in stream order.
+ *  - steps: synchronises the stream and reports the steps taken so far.
+ *  - finish: synchronises, folds the steps into the cache (window, pos) and frees the plan.
+ * While a cache has open plans, every other call on it fails with BEBELM_ERR_INVALID. */
+typedef struct bebelm_step_plan bebelm_step_plan;
+BEBELM_API int bebelm_step_plan_create(bebelm_kv* kv, int layer, int n_heads, size_t window,
+                                       bebelm_step_plan** out);
+BEBELM_API int bebelm_step_plan_launch(bebelm_step_plan* plan, const float* q, const float* k,
+                                       const float* v, const float* q_gain, const float* k_gain,
+                                       float theta, float eps, float* out, void* stream);
+BEBELM_API int bebelm_step_plan_steps(const bebelm_step_plan* plan, unsigned long long* n, void* stream);
+BEBELM_API int bebelm_step_plan_finish(bebelm_step_plan* plan, void* stream);
+
 /* ------------------------------------------- multi-GPU (KV-head sharding) --- */
 /* Fused decode + all-gather for KV-head sharding over NVLink, one process per
  * GPU. The reference runs every head on one CPU (src/model.rs:440-451); here
