@@ -28,8 +28,8 @@ _i64p = np.ctypeslib.ndpointer(np.int64, flags="C_CONTIGUOUS")
 
 def build(force: bool = False) -> str:
     """Compile the C restatement (seconds). Returns the library path."""
-    src = os.path.join(_HERE, "bebelm_oracle.c")
-    if force or not os.path.exists(_LIB_PATH) or os.path.getmtime(_LIB_PATH) < os.path.getmtime(src):
+    srcs = [os.path.join(_HERE, f) for f in ("bebelm_oracle.c", "quant_oracle.c")]
+    if force or not os.path.exists(_LIB_PATH) or any(os.path.getmtime(_LIB_PATH) < os.path.getmtime(f) for f in srcs):
         subprocess.run(["make", "-s", "-C", _HERE], check=True)
     return _LIB_PATH
 
@@ -55,6 +55,15 @@ def lib():
         L.orc_attn_step.argtypes = [_f32p, _f32p, _f32p, sz, _f32p, _f32p, C.c_float, C.c_float,
                                     C.c_int, C.c_int, C.c_int, _f32p, _f32p, C.POINTER(sz), _f32p, C.c_int]
         L.orc_max_threads.restype = C.c_int
+        u8p = np.ctypeslib.ndpointer(np.uint8, flags="C_CONTIGUOUS")
+        i8p = np.ctypeslib.ndpointer(np.int8, flags="C_CONTIGUOUS")
+        i32p = np.ctypeslib.ndpointer(np.int32, flags="C_CONTIGUOUS")
+        L.orc_f16_to_f32.argtypes = [C.c_uint16]
+        L.orc_f16_to_f32.restype = C.c_float
+        L.orc_dequantize.argtypes = [C.c_int, u8p, sz, _f32p]
+        L.orc_quantize_q8.argtypes = [_f32p, sz, i8p, _f32p, i32p]
+        L.orc_matvec.argtypes = [C.c_int, u8p, sz, sz, _f32p, _f32p, _f32p, i8p, _f32p, i32p]
+        L.orc_matmul.argtypes = [C.c_int, u8p, sz, sz, _f32p, sz, _f32p, _f32p, i8p, _f32p, i32p]
         _lib = L
     return _lib
 
@@ -197,3 +206,53 @@ class Cache:
         n_ctx = self.k[layer].shape[0]
         return attention_decode(q, self.k[layer], self.v[layer], n_ctx, n_heads, n_kv_heads,
                                 head_dim, n_threads=n_threads)
+
+
+# ------------------------------------------------------------- quantized path --
+# ggml type ids (src/tensor.rs:41-62)
+GG_F32, GG_F16, GG_Q4_K, GG_Q6_K = 0, 1, 12, 14
+BLOCK = {GG_F32: (1, 4), GG_F16: (1, 2), GG_Q4_K: (256, 144), GG_Q6_K: (256, 210)}
+
+
+def f16_to_f32(h: int) -> float:
+    """src/kernels/dequant.rs:22-54."""
+    return float(lib().orc_f16_to_f32(int(h) & 0xFFFF))
+
+
+def dequantize(dtype: int, data, n: int) -> np.ndarray:
+    """src/kernels/dequant.rs:151-186: n elements of dtype from the raw bytes."""
+    d = np.ascontiguousarray(np.frombuffer(bytes(data), np.uint8) if not isinstance(data, np.ndarray) else data,
+                             np.uint8).reshape(-1)
+    out = np.zeros(n, np.float32)
+    if lib().orc_dequantize(dtype, d, n, out):
+        raise ValueError(f"dequantize: unsupported dtype {dtype} or size {n}")
+    return out
+
+
+def quantize_q8(x):
+    """src/kernels/matmul.rs:141-164 -> (q int8 [n], scales f32 [n/256], sums int32 [n/32])."""
+    x = _f32(x).reshape(-1)
+    q = np.zeros(x.size, np.int8)
+    sc = np.zeros(x.size // 256, np.float32)
+    sm = np.zeros(x.size // 32, np.int32)
+    lib().orc_quantize_q8(x, x.size, q, sc, sm)
+    return q, sc, sm
+
+
+def matmul(dtype: int, w, n_in: int, n_out: int, x, n_tokens: int = 1) -> np.ndarray:
+    """src/kernels/matmul.rs:850-1013: y [n_tokens][n_out] = W x, W packed as dtype (row per output)."""
+    wb = np.ascontiguousarray(np.frombuffer(bytes(w), np.uint8) if not isinstance(w, np.ndarray) else w,
+                              np.uint8).reshape(-1)
+    x = _f32(x).reshape(-1)
+    y = np.zeros(n_tokens * n_out, np.float32)
+    scratch = np.zeros(max(n_in, 1), np.float32)
+    q8 = np.zeros(max(n_in, 1), np.int8)
+    q8s = np.zeros(max(n_in // 256, 1), np.float32)
+    q8m = np.zeros(max(n_in // 32, 1), np.int32)
+    if lib().orc_matmul(dtype, wb, n_in, n_out, x, n_tokens, y, scratch, q8, q8s, q8m):
+        raise ValueError(f"matmul: unsupported dtype {dtype} or n_in {n_in}")
+    return y.reshape(n_tokens, n_out) if n_tokens > 1 else y
+
+
+def matvec(dtype: int, w, n_in: int, n_out: int, x) -> np.ndarray:
+    return matmul(dtype, w, n_in, n_out, x, 1)

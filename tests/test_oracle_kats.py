@@ -146,3 +146,92 @@ def test_prng_is_deterministic():
     b = oracle.normal(123, (1000,))
     assert np.array_equal(a, b)
     assert abs(float(a.mean())) < 0.1 and abs(float(a.std()) - 1) < 0.1
+
+
+# ------------------------------------------------------------- quantized path --
+def _patched(case, blocks=1):
+    b = np.zeros(case["len"], np.uint8)
+    for k, v in case["set"].items():
+        b[int(k)] = v
+    return np.tile(b, blocks)
+
+
+def q4k_test_block():
+    b = np.zeros(144, np.uint8)
+    b[0:2] = [0x00, 0x3c]
+    b[2:4] = [0x00, 0x34]
+    b[4:16] = [(j * 17 + 5) & 255 for j in range(12)]
+    b[16:144] = [(i * 37 + 11) & 255 for i in range(128)]
+    return b, np.array([((i % 7) - 3) * 0.1 for i in range(256)], np.float32)
+
+
+def q6k_test_block():
+    b = np.zeros(210, np.uint8)
+    b[208:210] = [0x00, 0x3c]
+    b[0:128] = [(i * 53 + 17) & 255 for i in range(128)]
+    b[128:192] = [(i * 97 + 5) & 255 for i in range(64)]
+    b[192:208] = [(j * 29 + 3) & 255 for j in range(16)]
+    return b, np.array([((i % 5) - 2) * 0.1 for i in range(256)], np.float32)
+
+
+def test_quant_kats(kats):
+    q = kats["quant"]
+    for bits, val in q["f16"]["exact"]:
+        got = oracle.f16_to_f32(bits)
+        assert got == float(val) and math.copysign(1, got) == math.copysign(1, float(val)), (bits, got)
+    assert all(math.isnan(oracle.f16_to_f32(b)) for b in q["f16"]["nan"])
+    for bits, val, tol in q["f16"]["approx"]:
+        assert abs(oracle.f16_to_f32(bits) - val) < tol
+    for name, dtype in (("q4k_block", oracle.GG_Q4_K), ("q6k_block", oracle.GG_Q6_K)):
+        out = oracle.dequantize(dtype, _patched(q[name]), 256)
+        for i, v in q[name]["out"].items():
+            assert out[int(i)] == v, (name, i, out[int(i)])
+    f32 = np.array(q["dispatch_f32"]["values"], np.float32)
+    assert np.array_equal(oracle.dequantize(oracle.GG_F32, f32.view(np.uint8), 3), f32)
+    f16 = np.array(q["dispatch_f16"]["bits"], np.uint16).view(np.uint8)
+    assert list(oracle.dequantize(oracle.GG_F16, f16, 4)) == q["dispatch_f16"]["out"]
+    two = oracle.dequantize(oracle.GG_Q4_K, _patched(q["dispatch_two_q4k"], 2), 512)
+    assert all(two[int(i)] == v for i, v in q["dispatch_two_q4k"]["out"].items())
+
+
+def test_matvec_kats(kats):
+    q = kats["quant"]
+    c = q["matvec_f32_small"]
+    w = np.array(c["w"], np.float32).view(np.uint8)
+    for x, want in c["cases"]:
+        assert list(oracle.matvec(oracle.GG_F32, w, c["n_in"], c["n_out"], x)) == want
+    c = q["matvec_f16_small"]
+    w = np.array(c["bits"], np.uint16).view(np.uint8)
+    assert list(oracle.matvec(oracle.GG_F16, w, c["n_in"], c["n_out"], c["x"])) == c["out"]
+    c = q["matvec_q4k_single_row"]
+    x = np.zeros(256, np.float32)
+    x[0] = 1.0
+    assert oracle.matvec(oracle.GG_Q4_K, _patched(c), 256, 1, x)[0] == c["out"]
+    # the Q8 path equals the exact dot of the dequantized weights with the Q8-rounded activations
+    for (blk, x), dtype, name in ((q4k_test_block(), oracle.GG_Q4_K, "q4k_test_block"),
+                                  (q6k_test_block(), oracle.GG_Q6_K, "q6k_test_block")):
+        wts = oracle.dequantize(dtype, blk, 256)
+        qx, sx, _ = oracle.quantize_q8(x)
+        ref = np.float32(0)
+        for wi, qi in zip(wts, qx):
+            ref = np.float32(ref + np.float32(wi * np.float32(sx[0] * np.float32(qi))))
+        y = oracle.matvec(dtype, blk, 256, 1, x)[0]
+        assert abs(y - ref) <= q[name]["tol"] * max(abs(ref), 1.0), (name, y, ref)
+    # rows are independent dots, bit for bit
+    n_in, n_out = 40, 128
+    w = np.array([((i % 13) - 6) * 0.05 for i in range(n_in * n_out)], np.float32)
+    x = np.array([((i % 7) - 3) * 0.1 for i in range(n_in)], np.float32)
+    y = oracle.matvec(oracle.GG_F32, w.view(np.uint8), n_in, n_out, x)
+    for o in range(n_out):
+        assert y[o] == oracle.dot(w[o * n_in:(o + 1) * n_in], x)
+
+
+def test_matmul_is_matvec_per_token():
+    rng = np.random.default_rng(3)
+    blk = rng.integers(0, 256, size=8 * 144 * 4, dtype=np.uint8)
+    blk.reshape(-1, 144)[:, 1] = 0x38  # d = 0.5
+    blk.reshape(-1, 144)[:, 3] = 0x30  # dmin = 0.125
+    x = rng.standard_normal((3, 2048)).astype(np.float32)
+    y = oracle.matmul(oracle.GG_Q4_K, blk, 2048, 4, x, 3)
+    for t in range(3):
+        assert np.array_equal(y[t], oracle.matvec(oracle.GG_Q4_K, blk, 2048, 4, x[t]))
