@@ -41,8 +41,9 @@ EXPORTS = [
     "bebelm_kv_append", "bebelm_kv_read", "bebelm_attn_step", "bebelm_attn_decode_cached", "bebelm_attn_decode_cached_noalloc", "bebelm_attn_prefill", "bebelm_attn_decode_batched",
     "bebelm_kv_check", "bebelm_peer_group_create", "bebelm_peer_group_connect", "bebelm_peer_group_destroy",
     "bebelm_attn_step_allgather", "bebelm_step_plan_create", "bebelm_step_plan_launch", "bebelm_step_plan_steps",
-    "bebelm_step_plan_finish",
+    "bebelm_step_plan_finish", "bebelm_matvec", "bebelm_matmul", "bebelm_dequantize",
 ]
+GGML_F32, GGML_F16, GGML_Q4_K, GGML_Q6_K = 0, 1, 12, 14
 IPC_HANDLE_BYTES = 64
 
 
@@ -100,6 +101,9 @@ def load_library(path: str = LIB_PATH):
         "bebelm_step_plan_launch": ([vp, vp, vp, vp, vp, vp, f, f, vp, vp], i),
         "bebelm_step_plan_steps": ([vp, C.POINTER(C.c_ulonglong), vp], i),
         "bebelm_step_plan_finish": ([vp, vp], i),
+        "bebelm_matvec": ([i, vp, sz, sz, vp, vp, i, vp], i),
+        "bebelm_matmul": ([i, vp, sz, sz, vp, sz, vp, i, vp], i),
+        "bebelm_dequantize": ([i, vp, sz, vp, i, vp], i),
     }
     for name, (args, res) in sig.items():
         fn = getattr(L, name)
@@ -407,6 +411,45 @@ class Cache:
                 load_library().bebelm_kv_destroy(self._h)
         except Exception:
             pass
+
+
+def _raw(x):
+    """(pointer, mem, keepalive) for raw weight bytes: a uint8 numpy array / bytes, or a CUDA tensor."""
+    if _is_torch(x):
+        if not x.is_cuda:
+            x = x.detach().contiguous().numpy()
+        else:
+            return x.data_ptr(), MEM_DEVICE, x
+    a = np.ascontiguousarray(np.frombuffer(x, np.uint8) if isinstance(x, (bytes, bytearray)) else x).view(np.uint8)
+    return a.ctypes.data, MEM_HOST, a
+
+
+def matmul(dtype: int, w, n_in: int, n_out: int, x, n_tokens: int = 1, out=None, stream=None):
+    """``matmul`` / ``matvec`` (src/kernels/matmul.rs:850-1013) on the GPU: y [n_tokens, n_out] = W x.
+    w: the packed weight bytes (numpy uint8 / bytes, or a CUDA uint8 tensor); x float32 [n_tokens, n_in]."""
+    wp, wm, wk = _raw(w)
+    xb, xm, xk = _buf(x)
+    if wm != xm:
+        raise ValueError("weights and activations must both be host or both be device buffers")
+    if out is None:
+        out = np.zeros((n_tokens, n_out), np.float32) if xm == MEM_HOST else xk.new_empty((n_tokens, n_out))
+    ob, _, _ = _buf(out)
+    _check(load_library().bebelm_matmul(dtype, wp, n_in, n_out, xb, n_tokens, ob, xm, _stream_ptr(stream, xm)))
+    return out.reshape(-1) if n_tokens == 1 and out.ndim > 1 and xm == MEM_HOST else out
+
+
+def matvec(dtype: int, w, n_in: int, n_out: int, x, out=None, stream=None):
+    return matmul(dtype, w, n_in, n_out, x, 1, out=out, stream=stream)
+
+
+def dequantize(dtype: int, data, n: int, stream=None) -> np.ndarray:
+    """``dequantize`` (src/kernels/dequant.rs:151-186) on the GPU; host bytes in, float32 out."""
+    dp, dm, dk = _raw(data)
+    if dm != MEM_HOST:
+        raise ValueError("dequantize takes host bytes")
+    out = np.zeros(n, np.float32)
+    _check(load_library().bebelm_dequantize(dtype, dp, n, out.ctypes.data, MEM_HOST, None))
+    return out
 
 
 class StepPlan:

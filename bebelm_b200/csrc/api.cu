@@ -202,7 +202,7 @@ struct bebelm_kv_pool {
     int num_sms = 148;
     int n_seqs = 0;              // live sequences drawing from this pool
     // scratch shared by every call on this pool's sequences (stream-ordered)
-    DevBuf io, qn, part, counters, seqdesc, pf;
+    DevBuf io, qn, part, counters, seqdesc, pf, q8;
     ErrWord err;
     PinBuf pin;
     UploadRing uploads;
@@ -373,6 +373,7 @@ void pool_free(bebelm_kv_pool* P) {
     P->counters.release();
     P->seqdesc.release();
     P->pf.release();
+    P->q8.release();
     P->err.release();
     P->pin.release();
     delete P;
@@ -1629,6 +1630,92 @@ int bebelm_step_plan_finish(bebelm_step_plan* pl, void* stream) {
     kv->plans--;
     delete pl;
     return rc;
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Quantized products of the weights feeding the path (the q/k/v/o projections).
+// ---------------------------------------------------------------------------
+namespace {
+
+int check_ggml(int dtype, size_t n_in) {
+    if (dtype != kGgmlF32 && dtype != kGgmlF16 && dtype != kGgmlQ4K && dtype != kGgmlQ6K)
+        return fail(BEBELM_ERR_UNSUPPORTED, "weight dtype %d is not F32 (0), F16 (1), Q4_K (12) or Q6_K (14)", dtype);
+    if ((dtype == kGgmlQ4K || dtype == kGgmlQ6K) && n_in % 256)
+        return fail(BEBELM_ERR_INVALID, "n_in (%zu) must be a multiple of 256 for K-quant weights", n_in);
+    return 0;
+}
+
+}  // namespace
+
+extern "C" {
+
+int bebelm_matmul(int dtype, const void* w, size_t n_in, size_t n_out, const float* x, size_t n_tokens, float* y,
+                  int mem, void* stream) {
+    TRY(check_mem(mem));
+    TRY(check_ggml(dtype, n_in));
+    if (n_out == 0 || n_tokens == 0) return 0;
+    if (!y || (n_in && (!w || !x))) return fail(BEBELM_ERR_INVALID, "null buffer");
+    int dev;
+    TRY(current_device(&dev));
+    cudaStream_t s = as_stream(stream);
+    std::lock_guard<std::mutex> lk(g_scratch_mu);
+    bebelm_kv_pool* P = nullptr;
+    TRY(scratch_pool(dev, &P));
+    const size_t wbytes = ggml_row_bytes(dtype, n_in) * n_out, xn = n_in * n_tokens, yn = n_out * n_tokens;
+    const void* dw = w;
+    const float* dx = x;
+    float* dy = y;
+    if (mem == BEBELM_MEM_HOST) {
+        void *a0, *a1, *o;
+        Stage st[2] = {{w, wbytes, &a0}, {x, 4 * xn, &a1}};
+        TRY(stage_in(P, st, 2, 4 * yn, &o, s));
+        dw = a0;
+        dx = static_cast<const float*>(a1);
+        dy = static_cast<float*>(o);
+    }
+    int8_t* q8 = nullptr;
+    float* q8s = nullptr;
+    int* q8m = nullptr;
+    if (dtype == kGgmlQ4K || dtype == kGgmlQ6K) {
+        const size_t qb = (xn + 255) & ~size_t(255), sb = 4 * (xn / 256), mb = 4 * (xn / 32);
+        TRY(P->q8.ensure(qb + ((sb + 255) & ~size_t(255)) + mb + 256, false, s));
+        q8 = P->q8.as<int8_t>();
+        q8s = reinterpret_cast<float*>(P->q8.as<char>() + qb);
+        q8m = reinterpret_cast<int*>(P->q8.as<char>() + qb + ((sb + 255) & ~size_t(255)));
+        CUDA_TRY(launch_quantize_q8(dx, n_in, n_tokens, q8, q8s, q8m, s));
+    }
+    CUDA_TRY(launch_qmatmul(dtype, static_cast<const uint8_t*>(dw), n_in, n_out, dx, n_tokens, q8, q8s, q8m, dy, s));
+    if (mem == BEBELM_MEM_HOST) return stage_out(P, dy, y, 4 * yn, s);
+    return 0;
+}
+
+int bebelm_matvec(int dtype, const void* w, size_t n_in, size_t n_out, const float* x, float* y, int mem,
+                  void* stream) {
+    return bebelm_matmul(dtype, w, n_in, n_out, x, 1, y, mem, stream);
+}
+
+int bebelm_dequantize(int dtype, const void* data, size_t n_elements, float* out, int mem, void* stream) {
+    TRY(check_mem(mem));
+    TRY(check_ggml(dtype, n_elements));
+    if (n_elements == 0) return 0;
+    if (!data || !out) return fail(BEBELM_ERR_INVALID, "null buffer");
+    int dev;
+    TRY(current_device(&dev));
+    cudaStream_t s = as_stream(stream);
+    if (mem == BEBELM_MEM_DEVICE) {
+        CUDA_TRY(launch_dequantize(dtype, static_cast<const uint8_t*>(data), n_elements, out, s));
+        return 0;
+    }
+    std::lock_guard<std::mutex> lk(g_scratch_mu);
+    bebelm_kv_pool* P = nullptr;
+    TRY(scratch_pool(dev, &P));
+    void *a0, *o;
+    Stage st[1] = {{data, ggml_row_bytes(dtype, n_elements), &a0}};
+    TRY(stage_in(P, st, 1, 4 * n_elements, &o, s));
+    CUDA_TRY(launch_dequantize(dtype, static_cast<const uint8_t*>(a0), n_elements, static_cast<float*>(o), s));
+    return stage_out(P, o, out, 4 * n_elements, s);
 }
 
 }  // extern "C"

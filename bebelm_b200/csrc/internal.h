@@ -3,6 +3,7 @@
 #pragma once
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <stddef.h>
 #include <stdint.h>
 
@@ -206,5 +207,17 @@ cudaError_t launch_kv_gather_bf16(const PoolView& pv, const int* table, int cap,
 
 // device error codes written to DecodeArgs::err
 constexpr int kErrWaitTimeout = 1;
+
+// GGML weight types of the quantized products (ggml's type ids, src/tensor.rs:41-62)
+constexpr int kGgmlF32 = 0, kGgmlF16 = 1, kGgmlQ4K = 12, kGgmlQ6K = 14;
+size_t ggml_row_bytes(int dtype, size_t n_in);  // 0 for an unsupported dtype
+// activations [n_tokens][n_in] (n_in a multiple of 256) -> int8 quants, per-256 scales,
+// per-32 sums, in token-major order
+cudaError_t launch_quantize_q8(const float* x, size_t n_in, size_t n_tokens, int8_t* q, float* scales, int* sums,
+                               cudaStream_t s);
+// y [n_tokens][n_out] = W x; K-quant weights take the Q8 activations, F32/F16 weights x itself
+cudaError_t launch_qmatmul(int dtype, const uint8_t* w, size_t n_in, size_t n_out, const float* x, size_t n_tokens,
+                           const int8_t* q8, const float* q8_scales, const int* q8_sums, float* y, cudaStream_t s);
+cudaError_t launch_dequantize(int dtype, const uint8_t* data, size_t n, float* out, cudaStream_t s);
 
 }  // namespace bebelm

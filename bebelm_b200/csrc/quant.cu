@@ -1,0 +1,271 @@
+// Quantized weights feeding the attention path: GGML dequantization and the quantized
+// matrix-vector / matrix-matrix product of the reference (its q/k/v/o projections).
+//
+// Restates, per output row and token, the reference's arithmetic exactly:
+//   quantize_q8       src/kernels/matmul.rs:141-164  activations -> int8 per 256-block:
+//                     scale = max|x|/127, q = round_half_away(x * 127/max|x|) clamped to +-127,
+//                     plus the sum of each 32-wide sub-block's quants
+//   dot_q4k_block_q8  src/kernels/matmul.rs:220-244  exact i32 Σ_j sc_j·<nibbles_j, q_j> and
+//                     Σ_j m_j·sum_j, then sx * (d * sd - dmin * sm) in f32 (no contraction)
+//   dot_q6k_block_q8  src/kernels/matmul.rs:633-700  exact i32 Σ_k sc_k·<(q6 - 32)_k, q_k>, then
+//                     sx * (d * s)
+//   dot_q{4,6}k_row   src/kernels/matmul.rs:293-300, 748-754  f32 sum over blocks in order
+//   matvec / matmul   src/kernels/matmul.rs:850-1013  (matmul = matvec per token, bit for bit)
+//   F32/F16 weights:  the row dequantized, then `dot` (src/kernels/matmul.rs:36-65): 32 FMA
+//                     chains (lane = i mod 32), the 8-wide cleanup into the first 8, then
+//                     ((acc0+acc1)+(acc2+acc3)) and an 8-lane reduction, then an unfused
+//                     scalar tail. The 8-lane reduction order of the reference's SIMD library
+//                     is not visible; the order here is the CPU oracle's.
+//   dequantize_*      src/kernels/dequant.rs:22-176
+// The integer dots are exact and every f32 operation is written with round-to-nearest
+// intrinsics in the reference's order, so Q4_K/Q6_K results are the reference's bit for bit.
+//
+// Mapping: one warp per (output row, token); a 256-weight block per step, 8 weights per lane
+// (dp4a on packed int8), an exact integer warp reduction, and lane 0 adds the block's f32
+// value to the row's sum in block order. Activations are quantized once per token by a
+// separate kernel (one warp per 256-block).
+#include <algorithm>
+
+#include "internal.h"
+
+namespace bebelm {
+namespace {
+
+constexpr int kQK = 256;
+
+__device__ __forceinline__ float f16_bits_to_f32(uint32_t h) {
+    // exact for normals, subnormals, inf and nan (the hardware conversion is exact)
+    __half_raw r;
+    r.x = (unsigned short)h;
+    return __half2float(__half(r));
+}
+
+__device__ __forceinline__ float ld_f16(const uint8_t* p) {
+    return f16_bits_to_f32((uint32_t)p[0] | ((uint32_t)p[1] << 8));
+}
+
+__device__ __forceinline__ void scale_min_k4(int j, const uint8_t* s, int& sc, int& m) {
+    if (j < 4) {
+        sc = s[j] & 63;
+        m = s[j + 4] & 63;
+    } else {
+        sc = (s[j + 4] & 0x0f) | ((s[j - 4] >> 6) << 4);
+        m = (s[j + 4] >> 4) | ((s[j] >> 6) << 4);
+    }
+}
+
+__device__ __forceinline__ int warp_sum_i32(int v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+// One warp per 256-block of one token.
+__global__ void __launch_bounds__(256) quantize_q8_kernel(const float* x, size_t n_in, int8_t* q, float* scales,
+                                                          int* sums, size_t n_blocks_total) {
+    const size_t blk = (size_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+    if (blk >= n_blocks_total) return;
+    const int lane = threadIdx.x & 31;
+    const float* xb = x + blk * kQK + lane * 8;
+    const float4 a = *reinterpret_cast<const float4*>(xb), b = *reinterpret_cast<const float4*>(xb + 4);
+    const float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+    float amax = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    const float inv = amax > 0.f ? __fdiv_rn(127.0f, amax) : 0.f;
+    int8_t qv[8];
+    int s = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        float r = roundf(__fmul_rn(v[i], inv));  // half away from zero, as Rust's f32::round
+        r = fminf(fmaxf(r, -127.f), 127.f);
+        qv[i] = (int8_t)r;
+        s += qv[i];
+    }
+    *reinterpret_cast<uint2*>(q + blk * kQK + lane * 8) = *reinterpret_cast<const uint2*>(qv);
+    s += __shfl_xor_sync(0xffffffffu, s, 1);  // a 32-wide sub-block is 4 lanes
+    s += __shfl_xor_sync(0xffffffffu, s, 2);
+    if ((lane & 3) == 0) sums[blk * 8 + (lane >> 2)] = s;
+    if (lane == 0) scales[blk] = __fdiv_rn(amax, 127.0f);
+}
+
+// Q4_K block (144 B: d, dmin, scales[12], qs[128]) against its 256 int8 activations.
+// Lane l holds qs bytes 4l..4l+3: chunk c = l/8 (sub-blocks 2c: low nibbles, 2c+1: high).
+__device__ __forceinline__ float block_q4k(const uint8_t* blk, const int8_t* qx, float sx, const int* sums,
+                                           int lane) {
+    const int c = lane >> 3, p = (lane & 7) * 4;
+    const uint32_t w = *reinterpret_cast<const uint32_t*>(blk + 16 + c * 32 + p);
+    const int xlo = *reinterpret_cast<const int*>(qx + (2 * c) * 32 + p);
+    const int xhi = *reinterpret_cast<const int*>(qx + (2 * c + 1) * 32 + p);
+    int sc0, m0, sc1, m1;
+    scale_min_k4(2 * c, blk + 4, sc0, m0);
+    scale_min_k4(2 * c + 1, blk + 4, sc1, m1);
+    int sd = sc0 * __dp4a((int)(w & 0x0f0f0f0fu), xlo, 0) + sc1 * __dp4a((int)((w >> 4) & 0x0f0f0f0fu), xhi, 0);
+    int sm = 0;
+    if (lane < 8) {
+        int scj, mj;
+        scale_min_k4(lane, blk + 4, scj, mj);
+        sm = mj * sums[lane];
+    }
+    sd = warp_sum_i32(sd);
+    sm = warp_sum_i32(sm);
+    const float d = ld_f16(blk), dmin = ld_f16(blk + 2);
+    return __fmul_rn(sx, __fsub_rn(__fmul_rn(d, __int2float_rn(sd)), __fmul_rn(dmin, __int2float_rn(sm))));
+}
+
+// Q6_K block (210 B: ql[128], qh[64], scales[16] i8, d). Lane l holds 8 weights of the
+// 16-wide sub-block k = l/2: its low 4 bits from ql (low or high nibble), its top 2 from qh.
+__device__ __forceinline__ float block_q6k(const uint8_t* blk, const int8_t* qx, float sx, int lane) {
+    const int k = lane >> 1, h = lane & 1;
+    const int n = k >> 3, g = (k & 7) >> 1, sub = k & 1;
+    const int ql_off = n * 64 + (g & 1) * 32 + sub * 16 + h * 8;  // groups 0,2 read ql[0..32), 1,3 ql[32..64)
+    const bool high = g >= 2;
+    const int shift = 2 * g;
+    const int qh_off = 128 + n * 32 + sub * 16 + h * 8;
+    uint32_t wq[2];
+#pragma unroll
+    for (int part = 0; part < 2; ++part) {
+        uint32_t word = 0;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const uint32_t l = blk[ql_off + part * 4 + i];
+            const uint32_t hb = (blk[qh_off + part * 4 + i] >> shift) & 3u;
+            const uint32_t q = ((high ? (l >> 4) : (l & 0x0fu)) | (hb << 4)) - 32u;  // -32..31 as a byte
+            word |= (q & 0xffu) << (8 * i);
+        }
+        wq[part] = word;
+    }
+    const int8_t* x = qx + k * 16 + h * 8;
+    int t = __dp4a((int)wq[0], *reinterpret_cast<const int*>(x), 0);
+    t = __dp4a((int)wq[1], *reinterpret_cast<const int*>(x + 4), t);
+    int s = t * (int)(int8_t)blk[192 + k];
+    s = warp_sum_i32(s);
+    const float d = ld_f16(blk + 208);
+    return __fmul_rn(sx, __fmul_rn(d, __int2float_rn(s)));
+}
+
+// F32/F16 weight row against fp32 x: the reference's `dot` (see the file header).
+template <int DT>
+__device__ __forceinline__ float row_dot(const uint8_t* row, const float* x, size_t n, int lane) {
+    auto wv = [&](size_t i) -> float {
+        return DT == kGgmlF32 ? reinterpret_cast<const float*>(row)[i] : ld_f16(row + 2 * i);
+    };
+    float acc = 0.f;
+    size_t i = 0;
+    for (; i + 32 <= n; i += 32) acc = fmaf(wv(i + lane), x[i + lane], acc);
+    for (; i + 8 <= n; i += 8)
+        if (lane < 8) acc = fmaf(wv(i + lane), x[i + lane], acc);
+    acc = __fadd_rn(acc, __shfl_down_sync(0xffffffffu, acc, 8));   // acc0+acc1, acc2+acc3
+    acc = __fadd_rn(acc, __shfl_down_sync(0xffffffffu, acc, 16));  // (acc0+acc1)+(acc2+acc3)
+    acc = __fadd_rn(acc, __shfl_down_sync(0xffffffffu, acc, 4));   // lanes j and j+4
+    acc = __fadd_rn(acc, __shfl_down_sync(0xffffffffu, acc, 2));   // (0,2), (1,3)
+    acc = __fadd_rn(acc, __shfl_down_sync(0xffffffffu, acc, 1));   // the two halves
+    if (lane == 0)
+        for (; i < n; ++i) acc = __fadd_rn(acc, __fmul_rn(wv(i), x[i]));
+    return acc;
+}
+
+// grid (ceil(n_out/8), n_tokens), 8 warps: warp = one output row of one token.
+template <int DT>
+__global__ void __launch_bounds__(256) qmatmul_kernel(const uint8_t* w, size_t row_bytes, size_t n_in, size_t n_out,
+                                                      const float* x, const int8_t* q8, const float* q8_scales,
+                                                      const int* q8_sums, float* y) {
+    const size_t o = (size_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+    if (o >= n_out) return;
+    const int lane = threadIdx.x & 31;
+    const size_t t = blockIdx.y;
+    const uint8_t* row = w + o * row_bytes;
+    float acc;
+    if (DT == kGgmlQ4K || DT == kGgmlQ6K) {
+        const size_t nb = n_in / kQK;
+        const int8_t* qx = q8 + t * n_in;
+        const float* sx = q8_scales + t * nb;
+        acc = -0.0f;  // an f32 iterator sum over the blocks, in order
+        for (size_t b = 0; b < nb; ++b) {
+            const float v = DT == kGgmlQ4K ? block_q4k(row + b * 144, qx + b * kQK, sx[b], q8_sums + (t * nb + b) * 8, lane)
+                                           : block_q6k(row + b * 210, qx + b * kQK, sx[b], lane);
+            acc = __fadd_rn(acc, v);
+        }
+    } else {
+        acc = row_dot<DT>(row, x + t * n_in, n_in, lane);
+    }
+    if (lane == 0) y[t * n_out + o] = acc;
+}
+
+__global__ void dequant_kernel(int dtype, const uint8_t* data, size_t n, float* out) {
+    const size_t stride = (size_t)gridDim.x * blockDim.x;
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
+        float v;
+        if (dtype == kGgmlF32) {
+            v = reinterpret_cast<const float*>(data)[i];
+        } else if (dtype == kGgmlF16) {
+            v = ld_f16(data + 2 * i);
+        } else if (dtype == kGgmlQ4K) {
+            const uint8_t* b = data + (i / kQK) * 144;
+            const int e = (int)(i % kQK), chunk = e / 64, hi = (e % 64) / 32, l = e % 32;
+            int sc, m;
+            scale_min_k4(2 * chunk + hi, b + 4, sc, m);
+            const uint8_t q = b[16 + chunk * 32 + l];
+            const float d = ld_f16(b), dmin = ld_f16(b + 2);
+            v = __fsub_rn(__fmul_rn(__fmul_rn(d, (float)sc), (float)(hi ? q >> 4 : q & 0x0f)),
+                          __fmul_rn(dmin, (float)m));
+        } else {  // Q6_K
+            const uint8_t* b = data + (i / kQK) * 210;
+            const int e = (int)(i % kQK), nh = e / 128, r = e % 128, grp = r / 32, l = r % 32;
+            const uint8_t* ql = b + nh * 64;
+            const uint8_t* qh = b + 128 + nh * 32;
+            const int8_t* sc = reinterpret_cast<const int8_t*>(b + 192 + nh * 8);
+            const int lb = (grp & 1) ? ql[l + 32] : ql[l];
+            const int low = grp >= 2 ? lb >> 4 : lb & 0x0f;
+            const int q = (low | (((qh[l] >> (2 * grp)) & 3) << 4)) - 32;
+            v = __fmul_rn(__fmul_rn(ld_f16(b + 208), (float)sc[l / 16 + 2 * grp]), (float)q);
+        }
+        out[i] = v;
+    }
+}
+
+}  // namespace
+
+size_t ggml_row_bytes(int dtype, size_t n_in) {
+    switch (dtype) {
+        case kGgmlF32: return 4 * n_in;
+        case kGgmlF16: return 2 * n_in;
+        case kGgmlQ4K: return n_in / kQK * 144;
+        case kGgmlQ6K: return n_in / kQK * 210;
+        default: return 0;
+    }
+}
+
+cudaError_t launch_quantize_q8(const float* x, size_t n_in, size_t n_tokens, int8_t* q, float* scales, int* sums,
+                               cudaStream_t s) {
+    const size_t blocks = n_in / kQK * n_tokens;
+    if (blocks == 0) return cudaSuccess;
+    quantize_q8_kernel<<<(unsigned)((blocks + 7) / 8), 256, 0, s>>>(x, n_in, q, scales, sums, blocks);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_qmatmul(int dtype, const uint8_t* w, size_t n_in, size_t n_out, const float* x, size_t n_tokens,
+                           const int8_t* q8, const float* q8_scales, const int* q8_sums, float* y, cudaStream_t s) {
+    if (n_out == 0 || n_tokens == 0) return cudaSuccess;
+    const dim3 grid((unsigned)((n_out + 7) / 8), (unsigned)n_tokens);
+    const size_t rb = ggml_row_bytes(dtype, n_in);
+    switch (dtype) {
+        case kGgmlF32: qmatmul_kernel<kGgmlF32><<<grid, 256, 0, s>>>(w, rb, n_in, n_out, x, q8, q8_scales, q8_sums, y); break;
+        case kGgmlF16: qmatmul_kernel<kGgmlF16><<<grid, 256, 0, s>>>(w, rb, n_in, n_out, x, q8, q8_scales, q8_sums, y); break;
+        case kGgmlQ4K: qmatmul_kernel<kGgmlQ4K><<<grid, 256, 0, s>>>(w, rb, n_in, n_out, x, q8, q8_scales, q8_sums, y); break;
+        case kGgmlQ6K: qmatmul_kernel<kGgmlQ6K><<<grid, 256, 0, s>>>(w, rb, n_in, n_out, x, q8, q8_scales, q8_sums, y); break;
+        default: return cudaErrorInvalidValue;
+    }
+    return cudaGetLastError();
+}
+
+cudaError_t launch_dequantize(int dtype, const uint8_t* data, size_t n, float* out, cudaStream_t s) {
+    if (n == 0) return cudaSuccess;
+    const size_t blocks = std::min<size_t>((n + 255) / 256, 148 * 16);
+    dequant_kernel<<<(unsigned)blocks, 256, 0, s>>>(dtype, data, n, out);
+    return cudaGetLastError();
+}
+
+}  // namespace bebelm

@@ -192,6 +192,27 @@ BEBELM_API int bebelm_attn_decode_batched(bebelm_kv* const* seqs, int n_seqs, in
  * calls only enqueue work, so their callers check here. */
 BEBELM_API int bebelm_kv_check(const bebelm_kv* kv, void* stream);
 
+/* ---------------------------------------------- quantized weights (GGML) --- */
+/* The projections that feed the path (src/model.rs:434-436, 454) multiply GGML-quantized
+ * weights by f32 activations. Weight dtypes are ggml's type ids. W is [n_out rows][n_in],
+ * each row packed in the dtype's blocks (row-major by output, as stored in the GGUF). */
+enum { BEBELM_GGML_F32 = 0, BEBELM_GGML_F16 = 1, BEBELM_GGML_Q4_K = 12, BEBELM_GGML_Q6_K = 14 };
+/* `matvec(dtype, w, n_in, n_out, x, y)` (src/kernels/matmul.rs:850-905): y[n_out] = W x.
+ * Q4_K/Q6_K weights take the reference's Q8-activation integer dot (quantize_q8 of x per
+ * 256-block, exact i32 block dots, f32 block scaling, blocks summed in order): bit for bit
+ * the reference's result. F32/F16 weights use the reference's `dot` structure (its final
+ * 8-lane reduction order is not visible; within f32 rounding of the reference). n_in must be
+ * a multiple of 256 for K-quants. */
+BEBELM_API int bebelm_matvec(int dtype, const void* w, size_t n_in, size_t n_out, const float* x, float* y,
+                             int mem, void* stream);
+/* `matmul(..., n_tokens, y)` (src/kernels/matmul.rs:908-1013): token-major x [n_tokens][n_in],
+ * y [n_tokens][n_out]; bit-identical to matvec per token, as the reference's is. */
+BEBELM_API int bebelm_matmul(int dtype, const void* w, size_t n_in, size_t n_out, const float* x,
+                             size_t n_tokens, float* y, int mem, void* stream);
+/* `dequantize_into(dtype, data, out)` (src/kernels/dequant.rs:151-176): n_elements f32. */
+BEBELM_API int bebelm_dequantize(int dtype, const void* data, size_t n_elements, float* out, int mem,
+                                 void* stream);
+
 /* ---------------------------------------------------- step plans (graphs) --- */
 /* No counterpart in the reference. Device-driven decode steps, for a token loop captured
  * once in a CUDA graph and replayed: the host work of bebelm_attn_step (slot bookkeeping,
