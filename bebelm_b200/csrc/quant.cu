@@ -32,6 +32,10 @@ namespace bebelm {
 namespace {
 
 constexpr int kQK = 256;
+#ifndef BEBELM_QMM_TILED_MIN
+#define BEBELM_QMM_TILED_MIN 32
+#endif
+constexpr size_t kTiledMinTokens = BEBELM_QMM_TILED_MIN;  // from this many tokens on, the tiled kernel
 
 __device__ __forceinline__ float f16_bits_to_f32(uint32_t h) {
     // exact for normals, subnormals, inf and nan (the hardware conversion is exact)
@@ -194,6 +198,182 @@ __global__ void __launch_bounds__(256) qmatmul_kernel(const uint8_t* w, size_t r
     if (lane == 0) y[t * n_out + o] = acc;
 }
 
+// Many tokens: a CTA computes 64 rows x 64 tokens. For each 256-weight block it unpacks the
+// 64 rows' weights to int8 in shared memory (Q4_K: nibbles 0..15 in 8 sub-blocks of 32;
+// Q6_K: q - 32 in 16 sub-blocks of 16) with their integer sub-block scales, stages the 64
+// tokens' Q8 activations, and each thread forms 4 rows x 4 tokens of exact integer sub-block
+// dots with dp4a. The f32 block value and the in-order block sum per (row, token) are those
+// of qmatmul_kernel, so the results are identical.
+constexpr int kTR = 64, kTT = 64, kWStride = 256 + 16;  // int8 row stride: 16 B skew against bank conflicts
+template <int DT>
+__global__ void __launch_bounds__(256) qmatmul_tiled_kernel(const uint8_t* w, size_t row_bytes, size_t n_in,
+                                                            size_t n_out, size_t n_tokens, const int8_t* q8,
+                                                            const float* q8_scales, const int* q8_sums, float* y) {
+    constexpr int NSUB = DT == kGgmlQ4K ? 8 : 16;  // sub-blocks per block
+    constexpr int SW = kQK / NSUB;                 // sub-block width (32 or 16)
+    __shared__ __align__(16) int8_t s_w[kTR * kWStride];
+    __shared__ __align__(16) int8_t s_x[kTT * kWStride];
+    __shared__ int s_sc[kTR][NSUB];
+    __shared__ int s_m[kTR][8];       // Q4_K mins
+    __shared__ float s_d[kTR], s_dmin[kTR];
+    __shared__ float s_sx[kTT];
+    __shared__ int s_sums[kTT][8];
+    const int tid = threadIdx.x;
+    const size_t r0 = (size_t)blockIdx.x * kTR, t0 = (size_t)blockIdx.y * kTT;
+    const int tr = tid >> 4, tc = tid & 15;  // thread tile: rows tr + 16 i, tokens tc + 16 k
+    const size_t nb = n_in / kQK;
+    float acc[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int k = 0; k < 4; ++k) acc[i][k] = -0.0f;
+
+    for (size_t b = 0; b < nb; ++b) {
+        __syncthreads();  // the previous block's operands are no longer read
+        // weights of 64 rows -> int8 + scales
+        if (DT == kGgmlQ4K) {
+            for (int task = tid; task < kTR * 8; task += 256) {  // (row, 16-byte segment of qs)
+                const int r = task >> 3, seg = task & 7, c = seg >> 1, p = (seg & 1) * 16;
+                uint4 q = make_uint4(0, 0, 0, 0);
+                if (r0 + r < n_out) q = *reinterpret_cast<const uint4*>(w + (r0 + r) * row_bytes + b * 144 + 16 + c * 32 + p);
+                const uint32_t qw[4] = {q.x, q.y, q.z, q.w};
+                uint4 lo, hi;
+                uint32_t* lp = reinterpret_cast<uint32_t*>(&lo);
+                uint32_t* hp = reinterpret_cast<uint32_t*>(&hi);
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    lp[e] = qw[e] & 0x0f0f0f0fu;
+                    hp[e] = (qw[e] >> 4) & 0x0f0f0f0fu;
+                }
+                *reinterpret_cast<uint4*>(s_w + r * kWStride + (2 * c) * 32 + p) = lo;
+                *reinterpret_cast<uint4*>(s_w + r * kWStride + (2 * c + 1) * 32 + p) = hi;
+            }
+            if (tid < kTR) {
+                const int r = tid;
+                if (r0 + r < n_out) {
+                    const uint8_t* blk = w + (r0 + r) * row_bytes + b * 144;
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) scale_min_k4(j, blk + 4, s_sc[r][j], s_m[r][j]);
+                    s_d[r] = ld_f16(blk);
+                    s_dmin[r] = ld_f16(blk + 2);
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) s_sc[r][j] = s_m[r][j] = 0;
+                    s_d[r] = s_dmin[r] = 0.f;
+                }
+            }
+        } else {  // Q6_K: (row, sub-block k, half h): 8 weights
+            for (int task = tid; task < kTR * 32; task += 256) {
+                const int r = task >> 5, k = (task >> 1) & 15, h = task & 1;
+                uint2 out = make_uint2(0, 0);
+                if (r0 + r < n_out) {
+                    const uint8_t* blk = w + (r0 + r) * row_bytes + b * 210;
+                    const int n = k >> 3, g = (k & 7) >> 1, sub = k & 1;
+                    const int ql_off = n * 64 + (g & 1) * 32 + sub * 16 + h * 8;
+                    const int qh_off = 128 + n * 32 + sub * 16 + h * 8;
+                    const bool high = g >= 2;
+                    const int shift = 2 * g;
+                    uint32_t* op = reinterpret_cast<uint32_t*>(&out);
+#pragma unroll
+                    for (int part = 0; part < 2; ++part) {
+                        uint32_t word = 0;
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) {
+                            const uint32_t l = blk[ql_off + part * 4 + i];
+                            const uint32_t hb = (blk[qh_off + part * 4 + i] >> shift) & 3u;
+                            word |= ((((high ? (l >> 4) : (l & 0x0fu)) | (hb << 4)) - 32u) & 0xffu) << (8 * i);
+                        }
+                        op[part] = word;
+                    }
+                }
+                *reinterpret_cast<uint2*>(s_w + r * kWStride + k * 16 + h * 8) = out;
+            }
+            if (tid < kTR) {
+                const int r = tid;
+                const bool ok = r0 + r < n_out;
+                const uint8_t* blk = w + (ok ? (r0 + r) * row_bytes + b * 210 : 0);
+#pragma unroll
+                for (int k = 0; k < 16; ++k) s_sc[r][k] = ok ? (int)(int8_t)blk[192 + k] : 0;
+                s_d[r] = ok ? ld_f16(blk + 208) : 0.f;
+            }
+        }
+        // activations of 64 tokens
+        for (int task = tid; task < kTT * 16; task += 256) {
+            const int t = task >> 4, seg = task & 15;
+            uint4 v = make_uint4(0, 0, 0, 0);
+            if (t0 + t < n_tokens) v = *reinterpret_cast<const uint4*>(q8 + (t0 + t) * n_in + b * kQK + seg * 16);
+            *reinterpret_cast<uint4*>(s_x + t * kWStride + seg * 16) = v;
+        }
+        if (tid < kTT) {
+            const bool ok = t0 + tid < n_tokens;
+            s_sx[tid] = ok ? q8_scales[(t0 + tid) * nb + b] : 0.f;
+            if (DT == kGgmlQ4K)
+#pragma unroll
+                for (int j = 0; j < 8; ++j) s_sums[tid][j] = ok ? q8_sums[((t0 + tid) * nb + b) * 8 + j] : 0;
+        }
+        __syncthreads();
+
+        int sd[4][4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+            for (int k = 0; k < 4; ++k) sd[i][k] = 0;
+#pragma unroll 2
+        for (int j = 0; j < NSUB; ++j) {
+            int wv[4][SW / 4], xv[4][SW / 4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int q = 0; q < SW / 16; ++q)
+                    *reinterpret_cast<int4*>(&wv[i][4 * q]) =
+                        *reinterpret_cast<const int4*>(s_w + (tr + 16 * i) * kWStride + j * SW + 16 * q);
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+#pragma unroll
+                for (int q = 0; q < SW / 16; ++q)
+                    *reinterpret_cast<int4*>(&xv[k][4 * q]) =
+                        *reinterpret_cast<const int4*>(s_x + (tc + 16 * k) * kWStride + j * SW + 16 * q);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const int sc = s_sc[tr + 16 * i][j];
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    int dt = 0;
+#pragma unroll
+                    for (int e = 0; e < SW / 4; ++e) dt = __dp4a(wv[i][e], xv[k][e], dt);
+                    sd[i][k] += sc * dt;
+                }
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int r = tr + 16 * i;
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const int t = tc + 16 * k;
+                float v;
+                if (DT == kGgmlQ4K) {
+                    int sm = 0;
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) sm += s_m[r][j] * s_sums[t][j];
+                    v = __fmul_rn(s_sx[t], __fsub_rn(__fmul_rn(s_d[r], __int2float_rn(sd[i][k])),
+                                                     __fmul_rn(s_dmin[r], __int2float_rn(sm))));
+                } else {
+                    v = __fmul_rn(s_sx[t], __fmul_rn(s_d[r], __int2float_rn(sd[i][k])));
+                }
+                acc[i][k] = __fadd_rn(acc[i][k], v);
+            }
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const size_t r = r0 + tr + 16 * i, t = t0 + tc + 16 * k;
+            if (r < n_out && t < n_tokens) y[t * n_out + r] = acc[i][k];
+        }
+}
+
 __global__ void dequant_kernel(int dtype, const uint8_t* data, size_t n, float* out) {
     const size_t stride = (size_t)gridDim.x * blockDim.x;
     for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
@@ -249,8 +429,16 @@ cudaError_t launch_quantize_q8(const float* x, size_t n_in, size_t n_tokens, int
 cudaError_t launch_qmatmul(int dtype, const uint8_t* w, size_t n_in, size_t n_out, const float* x, size_t n_tokens,
                            const int8_t* q8, const float* q8_scales, const int* q8_sums, float* y, cudaStream_t s) {
     if (n_out == 0 || n_tokens == 0) return cudaSuccess;
-    const dim3 grid((unsigned)((n_out + 7) / 8), (unsigned)n_tokens);
     const size_t rb = ggml_row_bytes(dtype, n_in);
+    if ((dtype == kGgmlQ4K || dtype == kGgmlQ6K) && n_tokens >= kTiledMinTokens) {
+        const dim3 tg((unsigned)((n_out + kTR - 1) / kTR), (unsigned)((n_tokens + kTT - 1) / kTT));
+        if (dtype == kGgmlQ4K)
+            qmatmul_tiled_kernel<kGgmlQ4K><<<tg, 256, 0, s>>>(w, rb, n_in, n_out, n_tokens, q8, q8_scales, q8_sums, y);
+        else
+            qmatmul_tiled_kernel<kGgmlQ6K><<<tg, 256, 0, s>>>(w, rb, n_in, n_out, n_tokens, q8, q8_scales, q8_sums, y);
+        return cudaGetLastError();
+    }
+    const dim3 grid((unsigned)((n_out + 7) / 8), (unsigned)n_tokens);
     switch (dtype) {
         case kGgmlF32: qmatmul_kernel<kGgmlF32><<<grid, 256, 0, s>>>(w, rb, n_in, n_out, x, q8, q8_scales, q8_sums, y); break;
         case kGgmlF16: qmatmul_kernel<kGgmlF16><<<grid, 256, 0, s>>>(w, rb, n_in, n_out, x, q8, q8_scales, q8_sums, y); break;

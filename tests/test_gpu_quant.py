@@ -101,3 +101,13 @@ def test_edge_activations_and_device_buffers():
         bb.matvec(bb.GGML_Q4_K, w, 500, 64, np.zeros(500, np.float32))  # not a multiple of 256
     with pytest.raises(bb.BebelmError):
         bb.matvec(2, w, 512, 64, x)  # Q4_0: not supported
+
+
+@pytest.mark.parametrize("dtype,gen", [(bb.GGML_Q4_K, random_q4k), (bb.GGML_Q6_K, random_q6k)])
+@pytest.mark.parametrize("n_out,n_in,t", [(100, 512, 70), (512, 2048, 64), (130, 256, 33)])
+def test_tiled_matmul_bit_exact(dtype, gen, n_out, n_in, t):
+    """Many tokens take the 64 x 64 tiled kernel: ragged rows and tokens, same bits as matvec."""
+    w = gen(n_out, n_in, seed=n_out * 7 + t)
+    xs = oracle.normal(90 + t, (t, n_in))
+    xs[3] = 0.0  # a token whose quants are all zero
+    np.testing.assert_array_equal(bb.matmul(dtype, w, n_in, n_out, xs, t), oracle.matmul(dtype, w, n_in, n_out, xs, t))
