@@ -42,6 +42,7 @@ EXPORTS = [
     "bebelm_kv_check", "bebelm_peer_group_create", "bebelm_peer_group_connect", "bebelm_peer_group_destroy",
     "bebelm_attn_step_allgather", "bebelm_step_plan_create", "bebelm_step_plan_launch", "bebelm_step_plan_steps",
     "bebelm_step_plan_finish", "bebelm_matvec", "bebelm_matmul", "bebelm_dequantize",
+    "bebelm_attn_weights_create", "bebelm_attn_weights_destroy", "bebelm_attn_layer_step", "bebelm_attn_layer_batch",
 ]
 GGML_F32, GGML_F16, GGML_Q4_K, GGML_Q6_K = 0, 1, 12, 14
 IPC_HANDLE_BYTES = 64
@@ -104,6 +105,10 @@ def load_library(path: str = LIB_PATH):
         "bebelm_matvec": ([i, vp, sz, sz, vp, vp, i, vp], i),
         "bebelm_matmul": ([i, vp, sz, sz, vp, sz, vp, i, vp], i),
         "bebelm_dequantize": ([i, vp, sz, vp, i, vp], i),
+        "bebelm_attn_weights_create": ([i, i, i, sz, i, vp, i, vp, i, vp, i, vp, vp, vp, C.POINTER(vp)], i),
+        "bebelm_attn_weights_destroy": ([vp], i),
+        "bebelm_attn_layer_step": ([vp, i, vp, vp, sz, f, f, vp, i, vp], i),
+        "bebelm_attn_layer_batch": ([vp, i, vp, vp, sz, sz, i, f, f, vp, i, vp], i),
     }
     for name, (args, res) in sig.items():
         fn = getattr(L, name)
@@ -449,6 +454,60 @@ def dequantize(dtype: int, data, n: int, stream=None) -> np.ndarray:
         raise ValueError("dequantize takes host bytes")
     out = np.zeros(n, np.float32)
     _check(load_library().bebelm_dequantize(dtype, dp, n, out.ctypes.data, MEM_HOST, None))
+    return out
+
+
+class AttnWeights:
+    """A layer's attention weights on the device: GGUF tensors as stored (packed bytes + ggml
+    dtype) for attn_q / attn_k / attn_v / attn_output, and the q/k norm gains."""
+
+    def __init__(self, wq, wk, wv, wo, q_gain, k_gain, n_heads: int = N_HEADS, n_kv_heads: int = N_KV_HEADS,
+                 hidden: int = HIDDEN, device: int = 0):
+        """wq/wk/wv/wo: (dtype, bytes) pairs (bytes: numpy uint8 or bytes)."""
+        self.n_heads, self.n_kv, self.hidden = n_heads, n_kv_heads, hidden
+        keep = [np.ascontiguousarray(np.frombuffer(b, np.uint8) if isinstance(b, (bytes, bytearray)) else b).view(np.uint8)
+                for _, b in (wq, wk, wv, wo)]
+        g = [np.ascontiguousarray(x, np.float32) for x in (q_gain, k_gain)]
+        self._h = C.c_void_p()
+        _check(load_library().bebelm_attn_weights_create(
+            device, n_heads, n_kv_heads, hidden, wq[0], keep[0].ctypes.data, wk[0], keep[1].ctypes.data, wv[0],
+            keep[2].ctypes.data, wo[0], keep[3].ctypes.data, g[0].ctypes.data, g[1].ctypes.data, C.byref(self._h)))
+
+    def close(self):
+        if self._h:
+            load_library().bebelm_attn_weights_destroy(self._h)
+            self._h = C.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def attn_layer_step(cache: "Cache", layer: int, weights: AttnWeights, x, pos: int, theta: float = ROPE_THETA,
+                    eps: float = RMS_EPS, out=None, stream=None):
+    """``attn_step`` (src/model.rs:430-455) whole: x [hidden] -> out [hidden]."""
+    (xb,), mem = _bufs(x)
+    if out is None:
+        out = np.zeros(weights.hidden, np.float32) if mem == MEM_HOST else xb[2].new_empty(weights.hidden)
+    ob, _, _ = _buf(out)
+    _check(load_library().bebelm_attn_layer_step(cache._h, layer, weights._h, xb[0], pos, theta, eps, ob, mem,
+                                                 _stream_ptr(stream, mem)))
+    return out
+
+
+def attn_layer_batch(cache: "Cache", layer: int, weights: AttnWeights, x, pos0: int, tensor_cores: bool = True,
+                     theta: float = ROPE_THETA, eps: float = RMS_EPS, out=None, stream=None):
+    """``attn_batch`` (src/model.rs:224-258) whole: x [t, hidden] -> out [t, hidden]."""
+    (xb,), mem = _bufs(x)
+    n = xb[2].size if mem == MEM_HOST else xb[2].numel()
+    t = n // weights.hidden
+    if out is None:
+        out = np.zeros((t, weights.hidden), np.float32) if mem == MEM_HOST else xb[2].new_empty((t, weights.hidden))
+    ob, _, _ = _buf(out)
+    _check(load_library().bebelm_attn_layer_batch(cache._h, layer, weights._h, xb[0], t, pos0, 1 if tensor_cores else 0,
+                                                  theta, eps, ob, mem, _stream_ptr(stream, mem)))
     return out
 
 

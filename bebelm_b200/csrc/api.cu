@@ -202,7 +202,7 @@ struct bebelm_kv_pool {
     int num_sms = 148;
     int n_seqs = 0;              // live sequences drawing from this pool
     // scratch shared by every call on this pool's sequences (stream-ordered)
-    DevBuf io, qn, part, counters, seqdesc, pf, q8;
+    DevBuf io, qn, part, counters, seqdesc, pf, q8, proj;
     ErrWord err;
     PinBuf pin;
     UploadRing uploads;
@@ -374,6 +374,7 @@ void pool_free(bebelm_kv_pool* P) {
     P->seqdesc.release();
     P->pf.release();
     P->q8.release();
+    P->proj.release();
     P->err.release();
     P->pin.release();
     delete P;
@@ -1049,6 +1050,78 @@ int bebelm_attn_decode_batched(bebelm_kv* const* seqs, int n_seqs, int layer, in
 
 }  // extern "C"
 
+namespace {
+
+// Device part of a chunked prefill (src/model.rs:232-254 middle section): t tokens' q/k/v
+// (fp32, or bf16 when in_bf16) are normed, roped and appended, then attend causally to the
+// window. tc: the tensor-core kernel (bf16 operands; the inputs are rounded to bf16 by the
+// norm kernel when they are fp32), else the exact fp32 split-K path with one causal window
+// per token. dout [t][n_heads*64] fp32 on the device.
+int prefill_device(bebelm_kv* kv, int layer, int n_heads, const void* dq, const void* dk, const void* dv, bool in_bf16,
+                   bool tc, size_t t, size_t pos0, const float* dqg, const float* dkg, float theta, float eps,
+                   float* dout, cudaStream_t s) {
+    bebelm_kv_pool* P = kv->pool;
+    const size_t qn = (size_t)n_heads * kHeadDim * t;
+    long long slot0 = 0;
+    TRY(reserve(kv, layer, t, &slot0, s));
+    const long long len_before = kv->len[layer] - (long long)t;
+    if (tc) {
+        // tensor-core path: bf16 q and the bf16 window [prefix | new keys] feed kernel 2
+        const size_t kvrow = (size_t)P->n_kv * kHeadDim;
+        const size_t s_total = (size_t)len_before + t;
+        TRY(P->pf.ensure(2 * (qn + 2 * s_total * kvrow) + 1024, false, s));
+        __nv_bfloat16* qb = P->pf.as<__nv_bfloat16>();
+        __nv_bfloat16* kb = qb + ((qn + 127) & ~size_t(127));
+        __nv_bfloat16* vb = kb + ((s_total * kvrow + 127) & ~size_t(127));
+        // descriptors first, so the two kernels below go out back to back
+        PrefillArgs pa{};
+        pa.q = qb; pa.k = kb; pa.v = vb; pa.out = dout;
+        pa.t = (int)t; pa.len_before = (int)len_before; pa.n_heads = n_heads; pa.n_kv = P->n_kv;
+        pa.scale_log2 = 0.125f * 1.4426950408889634f;
+        pa.err = P->err.d;
+        PrefillMaps maps;
+        if (!prefill_make_maps(pa, &maps)) return fail(BEBELM_ERR_CUDA, "building the TMA tensor maps for prefill failed");
+        if (len_before > 0)
+            CUDA_TRY(launch_kv_gather_bf16(P->view(layer), kv->d_table, kv->cap, kv->base[layer], len_before, P->n_kv,
+                                           kb, vb, s));
+        NormRopeArgs a{};
+        a.q = (const float*)dq; a.k = (const float*)dk; a.v = (const float*)dv; a.q_gain = dqg; a.k_gain = dkg;
+        a.T = (int)t; a.n_heads = n_heads; a.n_kv = P->n_kv; a.head_dim = kHeadDim;
+        a.pos0 = (long long)pos0;
+        a.theta_scale = theta_scale_of(theta, kHeadDim);
+        a.eps = eps;
+        a.norm_q = 1; a.norm_k = 1;
+        a.q_bf16 = qb; a.k_bf16 = kb + (size_t)len_before * kvrow; a.v_bf16 = vb + (size_t)len_before * kvrow;
+        a.append = 1; a.pv = P->view(layer); a.table = kv->d_table; a.cap = kv->cap; a.slot0 = slot0;
+        a.in_bf16 = in_bf16 ? 1 : 0;  // norm + RoPE read the inputs in their own type
+        CUDA_TRY(launch_norm_rope(a, s));
+        P->last_writes.assign(1, {kv, layer, slot0});
+        CUDA_TRY(launch_prefill(pa, maps, s));
+        P->last_writes.clear();
+        return 0;
+    }
+    if (in_bf16) return fail(BEBELM_ERR_UNSUPPORTED, "bf16 inputs take the tensor-core path");
+    TRY(P->qn.ensure(4 * qn, false, s));
+    NormRopeArgs a{};
+    a.q = (const float*)dq; a.k = (const float*)dk; a.v = (const float*)dv; a.q_gain = dqg; a.k_gain = dkg;
+    a.T = (int)t; a.n_heads = n_heads; a.n_kv = P->n_kv; a.head_dim = kHeadDim;
+    a.pos0 = (long long)pos0;
+    a.theta_scale = theta_scale_of(theta, kHeadDim);
+    a.eps = eps;
+    a.norm_q = 1; a.norm_k = 1;
+    a.q_out = P->qn.as<float>();
+    a.append = 1; a.pv = P->view(layer); a.table = kv->d_table; a.cap = kv->cap; a.slot0 = slot0;
+    CUDA_TRY(launch_norm_rope(a, s));
+    P->last_writes.assign(1, {kv, layer, slot0});
+    // token i sees the window up to and including itself (src/model.rs:240-244)
+    std::vector<Window> w(t);
+    for (size_t i = 0; i < t; ++i) w[i] = {kv, kv->base[layer], len_before + (long long)i + 1, -1, 0};
+    TRY(run_decode(P, w, layer, n_heads, P->qn.as<float>(), dout, 0.125f, nullptr, s));
+    return 0;
+}
+
+}  // namespace
+
 extern "C" {
 
 int bebelm_attn_prefill(bebelm_kv* kv, int layer, int n_heads, const void* q, const void* k, const void* v,
@@ -1077,61 +1150,8 @@ int bebelm_attn_prefill(bebelm_kv* kv, int layer, int n_heads, const void* q, co
         dq = a0; dk = a1; dv = a2;
         dqg = (const float*)a3; dkg = (const float*)a4; dout = (float*)o;
     }
-    long long slot0 = 0;
-    TRY(reserve(kv, layer, t, &slot0, s));
-    const long long len_before = kv->len[layer] - (long long)t;
-    if (in_dtype == BEBELM_BF16) {
-        // tensor-core path: bf16 q and the bf16 window [prefix | new keys] feed kernel 2
-        const size_t kvrow = (size_t)P->n_kv * kHeadDim;
-        const size_t s_total = (size_t)len_before + t;
-        TRY(P->pf.ensure(2 * (qn + 2 * s_total * kvrow) + 1024, false, s));
-        __nv_bfloat16* qb = P->pf.as<__nv_bfloat16>();
-        __nv_bfloat16* kb = qb + ((qn + 127) & ~size_t(127));
-        __nv_bfloat16* vb = kb + ((s_total * kvrow + 127) & ~size_t(127));
-        // descriptors first, so the two kernels below go out back to back
-        PrefillArgs pa{};
-        pa.q = qb; pa.k = kb; pa.v = vb; pa.out = dout;
-        pa.t = (int)t; pa.len_before = (int)len_before; pa.n_heads = n_heads; pa.n_kv = P->n_kv;
-        pa.scale_log2 = 0.125f * 1.4426950408889634f;
-        pa.err = P->err.d;
-        PrefillMaps maps;
-        if (!prefill_make_maps(pa, &maps)) return fail(BEBELM_ERR_CUDA, "building the TMA tensor maps for prefill failed");
-        if (len_before > 0)
-            CUDA_TRY(launch_kv_gather_bf16(P->view(layer), kv->d_table, kv->cap, kv->base[layer], len_before, P->n_kv,
-                                           kb, vb, s));
-        NormRopeArgs a{};
-        a.q = (const float*)dq; a.k = (const float*)dk; a.v = (const float*)dv; a.q_gain = dqg; a.k_gain = dkg;
-        a.T = (int)t; a.n_heads = n_heads; a.n_kv = P->n_kv; a.head_dim = kHeadDim;
-        a.pos0 = (long long)pos0;
-        a.theta_scale = theta_scale_of(theta, kHeadDim);
-        a.eps = eps;
-        a.norm_q = 1; a.norm_k = 1;
-        a.q_bf16 = qb; a.k_bf16 = kb + (size_t)len_before * kvrow; a.v_bf16 = vb + (size_t)len_before * kvrow;
-        a.append = 1; a.pv = P->view(layer); a.table = kv->d_table; a.cap = kv->cap; a.slot0 = slot0;
-        a.in_bf16 = 1;  // norm + RoPE read the bf16 inputs directly
-        CUDA_TRY(launch_norm_rope(a, s));
-        P->last_writes.assign(1, {kv, layer, slot0});
-        CUDA_TRY(launch_prefill(pa, maps, s));
-        P->last_writes.clear();
-        if (mem == BEBELM_MEM_HOST) return stage_out(P, dout, out, 4 * qn, s);
-        return 0;
-    }
-    TRY(P->qn.ensure(4 * qn, false, s));
-    NormRopeArgs a{};
-    a.q = (const float*)dq; a.k = (const float*)dk; a.v = (const float*)dv; a.q_gain = dqg; a.k_gain = dkg;
-    a.T = (int)t; a.n_heads = n_heads; a.n_kv = P->n_kv; a.head_dim = kHeadDim;
-    a.pos0 = (long long)pos0;
-    a.theta_scale = theta_scale_of(theta, kHeadDim);
-    a.eps = eps;
-    a.norm_q = 1; a.norm_k = 1;
-    a.q_out = P->qn.as<float>();
-    a.append = 1; a.pv = P->view(layer); a.table = kv->d_table; a.cap = kv->cap; a.slot0 = slot0;
-    CUDA_TRY(launch_norm_rope(a, s));
-    P->last_writes.assign(1, {kv, layer, slot0});
-    // token i sees the window up to and including itself (src/model.rs:240-244)
-    std::vector<Window> w(t);
-    for (size_t i = 0; i < t; ++i) w[i] = {kv, kv->base[layer], len_before + (long long)i + 1, -1, 0};
-    TRY(run_decode(P, w, layer, n_heads, P->qn.as<float>(), dout, 0.125f, nullptr, s));
+    const bool bf = in_dtype == BEBELM_BF16;
+    TRY(prefill_device(kv, layer, n_heads, dq, dk, dv, bf, bf, t, pos0, dqg, dkg, theta, eps, dout, s));
     if (mem == BEBELM_MEM_HOST) return stage_out(P, dout, out, 4 * qn, s);
     return 0;
 }
@@ -1716,6 +1736,198 @@ int bebelm_dequantize(int dtype, const void* data, size_t n_elements, float* out
     TRY(stage_in(P, st, 1, 4 * n_elements, &o, s));
     CUDA_TRY(launch_dequantize(dtype, static_cast<const uint8_t*>(a0), n_elements, static_cast<float*>(o), s));
     return stage_out(P, o, out, 4 * n_elements, s);
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------------------
+// The whole attention operator of a layer: projections + the fused step / prefill + output
+// projection, on device-resident GGML weights (src/model.rs:430-455 attn_step, 224-258
+// attn_batch).
+// ---------------------------------------------------------------------------
+struct bebelm_attn_weights {
+    int device = 0, n_heads = 0, n_kv = 0;
+    size_t hidden = 0;
+    int dt[4] = {0, 0, 0, 0};  // q, k, v, o
+    DevBuf w[4], gains;        // gains: q_gain[64] then k_gain[64]
+};
+
+namespace {
+
+// Q8 activations of x [t][n_in] in the pool's scratch (for K-quant weights)
+struct Q8View {
+    int8_t* q = nullptr;
+    float* sc = nullptr;
+    int* sm = nullptr;
+};
+
+int quantize_into_scratch(bebelm_kv_pool* P, const float* x, size_t n_in, size_t t, Q8View* v, cudaStream_t s) {
+    const size_t xn = n_in * t, qb = (xn + 255) & ~size_t(255), sb = (4 * (xn / 256) + 255) & ~size_t(255);
+    TRY(P->q8.ensure(qb + sb + 4 * (xn / 32) + 256, false, s));
+    v->q = P->q8.as<int8_t>();
+    v->sc = reinterpret_cast<float*>(P->q8.as<char>() + qb);
+    v->sm = reinterpret_cast<int*>(P->q8.as<char>() + qb + sb);
+    CUDA_TRY(launch_quantize_q8(x, n_in, t, v->q, v->sc, v->sm, s));
+    return 0;
+}
+
+bool is_kquant(int dt) { return dt == kGgmlQ4K || dt == kGgmlQ6K; }
+
+// y = W x for the weights of one projection; x already quantized in q8 when needed
+int project(const bebelm_attn_weights* W, int which, size_t n_in, size_t n_out, const float* x, size_t t,
+            const Q8View& q8, float* y, cudaStream_t s) {
+    CUDA_TRY(launch_qmatmul(W->dt[which], W->w[which].as<uint8_t>(), n_in, n_out, x, t, q8.q, q8.sc, q8.sm, y, s));
+    return 0;
+}
+
+int check_weights(const bebelm_kv* kv, const bebelm_attn_weights* W) {
+    if (!W) return fail(BEBELM_ERR_INVALID, "null weights");
+    if (W->device != kv->pool->device) return fail(BEBELM_ERR_INVALID, "weights and cache are on different devices");
+    if (W->n_kv != kv->pool->n_kv)
+        return fail(BEBELM_ERR_INVALID, "weights have %d kv heads, the cache %d", W->n_kv, kv->pool->n_kv);
+    return 0;
+}
+
+// x [t][hidden] (device) -> q [t][nq], k/v [t][nkv] into the pool's projection scratch
+int project_qkv(bebelm_kv_pool* P, const bebelm_attn_weights* W, const float* dx, size_t t, float** q, float** k,
+                float** v, float** attn, cudaStream_t s) {
+    const size_t nq = (size_t)W->n_heads * kHeadDim, nkv = (size_t)W->n_kv * kHeadDim;
+    TRY(P->proj.ensure(4 * t * (2 * nq + 2 * nkv) + 1024, false, s));
+    *q = P->proj.as<float>();
+    *k = *q + t * nq;
+    *v = *k + t * nkv;
+    *attn = *v + t * nkv;
+    Q8View q8;
+    if (is_kquant(W->dt[0]) || is_kquant(W->dt[1]) || is_kquant(W->dt[2]))
+        TRY(quantize_into_scratch(P, dx, W->hidden, t, &q8, s));
+    TRY(project(W, 0, W->hidden, nq, dx, t, q8, *q, s));
+    TRY(project(W, 1, W->hidden, nkv, dx, t, q8, *k, s));
+    TRY(project(W, 2, W->hidden, nkv, dx, t, q8, *v, s));
+    return 0;
+}
+
+int project_out(bebelm_kv_pool* P, const bebelm_attn_weights* W, const float* attn, size_t t, float* dout,
+                cudaStream_t s) {
+    const size_t nq = (size_t)W->n_heads * kHeadDim;
+    Q8View q8;
+    if (is_kquant(W->dt[3])) TRY(quantize_into_scratch(P, attn, nq, t, &q8, s));
+    return project(W, 3, nq, W->hidden, attn, t, q8, dout, s);
+}
+
+}  // namespace
+
+extern "C" {
+
+int bebelm_attn_weights_create(int device, int n_heads, int n_kv_heads, size_t hidden, int dtype_q, const void* wq,
+                               int dtype_k, const void* wk, int dtype_v, const void* wv, int dtype_o, const void* wo,
+                               const float* q_gain, const float* k_gain, bebelm_attn_weights** out) {
+    if (!out) return fail(BEBELM_ERR_INVALID, "out is null");
+    *out = nullptr;
+    TRY(check_geometry(n_heads, n_kv_heads));
+    if (!wq || !wk || !wv || !wo || !q_gain || !k_gain) return fail(BEBELM_ERR_INVALID, "null buffer");
+    const size_t nq = (size_t)n_heads * kHeadDim, nkv = (size_t)n_kv_heads * kHeadDim;
+    const int dts[4] = {dtype_q, dtype_k, dtype_v, dtype_o};
+    const size_t n_in[4] = {hidden, hidden, hidden, nq}, n_out[4] = {nq, nkv, nkv, hidden};
+    for (int i = 0; i < 4; ++i) TRY(check_ggml(dts[i], n_in[i]));
+    int n_dev = 0;
+    CUDA_TRY(cudaGetDeviceCount(&n_dev));
+    if (device < 0 || device >= n_dev) return fail(BEBELM_ERR_INVALID, "device %d not present", device);
+    DeviceGuard g(device);
+    auto* W = new bebelm_attn_weights();
+    W->device = device;
+    W->n_heads = n_heads;
+    W->n_kv = n_kv_heads;
+    W->hidden = hidden;
+    const void* src[4] = {wq, wk, wv, wo};
+    int rc = 0;
+    for (int i = 0; i < 4 && !rc; ++i) {
+        W->dt[i] = dts[i];
+        const size_t bytes = ggml_row_bytes(dts[i], n_in[i]) * n_out[i];
+        rc = W->w[i].ensure(bytes);
+        if (!rc && cudaMemcpy(W->w[i].p, src[i], bytes, cudaMemcpyHostToDevice) != cudaSuccess)
+            rc = fail(BEBELM_ERR_CUDA, "uploading weight %d failed", i);
+    }
+    if (!rc) rc = W->gains.ensure(2 * 64 * sizeof(float));
+    if (!rc && (cudaMemcpy(W->gains.p, q_gain, 64 * sizeof(float), cudaMemcpyHostToDevice) != cudaSuccess ||
+                cudaMemcpy(W->gains.as<float>() + 64, k_gain, 64 * sizeof(float), cudaMemcpyHostToDevice) != cudaSuccess))
+        rc = fail(BEBELM_ERR_CUDA, "uploading the norm gains failed");
+    if (rc) {
+        for (auto& b : W->w) b.release();
+        W->gains.release();
+        delete W;
+        return rc;
+    }
+    *out = W;
+    return 0;
+}
+
+int bebelm_attn_weights_destroy(bebelm_attn_weights* W) {
+    if (!W) return 0;
+    DeviceGuard g(W->device);
+    cudaDeviceSynchronize();
+    for (auto& b : W->w) b.release();
+    W->gains.release();
+    delete W;
+    return 0;
+}
+
+int bebelm_attn_layer_step(bebelm_kv* kv, int layer, const bebelm_attn_weights* W, const float* x, size_t pos,
+                           float theta, float eps, float* out, int mem, void* stream) {
+    TRY(validate_layer(kv, layer));
+    TRY(check_mem(mem));
+    TRY(check_weights(kv, W));
+    if (!x || !out) return fail(BEBELM_ERR_INVALID, "null buffer");
+    bebelm_kv_pool* P = kv->pool;
+    DeviceGuard g(P->device);
+    cudaStream_t s = as_stream(stream);
+    const float* dx = x;
+    float* dout = out;
+    if (mem == BEBELM_MEM_HOST) {
+        void *a0, *o;
+        Stage st[1] = {{x, 4 * W->hidden, &a0}};
+        TRY(stage_in(P, st, 1, 4 * W->hidden, &o, s));
+        dx = static_cast<const float*>(a0);
+        dout = static_cast<float*>(o);
+    }
+    float *q, *k, *v, *attn;
+    TRY(project_qkv(P, W, dx, 1, &q, &k, &v, &attn, s));
+    long long slot0 = 0;
+    TRY(reserve(kv, layer, 1, &slot0, s));
+    const FusedStep fs{q, k, v, W->gains.as<float>(), W->gains.as<float>() + 64, theta_scale_of(theta, kHeadDim), eps};
+    std::vector<Window> w{{kv, kv->base[layer], kv->len[layer], slot0, (long long)pos}};
+    TRY(run_decode(P, w, layer, W->n_heads, nullptr, attn, 0.125f, &fs, s));
+    TRY(project_out(P, W, attn, 1, dout, s));
+    if (mem == BEBELM_MEM_HOST) return stage_out(P, dout, out, 4 * W->hidden, s);
+    return 0;
+}
+
+int bebelm_attn_layer_batch(bebelm_kv* kv, int layer, const bebelm_attn_weights* W, const float* x, size_t t,
+                            size_t pos0, int tensor_cores, float theta, float eps, float* out, int mem, void* stream) {
+    TRY(validate_layer(kv, layer));
+    TRY(check_mem(mem));
+    TRY(check_weights(kv, W));
+    if (t == 0) return 0;
+    if (!x || !out) return fail(BEBELM_ERR_INVALID, "null buffer");
+    bebelm_kv_pool* P = kv->pool;
+    DeviceGuard g(P->device);
+    cudaStream_t s = as_stream(stream);
+    const size_t xn = t * W->hidden;
+    const float* dx = x;
+    float* dout = out;
+    if (mem == BEBELM_MEM_HOST) {
+        void *a0, *o;
+        Stage st[1] = {{x, 4 * xn, &a0}};
+        TRY(stage_in(P, st, 1, 4 * xn, &o, s));
+        dx = static_cast<const float*>(a0);
+        dout = static_cast<float*>(o);
+    }
+    float *q, *k, *v, *attn;
+    TRY(project_qkv(P, W, dx, t, &q, &k, &v, &attn, s));
+    TRY(prefill_device(kv, layer, W->n_heads, q, k, v, false, tensor_cores != 0, t, pos0, W->gains.as<float>(),
+                       W->gains.as<float>() + 64, theta, eps, attn, s));
+    TRY(project_out(P, W, attn, t, dout, s));
+    if (mem == BEBELM_MEM_HOST) return stage_out(P, dout, out, 4 * xn, s);
+    return 0;
 }
 
 }  // extern "C"

@@ -213,6 +213,30 @@ BEBELM_API int bebelm_matmul(int dtype, const void* w, size_t n_in, size_t n_out
 BEBELM_API int bebelm_dequantize(int dtype, const void* data, size_t n_elements, float* out, int mem,
                                  void* stream);
 
+/* The whole attention operator of a layer on device-resident weights. The weights are the
+ * layer's GGUF tensors as stored (attn_q [n_heads*64][hidden], attn_k / attn_v
+ * [n_kv*64][hidden], attn_output [hidden][n_heads*64], each a GGML dtype above) plus the
+ * q/k norm gains [64]; create copies them to `device` once (host pointers). */
+typedef struct bebelm_attn_weights bebelm_attn_weights;
+BEBELM_API int bebelm_attn_weights_create(int device, int n_heads, int n_kv_heads, size_t hidden,
+                                          int dtype_q, const void* wq, int dtype_k, const void* wk,
+                                          int dtype_v, const void* wv, int dtype_o, const void* wo,
+                                          const float* q_gain, const float* k_gain,
+                                          bebelm_attn_weights** out);
+BEBELM_API int bebelm_attn_weights_destroy(bebelm_attn_weights* w);
+/* `attn_step(layer, x, pos, cache)` (src/model.rs:430-455) whole: q/k/v = W x (matvec),
+ * norm + RoPE, append, attention over the window, out = W_o attn. x, out [hidden]. */
+BEBELM_API int bebelm_attn_layer_step(bebelm_kv* kv, int layer, const bebelm_attn_weights* w,
+                                      const float* x, size_t pos, float theta, float eps, float* out,
+                                      int mem, void* stream);
+/* `attn_batch(layer, x, pos0, t, cache)` (src/model.rs:224-258) whole: the projections over
+ * t tokens (matmul), then the causal prefill of the chunk, then W_o. x, out [t][hidden].
+ * tensor_cores 1: attention on the tensor cores (bf16 operands, within 2e-2 relative);
+ * 0: the reference's fp32 arithmetic (within 1e-3). */
+BEBELM_API int bebelm_attn_layer_batch(bebelm_kv* kv, int layer, const bebelm_attn_weights* w,
+                                       const float* x, size_t t, size_t pos0, int tensor_cores,
+                                       float theta, float eps, float* out, int mem, void* stream);
+
 /* ---------------------------------------------------- step plans (graphs) --- */
 /* No counterpart in the reference. Device-driven decode steps, for a token loop captured
  * once in a CUDA graph and replayed: the host work of bebelm_attn_step (slot bookkeeping,
