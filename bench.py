@@ -286,7 +286,8 @@ def run_ours(args):
     # -- secondary: config 2 causal prefill (2048 tokens, bf16 inputs)
     prefill = None
     if rank == 0 and not args.no_prefill:
-        prefill = {"config2_2048": bench_prefill(bb, torch, dev, stream, bf16_peak, peak_kind, 2048, 6),
+        prefill = {"attn_layer": bench_attn_layer(bb, torch, dev, stream),
+                   "config2_2048": bench_prefill(bb, torch, dev, stream, bf16_peak, peak_kind, 2048, 6),
                    "config5_8192_one_layer": bench_prefill(bb, torch, dev, stream, bf16_peak, peak_kind, 8192, 2)}
 
     c3bf = bench_config3_bf16(bb, torch, dev, stream, world, args.steps)
@@ -384,6 +385,57 @@ def bench_prefill(bb, torch, dev, stream, bf16_peak, peak_kind, T=2048, reps=6):
             "ms": round(ms, 4), "value": round(tf, 3), "unit": "TFLOP/s",
             "roofline": {"bound": "tensor", "achieved": round(tf, 3), "peak": bf16_peak, "unit": "TFLOP/s",
                          "frac": round(tf / bf16_peak, 4), "peak_kind": peak_kind}}
+
+
+def bench_attn_layer(bb, torch, dev, stream, T=2048, steps=64):
+    """The whole attention operator of a layer (src/model.rs attn_batch / attn_step) on
+    device-resident GGML weights (synthetic Q4_K q/k/o and Q6_K v, the usual Q4_K_M mix): a
+    T-token chunk into an empty cache (projections over T tokens, tensor-core prefill, output
+    projection), then `steps` one-token steps on that window."""
+    import numpy as np
+    rng = np.random.default_rng(5)
+
+    def qk(rows, n_in, six=False):
+        bb_ = 210 if six else 144
+        w = rng.integers(0, 256, size=(rows, n_in // 256, bb_), dtype=np.uint8)
+        d = (rng.standard_normal((rows, n_in // 256)) * (0.002 if six else 0.01)).astype(np.float16)
+        w[:, :, (208 if six else 0):(210 if six else 2)] = d.view(np.uint8).reshape(rows, -1, 2)
+        if not six:
+            w[:, :, 2:4] = (np.abs(rng.standard_normal((rows, n_in // 256))) * 0.005).astype(
+                np.float16).view(np.uint8).reshape(rows, -1, 2)
+        return w.reshape(-1)
+
+    qg = (1 + 0.02 * rng.standard_normal(D)).astype(np.float32)
+    kg = (1 + 0.02 * rng.standard_normal(D)).astype(np.float32)
+    W = bb.AttnWeights((bb.GGML_Q4_K, qk(HID, HID)), (bb.GGML_Q4_K, qk(KVD, HID)), (bb.GGML_Q6_K, qk(KVD, HID, True)),
+                       (bb.GGML_Q4_K, qk(HID, HID)), qg, kg, device=dev.index)
+    g = torch.Generator(device=dev)
+    g.manual_seed(8)
+    x = 0.5 * torch.randn((T, HID), generator=g, device=dev)
+    xs = 0.5 * torch.randn((steps, HID), generator=g, device=dev)
+    out = torch.empty((T, HID), device=dev)
+    o1 = torch.empty(HID, device=dev)
+    caches = [bb.Cache(n_layers=1, max_context=T + steps + 64, device=dev.index) for _ in range(2)]
+    e = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+    for rep, c in enumerate(caches):  # the first is the warm-up
+        torch.cuda.synchronize()
+        e[0].record(stream)
+        bb.attn_layer_batch(c, 0, W, x, 0, tensor_cores=True, theta=THETA, out=out, stream=stream)
+        e[1].record(stream)
+        for s_ in range(steps):
+            bb.attn_layer_step(c, 0, W, xs[s_], T + s_, theta=THETA, out=o1, stream=stream)
+        e[2].record(stream)
+        torch.cuda.synchronize()
+    batch_ms, step_ms = e[0].elapsed_time(e[1]), e[1].elapsed_time(e[2]) / steps
+    for c in caches:
+        c.close()
+    W.close()
+    proj_macs = (2 * HID * HID + 2 * KVD * HID) * T
+    return {"workload": f"attention operator of one layer: {T}-token chunk (Q4_K/Q6_K projections + tensor-core "
+                        f"prefill + output projection), then {steps} single-token steps",
+            "batch_ms": round(batch_ms, 3), "batch_tok_per_s": round(T / (batch_ms * 1e-3), 1),
+            "projection_tmacs_per_s_upper_bound": round(proj_macs / (batch_ms * 1e-3) / 1e12, 2),
+            "step_ms": round(step_ms, 4), "step_tok_per_s": round(1 / (step_ms * 1e-3), 1)}
 
 
 def bench_config3_bf16(bb, torch, dev, stream, world, steps):
