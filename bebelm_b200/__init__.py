@@ -43,6 +43,7 @@ EXPORTS = [
     "bebelm_attn_step_allgather", "bebelm_step_plan_create", "bebelm_step_plan_launch", "bebelm_step_plan_steps",
     "bebelm_step_plan_finish", "bebelm_matvec", "bebelm_matmul", "bebelm_dequantize",
     "bebelm_attn_weights_create", "bebelm_attn_weights_destroy", "bebelm_attn_layer_step", "bebelm_attn_layer_batch",
+    "bebelm_step_plan_create_layer", "bebelm_step_plan_launch_layer",
 ]
 GGML_F32, GGML_F16, GGML_Q4_K, GGML_Q6_K = 0, 1, 12, 14
 IPC_HANDLE_BYTES = 64
@@ -109,6 +110,8 @@ def load_library(path: str = LIB_PATH):
         "bebelm_attn_weights_destroy": ([vp], i),
         "bebelm_attn_layer_step": ([vp, i, vp, vp, sz, f, f, vp, i, vp], i),
         "bebelm_attn_layer_batch": ([vp, i, vp, vp, sz, sz, i, f, f, vp, i, vp], i),
+        "bebelm_step_plan_create_layer": ([vp, i, vp, sz, C.POINTER(vp)], i),
+        "bebelm_step_plan_launch_layer": ([vp, vp, f, f, vp, vp], i),
     }
     for name, (args, res) in sig.items():
         fn = getattr(L, name)
@@ -520,10 +523,25 @@ class StepPlan:
     replays advance the sequence. Device tensors only. :meth:`finish` writes the steps back
     into the cache; until then other calls on the cache are refused."""
 
-    def __init__(self, cache: "Cache", layer: int, n_heads: int = N_HEADS, window: int = 0):
-        self.cache, self.layer, self.n_heads = cache, layer, n_heads
+    def __init__(self, cache: "Cache", layer: int, n_heads: int = N_HEADS, window: int = 0,
+                 weights: "AttnWeights | None" = None):
+        """With ``weights`` the plan is the whole operator (:meth:`launch_layer`)."""
+        self.cache, self.layer, self.n_heads, self.weights = cache, layer, n_heads, weights
         self._h = C.c_void_p()
-        _check(load_library().bebelm_step_plan_create(cache._h, layer, n_heads, window, C.byref(self._h)))
+        if weights is None:
+            _check(load_library().bebelm_step_plan_create(cache._h, layer, n_heads, window, C.byref(self._h)))
+        else:
+            _check(load_library().bebelm_step_plan_create_layer(cache._h, layer, weights._h, window,
+                                                                C.byref(self._h)))
+
+    def launch_layer(self, x, out, theta: float = ROPE_THETA, eps: float = RMS_EPS, stream=None):
+        """One token through the whole operator: x [hidden] -> out [hidden] (CUDA tensors)."""
+        for t in (x, out):
+            if not (_is_torch(t) and t.is_cuda and t.is_contiguous()):
+                raise ValueError("step plans take contiguous CUDA tensors")
+        _check(load_library().bebelm_step_plan_launch_layer(self._h, x.data_ptr(), theta, eps, out.data_ptr(),
+                                                            _stream_ptr(stream)))
+        return out
 
     def launch(self, q, k, v, q_gain, k_gain, out, theta: float = ROPE_THETA, eps: float = RMS_EPS, stream=None):
         for x in (q, k, v, q_gain, k_gain, out):

@@ -1475,6 +1475,9 @@ struct bebelm_step_plan {
     long long slot0 = 0, pos0 = 0, len0 = 0, window = 0;
     int n_splits = 0, per = 0, hpc = 0, n_sub = 0;
     DevBuf state, part, counters;  // StepState, split partials, combine counters
+    // whole-operator plans: the layer's weights and the scratch of its projections
+    const bebelm_attn_weights* W = nullptr;
+    DevBuf lbuf;  // q, k, v, attention output (f32), then Q8 activations (quants, scales, sums)
 };
 
 extern "C" {
@@ -1646,6 +1649,7 @@ int bebelm_step_plan_finish(bebelm_step_plan* pl, void* stream) {
         pl->state.release();
         pl->part.release();
         pl->counters.release();
+        pl->lbuf.release();
     }
     kv->plans--;
     delete pl;
@@ -1928,6 +1932,93 @@ int bebelm_attn_layer_batch(bebelm_kv* kv, int layer, const bebelm_attn_weights*
     TRY(project_out(P, W, attn, t, dout, s));
     if (mem == BEBELM_MEM_HOST) return stage_out(P, dout, out, 4 * xn, s);
     return 0;
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Whole-operator step plans: a plan's decode wrapped in the layer's projections, all on
+// scratch the plan owns, so a token's attention layers can be captured in one graph.
+// ---------------------------------------------------------------------------
+namespace {
+
+struct LayerScratch {
+    float *q, *k, *v, *attn;
+    int8_t* q8;
+    float* q8s;
+    int* q8m;
+};
+
+LayerScratch layer_scratch(const bebelm_step_plan* pl) {
+    const bebelm_attn_weights* W = pl->W;
+    const size_t nq = (size_t)W->n_heads * kHeadDim, nkv = (size_t)W->n_kv * kHeadDim;
+    const size_t nx = std::max(W->hidden, nq);
+    LayerScratch L;
+    L.q = pl->lbuf.as<float>();
+    L.k = L.q + nq;
+    L.v = L.k + nkv;
+    L.attn = L.v + nkv;
+    char* b = reinterpret_cast<char*>(L.attn + nq);
+    L.q8 = reinterpret_cast<int8_t*>(b);
+    L.q8s = reinterpret_cast<float*>(b + ((nx + 255) & ~size_t(255)));
+    L.q8m = reinterpret_cast<int*>(b + ((nx + 255) & ~size_t(255)) + ((4 * (nx / 256) + 255) & ~size_t(255)));
+    return L;
+}
+
+size_t layer_scratch_bytes(const bebelm_attn_weights* W) {
+    const size_t nq = (size_t)W->n_heads * kHeadDim, nkv = (size_t)W->n_kv * kHeadDim;
+    const size_t nx = std::max(W->hidden, nq);
+    return 4 * (2 * nq + 2 * nkv) + ((nx + 255) & ~size_t(255)) + ((4 * (nx / 256) + 255) & ~size_t(255)) +
+           4 * (nx / 32) + 256;
+}
+
+}  // namespace
+
+extern "C" {
+
+int bebelm_step_plan_create_layer(bebelm_kv* kv, int layer, const bebelm_attn_weights* w, size_t window,
+                                  bebelm_step_plan** out) {
+    if (!out) return fail(BEBELM_ERR_INVALID, "out is null");
+    *out = nullptr;
+    if (!kv || !kv->pool) return fail(BEBELM_ERR_INVALID, "null cache handle");
+    TRY(check_weights(kv, w));
+    TRY(bebelm_step_plan_create(kv, layer, w->n_heads, window, out));
+    bebelm_step_plan* pl = *out;
+    pl->W = w;
+    int rc;
+    {
+        DeviceGuard g(kv->pool->device);
+        rc = pl->lbuf.ensure(layer_scratch_bytes(w), true);
+        if (!rc && cudaDeviceSynchronize() != cudaSuccess) rc = fail(BEBELM_ERR_CUDA, "step plan scratch failed");
+    }
+    if (rc) {
+        bebelm_step_plan_finish(pl, nullptr);
+        *out = nullptr;
+        return rc;
+    }
+    return 0;
+}
+
+int bebelm_step_plan_launch_layer(bebelm_step_plan* pl, const float* x, float theta, float eps, float* out,
+                                  void* stream) {
+    if (!pl || !pl->kv) return fail(BEBELM_ERR_INVALID, "null step plan");
+    if (!pl->W) return fail(BEBELM_ERR_INVALID, "the plan was not created with layer weights");
+    if (!x || !out) return fail(BEBELM_ERR_INVALID, "null buffer");
+    const bebelm_attn_weights* W = pl->W;
+    DeviceGuard g(pl->kv->pool->device);
+    cudaStream_t s = as_stream(stream);
+    const size_t nq = (size_t)W->n_heads * kHeadDim, nkv = (size_t)W->n_kv * kHeadDim;
+    const LayerScratch L = layer_scratch(pl);
+    const Q8View q8{L.q8, L.q8s, L.q8m};
+    if (is_kquant(W->dt[0]) || is_kquant(W->dt[1]) || is_kquant(W->dt[2]))
+        CUDA_TRY(launch_quantize_q8(x, W->hidden, 1, L.q8, L.q8s, L.q8m, s));
+    TRY(project(W, 0, W->hidden, nq, x, 1, q8, L.q, s));
+    TRY(project(W, 1, W->hidden, nkv, x, 1, q8, L.k, s));
+    TRY(project(W, 2, W->hidden, nkv, x, 1, q8, L.v, s));
+    TRY(bebelm_step_plan_launch(pl, L.q, L.k, L.v, W->gains.as<float>(), W->gains.as<float>() + 64, theta, eps,
+                                L.attn, stream));
+    if (is_kquant(W->dt[3])) CUDA_TRY(launch_quantize_q8(L.attn, nq, 1, L.q8, L.q8s, L.q8m, s));
+    return project(W, 3, nq, W->hidden, L.attn, 1, q8, out, s);
 }
 
 }  // extern "C"

@@ -95,59 +95,111 @@ __global__ void __launch_bounds__(256) quantize_q8_kernel(const float* x, size_t
     if (lane == 0) scales[blk] = __fdiv_rn(amax, 127.0f);
 }
 
-// Q4_K block (144 B: d, dmin, scales[12], qs[128]) against its 256 int8 activations.
-// Lane l holds qs bytes 4l..4l+3: chunk c = l/8 (sub-blocks 2c: low nibbles, 2c+1: high).
-__device__ __forceinline__ float block_q4k(const uint8_t* blk, const int8_t* qx, float sx, const int* sums,
-                                           int lane) {
+// One 256-weight block for one warp, split into the loads and the arithmetic so the one-token
+// kernel can issue several blocks' loads before using any.
+// Q4_K block (144 B: d, dmin, scales[12], qs[128]): lane l holds qs bytes 4l..4l+3, chunk
+// c = l/8 (sub-blocks 2c: low nibbles, 2c+1: high).
+struct Q4Ld {
+    uint4 head;  // d, dmin, scales[12]
+    uint32_t w;
+    int xlo, xhi, sum;
+    float sx;
+};
+__device__ __forceinline__ Q4Ld load_q4k(const uint8_t* blk, const int8_t* qx, float sx, const int* sums, int lane) {
     const int c = lane >> 3, p = (lane & 7) * 4;
-    const uint32_t w = *reinterpret_cast<const uint32_t*>(blk + 16 + c * 32 + p);
-    const int xlo = *reinterpret_cast<const int*>(qx + (2 * c) * 32 + p);
-    const int xhi = *reinterpret_cast<const int*>(qx + (2 * c + 1) * 32 + p);
+    Q4Ld L;
+    L.head = *reinterpret_cast<const uint4*>(blk);
+    L.w = *reinterpret_cast<const uint32_t*>(blk + 16 + c * 32 + p);
+    L.xlo = *reinterpret_cast<const int*>(qx + (2 * c) * 32 + p);
+    L.xhi = *reinterpret_cast<const int*>(qx + (2 * c + 1) * 32 + p);
+    L.sum = lane < 8 ? sums[lane] : 0;
+    L.sx = sx;
+    return L;
+}
+// byte j of the 16-byte block head
+__device__ __forceinline__ int head_byte(const uint4& h, int j) {
+    const uint32_t w = j < 4 ? h.x : j < 8 ? h.y : j < 12 ? h.z : h.w;
+    return (int)((w >> (8 * (j & 3))) & 0xffu);
+}
+// get_scale_min_k4 on the scales held in the head's bytes 4..15
+__device__ __forceinline__ void scale_min_head(int j, const uint4& h, int& sc, int& m) {
+    if (j < 4) {
+        sc = head_byte(h, 4 + j) & 63;
+        m = head_byte(h, 8 + j) & 63;
+    } else {
+        sc = (head_byte(h, 8 + j) & 0x0f) | ((head_byte(h, j) >> 6) << 4);
+        m = (head_byte(h, 8 + j) >> 4) | ((head_byte(h, 4 + j) >> 6) << 4);
+    }
+}
+__device__ __forceinline__ float dot_q4k(const Q4Ld& L, int lane) {
+    const int c = lane >> 3;
     int sc0, m0, sc1, m1;
-    scale_min_k4(2 * c, blk + 4, sc0, m0);
-    scale_min_k4(2 * c + 1, blk + 4, sc1, m1);
-    int sd = sc0 * __dp4a((int)(w & 0x0f0f0f0fu), xlo, 0) + sc1 * __dp4a((int)((w >> 4) & 0x0f0f0f0fu), xhi, 0);
+    scale_min_head(2 * c, L.head, sc0, m0);
+    scale_min_head(2 * c + 1, L.head, sc1, m1);
+    int sd = sc0 * __dp4a((int)(L.w & 0x0f0f0f0fu), L.xlo, 0) + sc1 * __dp4a((int)((L.w >> 4) & 0x0f0f0f0fu), L.xhi, 0);
     int sm = 0;
     if (lane < 8) {
         int scj, mj;
-        scale_min_k4(lane, blk + 4, scj, mj);
-        sm = mj * sums[lane];
+        scale_min_head(lane, L.head, scj, mj);
+        sm = mj * L.sum;
     }
     sd = warp_sum_i32(sd);
     sm = warp_sum_i32(sm);
-    const float d = ld_f16(blk), dmin = ld_f16(blk + 2);
-    return __fmul_rn(sx, __fsub_rn(__fmul_rn(d, __int2float_rn(sd)), __fmul_rn(dmin, __int2float_rn(sm))));
+    const float d = f16_bits_to_f32(L.head.x & 0xffffu), dmin = f16_bits_to_f32(L.head.x >> 16);
+    return __fmul_rn(L.sx, __fsub_rn(__fmul_rn(d, __int2float_rn(sd)), __fmul_rn(dmin, __int2float_rn(sm))));
 }
 
-// Q6_K block (210 B: ql[128], qh[64], scales[16] i8, d). Lane l holds 8 weights of the
-// 16-wide sub-block k = l/2: its low 4 bits from ql (low or high nibble), its top 2 from qh.
-__device__ __forceinline__ float block_q6k(const uint8_t* blk, const int8_t* qx, float sx, int lane) {
+// Q6_K block (210 B: ql[128], qh[64], scales[16] i8, d): lane l holds 8 weights of the
+// 16-wide sub-block k = l/2, the low 4 bits from ql (low or high nibble), the top 2 from qh.
+struct Q6Ld {
+    uint32_t ql[2], qh[2];  // 8 bytes each, little-endian
+    int x0, x1, sc;
+    uint32_t dbits;
+    float sx;
+};
+__device__ __forceinline__ Q6Ld load_q6k(const uint8_t* blk, const int8_t* qx, float sx, int lane) {
     const int k = lane >> 1, h = lane & 1;
     const int n = k >> 3, g = (k & 7) >> 1, sub = k & 1;
-    const int ql_off = n * 64 + (g & 1) * 32 + sub * 16 + h * 8;  // groups 0,2 read ql[0..32), 1,3 ql[32..64)
+    const int ql_off = n * 64 + (g & 1) * 32 + sub * 16 + h * 8, qh_off = 128 + n * 32 + sub * 16 + h * 8;
+    Q6Ld L;
+#pragma unroll
+    for (int part = 0; part < 2; ++part) {
+        uint32_t a = 0, b = 0;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            a |= (uint32_t)blk[ql_off + 4 * part + i] << (8 * i);
+            b |= (uint32_t)blk[qh_off + 4 * part + i] << (8 * i);
+        }
+        L.ql[part] = a;
+        L.qh[part] = b;
+    }
+    const int8_t* x = qx + k * 16 + h * 8;
+    L.x0 = *reinterpret_cast<const int*>(x);
+    L.x1 = *reinterpret_cast<const int*>(x + 4);
+    L.sc = (int)(int8_t)blk[192 + k];
+    L.dbits = (uint32_t)blk[208] | ((uint32_t)blk[209] << 8);
+    L.sx = sx;
+    return L;
+}
+__device__ __forceinline__ float dot_q6k(const Q6Ld& L, int lane) {
+    const int k = lane >> 1, g = (k & 7) >> 1;
     const bool high = g >= 2;
     const int shift = 2 * g;
-    const int qh_off = 128 + n * 32 + sub * 16 + h * 8;
     uint32_t wq[2];
 #pragma unroll
     for (int part = 0; part < 2; ++part) {
         uint32_t word = 0;
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-            const uint32_t l = blk[ql_off + part * 4 + i];
-            const uint32_t hb = (blk[qh_off + part * 4 + i] >> shift) & 3u;
-            const uint32_t q = ((high ? (l >> 4) : (l & 0x0fu)) | (hb << 4)) - 32u;  // -32..31 as a byte
-            word |= (q & 0xffu) << (8 * i);
+            const uint32_t l = (L.ql[part] >> (8 * i)) & 0xffu, hb = ((L.qh[part] >> (8 * i)) >> shift) & 3u;
+            word |= ((((high ? (l >> 4) : (l & 0x0fu)) | (hb << 4)) - 32u) & 0xffu) << (8 * i);
         }
         wq[part] = word;
     }
-    const int8_t* x = qx + k * 16 + h * 8;
-    int t = __dp4a((int)wq[0], *reinterpret_cast<const int*>(x), 0);
-    t = __dp4a((int)wq[1], *reinterpret_cast<const int*>(x + 4), t);
-    int s = t * (int)(int8_t)blk[192 + k];
-    s = warp_sum_i32(s);
-    const float d = ld_f16(blk + 208);
-    return __fmul_rn(sx, __fmul_rn(d, __int2float_rn(s)));
+    int t = __dp4a((int)wq[0], L.x0, 0);
+    t = __dp4a((int)wq[1], L.x1, t);
+    const int s = warp_sum_i32(t * L.sc);
+    return __fmul_rn(L.sx, __fmul_rn(f16_bits_to_f32(L.dbits), __int2float_rn(s)));
 }
 
 // F32/F16 weight row against fp32 x: the reference's `dot` (see the file header).
@@ -187,10 +239,29 @@ __global__ void __launch_bounds__(256) qmatmul_kernel(const uint8_t* w, size_t r
         const int8_t* qx = q8 + t * n_in;
         const float* sx = q8_scales + t * nb;
         acc = -0.0f;  // an f32 iterator sum over the blocks, in order
-        for (size_t b = 0; b < nb; ++b) {
-            const float v = DT == kGgmlQ4K ? block_q4k(row + b * 144, qx + b * kQK, sx[b], q8_sums + (t * nb + b) * 8, lane)
-                                           : block_q6k(row + b * 210, qx + b * kQK, sx[b], lane);
-            acc = __fadd_rn(acc, v);
+        // up to 8 blocks' loads are issued before any of them is used, so a row costs one
+        // memory round trip per 8 blocks instead of one per block
+        constexpr int kU = 8;
+        for (size_t b0 = 0; b0 < nb; b0 += kU) {
+            if (DT == kGgmlQ4K) {
+                Q4Ld L[kU];
+#pragma unroll
+                for (int u = 0; u < kU; ++u)
+                    if (b0 + u < nb)
+                        L[u] = load_q4k(row + (b0 + u) * 144, qx + (b0 + u) * kQK, sx[b0 + u],
+                                        q8_sums + (t * nb + b0 + u) * 8, lane);
+#pragma unroll
+                for (int u = 0; u < kU; ++u)
+                    if (b0 + u < nb) acc = __fadd_rn(acc, dot_q4k(L[u], lane));
+            } else {
+                Q6Ld L[kU];
+#pragma unroll
+                for (int u = 0; u < kU; ++u)
+                    if (b0 + u < nb) L[u] = load_q6k(row + (b0 + u) * 210, qx + (b0 + u) * kQK, sx[b0 + u], lane);
+#pragma unroll
+                for (int u = 0; u < kU; ++u)
+                    if (b0 + u < nb) acc = __fadd_rn(acc, dot_q6k(L[u], lane));
+            }
         }
     } else {
         acc = row_dot<DT>(row, x + t * n_in, n_in, lane);

@@ -417,8 +417,8 @@ def bench_attn_layer(bb, torch, dev, stream, T=2048, steps=64):
     o1 = torch.empty(HID, device=dev)
     # both caches draw from one pool: the warm-up call sizes the pool's scratch, so the timed
     # call allocates nothing
-    pool = bb.Pool(n_layers=1, n_pages=2 * ((T + steps) // 64 + 4), device=dev.index)
-    caches = [bb.Cache(max_context=T + steps + 64, pool=pool) for _ in range(2)]
+    pool = bb.Pool(n_layers=1, n_pages=2 * ((T + 3 * steps) // 64 + 4), device=dev.index)
+    caches = [bb.Cache(max_context=T + 3 * steps + 64, pool=pool) for _ in range(2)]
     e = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
     for rep, c in enumerate(caches):  # the first is the warm-up
         torch.cuda.synchronize()
@@ -430,6 +430,24 @@ def bench_attn_layer(bb, torch, dev, stream, T=2048, steps=64):
         e[2].record(stream)
         torch.cuda.synchronize()
     batch_ms, step_ms = e[0].elapsed_time(e[1]), e[1].elapsed_time(e[2]) / steps
+    # the same single-token steps as one CUDA graph: a whole-operator step plan, `steps` tokens
+    # captured once (each node reads its own token's input), replayed twice (warm-up, timed)
+    c = caches[1]
+    c.pos = T + steps
+    plan = bb.StepPlan(c, 0, weights=W)
+    graph, cap = torch.cuda.CUDAGraph(), torch.cuda.Stream()
+    torch.cuda.synchronize()
+    with torch.cuda.graph(graph, stream=cap):
+        for s_ in range(steps):
+            plan.launch_layer(xs[s_], o1, theta=THETA)
+    graph.replay()
+    torch.cuda.synchronize()
+    e[0].record(stream)
+    graph.replay()
+    e[1].record(stream)
+    torch.cuda.synchronize()
+    graph_step_ms = e[0].elapsed_time(e[1]) / steps
+    plan.finish()
     for c in caches:
         c.close()
     pool.close()
@@ -439,7 +457,9 @@ def bench_attn_layer(bb, torch, dev, stream, T=2048, steps=64):
                         f"prefill + output projection), then {steps} single-token steps",
             "batch_ms": round(batch_ms, 3), "batch_tok_per_s": round(T / (batch_ms * 1e-3), 1),
             "projection_tmacs_per_s_upper_bound": round(proj_macs / (batch_ms * 1e-3) / 1e12, 2),
-            "step_ms": round(step_ms, 4), "step_tok_per_s": round(1 / (step_ms * 1e-3), 1)}
+            "step_ms": round(step_ms, 4), "step_tok_per_s": round(1 / (step_ms * 1e-3), 1),
+            "graph_step_ms": round(graph_step_ms, 4),
+            "graph_how": "whole-operator step plan, all steps captured in one CUDA graph"}
 
 
 def bench_config3_bf16(bb, torch, dev, stream, world, steps):

@@ -264,6 +264,16 @@ BEBELM_API int bebelm_step_plan_launch(bebelm_step_plan* plan, const float* q, c
                                        float theta, float eps, float* out, void* stream);
 BEBELM_API int bebelm_step_plan_steps(const bebelm_step_plan* plan, unsigned long long* n, void* stream);
 BEBELM_API int bebelm_step_plan_finish(bebelm_step_plan* plan, void* stream);
+/* The same for the whole attention operator (bebelm_attn_layer_step): a plan made with the
+ * layer's uploaded weights also owns the scratch of its projections, and each
+ * bebelm_step_plan_launch_layer is one token: x [hidden] -> out [hidden], device pointers.
+ * It enqueues the Q8 quantization of x, the q/k/v projections, the plan's decode step, the Q8
+ * quantization of the attention output and the output projection; none of them allocates,
+ * copies or synchronises. steps/finish as above. */
+BEBELM_API int bebelm_step_plan_create_layer(bebelm_kv* kv, int layer, const bebelm_attn_weights* w,
+                                             size_t window, bebelm_step_plan** out);
+BEBELM_API int bebelm_step_plan_launch_layer(bebelm_step_plan* plan, const float* x, float theta,
+                                             float eps, float* out, void* stream);
 
 /* ------------------------------------------- multi-GPU (KV-head sharding) --- */
 /* Fused decode + all-gather for KV-head sharding over NVLink, one process per

@@ -94,3 +94,45 @@ def test_layer_batch_against_its_pieces_and_the_oracle(tensor_cores):
         att = e.attn_prefill(0, q, k, v, qg, kg, 0, theta=THETA)
         np.testing.assert_array_equal(got, bb.matmul(bb.GGML_Q4_K, wo, HID, HID, att, 40))
     W.close()
+
+
+def test_whole_operator_step_plans_eager_and_in_a_graph():
+    """Whole-operator plans (projections + plan decode + W_o) for two layers against
+    attn_layer_step on a copy of the cache, eagerly and replayed from a CUDA graph. The plan's
+    decode splits differ from the ordinary step's (last-bit differences in the attention
+    output), which W_o's Q8 re-quantization can carry to one quantum."""
+    torch = pytest.importorskip("torch")
+    W, _ = _layer(seed=11)
+    dev = torch.device("cuda", 0)
+    a = bb.Cache(n_layers=2, max_context=400)
+    for layer in range(2):
+        a.append(layer, oracle.normal(40 + layer, (300, KVD)), oracle.normal(50 + layer, (300, KVD)))
+    a.pos = 300
+    b = a.clone()
+    plans = [bb.StepPlan(b, layer, weights=W) for layer in range(2)]
+    sx = torch.zeros(HID, device=dev)
+    outs = [torch.empty(HID, device=dev) for _ in range(2)]
+    graph, cap = torch.cuda.CUDAGraph(), torch.cuda.Stream()
+    for i in range(12):
+        x = torch.from_numpy(_x(200 + i, HID)).to(dev)
+        sx.copy_(x)
+        if i < 2:
+            for layer in range(2):
+                plans[layer].launch_layer(sx, outs[layer], theta=THETA)
+        else:
+            if i == 2:
+                torch.cuda.synchronize()
+                with torch.cuda.graph(graph, stream=cap):
+                    for layer in range(2):
+                        plans[layer].launch_layer(sx, outs[layer], theta=THETA)
+            graph.replay()
+        for layer in range(2):
+            want = bb.attn_layer_step(a, layer, W, x.cpu().numpy(), pos=300 + i, theta=THETA)
+            got = outs[layer].cpu().numpy()
+            assert np.abs(got - want).max() <= 5e-3 * max(1.0, np.abs(want).max()), (i, layer)
+    assert plans[0].steps() == 12
+    for p in plans:
+        p.finish()
+    assert b.kv_len() == a.kv_len() == 312 and b.pos == 312
+    np.testing.assert_array_equal(b.read(1)[0], a.read(1)[0])
+    W.close()
