@@ -1810,6 +1810,37 @@ int project_qkv(bebelm_kv_pool* P, const bebelm_attn_weights* W, const float* dx
     return 0;
 }
 
+// One token: q/k/v = W x in one launch (x quantized inside it), and out = W_o attn in one.
+int project_token(const bebelm_attn_weights* W, const float* x, float* q, float* k, float* v, cudaStream_t s) {
+    const size_t nq = (size_t)W->n_heads * kHeadDim, nkv = (size_t)W->n_kv * kHeadDim;
+    QmvSegs sg{};
+    sg.n = 3;
+    float* ys[3] = {q, k, v};
+    const size_t no[3] = {nq, nkv, nkv};
+    for (int i = 0; i < 3; ++i) {
+        sg.dtype[i] = W->dt[i];
+        sg.w[i] = W->w[i].as<uint8_t>();
+        sg.row_bytes[i] = ggml_row_bytes(W->dt[i], W->hidden);
+        sg.n_out[i] = no[i];
+        sg.y[i] = ys[i];
+    }
+    CUDA_TRY(launch_qmv_multi(sg, x, W->hidden, s));
+    return 0;
+}
+
+int project_token_out(const bebelm_attn_weights* W, const float* attn, float* out, cudaStream_t s) {
+    const size_t nq = (size_t)W->n_heads * kHeadDim;
+    QmvSegs sg{};
+    sg.n = 1;
+    sg.dtype[0] = W->dt[3];
+    sg.w[0] = W->w[3].as<uint8_t>();
+    sg.row_bytes[0] = ggml_row_bytes(W->dt[3], nq);
+    sg.n_out[0] = W->hidden;
+    sg.y[0] = out;
+    CUDA_TRY(launch_qmv_multi(sg, attn, nq, s));
+    return 0;
+}
+
 int project_out(bebelm_kv_pool* P, const bebelm_attn_weights* W, const float* attn, size_t t, float* dout,
                 cudaStream_t s) {
     const size_t nq = (size_t)W->n_heads * kHeadDim;
@@ -1833,6 +1864,8 @@ int bebelm_attn_weights_create(int device, int n_heads, int n_kv_heads, size_t h
     const int dts[4] = {dtype_q, dtype_k, dtype_v, dtype_o};
     const size_t n_in[4] = {hidden, hidden, hidden, nq}, n_out[4] = {nq, nkv, nkv, hidden};
     for (int i = 0; i < 4; ++i) TRY(check_ggml(dts[i], n_in[i]));
+    if (hidden > 8192 || nq > 8192)
+        return fail(BEBELM_ERR_UNSUPPORTED, "hidden (%zu) and n_heads*64 (%zu) must be at most 8192", hidden, nq);
     int n_dev = 0;
     CUDA_TRY(cudaGetDeviceCount(&n_dev));
     if (device < 0 || device >= n_dev) return fail(BEBELM_ERR_INVALID, "device %d not present", device);
@@ -1893,14 +1926,17 @@ int bebelm_attn_layer_step(bebelm_kv* kv, int layer, const bebelm_attn_weights* 
         dx = static_cast<const float*>(a0);
         dout = static_cast<float*>(o);
     }
-    float *q, *k, *v, *attn;
-    TRY(project_qkv(P, W, dx, 1, &q, &k, &v, &attn, s));
+    const size_t nq = (size_t)W->n_heads * kHeadDim, nkv = (size_t)W->n_kv * kHeadDim;
+    TRY(P->proj.ensure(4 * (2 * nq + 2 * nkv) + 1024, false, s));
+    float* q = P->proj.as<float>();
+    float *k = q + nq, *v = k + nkv, *attn = v + nkv;
+    TRY(project_token(W, dx, q, k, v, s));
     long long slot0 = 0;
     TRY(reserve(kv, layer, 1, &slot0, s));
     const FusedStep fs{q, k, v, W->gains.as<float>(), W->gains.as<float>() + 64, theta_scale_of(theta, kHeadDim), eps};
     std::vector<Window> w{{kv, kv->base[layer], kv->len[layer], slot0, (long long)pos}};
     TRY(run_decode(P, w, layer, W->n_heads, nullptr, attn, 0.125f, &fs, s));
-    TRY(project_out(P, W, attn, 1, dout, s));
+    TRY(project_token_out(W, attn, dout, s));
     if (mem == BEBELM_MEM_HOST) return stage_out(P, dout, out, 4 * W->hidden, s);
     return 0;
 }
@@ -2007,18 +2043,11 @@ int bebelm_step_plan_launch_layer(bebelm_step_plan* pl, const float* x, float th
     const bebelm_attn_weights* W = pl->W;
     DeviceGuard g(pl->kv->pool->device);
     cudaStream_t s = as_stream(stream);
-    const size_t nq = (size_t)W->n_heads * kHeadDim, nkv = (size_t)W->n_kv * kHeadDim;
     const LayerScratch L = layer_scratch(pl);
-    const Q8View q8{L.q8, L.q8s, L.q8m};
-    if (is_kquant(W->dt[0]) || is_kquant(W->dt[1]) || is_kquant(W->dt[2]))
-        CUDA_TRY(launch_quantize_q8(x, W->hidden, 1, L.q8, L.q8s, L.q8m, s));
-    TRY(project(W, 0, W->hidden, nq, x, 1, q8, L.q, s));
-    TRY(project(W, 1, W->hidden, nkv, x, 1, q8, L.k, s));
-    TRY(project(W, 2, W->hidden, nkv, x, 1, q8, L.v, s));
+    TRY(project_token(W, x, L.q, L.k, L.v, s));
     TRY(bebelm_step_plan_launch(pl, L.q, L.k, L.v, W->gains.as<float>(), W->gains.as<float>() + 64, theta, eps,
                                 L.attn, stream));
-    if (is_kquant(W->dt[3])) CUDA_TRY(launch_quantize_q8(L.attn, nq, 1, L.q8, L.q8s, L.q8m, s));
-    return project(W, 3, nq, W->hidden, L.attn, 1, q8, out, s);
+    return project_token_out(W, L.attn, out, s);
 }
 
 }  // extern "C"

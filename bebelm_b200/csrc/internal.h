@@ -219,5 +219,15 @@ cudaError_t launch_quantize_q8(const float* x, size_t n_in, size_t n_tokens, int
 cudaError_t launch_qmatmul(int dtype, const uint8_t* w, size_t n_in, size_t n_out, const float* x, size_t n_tokens,
                            const int8_t* q8, const float* q8_scales, const int* q8_sums, float* y, cudaStream_t s);
 cudaError_t launch_dequantize(int dtype, const uint8_t* data, size_t n, float* out, cudaStream_t s);
+// one token, up to 3 matrices sharing the input x [n_in <= 8192]: y_i = W_i x, x quantized
+// to Q8 inside the kernel (K-quant segments); results identical to launch_qmatmul
+struct QmvSegs {
+    int n;
+    int dtype[3];
+    const uint8_t* w[3];
+    size_t row_bytes[3], n_out[3];
+    float* y[3];
+};
+cudaError_t launch_qmv_multi(const QmvSegs& segs, const float* x, size_t n_in, cudaStream_t s);
 
 }  // namespace bebelm

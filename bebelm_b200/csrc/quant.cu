@@ -445,6 +445,97 @@ __global__ void __launch_bounds__(256) qmatmul_tiled_kernel(const uint8_t* w, si
         }
 }
 
+// One token through up to three matrices of the same input in one launch (the q/k/v
+// projections, or W_o alone): every CTA first quantizes x to Q8 in shared memory (the
+// arithmetic of quantize_q8_kernel, so the quants are the same), then each warp computes one
+// output row of one segment as qmatmul_kernel does. Saves the separate quantization launch and
+// one launch per extra matrix.
+constexpr int kMvMaxIn = 8192;  // x held in shared memory as int8
+__global__ void __launch_bounds__(256) qmv_multi_kernel(QmvSegs segs, const float* x, size_t n_in) {
+    __shared__ __align__(16) int8_t s_q[kMvMaxIn];
+    __shared__ float s_sc[kMvMaxIn / kQK];
+    __shared__ int s_sum[kMvMaxIn / 32];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const size_t nb = n_in / kQK;
+    bool kq = false;
+    for (int i = 0; i < segs.n; ++i) kq |= segs.dtype[i] == kGgmlQ4K || segs.dtype[i] == kGgmlQ6K;
+    if (kq) {
+        for (size_t blk = warp; blk < nb; blk += 8) {
+            const float* xb = x + blk * kQK + lane * 8;
+            const float4 a = *reinterpret_cast<const float4*>(xb), b = *reinterpret_cast<const float4*>(xb + 4);
+            const float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+            float amax = 0.f;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+            const float inv = amax > 0.f ? __fdiv_rn(127.0f, amax) : 0.f;
+            int8_t qv[8];
+            int sm = 0;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                float r = roundf(__fmul_rn(v[i], inv));
+                r = fminf(fmaxf(r, -127.f), 127.f);
+                qv[i] = (int8_t)r;
+                sm += qv[i];
+            }
+            *reinterpret_cast<uint2*>(s_q + blk * kQK + lane * 8) = *reinterpret_cast<const uint2*>(qv);
+            sm += __shfl_xor_sync(0xffffffffu, sm, 1);
+            sm += __shfl_xor_sync(0xffffffffu, sm, 2);
+            if ((lane & 3) == 0) s_sum[blk * 8 + (lane >> 2)] = sm;
+            if (lane == 0) s_sc[blk] = __fdiv_rn(amax, 127.0f);
+        }
+        __syncthreads();
+    }
+    // which segment and row this warp computes
+    size_t r = (size_t)blockIdx.x * 8 + warp;
+    int sg;
+    if (r < segs.n_out[0]) {
+        sg = 0;
+    } else if (segs.n > 1 && r < segs.n_out[0] + segs.n_out[1]) {
+        sg = 1;
+        r -= segs.n_out[0];
+    } else if (segs.n > 2 && r < segs.n_out[0] + segs.n_out[1] + segs.n_out[2]) {
+        sg = 2;
+        r -= segs.n_out[0] + segs.n_out[1];
+    } else {
+        return;
+    }
+    const int dt = sg == 0 ? segs.dtype[0] : sg == 1 ? segs.dtype[1] : segs.dtype[2];
+    const uint8_t* wbase = sg == 0 ? segs.w[0] : sg == 1 ? segs.w[1] : segs.w[2];
+    const size_t rb = sg == 0 ? segs.row_bytes[0] : sg == 1 ? segs.row_bytes[1] : segs.row_bytes[2];
+    float* ybase = sg == 0 ? segs.y[0] : sg == 1 ? segs.y[1] : segs.y[2];
+    const uint8_t* row = wbase + r * rb;
+    float acc;
+    if (dt == kGgmlQ4K || dt == kGgmlQ6K) {
+        acc = -0.0f;
+        constexpr int kU = 4;
+        for (size_t b0 = 0; b0 < nb; b0 += kU) {
+            if (dt == kGgmlQ4K) {
+                Q4Ld L[kU];
+#pragma unroll
+                for (int u = 0; u < kU; ++u)
+                    if (b0 + u < nb)
+                        L[u] = load_q4k(row + (b0 + u) * 144, s_q + (b0 + u) * kQK, s_sc[b0 + u], s_sum + (b0 + u) * 8, lane);
+#pragma unroll
+                for (int u = 0; u < kU; ++u)
+                    if (b0 + u < nb) acc = __fadd_rn(acc, dot_q4k(L[u], lane));
+            } else {
+                Q6Ld L[kU];
+#pragma unroll
+                for (int u = 0; u < kU; ++u)
+                    if (b0 + u < nb) L[u] = load_q6k(row + (b0 + u) * 210, s_q + (b0 + u) * kQK, s_sc[b0 + u], lane);
+#pragma unroll
+                for (int u = 0; u < kU; ++u)
+                    if (b0 + u < nb) acc = __fadd_rn(acc, dot_q6k(L[u], lane));
+            }
+        }
+    } else {
+        acc = dt == kGgmlF32 ? row_dot<kGgmlF32>(row, x, n_in, lane) : row_dot<kGgmlF16>(row, x, n_in, lane);
+    }
+    if (lane == 0) ybase[r] = acc;
+}
+
 __global__ void dequant_kernel(int dtype, const uint8_t* data, size_t n, float* out) {
     const size_t stride = (size_t)gridDim.x * blockDim.x;
     for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
@@ -517,6 +608,15 @@ cudaError_t launch_qmatmul(int dtype, const uint8_t* w, size_t n_in, size_t n_ou
         case kGgmlQ6K: qmatmul_kernel<kGgmlQ6K><<<grid, 256, 0, s>>>(w, rb, n_in, n_out, x, q8, q8_scales, q8_sums, y); break;
         default: return cudaErrorInvalidValue;
     }
+    return cudaGetLastError();
+}
+
+cudaError_t launch_qmv_multi(const QmvSegs& segs, const float* x, size_t n_in, cudaStream_t s) {
+    if (n_in > (size_t)kMvMaxIn || segs.n < 1 || segs.n > 3) return cudaErrorInvalidValue;
+    size_t rows = 0;
+    for (int i = 0; i < segs.n; ++i) rows += segs.n_out[i];
+    if (rows == 0) return cudaSuccess;
+    qmv_multi_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, s>>>(segs, x, n_in);
     return cudaGetLastError();
 }
 
