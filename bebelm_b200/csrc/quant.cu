@@ -536,6 +536,146 @@ __global__ void __launch_bounds__(256) qmv_multi_kernel(QmvSegs segs, const floa
     if (lane == 0) ybase[r] = acc;
 }
 
+// One token, K-quant weights only: one LANE per 256-weight block. A row's nb blocks sit on
+// nb lanes (L = nb rounded up to a power of two lanes per row, 32/L rows per warp); each lane
+// forms its block's exact integer dot alone (64 dp4a, no cross-lane reduction) and the f32
+// block value as qmatmul_kernel does, then the row's values are added in block order through
+// shuffles. Same bits as qmatmul_kernel, with ~30x fewer instructions per block.
+constexpr int kQStride = 272;  // Q8 activations of a block in shared memory, padded against bank conflicts
+
+__device__ __forceinline__ float lane_block_q4k(const uint8_t* blk, const int8_t* qx, float sx, const int* sums) {
+    const uint4* p = reinterpret_cast<const uint4*>(blk);
+    const uint4 head = p[0];
+    int sd = 0, sm = 0;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+        int sc0, m0, sc1, m1;
+        scale_min_head(2 * c, head, sc0, m0);
+        scale_min_head(2 * c + 1, head, sc1, m1);
+        sm += m0 * sums[2 * c] + m1 * sums[2 * c + 1];
+        const uint4 q0 = p[1 + 2 * c], q1 = p[2 + 2 * c];
+        const uint32_t qw[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+        const int4* xl = reinterpret_cast<const int4*>(qx + (2 * c) * 32);
+        const int4* xh = reinterpret_cast<const int4*>(qx + (2 * c + 1) * 32);
+        const int4 a0 = xl[0], a1 = xl[1], b0 = xh[0], b1 = xh[1];
+        const int xa[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+        const int xb[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+        int lo = 0, hi = 0;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            lo = __dp4a((int)(qw[i] & 0x0f0f0f0fu), xa[i], lo);
+            hi = __dp4a((int)((qw[i] >> 4) & 0x0f0f0f0fu), xb[i], hi);
+        }
+        sd += sc0 * lo + sc1 * hi;
+    }
+    const float d = f16_bits_to_f32(head.x & 0xffffu), dmin = f16_bits_to_f32(head.x >> 16);
+    return __fmul_rn(sx, __fsub_rn(__fmul_rn(d, __int2float_rn(sd)), __fmul_rn(dmin, __int2float_rn(sm))));
+}
+
+// 16 bytes from a 2-byte-aligned address, as four little-endian words
+__device__ __forceinline__ void ld16_a2(const uint8_t* p, uint32_t* w) {
+    const uint16_t* h = reinterpret_cast<const uint16_t*>(p);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) w[i] = (uint32_t)h[2 * i] | ((uint32_t)h[2 * i + 1] << 16);
+}
+
+__device__ __forceinline__ float lane_block_q6k(const uint8_t* blk, const int8_t* qx, float sx) {
+    uint32_t scw[4];
+    ld16_a2(blk + 192, scw);
+    int s = 0;
+#pragma unroll
+    for (int n = 0; n < 2; ++n)
+#pragma unroll
+        for (int sub = 0; sub < 2; ++sub) {
+            uint32_t lo[4], hi[4], qh[4];
+            ld16_a2(blk + n * 64 + sub * 16, lo);       // ql[0..32) part: groups 0 (low) and 2 (high)
+            ld16_a2(blk + n * 64 + 32 + sub * 16, hi);  // ql[32..64) part: groups 1 and 3
+            ld16_a2(blk + 128 + n * 32 + sub * 16, qh);
+#pragma unroll
+            for (int g = 0; g < 4; ++g) {
+                const int k = n * 8 + 2 * g + sub;
+                const int4 xv = *reinterpret_cast<const int4*>(qx + k * 16);
+                const int xw[4] = {xv.x, xv.y, xv.z, xv.w};
+                int t = 0;
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const uint32_t src = (g & 1) ? hi[i] : lo[i];
+                    const uint32_t nib = (g >= 2 ? src >> 4 : src) & 0x0f0f0f0fu;
+                    const uint32_t hb = (qh[i] >> (2 * g)) & 0x03030303u;
+                    t = __dp4a((int)__vsub4(nib | (hb << 4), 0x20202020u), xw[i], t);  // bytes q - 32
+                }
+                const int sc = (int)(int8_t)((scw[k >> 2] >> (8 * (k & 3))) & 0xffu);
+                s += t * sc;
+            }
+        }
+    const float d = f16_bits_to_f32(*reinterpret_cast<const uint16_t*>(blk + 208));
+    return __fmul_rn(sx, __fmul_rn(d, __int2float_rn(s)));
+}
+
+__global__ void __launch_bounds__(256) qmv_lane_kernel(QmvSegs segs, const float* x, size_t n_in) {
+    __shared__ __align__(16) int8_t s_q[(kMvMaxIn / kQK) * kQStride];
+    __shared__ float s_sc[kMvMaxIn / kQK];
+    __shared__ int s_sum[kMvMaxIn / 32];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nb = (int)(n_in / kQK);
+    for (int blk = warp; blk < nb; blk += 8) {  // Q8 of x, as quantize_q8_kernel
+        const float* xb = x + (size_t)blk * kQK + lane * 8;
+        const float4 a = *reinterpret_cast<const float4*>(xb), b = *reinterpret_cast<const float4*>(xb + 4);
+        const float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+        float amax = 0.f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+        const float inv = amax > 0.f ? __fdiv_rn(127.0f, amax) : 0.f;
+        int8_t qv[8];
+        int sm = 0;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            float r = roundf(__fmul_rn(v[i], inv));
+            r = fminf(fmaxf(r, -127.f), 127.f);
+            qv[i] = (int8_t)r;
+            sm += qv[i];
+        }
+        *reinterpret_cast<uint2*>(s_q + blk * kQStride + lane * 8) = *reinterpret_cast<const uint2*>(qv);
+        sm += __shfl_xor_sync(0xffffffffu, sm, 1);
+        sm += __shfl_xor_sync(0xffffffffu, sm, 2);
+        if ((lane & 3) == 0) s_sum[blk * 8 + (lane >> 2)] = sm;
+        if (lane == 0) s_sc[blk] = __fdiv_rn(amax, 127.0f);
+    }
+    __syncthreads();
+    int L = 1;
+    while (L < nb) L <<= 1;
+    const int b = lane & (L - 1);
+    size_t r = ((size_t)blockIdx.x * 8 + warp) * (32 / L) + lane / L;
+    int sg = -1;
+    if (r < segs.n_out[0]) {
+        sg = 0;
+    } else if (segs.n > 1 && r < segs.n_out[0] + segs.n_out[1]) {
+        sg = 1;
+        r -= segs.n_out[0];
+    } else if (segs.n > 2 && r < segs.n_out[0] + segs.n_out[1] + segs.n_out[2]) {
+        sg = 2;
+        r -= segs.n_out[0] + segs.n_out[1];
+    }
+    float v = 0.f;
+    if (sg >= 0 && b < nb) {
+        const int dt = sg == 0 ? segs.dtype[0] : sg == 1 ? segs.dtype[1] : segs.dtype[2];
+        const uint8_t* wb = sg == 0 ? segs.w[0] : sg == 1 ? segs.w[1] : segs.w[2];
+        const size_t rb = sg == 0 ? segs.row_bytes[0] : sg == 1 ? segs.row_bytes[1] : segs.row_bytes[2];
+        const uint8_t* row = wb + r * rb;
+        v = dt == kGgmlQ4K ? lane_block_q4k(row + (size_t)b * 144, s_q + b * kQStride, s_sc[b], s_sum + b * 8)
+                           : lane_block_q6k(row + (size_t)b * 210, s_q + b * kQStride, s_sc[b]);
+    }
+    const int base = lane & ~(L - 1);
+    float acc = -0.0f;  // the blocks of the row, added in order
+    for (int j = 0; j < nb; ++j) acc = __fadd_rn(acc, __shfl_sync(0xffffffffu, v, base + j));
+    if (sg >= 0 && b == 0) {
+        float* yb = sg == 0 ? segs.y[0] : sg == 1 ? segs.y[1] : segs.y[2];
+        yb[r] = acc;
+    }
+}
+
 __global__ void dequant_kernel(int dtype, const uint8_t* data, size_t n, float* out) {
     const size_t stride = (size_t)gridDim.x * blockDim.x;
     for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
@@ -616,7 +756,16 @@ cudaError_t launch_qmv_multi(const QmvSegs& segs, const float* x, size_t n_in, c
     size_t rows = 0;
     for (int i = 0; i < segs.n; ++i) rows += segs.n_out[i];
     if (rows == 0) return cudaSuccess;
-    qmv_multi_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, s>>>(segs, x, n_in);
+    bool kq = true;
+    for (int i = 0; i < segs.n; ++i) kq &= segs.dtype[i] == kGgmlQ4K || segs.dtype[i] == kGgmlQ6K;
+    if (kq && n_in % kQK == 0) {
+        size_t L = 1;
+        while (L < n_in / kQK) L <<= 1;
+        const size_t rows_per_cta = 8 * (32 / L);
+        qmv_lane_kernel<<<(unsigned)((rows + rows_per_cta - 1) / rows_per_cta), 256, 0, s>>>(segs, x, n_in);
+    } else {
+        qmv_multi_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, s>>>(segs, x, n_in);
+    }
     return cudaGetLastError();
 }
 

@@ -136,3 +136,26 @@ def test_whole_operator_step_plans_eager_and_in_a_graph():
     assert b.kv_len() == a.kv_len() == 312 and b.pos == 312
     np.testing.assert_array_equal(b.read(1)[0], a.read(1)[0])
     W.close()
+
+
+def test_layer_step_at_a_ragged_shape():
+    """hidden 768 (3 blocks per row: the one-token kernel's lanes per row are padded to 4),
+    8 query / 2 kv heads, Q6_K on k and W_o: the one call equals its pieces bit for bit."""
+    hid, nh, nkv = 768, 8, 2
+    wq, wk = random_q4k(nh * D, hid, 61), random_q6k(nkv * D, hid, 62)
+    wv, wo = random_q4k(nkv * D, hid, 63), random_q6k(hid, nh * D, 64)
+    qg, kg = (1 + 0.02 * oracle.normal(s, D) for s in (65, 66))
+    W = bb.AttnWeights((bb.GGML_Q4_K, wq), (bb.GGML_Q6_K, wk), (bb.GGML_Q4_K, wv), (bb.GGML_Q6_K, wo), qg, kg,
+                       n_heads=nh, n_kv_heads=nkv, hidden=hid)
+    a = bb.Cache(n_layers=1, n_kv_heads=nkv, max_context=256)
+    b = a.clone()
+    for i in range(4):
+        x = _x(300 + i, hid)
+        got = bb.attn_layer_step(a, 0, W, x, pos=i, theta=THETA)
+        q = bb.matvec(bb.GGML_Q4_K, wq, hid, nh * D, x)
+        k = bb.matvec(bb.GGML_Q6_K, wk, hid, nkv * D, x)
+        v = bb.matvec(bb.GGML_Q4_K, wv, hid, nkv * D, x)
+        att = b.attn_step(0, q, k, v, qg, kg, pos=i, theta=THETA)
+        np.testing.assert_array_equal(got, bb.matvec(bb.GGML_Q6_K, wo, nh * D, hid, att))
+        np.testing.assert_array_equal(q, oracle.matvec(oracle.GG_Q4_K, wq, hid, nh * D, x))
+    W.close()
