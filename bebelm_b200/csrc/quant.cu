@@ -276,19 +276,34 @@ __global__ void __launch_bounds__(256) qmatmul_kernel(const uint8_t* w, size_t r
 // dots with dp4a. The f32 block value and the in-order block sum per (row, token) are those
 // of qmatmul_kernel, so the results are identical.
 constexpr int kTR = 64, kTT = 64, kWStride = 256 + 16;  // int8 row stride: 16 B skew against bank conflicts
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem, bool valid) {
+    const uint32_t sa = (uint32_t)__cvta_generic_to_shared(smem);
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(sa), "l"(gmem), "r"(valid ? 16 : 0) : "memory");
+}
+__device__ __forceinline__ void cp_async4(void* smem, const void* gmem, bool valid) {
+    const uint32_t sa = (uint32_t)__cvta_generic_to_shared(smem);
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(sa), "l"(gmem), "r"(valid ? 4 : 0) : "memory");
+}
+
+// dynamic shared memory of the tiled kernel: two stages of the tokens' Q8 activations and (Q4_K)
+// of the rows' raw block bytes, filled with cp.async while the other stage is computed on
+constexpr int kTiledDynBytes = 2 * kTT * kWStride + 2 * kTR * 144;
+
 template <int DT>
 __global__ void __launch_bounds__(256) qmatmul_tiled_kernel(const uint8_t* w, size_t row_bytes, size_t n_in,
                                                             size_t n_out, size_t n_tokens, const int8_t* q8,
                                                             const float* q8_scales, const int* q8_sums, float* y) {
     constexpr int NSUB = DT == kGgmlQ4K ? 8 : 16;  // sub-blocks per block
     constexpr int SW = kQK / NSUB;                 // sub-block width (32 or 16)
+    extern __shared__ __align__(16) uint8_t s_dyn[];
+    int8_t* const s_x2 = reinterpret_cast<int8_t*>(s_dyn);          // [2][kTT][kWStride]
+    uint8_t* const s_wraw = s_dyn + 2 * kTT * kWStride;             // [2][kTR][144] (Q4_K)
     __shared__ __align__(16) int8_t s_w[kTR * kWStride];
-    __shared__ __align__(16) int8_t s_x[kTT * kWStride];
     __shared__ int s_sc[kTR][NSUB];
     __shared__ int s_m[kTR][8];       // Q4_K mins
     __shared__ float s_d[kTR], s_dmin[kTR];
-    __shared__ float s_sx[kTT];
-    __shared__ int s_sums[kTT][8];
+    __shared__ __align__(16) float s_sx2[2][kTT];
+    __shared__ __align__(16) int s_sums2[2][kTT][8];
     const int tid = threadIdx.x;
     const size_t r0 = (size_t)blockIdx.x * kTR, t0 = (size_t)blockIdx.y * kTT;
     const int tr = tid >> 4, tc = tid & 15;  // thread tile: rows tr + 16 i, tokens tc + 16 k
@@ -299,14 +314,52 @@ __global__ void __launch_bounds__(256) qmatmul_tiled_kernel(const uint8_t* w, si
 #pragma unroll
         for (int k = 0; k < 4; ++k) acc[i][k] = -0.0f;
 
+    // block bb's activations (and Q4_K raw weights) into stage st, asynchronously
+    auto stage = [&](size_t bb, int st) {
+        int8_t* sx = s_x2 + st * kTT * kWStride;
+        for (int task = tid; task < kTT * 16; task += 256) {
+            const int t = task >> 4, seg = task & 15;
+            const bool ok = t0 + t < n_tokens;
+            cp_async16(sx + t * kWStride + seg * 16, ok ? q8 + (t0 + t) * n_in + bb * kQK + seg * 16 : q8, ok);
+        }
+        if (tid < kTT) {
+            const bool ok = t0 + tid < n_tokens;
+            cp_async4(&s_sx2[st][tid], ok ? q8_scales + (t0 + tid) * nb + bb : q8_scales, ok);
+            if (DT == kGgmlQ4K) {
+                const int* src = ok ? q8_sums + ((t0 + tid) * nb + bb) * 8 : q8_sums;
+                cp_async16(&s_sums2[st][tid][0], src, ok);
+                cp_async16(&s_sums2[st][tid][4], ok ? src + 4 : q8_sums, ok);
+            }
+        }
+        if (DT == kGgmlQ4K) {
+            uint8_t* wr = s_wraw + st * kTR * 144;
+            for (int task = tid; task < kTR * 9; task += 256) {
+                const int r = task / 9, seg = task % 9;
+                const bool ok = r0 + r < n_out;
+                cp_async16(wr + r * 144 + seg * 16, ok ? w + (r0 + r) * row_bytes + bb * 144 + seg * 16 : w, ok);
+            }
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+
+    stage(0, 0);
     for (size_t b = 0; b < nb; ++b) {
+        const int st = (int)(b & 1);
         __syncthreads();  // the previous block's operands are no longer read
+        if (b + 1 < nb)
+            stage(b + 1, st ^ 1);
+        else
+            asm volatile("cp.async.commit_group;" ::: "memory");  // keep one group per iteration
+        asm volatile("cp.async.wait_group 1;" ::: "memory");     // block b's copies have landed
+        __syncthreads();
+        const int8_t* s_x = s_x2 + st * kTT * kWStride;
+        const float* s_sx = s_sx2[st];
+        int (*s_sums)[8] = s_sums2[st];
         // weights of 64 rows -> int8 + scales
         if (DT == kGgmlQ4K) {
             for (int task = tid; task < kTR * 8; task += 256) {  // (row, 16-byte segment of qs)
                 const int r = task >> 3, seg = task & 7, c = seg >> 1, p = (seg & 1) * 16;
-                uint4 q = make_uint4(0, 0, 0, 0);
-                if (r0 + r < n_out) q = *reinterpret_cast<const uint4*>(w + (r0 + r) * row_bytes + b * 144 + 16 + c * 32 + p);
+                const uint4 q = *reinterpret_cast<const uint4*>(s_wraw + st * kTR * 144 + r * 144 + 16 + c * 32 + p);
                 const uint32_t qw[4] = {q.x, q.y, q.z, q.w};
                 uint4 lo, hi;
                 uint32_t* lp = reinterpret_cast<uint32_t*>(&lo);
@@ -322,7 +375,7 @@ __global__ void __launch_bounds__(256) qmatmul_tiled_kernel(const uint8_t* w, si
             if (tid < kTR) {
                 const int r = tid;
                 if (r0 + r < n_out) {
-                    const uint8_t* blk = w + (r0 + r) * row_bytes + b * 144;
+                    const uint8_t* blk = s_wraw + st * kTR * 144 + r * 144;
 #pragma unroll
                     for (int j = 0; j < 8; ++j) scale_min_k4(j, blk + 4, s_sc[r][j], s_m[r][j]);
                     s_d[r] = ld_f16(blk);
@@ -367,20 +420,6 @@ __global__ void __launch_bounds__(256) qmatmul_tiled_kernel(const uint8_t* w, si
                 for (int k = 0; k < 16; ++k) s_sc[r][k] = ok ? (int)(int8_t)blk[192 + k] : 0;
                 s_d[r] = ok ? ld_f16(blk + 208) : 0.f;
             }
-        }
-        // activations of 64 tokens
-        for (int task = tid; task < kTT * 16; task += 256) {
-            const int t = task >> 4, seg = task & 15;
-            uint4 v = make_uint4(0, 0, 0, 0);
-            if (t0 + t < n_tokens) v = *reinterpret_cast<const uint4*>(q8 + (t0 + t) * n_in + b * kQK + seg * 16);
-            *reinterpret_cast<uint4*>(s_x + t * kWStride + seg * 16) = v;
-        }
-        if (tid < kTT) {
-            const bool ok = t0 + tid < n_tokens;
-            s_sx[tid] = ok ? q8_scales[(t0 + tid) * nb + b] : 0.f;
-            if (DT == kGgmlQ4K)
-#pragma unroll
-                for (int j = 0; j < 8; ++j) s_sums[tid][j] = ok ? q8_sums[((t0 + tid) * nb + b) * 8 + j] : 0;
         }
         __syncthreads();
 
@@ -734,10 +773,24 @@ cudaError_t launch_qmatmul(int dtype, const uint8_t* w, size_t n_in, size_t n_ou
     const size_t rb = ggml_row_bytes(dtype, n_in);
     if ((dtype == kGgmlQ4K || dtype == kGgmlQ6K) && n_tokens >= kTiledMinTokens) {
         const dim3 tg((unsigned)((n_out + kTR - 1) / kTR), (unsigned)((n_tokens + kTT - 1) / kTT));
+        static bool attr_set[64][2] = {};
+        int dev = 0;
+        cudaGetDevice(&dev);
+        const int which = dtype == kGgmlQ4K ? 0 : 1;
+        if (dev < 0 || dev >= 64 || !attr_set[dev][which]) {
+            cudaError_t e = which == 0 ? cudaFuncSetAttribute(qmatmul_tiled_kernel<kGgmlQ4K>,
+                                                              cudaFuncAttributeMaxDynamicSharedMemorySize, kTiledDynBytes)
+                                       : cudaFuncSetAttribute(qmatmul_tiled_kernel<kGgmlQ6K>,
+                                                              cudaFuncAttributeMaxDynamicSharedMemorySize, kTiledDynBytes);
+            if (e != cudaSuccess) return e;
+            if (dev >= 0 && dev < 64) attr_set[dev][which] = true;
+        }
         if (dtype == kGgmlQ4K)
-            qmatmul_tiled_kernel<kGgmlQ4K><<<tg, 256, 0, s>>>(w, rb, n_in, n_out, n_tokens, q8, q8_scales, q8_sums, y);
+            qmatmul_tiled_kernel<kGgmlQ4K><<<tg, 256, kTiledDynBytes, s>>>(w, rb, n_in, n_out, n_tokens, q8, q8_scales,
+                                                                          q8_sums, y);
         else
-            qmatmul_tiled_kernel<kGgmlQ6K><<<tg, 256, 0, s>>>(w, rb, n_in, n_out, n_tokens, q8, q8_scales, q8_sums, y);
+            qmatmul_tiled_kernel<kGgmlQ6K><<<tg, 256, kTiledDynBytes, s>>>(w, rb, n_in, n_out, n_tokens, q8, q8_scales,
+                                                                          q8_sums, y);
         return cudaGetLastError();
     }
     const dim3 grid((unsigned)((n_out + 7) / 8), (unsigned)n_tokens);
