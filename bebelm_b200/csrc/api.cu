@@ -1710,7 +1710,8 @@ int bebelm_matmul(int dtype, const void* w, size_t n_in, size_t n_out, const flo
         q8m = reinterpret_cast<int*>(P->q8.as<char>() + qb + ((sb + 255) & ~size_t(255)));
         CUDA_TRY(launch_quantize_q8(dx, n_in, n_tokens, q8, q8s, q8m, s));
     }
-    CUDA_TRY(launch_qmatmul(dtype, static_cast<const uint8_t*>(dw), n_in, n_out, dx, n_tokens, q8, q8s, q8m, dy, s));
+    CUDA_TRY(launch_qmatmul(dtype, static_cast<const uint8_t*>(dw), n_in, n_out, dx, n_tokens, q8, q8s, q8m, dy,
+                             P->err.d, s));
     if (mem == BEBELM_MEM_HOST) return stage_out(P, dy, y, 4 * yn, s);
     return 0;
 }
@@ -1779,8 +1780,8 @@ bool is_kquant(int dt) { return dt == kGgmlQ4K || dt == kGgmlQ6K; }
 
 // y = W x for the weights of one projection; x already quantized in q8 when needed
 int project(const bebelm_attn_weights* W, int which, size_t n_in, size_t n_out, const float* x, size_t t,
-            const Q8View& q8, float* y, cudaStream_t s) {
-    CUDA_TRY(launch_qmatmul(W->dt[which], W->w[which].as<uint8_t>(), n_in, n_out, x, t, q8.q, q8.sc, q8.sm, y, s));
+            const Q8View& q8, float* y, int* err, cudaStream_t s) {
+    CUDA_TRY(launch_qmatmul(W->dt[which], W->w[which].as<uint8_t>(), n_in, n_out, x, t, q8.q, q8.sc, q8.sm, y, err, s));
     return 0;
 }
 
@@ -1804,9 +1805,9 @@ int project_qkv(bebelm_kv_pool* P, const bebelm_attn_weights* W, const float* dx
     Q8View q8;
     if (is_kquant(W->dt[0]) || is_kquant(W->dt[1]) || is_kquant(W->dt[2]))
         TRY(quantize_into_scratch(P, dx, W->hidden, t, &q8, s));
-    TRY(project(W, 0, W->hidden, nq, dx, t, q8, *q, s));
-    TRY(project(W, 1, W->hidden, nkv, dx, t, q8, *k, s));
-    TRY(project(W, 2, W->hidden, nkv, dx, t, q8, *v, s));
+    TRY(project(W, 0, W->hidden, nq, dx, t, q8, *q, P->err.d, s));
+    TRY(project(W, 1, W->hidden, nkv, dx, t, q8, *k, P->err.d, s));
+    TRY(project(W, 2, W->hidden, nkv, dx, t, q8, *v, P->err.d, s));
     return 0;
 }
 
@@ -1846,7 +1847,7 @@ int project_out(bebelm_kv_pool* P, const bebelm_attn_weights* W, const float* at
     const size_t nq = (size_t)W->n_heads * kHeadDim;
     Q8View q8;
     if (is_kquant(W->dt[3])) TRY(quantize_into_scratch(P, attn, nq, t, &q8, s));
-    return project(W, 3, nq, W->hidden, attn, t, q8, dout, s);
+    return project(W, 3, nq, W->hidden, attn, t, q8, dout, P->err.d, s);
 }
 
 }  // namespace

@@ -26,6 +26,8 @@
 // separate kernel (one warp per 256-block).
 #include <algorithm>
 
+#include <cstdlib>
+
 #include "internal.h"
 
 namespace bebelm {
@@ -36,6 +38,7 @@ constexpr int kQK = 256;
 #define BEBELM_QMM_TILED_MIN 32
 #endif
 constexpr size_t kTiledMinTokens = BEBELM_QMM_TILED_MIN;  // from this many tokens on, the tiled kernel
+constexpr size_t kTcMinTokens = 64;  // from this many tokens on, Q4_K goes to the tensor cores
 
 __device__ __forceinline__ float f16_bits_to_f32(uint32_t h) {
     // exact for normals, subnormals, inf and nan (the hardware conversion is exact)
@@ -759,6 +762,14 @@ size_t ggml_row_bytes(int dtype, size_t n_in) {
     }
 }
 
+bool q4k_tc_enabled() {
+    static const bool on = [] {
+        const char* e = getenv("BEBELM_QMM_TC");
+        return !(e && e[0] == '0');
+    }();
+    return on;
+}
+
 cudaError_t launch_quantize_q8(const float* x, size_t n_in, size_t n_tokens, int8_t* q, float* scales, int* sums,
                                cudaStream_t s) {
     const size_t blocks = n_in / kQK * n_tokens;
@@ -768,9 +779,12 @@ cudaError_t launch_quantize_q8(const float* x, size_t n_in, size_t n_tokens, int
 }
 
 cudaError_t launch_qmatmul(int dtype, const uint8_t* w, size_t n_in, size_t n_out, const float* x, size_t n_tokens,
-                           const int8_t* q8, const float* q8_scales, const int* q8_sums, float* y, cudaStream_t s) {
+                           const int8_t* q8, const float* q8_scales, const int* q8_sums, float* y, int* err,
+                           cudaStream_t s) {
     if (n_out == 0 || n_tokens == 0) return cudaSuccess;
     const size_t rb = ggml_row_bytes(dtype, n_in);
+    if (dtype == kGgmlQ4K && n_tokens >= kTcMinTokens && err && q4k_tc_enabled())
+        return launch_q4k_tc(w, n_in, n_out, n_tokens, q8, q8_scales, y, err, s);
     if ((dtype == kGgmlQ4K || dtype == kGgmlQ6K) && n_tokens >= kTiledMinTokens) {
         const dim3 tg((unsigned)((n_out + kTR - 1) / kTR), (unsigned)((n_tokens + kTT - 1) / kTT));
         static bool attr_set[64][2] = {};

@@ -111,3 +111,15 @@ def test_tiled_matmul_bit_exact(dtype, gen, n_out, n_in, t):
     xs = oracle.normal(90 + t, (t, n_in))
     xs[3] = 0.0  # a token whose quants are all zero
     np.testing.assert_array_equal(bb.matmul(dtype, w, n_in, n_out, xs, t), oracle.matmul(dtype, w, n_in, n_out, xs, t))
+
+
+@pytest.mark.parametrize("n_out,n_in,t", [(300, 1024, 200), (2048, 2048, 128), (128, 256, 64)])
+def test_q4k_tensor_core_matmul_bit_exact(n_out, n_in, t):
+    """From 64 tokens on, Q4_K takes the tensor-core kernel (tcgen05 kind::i8, exact integer
+    sub-block dots): ragged row and token tiles, a zero token and a saturated token, same bits."""
+    w = random_q4k(n_out, n_in, seed=n_out + t)
+    xs = oracle.normal(120 + t, (t, n_in))
+    xs[5] = 0.0
+    xs[t - 1] = np.where(np.arange(n_in) % 3, 1e3, -1e3)  # every quant at +-127
+    np.testing.assert_array_equal(bb.matmul(bb.GGML_Q4_K, w, n_in, n_out, xs, t),
+                                  oracle.matmul(oracle.GG_Q4_K, w, n_in, n_out, xs, t))
