@@ -220,7 +220,8 @@ cudaError_t launch_qmatmul(int dtype, const uint8_t* w, size_t n_in, size_t n_ou
                            const int8_t* q8, const float* q8_scales, const int* q8_sums, float* y, int* err,
                            cudaStream_t s);
 // Q4_K weights, many tokens, on the tensor cores (tcgen05 kind::i8); same bits as launch_qmatmul.
-// A bounded wait that gives up stores kErrWaitTimeout to *err.
+// A bounded wait that gives up stores kErrWaitTimeout to *err. cudaErrorNotSupported (nothing
+// launched) when the buffers cannot be described to TMA.
 cudaError_t launch_q4k_tc(const uint8_t* w, size_t n_in, size_t n_out, size_t n_tokens, const int8_t* q8,
                           const float* q8_scales, float* y, int* err, cudaStream_t s);
 // whether launch_qmatmul sends Q4_K batches to launch_q4k_tc (on unless BEBELM_QMM_TC=0)

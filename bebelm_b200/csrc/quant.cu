@@ -783,8 +783,10 @@ cudaError_t launch_qmatmul(int dtype, const uint8_t* w, size_t n_in, size_t n_ou
                            cudaStream_t s) {
     if (n_out == 0 || n_tokens == 0) return cudaSuccess;
     const size_t rb = ggml_row_bytes(dtype, n_in);
-    if (dtype == kGgmlQ4K && n_tokens >= kTcMinTokens && err && q4k_tc_enabled())
-        return launch_q4k_tc(w, n_in, n_out, n_tokens, q8, q8_scales, y, err, s);
+    if (dtype == kGgmlQ4K && n_tokens >= kTcMinTokens && err && q4k_tc_enabled()) {
+        const cudaError_t e = launch_q4k_tc(w, n_in, n_out, n_tokens, q8, q8_scales, y, err, s);
+        if (e != cudaErrorNotSupported) return e;  // else: no tensor maps for these buffers; dp4a below
+    }
     if ((dtype == kGgmlQ4K || dtype == kGgmlQ6K) && n_tokens >= kTiledMinTokens) {
         const dim3 tg((unsigned)((n_out + kTR - 1) / kTR), (unsigned)((n_tokens + kTT - 1) / kTT));
         static bool attr_set[64][2] = {};
