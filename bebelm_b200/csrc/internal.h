@@ -219,13 +219,13 @@ cudaError_t launch_quantize_q8(const float* x, size_t n_in, size_t n_tokens, int
 cudaError_t launch_qmatmul(int dtype, const uint8_t* w, size_t n_in, size_t n_out, const float* x, size_t n_tokens,
                            const int8_t* q8, const float* q8_scales, const int* q8_sums, float* y, int* err,
                            cudaStream_t s);
-// Q4_K weights, many tokens, on the tensor cores (tcgen05 kind::i8); same bits as launch_qmatmul.
-// A bounded wait that gives up stores kErrWaitTimeout to *err. cudaErrorNotSupported (nothing
-// launched) when the buffers cannot be described to TMA.
-cudaError_t launch_q4k_tc(const uint8_t* w, size_t n_in, size_t n_out, size_t n_tokens, const int8_t* q8,
-                          const float* q8_scales, float* y, int* err, cudaStream_t s);
-// whether launch_qmatmul sends Q4_K batches to launch_q4k_tc (on unless BEBELM_QMM_TC=0)
-bool q4k_tc_enabled();
+// Q4_K / Q6_K weights, many tokens, on the tensor cores (tcgen05 kind::i8); same bits as
+// launch_qmatmul. A bounded wait that gives up stores kErrWaitTimeout to *err.
+// cudaErrorNotSupported (nothing launched) when the buffers cannot be described to TMA.
+cudaError_t launch_kquant_tc(int dtype, const uint8_t* w, size_t n_in, size_t n_out, size_t n_tokens,
+                             const int8_t* q8, const float* q8_scales, float* y, int* err, cudaStream_t s);
+// whether launch_qmatmul sends K-quant batches to launch_kquant_tc (on unless BEBELM_QMM_TC=0)
+bool kquant_tc_enabled();
 cudaError_t launch_dequantize(int dtype, const uint8_t* data, size_t n, float* out, cudaStream_t s);
 // one token, up to 3 matrices sharing the input x [n_in <= 8192]: y_i = W_i x, x quantized
 // to Q8 inside the kernel (K-quant segments); results identical to launch_qmatmul

@@ -38,7 +38,7 @@ constexpr int kQK = 256;
 #define BEBELM_QMM_TILED_MIN 32
 #endif
 constexpr size_t kTiledMinTokens = BEBELM_QMM_TILED_MIN;  // from this many tokens on, the tiled kernel
-constexpr size_t kTcMinTokens = 64;  // from this many tokens on, Q4_K goes to the tensor cores
+constexpr size_t kTcMinTokens = 64;  // from this many tokens on, K-quants go to the tensor cores
 
 __device__ __forceinline__ float f16_bits_to_f32(uint32_t h) {
     // exact for normals, subnormals, inf and nan (the hardware conversion is exact)
@@ -762,7 +762,7 @@ size_t ggml_row_bytes(int dtype, size_t n_in) {
     }
 }
 
-bool q4k_tc_enabled() {
+bool kquant_tc_enabled() {
     static const bool on = [] {
         const char* e = getenv("BEBELM_QMM_TC");
         return !(e && e[0] == '0');
@@ -783,8 +783,8 @@ cudaError_t launch_qmatmul(int dtype, const uint8_t* w, size_t n_in, size_t n_ou
                            cudaStream_t s) {
     if (n_out == 0 || n_tokens == 0) return cudaSuccess;
     const size_t rb = ggml_row_bytes(dtype, n_in);
-    if (dtype == kGgmlQ4K && n_tokens >= kTcMinTokens && err && q4k_tc_enabled()) {
-        const cudaError_t e = launch_q4k_tc(w, n_in, n_out, n_tokens, q8, q8_scales, y, err, s);
+    if ((dtype == kGgmlQ4K || dtype == kGgmlQ6K) && n_tokens >= kTcMinTokens && err && kquant_tc_enabled()) {
+        const cudaError_t e = launch_kquant_tc(dtype, w, n_in, n_out, n_tokens, q8, q8_scales, y, err, s);
         if (e != cudaErrorNotSupported) return e;  // else: no tensor maps for these buffers; dp4a below
     }
     if ((dtype == kGgmlQ4K || dtype == kGgmlQ6K) && n_tokens >= kTiledMinTokens) {

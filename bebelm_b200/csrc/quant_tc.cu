@@ -1,4 +1,4 @@
-// Q4_K x Q8 matmul on the 5th-generation tensor cores (many tokens).
+// K-quant (Q4_K, Q6_K) x Q8 matmul on the 5th-generation tensor cores (many tokens).
 //
 // The same arithmetic as qmatmul_tiled_kernel (quant.cu), which restates the reference's
 // dot_q4k_block_q8 (src/kernels/matmul.rs:220-244): per 256-weight block of a row and a token,
@@ -38,14 +38,24 @@ constexpr int kM = 128, kN = 128, kWorkers = 512, kThreads = kWorkers + 32;
 constexpr int kAtomA = kM * 128;  // one 128-byte-wide swizzle atom of A (K 0..127 or 128..255): 16 KB
 constexpr int kAtomB = kN * 128;  // of B: 16 KB
 constexpr int kTileA = 2 * kAtomA, kTileB = 2 * kAtomB;
-constexpr int kRawRow = 144, kRawTile = kM * kRawRow;
-constexpr int kOffA = 0;                          // A tiles: lo, hi, min
-constexpr int kOffB = kOffA + 3 * kTileA;         // 2 slots x B tile
-constexpr int kOffRaw = kOffB + 2 * kTileB;       // 2 slots x 128 rows x 144 B
-constexpr int kOffSx = kOffRaw + 2 * kRawTile;    // 2 x 128 token scales
-constexpr int kOffBar = kOffSx + 2 * kN * 4;      // full[2], a_full, mma_done
-constexpr int kSmemBytes = kOffBar + 64 + 1024;   // + alignment slack
-constexpr uint32_t kTxBytes = kRawTile + kTileB;  // one block's TMA bytes
+constexpr int kOffA = 0;                   // A tiles (3)
+constexpr int kOffB = kOffA + 3 * kTileA;  // 2 slots x B tile
+// Per weight type: the raw rows of a block are one TMA box per slot. A Q4_K block (144 B) is
+// 16-byte aligned in its row; a Q6_K block (210 B) is not, so its box starts at the block's
+// offset rounded down to 16 bytes and is 240 bytes wide (the block starts (210 b) mod 16 in).
+template <bool Q6>
+struct Lay {
+    static constexpr int kBlockBytes = Q6 ? 210 : 144;
+    static constexpr int kRawRow = Q6 ? 240 : 144;
+    static constexpr int kRawTile = kM * kRawRow;
+    static constexpr int kOffRaw = kOffB + 2 * kTileB;       // 2 slots x 128 rows
+    static constexpr int kOffSx = kOffRaw + 2 * kRawTile;    // 2 x 128 token scales
+    static constexpr int kOffBar = kOffSx + 2 * kN * 4;      // full[2], a_full, mma_done
+    static constexpr int kOffLut = kOffBar + 64;             // Q6_K: scale digits, 256 x u16
+    static constexpr int kSmemBytes = kOffLut + (Q6 ? 512 : 0) + 1024;  // + alignment slack
+    static constexpr uint32_t kTxBytes = kRawTile + kTileB;  // one block's TMA bytes
+    static_assert(kSmemBytes <= 227 * 1024, "shared memory");
+};
 constexpr uint32_t kTmemCols = 512;               // 3 accumulators x 128 columns, rounded up
 constexpr long long kWaitLimit = 1ll << 22;
 
@@ -126,9 +136,33 @@ __device__ __forceinline__ float f16f(uint32_t h) {
     return __half2float(__half(r));
 }
 
+// W 32-bit words starting at byte `start` (even) of a 16-byte aligned shared-memory row:
+// aligned 16-byte loads, then a word shift by (start % 16) / 4 and a funnel shift by 16 bits
+// when start % 4 = 2 (both uniform across the CTA)
+template <int W>
+__device__ __forceinline__ void load_realigned(const unsigned char* row16, int start, uint32_t* out) {
+    uint32_t v[W + 4];
+    const uint4* p = reinterpret_cast<const uint4*>(row16 + (start & ~15));
+#pragma unroll
+    for (int i = 0; i < W / 4 + 1; ++i) {
+        const uint4 t = p[i];
+        v[4 * i] = t.x, v[4 * i + 1] = t.y, v[4 * i + 2] = t.z, v[4 * i + 3] = t.w;
+    }
+    const int ws = (start & 15) >> 2;
+    const uint32_t bs = (uint32_t)(start & 3) * 8;
+#pragma unroll
+    for (int i = 0; i < W + 2; ++i) v[i] = (ws & 2) ? v[i + 2] : v[i];
+#pragma unroll
+    for (int i = 0; i < W + 1; ++i) v[i] = (ws & 1) ? v[i + 1] : v[i];
+#pragma unroll
+    for (int i = 0; i < W; ++i) out[i] = __funnelshift_r(v[i], v[i + 1], bs);
+}
+
+template <bool Q6>
 __global__ void __launch_bounds__(kThreads, 1)
-    q4k_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_q, size_t n_in,
+    kquant_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_q, size_t n_in,
                   size_t n_out, size_t n_tokens, const float* q8_scales, float* y, int* err) {
+    using L = Lay<Q6>;
     extern __shared__ unsigned char smem_raw[];
     unsigned char* sm = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const uint32_t sb = smem_u32(sm);
@@ -137,7 +171,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int tid = threadIdx.x, warp = tid >> 5;
     const size_t r0 = (size_t)blockIdx.x * kM, t0 = (size_t)blockIdx.y * kN;
     const size_t nb = n_in / kQK;
-    const uint32_t full0 = sb + kOffBar, a_full = full0 + 16, mma_done = full0 + 24;
+    const uint32_t full0 = sb + L::kOffBar, a_full = full0 + 16, mma_done = full0 + 24;
 
     if (warp == 0) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&s_tmem)),
@@ -149,6 +183,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         s_fail = s_wfail = 0;
     }
+    if constexpr (Q6) {  // balanced base-7 digits (e0, e1, e2) of every int8 scale, each + 3
+        if (tid < 256) {
+            int r = tid - 128, dg = 0;
+            for (int i = 0; i < 3; ++i) {
+                const int qt = (r + 3 + 7 * 25) / 7 - 25;  // floor((r + 3) / 7), r >= -171
+                dg |= (r - 7 * qt + 3) << (4 * i);
+                r = qt;
+            }
+            reinterpret_cast<unsigned short*>(sm + L::kOffLut)[tid] = (unsigned short)dg;
+        }
+    }
     tc_before();
     __syncthreads();
     tc_after();
@@ -159,9 +204,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         if ((tid & 31) == 0) {
             auto load = [&](size_t bb) {
                 const uint32_t full = full0 + 8 * (uint32_t)(bb & 1), slot = (uint32_t)(bb & 1);
-                asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(full), "r"(kTxBytes)
+                asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(full), "r"(L::kTxBytes)
                              : "memory");
-                tma_load_2d(sb + kOffRaw + slot * kRawTile, &tm_w, (int)(bb * 144), (int)r0, full);
+                tma_load_2d(sb + L::kOffRaw + slot * L::kRawTile, &tm_w, (int)((bb * L::kBlockBytes) & ~size_t(15)), (int)r0,
+                            full);
                 tma_load_2d(sb + kOffB + slot * kTileB, &tm_q, (int)(bb * kQK), (int)t0, full);
                 tma_load_2d(sb + kOffB + slot * kTileB + kAtomB, &tm_q, (int)(bb * kQK + 128), (int)t0, full);
             };
@@ -232,19 +278,25 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (b < nb) mbar_try(full0 + 8 * (uint32_t)(b & 1), (unsigned)((b >> 1) & 1));
             if (b >= 1) {  // epilogue of block b-1
                 tc_after();
-                const float* sx = reinterpret_cast<const float*>(sm + kOffSx + ((b - 1) & 1) * kN * 4) + 32 * quarter;
+                const float* sx = reinterpret_cast<const float*>(sm + L::kOffSx + ((b - 1) & 1) * kN * 4) + 32 * quarter;
 #pragma unroll
                 for (int h = 0; h < 2; ++h) {
-                    int lo[16], hi[16], mv[16];
-                    tmem_ld16(t_lane + 16 * h, lo);
-                    tmem_ld16(t_lane + kN + 16 * h, hi);
-                    tmem_ld16(t_lane + 2 * kN + 16 * h, mv);
+                    int a0[16], a1[16], a2[16];
+                    tmem_ld16(t_lane + 16 * h, a0);
+                    tmem_ld16(t_lane + kN + 16 * h, a1);
+                    tmem_ld16(t_lane + 2 * kN + 16 * h, a2);
                     tmem_wait();
 #pragma unroll
                     for (int i = 0; i < 16; ++i) {
-                        const int sd = lo[i] + 8 * hi[i];
-                        const float v = __fmul_rn(sx[16 * h + i], __fsub_rn(__fmul_rn(d, __int2float_rn(sd)),
-                                                                            __fmul_rn(dmin, __int2float_rn(mv[i]))));
+                        float v;
+                        if constexpr (Q6) {  // s = a0 + 7 a1 + 49 a2; sx * (d * s)
+                            const int isum = a0[i] + 7 * a1[i] + 49 * a2[i];
+                            v = __fmul_rn(sx[16 * h + i], __fmul_rn(d, __int2float_rn(isum)));
+                        } else {  // sd = lo + 8 hi, sm = min; sx * (d * sd - dmin * sm)
+                            const int sd = a0[i] + 8 * a1[i];
+                            v = __fmul_rn(sx[16 * h + i], __fsub_rn(__fmul_rn(d, __int2float_rn(sd)),
+                                                                    __fmul_rn(dmin, __int2float_rn(a2[i]))));
+                        }
                         acc[16 * h + i] = __fadd_rn(acc[16 * h + i], v);
                     }
                 }
@@ -252,48 +304,98 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             QTRACE(1);
             if (b == nb) break;
-            // unpack chunk `quarter` (64 weights: sub-blocks 2q (low nibbles), 2q+1 (high)) of `row`
-            const unsigned char* raw = sm + kOffRaw + (b & 1) * kRawTile + row * kRawRow;
-            const uint4 sc4 = *reinterpret_cast<const uint4*>(raw);  // d, dmin, scales[0..11]
-            d = f16f(sc4.x & 0xffffu);
-            dmin = f16f(sc4.x >> 16);
-            const uint32_t s0 = sc4.y, s1 = sc4.z, s2 = sc4.w;  // scale bytes 0-3, 4-7, 8-11
-            uint32_t sc[2], mn[2];
+            if constexpr (Q6) {
+                // unpack weights 64 quarter .. +63 of `row`: half n = quarter / 2, groups g = 2 (quarter
+                // % 2) + gi of 32 weights, each two 16-wide sub-blocks with one int8 scale (layout of
+                // dot_q6k_block_q8: ql low/high nibbles, qh 2-bit fields). The block starts o bytes
+                // into its 16-byte aligned box row, so its bytes are read with aligned 16-byte loads
+                // (conflict-free at the 240-byte row stride) and realigned in registers.
+                const int o = (int)((b * L::kBlockBytes) & 15);
+                const unsigned char* rowp = sm + L::kOffRaw + (b & 1) * L::kRawTile + row * L::kRawRow;
+                d = f16f(*reinterpret_cast<const unsigned short*>(rowp + o + 208));
+                const int n = quarter >> 1, hi_nib = quarter & 1;
+                uint32_t qlw[16], qhw[8];
+                load_realigned<16>(rowp, 64 * n + o, qlw);
+                load_realigned<8>(rowp, 128 + 32 * n + o, qhw);
+                const signed char* scs = reinterpret_cast<const signed char*>(rowp + o + 192 + 8 * n);
+                const unsigned short* lut = reinterpret_cast<const unsigned short*>(sm + L::kOffLut);
 #pragma unroll
-            for (int h = 0; h < 2; ++h) {
-                const int j = 2 * quarter + h;
-                // 6-bit scale and min of sub-block j (ggml's get_scale_min_k4)
-                if (j < 4) {
-                    sc[h] = (s0 >> (8 * j)) & 63;
-                    mn[h] = (s1 >> (8 * j)) & 63;
-                } else {
-                    const uint32_t b8 = (s2 >> (8 * (j - 4))) & 0xff;
-                    sc[h] = (b8 & 0x0f) | (((s0 >> (8 * (j - 4) + 6)) & 3) << 4);
-                    mn[h] = (b8 >> 4) | (((s1 >> (8 * (j - 4) + 6)) & 3) << 4);
+                for (int gi = 0; gi < 2; ++gi) {
+                    const int g = 2 * hi_nib + gi;
+#pragma unroll
+                    for (int sub = 0; sub < 2; ++sub) {
+                        // balanced base-7 digits of the scale: s = e0 + 7 e1 + 49 e2, e_i in [-3, 3]
+                        const uint32_t dg = lut[scs[2 * g + sub] + 128];
+                        int e[3];
+                        uint32_t c[3];
+#pragma unroll
+                        for (int i = 0; i < 3; ++i) {
+                            e[i] = (int)((dg >> (4 * i)) & 15) - 3;
+                            c[i] = (uint32_t)(128 - 32 * e[i]) * 0x01010101u;
+                        }
+                        uint32_t av[3][4];
+#pragma unroll
+                        for (int w4 = 0; w4 < 4; ++w4) {
+                            const uint32_t l = qlw[8 * gi + 4 * sub + w4];
+                            const uint32_t nib = hi_nib ? (l >> 4) & 0x0f0f0f0fu : l & 0x0f0f0f0fu;
+                            const uint32_t q6 = nib | (((qhw[4 * sub + w4] >> (2 * g)) & 0x03030303u) << 4);
+                            // bytewise (q6 - 32) e: q6 e + 128 - 32 e lies in [32, 224] for every byte,
+                            // so the 32-bit multiply-add has no carries or borrows between bytes, and
+                            // flipping the top bit subtracts the 128 again as an s8
+#pragma unroll
+                            for (int i = 0; i < 3; ++i) av[i][w4] = (q6 * (uint32_t)e[i] + c[i]) ^ 0x80808080u;
+                        }
+                        const uint32_t off = swz_a(row, 128 * n + 32 * g + 16 * sub);
+#pragma unroll
+                        for (int i = 0; i < 3; ++i)
+                            *reinterpret_cast<uint4*>(sm + kOffA + i * kTileA + off) =
+                                make_uint4(av[i][0], av[i][1], av[i][2], av[i][3]);
+                    }
                 }
-            }
-#pragma unroll
-            for (int p = 0; p < 32; p += 16) {
-                const uint4 q = *reinterpret_cast<const uint4*>(raw + 16 + quarter * 32 + p);
-                const uint32_t qw[4] = {q.x, q.y, q.z, q.w};
+            } else {
+                // unpack chunk `quarter` (64 weights: sub-blocks 2q (low nibbles), 2q+1 (high)) of `row`
+                const unsigned char* raw = sm + L::kOffRaw + (b & 1) * L::kRawTile + row * L::kRawRow;
+                const uint4 sc4 = *reinterpret_cast<const uint4*>(raw);  // d, dmin, scales[0..11]
+                d = f16f(sc4.x & 0xffffu);
+                dmin = f16f(sc4.x >> 16);
+                const uint32_t s0 = sc4.y, s1 = sc4.z, s2 = sc4.w;  // scale bytes 0-3, 4-7, 8-11
+                uint32_t sc[2], mn[2];
 #pragma unroll
                 for (int h = 0; h < 2; ++h) {
-                    uint32_t lo[4], hi[4];
-#pragma unroll
-                    for (int e = 0; e < 4; ++e) {
-                        const uint32_t nib = h ? (qw[e] >> 4) & 0x0f0f0f0fu : qw[e] & 0x0f0f0f0fu;
-                        lo[e] = nib * (sc[h] & 7);  // bytewise: 15 * 7 < 256, no carries
-                        hi[e] = nib * (sc[h] >> 3);
+                    const int j = 2 * quarter + h;
+                    // 6-bit scale and min of sub-block j (ggml's get_scale_min_k4)
+                    if (j < 4) {
+                        sc[h] = (s0 >> (8 * j)) & 63;
+                        mn[h] = (s1 >> (8 * j)) & 63;
+                    } else {
+                        const uint32_t b8 = (s2 >> (8 * (j - 4))) & 0xff;
+                        sc[h] = (b8 & 0x0f) | (((s0 >> (8 * (j - 4) + 6)) & 3) << 4);
+                        mn[h] = (b8 >> 4) | (((s1 >> (8 * (j - 4) + 6)) & 3) << 4);
                     }
-                    const uint32_t m4 = mn[h] * 0x01010101u;
-                    const uint32_t off = swz_a(row, (2 * quarter + h) * 32 + p);
-                    *reinterpret_cast<uint4*>(sm + kOffA + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
-                    *reinterpret_cast<uint4*>(sm + kOffA + kTileA + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-                    *reinterpret_cast<uint4*>(sm + kOffA + 2 * kTileA + off) = make_uint4(m4, m4, m4, m4);
+                }
+#pragma unroll
+                for (int p = 0; p < 32; p += 16) {
+                    const uint4 q = *reinterpret_cast<const uint4*>(raw + 16 + quarter * 32 + p);
+                    const uint32_t qw[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) {
+                        uint32_t lo[4], hi[4];
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            const uint32_t nib = h ? (qw[e] >> 4) & 0x0f0f0f0fu : qw[e] & 0x0f0f0f0fu;
+                            lo[e] = nib * (sc[h] & 7);  // bytewise: 15 * 7 < 256, no carries
+                            hi[e] = nib * (sc[h] >> 3);
+                        }
+                        const uint32_t m4 = mn[h] * 0x01010101u;
+                        const uint32_t off = swz_a(row, (2 * quarter + h) * 32 + p);
+                        *reinterpret_cast<uint4*>(sm + kOffA + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+                        *reinterpret_cast<uint4*>(sm + kOffA + kTileA + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+                        *reinterpret_cast<uint4*>(sm + kOffA + 2 * kTileA + off) = make_uint4(m4, m4, m4, m4);
+                    }
                 }
             }
             if (tid < kN) {  // this block's token scales for the epilogue; the next block's from memory
-                reinterpret_cast<float*>(sm + kOffSx + (b & 1) * kN * 4)[tid] = sx_next;
+                reinterpret_cast<float*>(sm + L::kOffSx + (b & 1) * kN * 4)[tid] = sx_next;
                 sx_next = sx_ok && b + 1 < nb ? sx_src[b + 1] : 0.f;
             }
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // A -> tensor core
@@ -346,27 +448,41 @@ bool byte_map(CUtensorMap* m, const void* base, size_t row_bytes, size_t rows, u
 
 }  // namespace
 
-cudaError_t launch_q4k_tc(const uint8_t* w, size_t n_in, size_t n_out, size_t n_tokens, const int8_t* q8,
-                          const float* q8_scales, float* y, int* err, cudaStream_t s) {
-    // TMA wants 16-byte aligned bases; rows and tokens must fit the 32-bit coordinates
-    if ((reinterpret_cast<uintptr_t>(w) & 15) || (reinterpret_cast<uintptr_t>(q8) & 15) || n_out >= (1u << 31) ||
-        n_tokens >= (1u << 31) || n_in / kQK * 144 >= (1u << 31))
+namespace {
+template <bool Q6>
+cudaError_t launch_tc(const uint8_t* w, size_t n_in, size_t n_out, size_t n_tokens, const int8_t* q8,
+                      const float* q8_scales, float* y, int* err, cudaStream_t s) {
+    using L = Lay<Q6>;
+    const size_t row_bytes = n_in / kQK * L::kBlockBytes;
+    // TMA wants 16-byte aligned bases and row strides; rows and tokens must fit the 32-bit
+    // coordinates
+    if ((reinterpret_cast<uintptr_t>(w) & 15) || (reinterpret_cast<uintptr_t>(q8) & 15) || (row_bytes & 15) ||
+        n_out >= (1u << 31) || n_tokens >= (1u << 31) || row_bytes >= (1u << 31))
         return cudaErrorNotSupported;
     CUtensorMap tw, tq;
-    if (!byte_map(&tw, w, n_in / kQK * 144, n_out, kRawRow, kM, CU_TENSOR_MAP_SWIZZLE_NONE) ||
+    if (!byte_map(&tw, w, row_bytes, n_out, L::kRawRow, kM, CU_TENSOR_MAP_SWIZZLE_NONE) ||
         !byte_map(&tq, q8, n_in, n_tokens, 128, kN, CU_TENSOR_MAP_SWIZZLE_128B))
         return cudaErrorNotSupported;
     static bool attr_set[64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 0 || dev >= 64 || !attr_set[dev]) {
-        cudaError_t e = cudaFuncSetAttribute(q4k_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+        cudaError_t e =
+            cudaFuncSetAttribute(kquant_tc_kernel<Q6>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kSmemBytes);
         if (e != cudaSuccess) return e;
         if (dev >= 0 && dev < 64) attr_set[dev] = true;
     }
     const dim3 grid((unsigned)((n_out + kM - 1) / kM), (unsigned)((n_tokens + kN - 1) / kN));
-    q4k_tc_kernel<<<grid, kThreads, kSmemBytes, s>>>(tw, tq, n_in, n_out, n_tokens, q8_scales, y, err);
+    kquant_tc_kernel<Q6><<<grid, kThreads, L::kSmemBytes, s>>>(tw, tq, n_in, n_out, n_tokens, q8_scales, y, err);
     return cudaGetLastError();
+}
+}  // namespace
+
+cudaError_t launch_kquant_tc(int dtype, const uint8_t* w, size_t n_in, size_t n_out, size_t n_tokens,
+                             const int8_t* q8, const float* q8_scales, float* y, int* err, cudaStream_t s) {
+    if (dtype == kGgmlQ4K) return launch_tc<false>(w, n_in, n_out, n_tokens, q8, q8_scales, y, err, s);
+    if (dtype == kGgmlQ6K) return launch_tc<true>(w, n_in, n_out, n_tokens, q8, q8_scales, y, err, s);
+    return cudaErrorNotSupported;
 }
 
 }  // namespace bebelm

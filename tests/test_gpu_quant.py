@@ -113,13 +113,17 @@ def test_tiled_matmul_bit_exact(dtype, gen, n_out, n_in, t):
     np.testing.assert_array_equal(bb.matmul(dtype, w, n_in, n_out, xs, t), oracle.matmul(dtype, w, n_in, n_out, xs, t))
 
 
-@pytest.mark.parametrize("n_out,n_in,t", [(300, 1024, 200), (2048, 2048, 128), (128, 256, 64)])
-def test_q4k_tensor_core_matmul_bit_exact(n_out, n_in, t):
-    """From 64 tokens on, Q4_K takes the tensor-core kernel (tcgen05 kind::i8, exact integer
+@pytest.mark.parametrize("dtype,gen,n_out,n_in,t", [
+    (bb.GGML_Q4_K, random_q4k, 300, 1024, 200), (bb.GGML_Q4_K, random_q4k, 2048, 2048, 128),
+    (bb.GGML_Q4_K, random_q4k, 128, 256, 64),
+    (bb.GGML_Q6_K, random_q6k, 512, 2048, 130), (bb.GGML_Q6_K, random_q6k, 200, 4096, 64),
+    (bb.GGML_Q6_K, random_q6k, 96, 1024, 70)])  # n_in 1024: Q6_K rows not 16-byte multiples -> dp4a
+def test_kquant_tensor_core_matmul_bit_exact(dtype, gen, n_out, n_in, t):
+    """From 64 tokens on, K-quants take the tensor-core kernel (tcgen05 kind::i8, exact integer
     sub-block dots): ragged row and token tiles, a zero token and a saturated token, same bits."""
-    w = random_q4k(n_out, n_in, seed=n_out + t)
+    w = gen(n_out, n_in, seed=n_out + t)
     xs = oracle.normal(120 + t, (t, n_in))
     xs[5] = 0.0
     xs[t - 1] = np.where(np.arange(n_in) % 3, 1e3, -1e3)  # every quant at +-127
-    np.testing.assert_array_equal(bb.matmul(bb.GGML_Q4_K, w, n_in, n_out, xs, t),
-                                  oracle.matmul(oracle.GG_Q4_K, w, n_in, n_out, xs, t))
+    np.testing.assert_array_equal(bb.matmul(dtype, w, n_in, n_out, xs, t),
+                                  oracle.matmul(dtype, w, n_in, n_out, xs, t))
