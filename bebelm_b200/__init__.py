@@ -43,7 +43,8 @@ EXPORTS = [
     "bebelm_attn_step_allgather", "bebelm_step_plan_create", "bebelm_step_plan_launch", "bebelm_step_plan_steps",
     "bebelm_step_plan_finish", "bebelm_matvec", "bebelm_matmul", "bebelm_dequantize",
     "bebelm_attn_weights_create", "bebelm_attn_weights_destroy", "bebelm_attn_layer_step", "bebelm_attn_layer_batch",
-    "bebelm_step_plan_create_layer", "bebelm_step_plan_launch_layer",
+    "bebelm_step_plan_create_layer", "bebelm_step_plan_launch_layer", "bebelm_head_create", "bebelm_head_destroy",
+    "bebelm_head_logits", "bebelm_sample_greedy",
 ]
 GGML_F32, GGML_F16, GGML_Q4_K, GGML_Q6_K = 0, 1, 12, 14
 IPC_HANDLE_BYTES = 64
@@ -112,6 +113,10 @@ def load_library(path: str = LIB_PATH):
         "bebelm_attn_layer_batch": ([vp, i, vp, vp, sz, sz, i, f, f, vp, i, vp], i),
         "bebelm_step_plan_create_layer": ([vp, i, vp, sz, C.POINTER(vp)], i),
         "bebelm_step_plan_launch_layer": ([vp, vp, f, f, vp, vp], i),
+        "bebelm_head_create": ([i, i, vp, sz, sz, vp, C.POINTER(vp)], i),
+        "bebelm_head_destroy": ([vp], i),
+        "bebelm_head_logits": ([vp, vp, f, vp, vp, i, vp], i),
+        "bebelm_sample_greedy": ([vp, sz, vp, sz, f, vp, i, vp], i),
     }
     for name, (args, res) in sig.items():
         fn = getattr(L, name)
@@ -486,6 +491,72 @@ class AttnWeights:
             self.close()
         except Exception:
             pass
+
+
+class Head:
+    """The logits head on the device (``logits_from_hidden``, src/model.rs:379-388): the final
+    RMSNorm (``token_embd_norm``) and the tied ``token_embd`` matvec, as stored (ggml dtype,
+    [vocab][hidden] packed bytes), plus the greedy token."""
+
+    def __init__(self, dtype: int, token_embd, hidden: int, vocab: int, norm_gain, device: int = 0):
+        w = np.ascontiguousarray(np.frombuffer(token_embd, np.uint8) if isinstance(token_embd, (bytes, bytearray))
+                                 else token_embd).view(np.uint8)
+        g = np.ascontiguousarray(norm_gain, np.float32)
+        self.hidden, self.vocab = hidden, vocab
+        self._h = C.c_void_p()
+        _check(load_library().bebelm_head_create(device, dtype, w.ctypes.data, hidden, vocab, g.ctypes.data,
+                                                 C.byref(self._h)))
+
+    def logits(self, h, eps: float = RMS_EPS, logits=True, token=True, stream=None):
+        """h [hidden] -> (logits [vocab] or None, token or None). Host arrays give numpy results
+        (token an int); device tensors give device results (token an int32 tensor [1]) computed
+        without leaving the device."""
+        (hb,), mem = _bufs(h)
+        if mem == MEM_HOST:
+            lg = np.zeros(self.vocab, np.float32) if logits else None
+            tk = np.zeros(1, np.uint32) if token else None
+        else:
+            import torch
+            lg = hb[2].new_empty(self.vocab) if logits else None
+            tk = hb[2].new_zeros(1, dtype=torch.int32) if token else None
+        lp = _buf(lg)[0] if lg is not None else None
+        tp = None if tk is None else (tk.ctypes.data if mem == MEM_HOST else tk.data_ptr())
+        _check(load_library().bebelm_head_logits(self._h, hb[0], eps, lp, tp, mem, _stream_ptr(stream, mem)))
+        if mem == MEM_HOST and tk is not None:
+            tk = int(tk[0])
+        return lg, tk
+
+    def close(self):
+        if self._h:
+            load_library().bebelm_head_destroy(self._h)
+            self._h = C.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def sample_greedy(logits, history=(), repeat_penalty: float = 1.0, stream=None):
+    """``Sampler::sample`` with temperature <= 0 (src/sampler.rs:64-88): presence penalty on
+    ``logits`` in place, then ``argmax``. Host: returns the token id; device (CUDA float32
+    tensor logits, history a CUDA int32 tensor or empty): returns an int32 tensor [1]."""
+    (lb,), mem = _bufs(logits)
+    n = lb[2].size if mem == MEM_HOST else lb[2].numel()
+    if mem == MEM_HOST:
+        hist = np.ascontiguousarray(np.asarray(history, np.uint32))
+        tok = np.zeros(1, np.uint32)
+        _check(load_library().bebelm_sample_greedy(lb[0], n, hist.ctypes.data if hist.size else None, hist.size,
+                                                   repeat_penalty, tok.ctypes.data, mem, None))
+        return int(tok[0])
+    import torch
+    hist = history if hasattr(history, "data_ptr") else torch.tensor(list(history), dtype=torch.int32,
+                                                                      device=lb[2].device)
+    tok = torch.zeros(1, dtype=torch.int32, device=lb[2].device)
+    _check(load_library().bebelm_sample_greedy(lb[0], n, hist.data_ptr() if hist.numel() else None, hist.numel(),
+                                               repeat_penalty, tok.data_ptr(), mem, _stream_ptr(stream, mem)))
+    return tok
 
 
 def attn_layer_step(cache: "Cache", layer: int, weights: AttnWeights, x, pos: int, theta: float = ROPE_THETA,

@@ -12,7 +12,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libbebelm_attn.so")
-SOURCES = ["api.cu", "norm_rope.cu", "decode.cu", "prefill.cu", "quant.cu", "quant_tc.cu"]
+SOURCES = ["api.cu", "norm_rope.cu", "decode.cu", "prefill.cu", "quant.cu", "quant_tc.cu", "head.cu"]
 HEADERS = ["internal.h"]
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]

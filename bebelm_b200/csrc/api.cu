@@ -202,7 +202,7 @@ struct bebelm_kv_pool {
     int num_sms = 148;
     int n_seqs = 0;              // live sequences drawing from this pool
     // scratch shared by every call on this pool's sequences (stream-ordered)
-    DevBuf io, qn, part, counters, seqdesc, pf, q8, proj;
+    DevBuf io, qn, part, counters, seqdesc, pf, q8, proj, sample;
     ErrWord err;
     PinBuf pin;
     UploadRing uploads;
@@ -375,6 +375,7 @@ void pool_free(bebelm_kv_pool* P) {
     P->pf.release();
     P->q8.release();
     P->proj.release();
+    P->sample.release();
     P->err.release();
     P->pin.release();
     delete P;
@@ -2049,6 +2050,138 @@ int bebelm_step_plan_launch_layer(bebelm_step_plan* pl, const float* x, float th
     TRY(bebelm_step_plan_launch(pl, L.q, L.k, L.v, W->gains.as<float>(), W->gains.as<float>() + 64, theta, eps,
                                 L.attn, stream));
     return project_token_out(W, L.attn, out, s);
+}
+
+// ---------------------------------------------------------------- logits head ---
+
+struct bebelm_head {
+    int device = 0, dtype = 0;
+    size_t hidden = 0, vocab = 0;
+    DevBuf w, gain, normed, logits, token;
+};
+
+int bebelm_head_create(int device, int dtype, const void* token_embd, size_t hidden, size_t vocab,
+                       const float* norm_gain, bebelm_head** out) {
+    if (!out) return fail(BEBELM_ERR_INVALID, "out is null");
+    *out = nullptr;
+    if (!token_embd || !norm_gain) return fail(BEBELM_ERR_INVALID, "null buffer");
+    TRY(check_ggml(dtype, hidden));
+    if (hidden == 0 || hidden > 8192) return fail(BEBELM_ERR_UNSUPPORTED, "hidden (%zu) must be 1..8192", hidden);
+    if (vocab == 0 || vocab >= (1ull << 32)) return fail(BEBELM_ERR_INVALID, "vocab (%zu) must be 1..2^32-1", vocab);
+    int n_dev = 0;
+    CUDA_TRY(cudaGetDeviceCount(&n_dev));
+    if (device < 0 || device >= n_dev) return fail(BEBELM_ERR_INVALID, "device %d not present", device);
+    DeviceGuard g(device);
+    auto* H = new bebelm_head();
+    H->device = device;
+    H->dtype = dtype;
+    H->hidden = hidden;
+    H->vocab = vocab;
+    const size_t wbytes = ggml_row_bytes(dtype, hidden) * vocab;
+    int rc = H->w.ensure(wbytes);
+    if (!rc && cudaMemcpy(H->w.p, token_embd, wbytes, cudaMemcpyHostToDevice) != cudaSuccess)
+        rc = fail(BEBELM_ERR_CUDA, "uploading token_embd failed");
+    if (!rc) rc = H->gain.ensure(hidden * sizeof(float));
+    if (!rc && cudaMemcpy(H->gain.p, norm_gain, hidden * sizeof(float), cudaMemcpyHostToDevice) != cudaSuccess)
+        rc = fail(BEBELM_ERR_CUDA, "uploading the norm gain failed");
+    if (!rc) rc = H->normed.ensure(hidden * sizeof(float));
+    if (!rc) rc = H->logits.ensure(vocab * sizeof(float));
+    if (!rc) rc = H->token.ensure(256);
+    if (rc) {
+        H->w.release();
+        H->gain.release();
+        H->normed.release();
+        H->logits.release();
+        H->token.release();
+        delete H;
+        return rc;
+    }
+    *out = H;
+    return 0;
+}
+
+int bebelm_head_destroy(bebelm_head* H) {
+    if (!H) return 0;
+    DeviceGuard g(H->device);
+    cudaDeviceSynchronize();
+    H->w.release();
+    H->gain.release();
+    H->normed.release();
+    H->logits.release();
+    H->token.release();
+    delete H;
+    return 0;
+}
+
+int bebelm_head_logits(bebelm_head* H, const float* h, float eps, float* logits, uint32_t* token, int mem,
+                       void* stream) {
+    if (!H) return fail(BEBELM_ERR_INVALID, "null head");
+    TRY(check_mem(mem));
+    if (!h) return fail(BEBELM_ERR_INVALID, "null buffer");
+    DeviceGuard g(H->device);
+    cudaStream_t s = as_stream(stream);
+    auto run = [&](const float* dh, float* dlogits, uint32_t* dtoken) -> int {
+        CUDA_TRY(launch_rmsnorm_row(dh, H->gain.as<float>(), (int)H->hidden, eps, H->normed.as<float>(), s));
+        QmvSegs sg{};
+        sg.n = 1;
+        sg.dtype[0] = H->dtype;
+        sg.w[0] = H->w.as<uint8_t>();
+        sg.row_bytes[0] = ggml_row_bytes(H->dtype, H->hidden);
+        sg.n_out[0] = H->vocab;
+        sg.y[0] = dlogits;
+        CUDA_TRY(launch_qmv_multi(sg, H->normed.as<float>(), H->hidden, s));
+        if (dtoken) CUDA_TRY(launch_greedy(dlogits, H->vocab, nullptr, 0, 1.0f, nullptr, dtoken, s));
+        return 0;
+    };
+    if (mem == BEBELM_MEM_DEVICE)
+        return run(h, logits ? logits : H->logits.as<float>(), token);
+    std::lock_guard<std::mutex> lk(g_scratch_mu);
+    bebelm_kv_pool* P = nullptr;
+    TRY(scratch_pool(H->device, &P));
+    const size_t lbytes = logits ? 4 * H->vocab : 0, out_bytes = 256 + lbytes;
+    void *a0, *o;
+    Stage st[1] = {{h, 4 * H->hidden, &a0}};
+    TRY(stage_in(P, st, 1, out_bytes, &o, s));
+    char* dout = static_cast<char*>(o);
+    TRY(run(static_cast<const float*>(a0), logits ? reinterpret_cast<float*>(dout + 256) : H->logits.as<float>(),
+            reinterpret_cast<uint32_t*>(dout)));
+    std::vector<char> back(out_bytes);
+    TRY(stage_out(P, o, back.data(), out_bytes, s));
+    if (token) std::memcpy(token, back.data(), 4);
+    if (logits) std::memcpy(logits, back.data() + 256, lbytes);
+    return 0;
+}
+
+int bebelm_sample_greedy(float* logits, size_t n, const uint32_t* history, size_t n_history, float repeat_penalty,
+                         uint32_t* token, int mem, void* stream) {
+    TRY(check_mem(mem));
+    if (!logits || !token || (n_history && !history)) return fail(BEBELM_ERR_INVALID, "null buffer");
+    if (n == 0 || n >= (1ull << 32)) return fail(BEBELM_ERR_INVALID, "n (%zu) must be 1..2^32-1", n);
+    const bool pen = repeat_penalty != 1.0f && n_history > 0;
+    if (pen && mem == BEBELM_MEM_HOST)
+        for (size_t i = 0; i < n_history; ++i)
+            if (history[i] >= n) return fail(BEBELM_ERR_INVALID, "history token %u out of range", history[i]);
+    int dev;
+    TRY(current_device(&dev));
+    cudaStream_t s = as_stream(stream);
+    std::lock_guard<std::mutex> lk(g_scratch_mu);
+    bebelm_kv_pool* P = nullptr;
+    TRY(scratch_pool(dev, &P));
+    if (pen) TRY(P->sample.ensure((n + 31) / 32 * 4, false, s));
+    uint32_t* bitmap = pen ? P->sample.as<uint32_t>() : nullptr;
+    if (mem == BEBELM_MEM_DEVICE) {
+        CUDA_TRY(launch_greedy(logits, n, history, pen ? n_history : 0, repeat_penalty, bitmap, token, s));
+        return 0;
+    }
+    void *a0, *a1, *o;
+    Stage st[2] = {{logits, 4 * n, &a0}, {pen ? history : nullptr, pen ? 4 * n_history : 0, &a1}};
+    TRY(stage_in(P, st, 2, 4, &o, s));
+    CUDA_TRY(launch_greedy(static_cast<float*>(a0), n, static_cast<const uint32_t*>(a1), pen ? n_history : 0,
+                           repeat_penalty, bitmap, static_cast<uint32_t*>(o), s));
+    TRY(stage_out(P, o, token, 4, s));
+    // the penalty rewrites the seen tokens' logits in place, as the reference's sampler does
+    if (pen) CUDA_TRY(cudaMemcpy(logits, a0, 4 * n, cudaMemcpyDeviceToHost));
+    return 0;
 }
 
 }  // extern "C"

@@ -238,4 +238,12 @@ struct QmvSegs {
 };
 cudaError_t launch_qmv_multi(const QmvSegs& segs, const float* x, size_t n_in, cudaStream_t s);
 
+// logits head (head.cu): final RMSNorm of one hidden state [n <= 8192], one CTA
+cudaError_t launch_rmsnorm_row(const float* x, const float* gain, int n, float eps, float* out, cudaStream_t s);
+// Sampler::sample with temperature <= 0: presence penalty (when penalty != 1 and history is
+// non-empty; bitmap = (n + 31) / 32 words of scratch) on logits in place, then argmax -> *token
+cudaError_t launch_greedy(float* logits, size_t n, const uint32_t* history, size_t n_history, float penalty,
+                          uint32_t* bitmap, uint32_t* token, cudaStream_t s);
+
+
 }  // namespace bebelm

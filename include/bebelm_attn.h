@@ -308,6 +308,27 @@ BEBELM_API int bebelm_attn_step_allgather(bebelm_kv* kv, bebelm_peer_group* g, i
                                           const float* q_gain, const float* k_gain, float theta,
                                           float eps, size_t pos, float* out, int mem, void* stream);
 
+/* ---- logits head and greedy token choice (next after the projections) ----
+ * Replaces Model::logits_from_hidden (src/model.rs:379-388: final RMSNorm with
+ * token_embd_norm, then the tied token_embd matvec) and, for temperature <= 0,
+ * Sampler::sample (src/sampler.rs:64-88) with argmax (src/sampler.rs:139-149).
+ * token_embd is uploaded once as stored (ggml dtype, [vocab][hidden], hidden <= 8192). */
+typedef struct bebelm_head bebelm_head;
+BEBELM_API int bebelm_head_create(int device, int dtype, const void* token_embd, size_t hidden, size_t vocab,
+                                  const float* norm_gain, bebelm_head** out);
+BEBELM_API int bebelm_head_destroy(bebelm_head* head);
+/* h [hidden] -> logits [vocab] (nullable) and the greedy token (argmax, nullable). Device
+ * memory: with logits null the head's own buffer holds them; nothing leaves the device. */
+BEBELM_API int bebelm_head_logits(bebelm_head* head, const float* h, float eps, float* logits,
+                                  uint32_t* token, int mem, void* stream);
+/* Sampler::sample with temperature <= 0: when repeat_penalty != 1, each distinct token of
+ * history [n_history] once: l > 0 ? l / p : l * p (logits rewritten in place, as the
+ * reference does); then the first index of the maximum (NaN never wins; 0 when no logit
+ * is above -inf). Host history ids must be < n (BEBELM_ERR_INVALID otherwise); device
+ * history ids >= n are ignored. */
+BEBELM_API int bebelm_sample_greedy(float* logits, size_t n, const uint32_t* history, size_t n_history,
+                                    float repeat_penalty, uint32_t* token, int mem, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -64,6 +64,10 @@ def lib():
         L.orc_quantize_q8.argtypes = [_f32p, sz, i8p, _f32p, i32p]
         L.orc_matvec.argtypes = [C.c_int, u8p, sz, sz, _f32p, _f32p, _f32p, i8p, _f32p, i32p]
         L.orc_matmul.argtypes = [C.c_int, u8p, sz, sz, _f32p, sz, _f32p, _f32p, i8p, _f32p, i32p]
+        u32p = np.ctypeslib.ndpointer(np.uint32, flags="C_CONTIGUOUS")
+        L.orc_argmax.argtypes = [_f32p, sz]
+        L.orc_argmax.restype = sz
+        L.orc_sample_greedy.argtypes = [_f32p, sz, u32p, sz, C.c_float, u32p]
         _lib = L
     return _lib
 
@@ -256,3 +260,27 @@ def matmul(dtype: int, w, n_in: int, n_out: int, x, n_tokens: int = 1) -> np.nda
 
 def matvec(dtype: int, w, n_in: int, n_out: int, x) -> np.ndarray:
     return matmul(dtype, w, n_in, n_out, x, 1)
+
+
+# ------------------------------------------------------- greedy token choice --
+def argmax(x) -> int:
+    """src/sampler.rs:139-149."""
+    x = _f32(x)
+    return int(lib().orc_argmax(x, x.size))
+
+
+def sample_greedy(logits: np.ndarray, history=(), repeat_penalty: float = 1.0) -> int:
+    """Sampler::sample with temperature <= 0 (src/sampler.rs:64-88); logits (float32) are
+    rewritten in place by the penalty, as in the reference."""
+    if logits.dtype != np.float32 or not logits.flags.c_contiguous:
+        raise ValueError("logits must be a contiguous float32 array (rewritten in place)")
+    h = np.ascontiguousarray(np.asarray(history, np.uint32).reshape(-1))
+    tok = np.zeros(1, np.uint32)
+    if lib().orc_sample_greedy(logits, logits.size, h, h.size, repeat_penalty, tok):
+        raise ValueError("history token out of range")
+    return int(tok[0])
+
+
+def logits_head(dtype: int, token_embd, hidden: int, vocab: int, norm_gain, h, eps: float = 1e-5):
+    """Model::logits_from_hidden (src/model.rs:379-388): rmsnorm, then the tied matvec."""
+    return matvec(dtype, token_embd, hidden, vocab, rmsnorm(h, norm_gain, eps))

@@ -50,3 +50,12 @@ def test_argument_validation_without_device():
     assert L.bebelm_attn_decode_host(None, None, None, 1, 3, 2, 64, None) == bb.ERR_INVALID
     buf = C.create_string_buffer(64)
     assert L.bebelm_last_error(buf, 64) == 0 and buf.value
+
+    # logits head and greedy sampling: argument errors come before any device work
+    assert L.bebelm_head_create(0, 12, None, 2048, 100, None, C.byref(C.c_void_p())) == bb.ERR_INVALID
+    assert L.bebelm_head_logits(None, None, 1e-5, None, None, 0, None) == bb.ERR_INVALID
+    assert L.bebelm_sample_greedy(None, 4, None, 0, 1.0, None, 0, None) == bb.ERR_INVALID
+    lg = (C.c_float * 2)(1.0, 2.0)
+    hist = (C.c_uint32 * 1)(5)
+    tok = C.c_uint32()
+    assert L.bebelm_sample_greedy(lg, 2, hist, 1, 2.0, C.byref(tok), 0, None) == bb.ERR_INVALID  # id >= n

@@ -235,3 +235,26 @@ def test_matmul_is_matvec_per_token():
     y = oracle.matmul(oracle.GG_Q4_K, blk, 2048, 4, x, 3)
     for t in range(3):
         assert np.array_equal(y[t], oracle.matvec(oracle.GG_Q4_K, blk, 2048, 4, x[t]))
+
+
+def test_sampler_kats(kats):
+    """Greedy sampling (src/sampler.rs:64-88, argmax :139-149) against the reference's tests."""
+    for c in kats["sampler"]:
+        logits = np.array(c["logits"], np.float32)
+        assert oracle.sample_greedy(logits, c["history"], c["repeat_penalty"]) == c["token"], c["src"]
+    # the penalty rewrites the seen logits in place, each distinct token once
+    logits = np.array([10.0, 4.0, -1.0], np.float32)
+    oracle.sample_greedy(logits, [0, 0, 2], 2.0)
+    assert list(logits) == [5.0, 4.0, -2.0]
+
+
+def test_argmax_scan_semantics():
+    """The reference's strict `>` scan from -inf: first index on ties, NaN never wins, and 0
+    when nothing is above -inf."""
+    nan, inf = float("nan"), float("inf")
+    assert oracle.argmax([2.0, 5.0, 5.0, 1.0]) == 1
+    assert oracle.argmax([nan, 1.0, nan, 3.0]) == 3
+    assert oracle.argmax([-inf, -inf]) == 0
+    assert oracle.argmax([nan, nan]) == 0
+    assert oracle.argmax([-0.0, 0.0]) == 0
+    assert oracle.argmax([-inf, -3.0]) == 1
