@@ -2054,10 +2054,14 @@ int bebelm_step_plan_launch_layer(bebelm_step_plan* pl, const float* x, float th
 
 // ---------------------------------------------------------------- logits head ---
 
+constexpr size_t kHeadCandSlots = 1024;  // >= SMs per device
+constexpr size_t kHeadCandBytes = 2 * 4 * kHeadCandSlots + 256;
+
 struct bebelm_head {
     int device = 0, dtype = 0;
     size_t hidden = 0, vocab = 0;
-    DevBuf w, gain, normed, logits, token;
+    DevBuf w, gain, normed, logits, token, cand;  // cand: per-SM argmax candidates + counter
+    ErrWord err;  // a bounded wait of the streaming matvec that gave up
 };
 
 int bebelm_head_create(int device, int dtype, const void* token_embd, size_t hidden, size_t vocab,
@@ -2087,12 +2091,16 @@ int bebelm_head_create(int device, int dtype, const void* token_embd, size_t hid
     if (!rc) rc = H->normed.ensure(hidden * sizeof(float));
     if (!rc) rc = H->logits.ensure(vocab * sizeof(float));
     if (!rc) rc = H->token.ensure(256);
+    if (!rc) rc = H->err.ensure();
+    if (!rc) rc = H->cand.ensure(kHeadCandBytes, true);
     if (rc) {
         H->w.release();
         H->gain.release();
         H->normed.release();
         H->logits.release();
         H->token.release();
+        H->err.release();
+        H->cand.release();
         delete H;
         return rc;
     }
@@ -2109,6 +2117,8 @@ int bebelm_head_destroy(bebelm_head* H) {
     H->normed.release();
     H->logits.release();
     H->token.release();
+    H->err.release();
+    H->cand.release();
     delete H;
     return 0;
 }
@@ -2120,7 +2130,26 @@ int bebelm_head_logits(bebelm_head* H, const float* h, float eps, float* logits,
     if (!h) return fail(BEBELM_ERR_INVALID, "null buffer");
     DeviceGuard g(H->device);
     cudaStream_t s = as_stream(stream);
+    // a device-side timeout of an earlier device-memory call is reported here
+    if (H->err.read()) {
+        const int e = H->err.read();
+        H->err.clear();
+        return fail(BEBELM_ERR_TIMEOUT, "a device-side wait of the logits head timed out (code %d)", e);
+    }
     auto run = [&](const float* dh, float* dlogits, uint32_t* dtoken) -> int {
+        // vocab-sized K-quant matrices: one streaming launch (norm, matvec, argmax); otherwise
+        // the norm, the lane matvec and the argmax as three launches (same bits)
+        if (H->vocab >= 8192) {
+            float* cv = H->cand.as<float>();
+            const cudaError_t se = launch_head_stream(
+                H->dtype, H->w.as<uint8_t>(), H->vocab, dh, H->gain.as<float>(), eps, H->hidden, dlogits, dtoken, cv,
+                reinterpret_cast<uint32_t*>(cv + kHeadCandSlots), reinterpret_cast<unsigned*>(cv + 2 * kHeadCandSlots),
+                H->err.d, s);
+            if (se != cudaErrorNotSupported) {
+                CUDA_TRY(se);
+                return 0;
+            }
+        }
         CUDA_TRY(launch_rmsnorm_row(dh, H->gain.as<float>(), (int)H->hidden, eps, H->normed.as<float>(), s));
         QmvSegs sg{};
         sg.n = 1;
@@ -2147,6 +2176,11 @@ int bebelm_head_logits(bebelm_head* H, const float* h, float eps, float* logits,
             reinterpret_cast<uint32_t*>(dout)));
     std::vector<char> back(out_bytes);
     TRY(stage_out(P, o, back.data(), out_bytes, s));
+    if (H->err.read()) {
+        const int e = H->err.read();
+        H->err.clear();
+        return fail(BEBELM_ERR_TIMEOUT, "a device-side wait of the logits head timed out (code %d)", e);
+    }
     if (token) std::memcpy(token, back.data(), 4);
     if (logits) std::memcpy(logits, back.data() + 256, lbytes);
     return 0;

@@ -237,6 +237,17 @@ struct QmvSegs {
     float* y[3];
 };
 cudaError_t launch_qmv_multi(const QmvSegs& segs, const float* x, size_t n_in, cudaStream_t s);
+// one token against a large K-quant matrix (rows streamed by bulk copies; same bits as
+// launch_qmv_multi). cudaErrorNotSupported (nothing launched) for other dtypes, row sizes that
+// are not 16-byte multiples or unaligned weights. A wait that gives up stores to *err.
+cudaError_t launch_qmv_stream(int dtype, const uint8_t* w, size_t n_out, const float* x, size_t n_in, float* y,
+                              int* err, cudaStream_t s);
+// the logits head in one launch (same bits as launch_rmsnorm_row + launch_qmv_multi +
+// launch_greedy): logits [vocab] = W rmsnorm(h, gain, eps), *token = argmax (nullable).
+// cand_v / cand_i: one slot per SM; *counter: 0 between calls (re-armed by the kernel).
+cudaError_t launch_head_stream(int dtype, const uint8_t* w, size_t vocab, const float* h, const float* gain, float eps,
+                               size_t hidden, float* logits, uint32_t* token, float* cand_v, uint32_t* cand_i,
+                               unsigned* counter, int* err, cudaStream_t s);
 
 // logits head (head.cu): final RMSNorm of one hidden state [n <= 8192], one CTA
 cudaError_t launch_rmsnorm_row(const float* x, const float* gain, int n, float eps, float* out, cudaStream_t s);

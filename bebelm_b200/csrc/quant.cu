@@ -26,6 +26,8 @@
 // separate kernel (one warp per 256-block).
 #include <algorithm>
 
+#include <math_constants.h>
+
 #include <cstdlib>
 
 #include "internal.h"
@@ -654,13 +656,11 @@ __device__ __forceinline__ float lane_block_q6k(const uint8_t* blk, const int8_t
     return __fmul_rn(sx, __fmul_rn(d, __int2float_rn(s)));
 }
 
-__global__ void __launch_bounds__(256) qmv_lane_kernel(QmvSegs segs, const float* x, size_t n_in) {
-    __shared__ __align__(16) int8_t s_q[(kMvMaxIn / kQK) * kQStride];
-    __shared__ float s_sc[kMvMaxIn / kQK];
-    __shared__ int s_sum[kMvMaxIn / 32];
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int nb = (int)(n_in / kQK);
-    for (int blk = warp; blk < nb; blk += 8) {  // Q8 of x, as quantize_q8_kernel
+// Q8 of x [nb blocks] into shared memory (as quantize_q8_kernel: same bits), one warp per block;
+// a block's quants at stride kQStride
+__device__ __forceinline__ void q8_into_smem(const float* x, int nb, int8_t* s_q, float* s_sc, int* s_sum) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, n_warps = blockDim.x >> 5;
+    for (int blk = warp; blk < nb; blk += n_warps) {  // Q8 of x, as quantize_q8_kernel
         const float* xb = x + (size_t)blk * kQK + lane * 8;
         const float4 a = *reinterpret_cast<const float4*>(xb), b = *reinterpret_cast<const float4*>(xb + 4);
         const float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
@@ -685,6 +685,15 @@ __global__ void __launch_bounds__(256) qmv_lane_kernel(QmvSegs segs, const float
         if ((lane & 3) == 0) s_sum[blk * 8 + (lane >> 2)] = sm;
         if (lane == 0) s_sc[blk] = __fdiv_rn(amax, 127.0f);
     }
+}
+
+__global__ void __launch_bounds__(256) qmv_lane_kernel(QmvSegs segs, const float* x, size_t n_in) {
+    __shared__ __align__(16) int8_t s_q[(kMvMaxIn / kQK) * kQStride];
+    __shared__ float s_sc[kMvMaxIn / kQK];
+    __shared__ int s_sum[kMvMaxIn / 32];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nb = (int)(n_in / kQK);
+    q8_into_smem(x, nb, s_q, s_sc, s_sum);
     __syncthreads();
     int L = 1;
     while (L < nb) L <<= 1;
@@ -715,6 +724,192 @@ __global__ void __launch_bounds__(256) qmv_lane_kernel(QmvSegs segs, const float
     if (sg >= 0 && b == 0) {
         float* yb = sg == 0 ? segs.y[0] : sg == 1 ? segs.y[1] : segs.y[2];
         yb[r] = acc;
+    }
+}
+
+// One token against a large matrix (the vocab-sized logits head): persistent CTAs, each
+// quantizing x once and streaming its chunks of 256 blocks (rows * row_bytes, contiguous) into
+// a 3-slot shared-memory ring with 1-D bulk copies (cp.async.bulk, mbarrier complete_tx), so
+// each SM keeps ~100 KB of weights in flight. The arithmetic is qmv_lane_kernel's (one lane
+// per block, the row's block values added in order): same bits. Waits are bounded; on timeout
+// the CTA stores kErrWaitTimeout to *err, waits (bounded) for its copies in flight, returns.
+constexpr int kStreamStages = 3;
+constexpr int kStreamChunkMax = 256 * 210;
+
+__device__ __forceinline__ bool stream_wait(uint32_t bar, unsigned parity) {
+    for (long long it = 0; it < (1ll << 22); ++it) {
+        uint32_t ok;
+        asm volatile(
+            "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+            : "=r"(ok)
+            : "r"(bar), "r"(parity)
+            : "memory");
+        if (ok) return true;
+    }
+    return false;
+}
+
+// The logits head variant (kHead) also does the final RMSNorm of x and the greedy argmax:
+// every CTA normalizes x itself with rmsnorm_row_kernel's arithmetic and reduction tree (a
+// 1024-wide tree of f64 partial sums, evaluated by 256 threads four virtual threads each), so
+// the normalized x has the same bits; each CTA keeps the first index of its rows' maximum
+// (strict `>` in increasing row order, NaN never wins) and the last CTA to finish reduces the
+// CTAs' candidates to the token (ties to the lower index) and re-arms the counter.
+struct HeadArgs {
+    const float* gain = nullptr;
+    float eps = 0.f;
+    float* cand_v = nullptr;  // [gridDim.x]
+    uint32_t* cand_i = nullptr;
+    unsigned* counter = nullptr;  // 0 between calls
+    uint32_t* token = nullptr;    // nullable
+};
+
+__device__ __forceinline__ double warp_sum_d(double v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+__device__ __forceinline__ void better_of(float& v, uint32_t& i, float ov, uint32_t oi) {
+    if (oi == 0xffffffffu) return;
+    if (i == 0xffffffffu || ov > v || (ov == v && oi < i)) v = ov, i = oi;
+}
+
+template <bool kHead>
+__global__ void __launch_bounds__(256, 1) qmv_stream_kernel(int dtype, const uint8_t* w, size_t rb, size_t n_out,
+                                                            const float* x, size_t n_in, int rows_per_chunk, float* y,
+                                                            int* err, HeadArgs ha) {
+    extern __shared__ __align__(128) unsigned char ring[];
+    __shared__ __align__(16) int8_t s_q[(kMvMaxIn / kQK) * kQStride];
+    __shared__ float s_sc[kMvMaxIn / kQK];
+    __shared__ int s_sum[kMvMaxIn / 32];
+    __shared__ int s_fail;
+    __shared__ __align__(16) float s_x[kHead ? kMvMaxIn : 1];
+    __shared__ double s_part[32];
+    __shared__ float s_bv[8];
+    __shared__ uint32_t s_bi[8];
+    __shared__ bool s_last;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int nb = (int)(n_in / kQK);
+    const size_t chunk_bytes = (size_t)rows_per_chunk * rb;
+    const uint32_t ring_s = (uint32_t)__cvta_generic_to_shared(ring);
+    const uint32_t bar0 = ring_s + kStreamStages * kStreamChunkMax;
+    const size_t n_chunks = (n_out + rows_per_chunk - 1) / rows_per_chunk;
+    size_t issued = 0;  // thread 0: chunks of this CTA whose copies were issued
+    auto issue = [&](size_t k) {
+        const size_t c = blockIdx.x + k * gridDim.x;
+        if (c >= n_chunks) return;
+        const size_t r0 = c * rows_per_chunk;
+        const uint32_t bytes = (uint32_t)(std::min<size_t>(rows_per_chunk, n_out - r0) * rb);
+        const uint32_t bar = bar0 + 8 * (uint32_t)(k % kStreamStages);
+        asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+        asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                         ring_s + (uint32_t)(k % kStreamStages) * kStreamChunkMax),
+                     "l"(w + r0 * rb), "r"(bytes), "r"(bar)
+                     : "memory");
+        issued = k + 1;
+    };
+    if (tid == 0) {
+        for (int i = 0; i < kStreamStages; ++i) asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(bar0 + 8 * i));
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        s_fail = 0;
+        for (int k = 0; k < kStreamStages; ++k) issue(k);
+    }
+    if constexpr (kHead) {  // x <- rmsnorm(x, gain, eps) in shared memory
+        const int n = (int)n_in;
+        double ss[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {  // virtual thread tid + 256 j of the 1024-wide tree
+            double a = 0.0;
+            for (int i = tid + 256 * j; i < n; i += 1024) a += (double)__fmul_rn(x[i], x[i]);
+            ss[j] = warp_sum_d(a);
+        }
+        if (lane == 0)
+#pragma unroll
+            for (int j = 0; j < 4; ++j) s_part[warp + 8 * j] = ss[j];
+        __syncthreads();
+        if (warp == 0) {
+            const double v = warp_sum_d(s_part[lane]);
+            if (lane == 0) {
+                const float mean = __double2float_rn(v / (double)n);
+                s_part[0] = (double)__fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, ha.eps)));
+            }
+        }
+        __syncthreads();
+        const float scale = (float)s_part[0];
+        for (int i = tid; i < n; i += 256) s_x[i] = __fmul_rn(__fmul_rn(x[i], scale), ha.gain[i]);
+        __syncthreads();
+        q8_into_smem(s_x, nb, s_q, s_sc, s_sum);
+    } else {
+        q8_into_smem(x, nb, s_q, s_sc, s_sum);
+    }
+    __syncthreads();
+    int L = 1;
+    while (L < nb) L <<= 1;
+    const int b = lane & (L - 1), rloc = warp * (32 / L) + lane / L, base = lane & ~(L - 1);
+    const int bbytes = dtype == kGgmlQ4K ? 144 : 210;
+    float best_v = 0.f;
+    uint32_t best_i = 0xffffffffu;
+    size_t k = 0;
+    for (; blockIdx.x + k * gridDim.x < n_chunks; ++k) {
+        const uint32_t bar = bar0 + 8 * (uint32_t)(k % kStreamStages);
+        const unsigned parity = (unsigned)((k / kStreamStages) & 1);
+        if (tid == 0 && !stream_wait(bar, parity)) s_fail = 1;
+        __syncthreads();
+        if (s_fail) break;
+        stream_wait(bar, parity);  // this thread's own acquire of the landed bytes (succeeds at once)
+        const size_t r = (blockIdx.x + k * gridDim.x) * rows_per_chunk + rloc;
+        const unsigned char* row = ring + (k % kStreamStages) * kStreamChunkMax + (size_t)rloc * rb;
+        float v = 0.f;
+        if (r < n_out && b < nb && rloc < rows_per_chunk)
+            v = dtype == kGgmlQ4K ? lane_block_q4k(row + (size_t)b * bbytes, s_q + b * kQStride, s_sc[b], s_sum + b * 8)
+                                  : lane_block_q6k(row + (size_t)b * bbytes, s_q + b * kQStride, s_sc[b]);
+        float acc = -0.0f;  // the blocks of the row, added in order
+        for (int j = 0; j < nb; ++j) acc = __fadd_rn(acc, __shfl_sync(0xffffffffu, v, base + j));
+        if (r < n_out && b == 0 && rloc < rows_per_chunk) {
+            y[r] = acc;
+            if constexpr (kHead)
+                if (acc > -CUDART_INF_F && (best_i == 0xffffffffu || acc > best_v)) best_v = acc, best_i = (uint32_t)r;
+        }
+        __syncthreads();  // the slot is consumed
+        if (tid == 0) issue(k + kStreamStages);
+    }
+    if (tid == 0 && s_fail) {
+        *reinterpret_cast<volatile int*>(err) = kErrWaitTimeout;
+        for (size_t i = k; i < issued; ++i)  // copies still in flight must land before the CTA exits
+            stream_wait(bar0 + 8 * (uint32_t)(i % kStreamStages), (unsigned)((i / kStreamStages) & 1));
+    }
+    (void)chunk_bytes;
+    if constexpr (kHead) {
+        // a CTA whose wait gave up still takes part (with what it has), so the counter is
+        // re-armed; the error word marks the result invalid
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1)
+            better_of(best_v, best_i, __shfl_xor_sync(0xffffffffu, best_v, o), __shfl_xor_sync(0xffffffffu, best_i, o));
+        if (lane == 0) s_bv[warp] = best_v, s_bi[warp] = best_i;
+        __syncthreads();
+        if (tid == 0) {
+            for (int i = 1; i < 8; ++i) better_of(s_bv[0], s_bi[0], s_bv[i], s_bi[i]);
+            ha.cand_v[blockIdx.x] = s_bv[0];
+            ha.cand_i[blockIdx.x] = s_bi[0];
+            __threadfence();
+            s_last = atomicAdd(ha.counter, 1u) == gridDim.x - 1;
+        }
+        __syncthreads();
+        if (s_last && warp == 0) {  // the last CTA: every candidate is written (fence + counter)
+            __threadfence();
+            float v = 0.f;
+            uint32_t i = 0xffffffffu;
+            for (unsigned c = lane; c < gridDim.x; c += 32)
+                better_of(v, i, reinterpret_cast<volatile float*>(ha.cand_v)[c],
+                          reinterpret_cast<volatile uint32_t*>(ha.cand_i)[c]);
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1)
+                better_of(v, i, __shfl_xor_sync(0xffffffffu, v, o), __shfl_xor_sync(0xffffffffu, i, o));
+            if (lane == 0) {
+                if (ha.token) *ha.token = i == 0xffffffffu ? 0u : i;
+                *ha.counter = 0;  // re-armed for the next call (or graph replay)
+            }
+        }
     }
 }
 
@@ -836,6 +1031,58 @@ cudaError_t launch_qmv_multi(const QmvSegs& segs, const float* x, size_t n_in, c
         qmv_multi_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, s>>>(segs, x, n_in);
     }
     return cudaGetLastError();
+}
+
+static cudaError_t qmv_stream_impl(int dtype, const uint8_t* w, size_t n_out, const float* x, size_t n_in, float* y,
+                                   int* err, cudaStream_t s, const HeadArgs* head) {
+    if ((dtype != kGgmlQ4K && dtype != kGgmlQ6K) || n_in % kQK || n_in > (size_t)kMvMaxIn || n_out == 0 || !err)
+        return cudaErrorNotSupported;
+    const size_t rb = ggml_row_bytes(dtype, n_in);
+    if ((rb & 15) || (reinterpret_cast<uintptr_t>(w) & 15)) return cudaErrorNotSupported;
+    int L = 1;
+    while ((size_t)L < n_in / kQK) L <<= 1;
+    const int rows_per_chunk = 8 * (32 / L);
+    if ((size_t)rows_per_chunk * rb > (size_t)kStreamChunkMax) return cudaErrorNotSupported;
+    static int n_sm[64] = {};
+    static bool attr_set[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64) return cudaErrorNotSupported;
+    const int dyn = kStreamStages * kStreamChunkMax + 64;
+    if (!attr_set[dev]) {
+        cudaError_t e = cudaFuncSetAttribute(qmv_stream_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, dyn);
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(qmv_stream_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, dyn);
+        if (e != cudaSuccess) return e;
+        e = cudaDeviceGetAttribute(&n_sm[dev], cudaDevAttrMultiProcessorCount, dev);
+        if (e != cudaSuccess) return e;
+        attr_set[dev] = true;
+    }
+    const size_t n_chunks = (n_out + rows_per_chunk - 1) / rows_per_chunk;
+    const unsigned grid = (unsigned)std::min<size_t>(n_chunks, (size_t)n_sm[dev]);
+    if (head)
+        qmv_stream_kernel<true><<<grid, 256, dyn, s>>>(dtype, w, rb, n_out, x, n_in, rows_per_chunk, y, err, *head);
+    else
+        qmv_stream_kernel<false><<<grid, 256, dyn, s>>>(dtype, w, rb, n_out, x, n_in, rows_per_chunk, y, err, HeadArgs{});
+    return cudaGetLastError();
+}
+
+cudaError_t launch_qmv_stream(int dtype, const uint8_t* w, size_t n_out, const float* x, size_t n_in, float* y,
+                              int* err, cudaStream_t s) {
+    return qmv_stream_impl(dtype, w, n_out, x, n_in, y, err, s, nullptr);
+}
+
+cudaError_t launch_head_stream(int dtype, const uint8_t* w, size_t vocab, const float* h, const float* gain, float eps,
+                               size_t hidden, float* logits, uint32_t* token, float* cand_v, uint32_t* cand_i,
+                               unsigned* counter, int* err, cudaStream_t s) {
+    HeadArgs ha;
+    ha.gain = gain;
+    ha.eps = eps;
+    ha.cand_v = cand_v;
+    ha.cand_i = cand_i;
+    ha.counter = counter;
+    ha.token = token;
+    return qmv_stream_impl(dtype, w, vocab, h, hidden, logits, err, s, &ha);
 }
 
 cudaError_t launch_dequantize(int dtype, const uint8_t* data, size_t n, float* out, cudaStream_t s) {

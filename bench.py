@@ -290,6 +290,7 @@ def run_ours(args):
                    "config2_2048": bench_prefill(bb, torch, dev, stream, bf16_peak, peak_kind, 2048, 6),
                    "config5_8192_one_layer": bench_prefill(bb, torch, dev, stream, bf16_peak, peak_kind, 8192, 2)}
 
+    head = bench_logits_head(bb, torch, dev, stream, hbm_peak, peak_kind) if rank == 0 and not args.no_prefill else None
     c3bf = bench_config3_bf16(bb, torch, dev, stream, world, args.steps)
     cfg4 = None if args.no_cfg4 else bench_config4(bb, torch, dev, stream, world, rank)
     hbm_peak_, bf16_peak_, _ = peaks()
@@ -329,6 +330,7 @@ def run_ours(args):
             "cpu_baseline": cpu,
             "prefill": prefill,
             "config3_bf16_kv": c3bf,
+            "logits_head": head,
             "config4": cfg4,
             "config5": cfg5,
         }
@@ -460,6 +462,43 @@ def bench_attn_layer(bb, torch, dev, stream, T=2048, steps=64):
             "step_ms": round(step_ms, 4), "step_tok_per_s": round(1 / (step_ms * 1e-3), 1),
             "graph_step_ms": round(graph_step_ms, 4),
             "graph_how": "whole-operator step plan, all steps captured in one CUDA graph"}
+
+
+def bench_logits_head(bb, torch, dev, stream, hbm_peak, peak_kind, vocab=128000, steps=50):
+    """The logits head (src/model.rs:379-388) and greedy token (src/sampler.rs:139-149) per
+    decode token, on the device: RMSNorm, the tied token_embd matvec (synthetic Q6_K,
+    [128000][2048] = 215 MB, read once per token; larger than L2) and argmax."""
+    import numpy as np
+    rng = np.random.default_rng(11)
+    nb = HID // 256
+    w = rng.integers(0, 256, size=(vocab, nb, 210), dtype=np.uint8)
+    w[:, :, 208:210] = (rng.standard_normal((vocab, nb)) * 0.002).astype(np.float16).view(np.uint8).reshape(vocab, nb, 2)
+    head = bb.Head(bb.GGML_Q6_K, w.reshape(-1), HID, vocab, np.ones(HID, np.float32), device=dev.index)
+    del w
+    g = torch.Generator(device=dev)
+    g.manual_seed(12)
+    hs = torch.randn((steps, HID), generator=g, device=dev)
+    tok = torch.zeros(1, dtype=torch.int32, device=dev)
+    lib = bb.load_library()
+    sp = stream.cuda_stream
+    for i in range(3):
+        lib.bebelm_head_logits(head._h, hs[i].data_ptr(), 1e-5, None, tok.data_ptr(), bb.MEM_DEVICE, sp)
+    e = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+    torch.cuda.synchronize()
+    e[0].record(stream)
+    for i in range(steps):
+        lib.bebelm_head_logits(head._h, hs[i].data_ptr(), 1e-5, None, tok.data_ptr(), bb.MEM_DEVICE, sp)
+    e[1].record(stream)
+    torch.cuda.synchronize()
+    head.close()
+    ms = e[0].elapsed_time(e[1]) / steps
+    wbytes = vocab * nb * 210
+    gbs = wbytes / (ms * 1e-3) / 1e9
+    return {"workload": f"logits head per decode token: RMSNorm + Q6_K token_embd [{vocab}][{HID}] matvec + argmax, "
+                        "device in/out (3 launches)",
+            "ms_per_token": round(ms, 4), "weight_gbs": round(gbs, 1),
+            "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": hbm_peak, "unit": "GB/s",
+                         "frac": round(gbs / hbm_peak, 4), "peak_kind": peak_kind}}
 
 
 def bench_config3_bf16(bb, torch, dev, stream, world, steps):
