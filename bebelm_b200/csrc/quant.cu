@@ -623,7 +623,9 @@ __device__ __forceinline__ void ld16_a2(const uint8_t* p, uint32_t* w) {
     for (int i = 0; i < 4; ++i) w[i] = (uint32_t)h[2 * i] | ((uint32_t)h[2 * i + 1] << 16);
 }
 
-__device__ __forceinline__ float lane_block_q6k(const uint8_t* blk, const int8_t* qx, float sx) {
+// sums16: the 16-wide sub-block sums of qx, so that Σ (q - 32) x = Σ q x - 32 Σ x (exact): the
+// 6-bit q (0..63, a non-negative s8) goes into dp4a as it is
+__device__ __forceinline__ float lane_block_q6k(const uint8_t* blk, const int8_t* qx, float sx, const int* sums16) {
     uint32_t scw[4];
     ld16_a2(blk + 192, scw);
     int s = 0;
@@ -645,11 +647,12 @@ __device__ __forceinline__ float lane_block_q6k(const uint8_t* blk, const int8_t
                 for (int i = 0; i < 4; ++i) {
                     const uint32_t src = (g & 1) ? hi[i] : lo[i];
                     const uint32_t nib = (g >= 2 ? src >> 4 : src) & 0x0f0f0f0fu;
-                    const uint32_t hb = (qh[i] >> (2 * g)) & 0x03030303u;
-                    t = __dp4a((int)__vsub4(nib | (hb << 4), 0x20202020u), xw[i], t);  // bytes q - 32
+                    // the 2-bit field (qh >> 2g) & 3, moved to bits 4-5 of each byte
+                    const uint32_t hq = g == 0 ? qh[i] << 4 : g == 1 ? qh[i] << 2 : g == 2 ? qh[i] : qh[i] >> 2;
+                    t = __dp4a((int)(nib | (hq & 0x30303030u)), xw[i], t);  // bytes q in [0, 63]
                 }
                 const int sc = (int)(int8_t)((scw[k >> 2] >> (8 * (k & 3))) & 0xffu);
-                s += t * sc;
+                s += (t - 32 * sums16[k]) * sc;
             }
         }
     const float d = f16_bits_to_f32(*reinterpret_cast<const uint16_t*>(blk + 208));
@@ -658,7 +661,8 @@ __device__ __forceinline__ float lane_block_q6k(const uint8_t* blk, const int8_t
 
 // Q8 of x [nb blocks] into shared memory (as quantize_q8_kernel: same bits), one warp per block;
 // a block's quants at stride kQStride
-__device__ __forceinline__ void q8_into_smem(const float* x, int nb, int8_t* s_q, float* s_sc, int* s_sum) {
+__device__ __forceinline__ void q8_into_smem(const float* x, int nb, int8_t* s_q, float* s_sc, int* s_sum,
+                                             int* s_sum16) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, n_warps = blockDim.x >> 5;
     for (int blk = warp; blk < nb; blk += n_warps) {  // Q8 of x, as quantize_q8_kernel
         const float* xb = x + (size_t)blk * kQK + lane * 8;
@@ -680,7 +684,8 @@ __device__ __forceinline__ void q8_into_smem(const float* x, int nb, int8_t* s_q
             sm += qv[i];
         }
         *reinterpret_cast<uint2*>(s_q + blk * kQStride + lane * 8) = *reinterpret_cast<const uint2*>(qv);
-        sm += __shfl_xor_sync(0xffffffffu, sm, 1);
+        sm += __shfl_xor_sync(0xffffffffu, sm, 1);  // a 16-wide sub-block is 2 lanes
+        if ((lane & 1) == 0) s_sum16[blk * 16 + (lane >> 1)] = sm;
         sm += __shfl_xor_sync(0xffffffffu, sm, 2);
         if ((lane & 3) == 0) s_sum[blk * 8 + (lane >> 2)] = sm;
         if (lane == 0) s_sc[blk] = __fdiv_rn(amax, 127.0f);
@@ -691,9 +696,10 @@ __global__ void __launch_bounds__(256) qmv_lane_kernel(QmvSegs segs, const float
     __shared__ __align__(16) int8_t s_q[(kMvMaxIn / kQK) * kQStride];
     __shared__ float s_sc[kMvMaxIn / kQK];
     __shared__ int s_sum[kMvMaxIn / 32];
+    __shared__ int s_sum16[kMvMaxIn / 16];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int nb = (int)(n_in / kQK);
-    q8_into_smem(x, nb, s_q, s_sc, s_sum);
+    q8_into_smem(x, nb, s_q, s_sc, s_sum, s_sum16);
     __syncthreads();
     int L = 1;
     while (L < nb) L <<= 1;
@@ -716,7 +722,7 @@ __global__ void __launch_bounds__(256) qmv_lane_kernel(QmvSegs segs, const float
         const size_t rb = sg == 0 ? segs.row_bytes[0] : sg == 1 ? segs.row_bytes[1] : segs.row_bytes[2];
         const uint8_t* row = wb + r * rb;
         v = dt == kGgmlQ4K ? lane_block_q4k(row + (size_t)b * 144, s_q + b * kQStride, s_sc[b], s_sum + b * 8)
-                           : lane_block_q6k(row + (size_t)b * 210, s_q + b * kQStride, s_sc[b]);
+                           : lane_block_q6k(row + (size_t)b * 210, s_q + b * kQStride, s_sc[b], s_sum16 + b * 16);
     }
     const int base = lane & ~(L - 1);
     float acc = -0.0f;  // the blocks of the row, added in order
@@ -727,6 +733,55 @@ __global__ void __launch_bounds__(256) qmv_lane_kernel(QmvSegs segs, const float
     }
 }
 
+// A Q6_K block at a 2-byte aligned shared-memory address whose offset mod 16 is the same for
+// the whole warp: 14 aligned 16-byte loads, realigned in registers (warp-uniform selects and a
+// funnel shift), then lane_block_q6k's arithmetic on the words (same integer sums).
+__device__ __forceinline__ float q6k_block_realigned(const unsigned char* blk, const int8_t* qx, float sx,
+                                                     const int* sums16) {
+    const int o = (int)(reinterpret_cast<uintptr_t>(blk) & 15);
+    const uint4* p = reinterpret_cast<const uint4*>(blk - o);
+    uint32_t v[59];
+#pragma unroll
+    for (int i = 0; i < 14; ++i) {
+        const uint4 t = p[i];
+        v[4 * i] = t.x, v[4 * i + 1] = t.y, v[4 * i + 2] = t.z, v[4 * i + 3] = t.w;
+    }
+    v[56] = v[57] = v[58] = 0;
+    const int ws = o >> 2;
+    const uint32_t bs = (uint32_t)(o & 3) * 8;
+#pragma unroll
+    for (int i = 0; i < 57; ++i) v[i] = (ws & 2) ? v[i + 2] : v[i];
+#pragma unroll
+    for (int i = 0; i < 56; ++i) v[i] = (ws & 1) ? v[i + 1] : v[i];
+    uint32_t w[53];  // ql: 0..31, qh: 32..47, scales: 48..51, d: low half of 52
+#pragma unroll
+    for (int i = 0; i < 53; ++i) w[i] = __funnelshift_r(v[i], v[i + 1], bs);
+    int s = 0;
+#pragma unroll
+    for (int n = 0; n < 2; ++n)
+#pragma unroll
+        for (int sub = 0; sub < 2; ++sub)
+#pragma unroll
+            for (int g = 0; g < 4; ++g) {
+                const int k = n * 8 + 2 * g + sub;
+                const int4 xv = *reinterpret_cast<const int4*>(qx + k * 16);
+                const int xw[4] = {xv.x, xv.y, xv.z, xv.w};
+                int t = 0;
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const uint32_t src = w[n * 16 + (g & 1) * 8 + sub * 4 + i];
+                    const uint32_t qh = w[32 + n * 8 + sub * 4 + i];
+                    const uint32_t nib = (g >= 2 ? src >> 4 : src) & 0x0f0f0f0fu;
+                    const uint32_t hq = g == 0 ? qh << 4 : g == 1 ? qh << 2 : g == 2 ? qh : qh >> 2;
+                    t = __dp4a((int)(nib | (hq & 0x30303030u)), xw[i], t);
+                }
+                const int sc = (int)(int8_t)((w[48 + (k >> 2)] >> (8 * (k & 3))) & 0xffu);
+                s += (t - 32 * sums16[k]) * sc;
+            }
+    const float d = f16_bits_to_f32(w[52] & 0xffffu);
+    return __fmul_rn(sx, __fmul_rn(d, __int2float_rn(s)));
+}
+
 // One token against a large matrix (the vocab-sized logits head): persistent CTAs, each
 // quantizing x once and streaming its chunks of 256 blocks (rows * row_bytes, contiguous) into
 // a 3-slot shared-memory ring with 1-D bulk copies (cp.async.bulk, mbarrier complete_tx), so
@@ -735,6 +790,7 @@ __global__ void __launch_bounds__(256) qmv_lane_kernel(QmvSegs segs, const float
 // the CTA stores kErrWaitTimeout to *err, waits (bounded) for its copies in flight, returns.
 constexpr int kStreamStages = 3;
 constexpr int kStreamChunkMax = 256 * 210;
+constexpr int kStreamThreads = 512;  // two groups of 8 warps
 
 __device__ __forceinline__ bool stream_wait(uint32_t bar, unsigned parity) {
     for (long long it = 0; it < (1ll << 22); ++it) {
@@ -775,27 +831,33 @@ __device__ __forceinline__ void better_of(float& v, uint32_t& i, float ov, uint3
 }
 
 template <bool kHead>
-__global__ void __launch_bounds__(256, 1) qmv_stream_kernel(int dtype, const uint8_t* w, size_t rb, size_t n_out,
-                                                            const float* x, size_t n_in, int rows_per_chunk, float* y,
-                                                            int* err, HeadArgs ha) {
+__global__ void __launch_bounds__(kStreamThreads, 1)
+    qmv_stream_kernel(int dtype, const uint8_t* w, size_t rb, size_t n_out, const float* x, size_t n_in,
+                      int rows_per_chunk, float* y, int* err, HeadArgs ha) {
     extern __shared__ __align__(128) unsigned char ring[];
     __shared__ __align__(16) int8_t s_q[(kMvMaxIn / kQK) * kQStride];
     __shared__ float s_sc[kMvMaxIn / kQK];
     __shared__ int s_sum[kMvMaxIn / 32];
-    __shared__ int s_fail;
+    __shared__ int s_sum16[kMvMaxIn / 16];
+    __shared__ int s_fail[2];
+    // the chunk last issued into each ring slot: a group waits for its chunk to be issued before
+    // it waits on the slot's mbarrier, so it never tests a phase parity one phase early (the
+    // other group may still hold the slot's previous chunk)
+    __shared__ long long s_issued[kStreamStages];
     __shared__ __align__(16) float s_x[kHead ? kMvMaxIn : 1];
     __shared__ double s_part[32];
-    __shared__ float s_bv[8];
-    __shared__ uint32_t s_bi[8];
+    __shared__ float s_bv[kStreamThreads / 32];
+    __shared__ uint32_t s_bi[kStreamThreads / 32];
     __shared__ bool s_last;
+    __shared__ float s_v[2][32 * 9];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    // two groups of 8 warps take alternate chunks of the ring (group g: chunks k = g, g + 2, ...)
+    const int grp = warp >> 3, gw = warp & 7, gtid = tid & 255;
     const int nb = (int)(n_in / kQK);
-    const size_t chunk_bytes = (size_t)rows_per_chunk * rb;
     const uint32_t ring_s = (uint32_t)__cvta_generic_to_shared(ring);
     const uint32_t bar0 = ring_s + kStreamStages * kStreamChunkMax;
     const size_t n_chunks = (n_out + rows_per_chunk - 1) / rows_per_chunk;
-    size_t issued = 0;  // thread 0: chunks of this CTA whose copies were issued
-    auto issue = [&](size_t k) {
+    auto issue = [&](size_t k) {  // by one thread: chunk k of this CTA into ring slot k % 3
         const size_t c = blockIdx.x + k * gridDim.x;
         if (c >= n_chunks) return;
         const size_t r0 = c * rows_per_chunk;
@@ -806,26 +868,32 @@ __global__ void __launch_bounds__(256, 1) qmv_stream_kernel(int dtype, const uin
                          ring_s + (uint32_t)(k % kStreamStages) * kStreamChunkMax),
                      "l"(w + r0 * rb), "r"(bytes), "r"(bar)
                      : "memory");
-        issued = k + 1;
+        __threadfence_block();  // the expect_tx before the record
+        reinterpret_cast<volatile long long*>(s_issued)[k % kStreamStages] = (long long)k;
     };
+    auto issued_wait = [&](size_t k) {  // bounded
+        for (long long it = 0; it < (1ll << 22); ++it)
+            if (reinterpret_cast<volatile long long*>(s_issued)[k % kStreamStages] == (long long)k) return true;
+        return false;
+    };
+    auto group_sync = [&]() { asm volatile("bar.sync %0, 256;" ::"r"(1 + grp) : "memory"); };
     if (tid == 0) {
         for (int i = 0; i < kStreamStages; ++i) asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(bar0 + 8 * i));
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-        s_fail = 0;
+        s_fail[0] = s_fail[1] = 0;
+        for (int k = 0; k < kStreamStages; ++k) s_issued[k] = -1;
         for (int k = 0; k < kStreamStages; ++k) issue(k);
     }
     if constexpr (kHead) {  // x <- rmsnorm(x, gain, eps) in shared memory
         const int n = (int)n_in;
-        double ss[4];
+        double ss[2];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {  // virtual thread tid + 256 j of the 1024-wide tree
-            double a = 0.0;
-            for (int i = tid + 256 * j; i < n; i += 1024) a += (double)__fmul_rn(x[i], x[i]);
-            ss[j] = warp_sum_d(a);
+        for (int j = 0; j < 2; ++j) {  // virtual thread tid + 512 j of the 1024-wide tree
+            double acc = 0.0;
+            for (int i = tid + kStreamThreads * j; i < n; i += 1024) acc += (double)__fmul_rn(x[i], x[i]);
+            ss[j] = warp_sum_d(acc);
         }
-        if (lane == 0)
-#pragma unroll
-            for (int j = 0; j < 4; ++j) s_part[warp + 8 * j] = ss[j];
+        if (lane == 0) s_part[warp] = ss[0], s_part[warp + 16] = ss[1];
         __syncthreads();
         if (warp == 0) {
             const double v = warp_sum_d(s_part[lane]);
@@ -836,49 +904,74 @@ __global__ void __launch_bounds__(256, 1) qmv_stream_kernel(int dtype, const uin
         }
         __syncthreads();
         const float scale = (float)s_part[0];
-        for (int i = tid; i < n; i += 256) s_x[i] = __fmul_rn(__fmul_rn(x[i], scale), ha.gain[i]);
+        for (int i = tid; i < n; i += kStreamThreads) s_x[i] = __fmul_rn(__fmul_rn(x[i], scale), ha.gain[i]);
         __syncthreads();
-        q8_into_smem(s_x, nb, s_q, s_sc, s_sum);
+        q8_into_smem(s_x, nb, s_q, s_sc, s_sum, s_sum16);
     } else {
-        q8_into_smem(x, nb, s_q, s_sc, s_sum);
+        q8_into_smem(x, nb, s_q, s_sc, s_sum, s_sum16);
     }
     __syncthreads();
     int L = 1;
     while (L < nb) L <<= 1;
-    const int b = lane & (L - 1), rloc = warp * (32 / L) + lane / L, base = lane & ~(L - 1);
+    const int b = lane & (L - 1), rloc = gw * (32 / L) + lane / L, base = lane & ~(L - 1);
     const int bbytes = dtype == kGgmlQ4K ? 144 : 210;
     float best_v = 0.f;
     uint32_t best_i = 0xffffffffu;
-    size_t k = 0;
-    for (; blockIdx.x + k * gridDim.x < n_chunks; ++k) {
+    // Q6_K blocks sit at 2-byte offsets: with at most 8 blocks a row, a warp takes one block
+    // column of 32 rows, so its lanes share the block's offset mod 16 (aligned loads, no conflicts
+    // at the row stride), and the group's warp 0 adds each row's block values in order
+    const bool q6_cols = dtype == kGgmlQ6K && rows_per_chunk == 32 && nb <= 8;
+    size_t k = grp;
+    for (; blockIdx.x + k * gridDim.x < n_chunks; k += 2) {
         const uint32_t bar = bar0 + 8 * (uint32_t)(k % kStreamStages);
         const unsigned parity = (unsigned)((k / kStreamStages) & 1);
-        if (tid == 0 && !stream_wait(bar, parity)) s_fail = 1;
-        __syncthreads();
-        if (s_fail) break;
+        if (gtid == 0 && !(issued_wait(k) && stream_wait(bar, parity))) s_fail[grp] = 1;
+        group_sync();
+        if (*reinterpret_cast<volatile int*>(&s_fail[grp])) break;  // written only before the barrier
         stream_wait(bar, parity);  // this thread's own acquire of the landed bytes (succeeds at once)
-        const size_t r = (blockIdx.x + k * gridDim.x) * rows_per_chunk + rloc;
-        const unsigned char* row = ring + (k % kStreamStages) * kStreamChunkMax + (size_t)rloc * rb;
-        float v = 0.f;
-        if (r < n_out && b < nb && rloc < rows_per_chunk)
-            v = dtype == kGgmlQ4K ? lane_block_q4k(row + (size_t)b * bbytes, s_q + b * kQStride, s_sc[b], s_sum + b * 8)
-                                  : lane_block_q6k(row + (size_t)b * bbytes, s_q + b * kQStride, s_sc[b]);
+        const size_t c0 = (blockIdx.x + k * gridDim.x) * rows_per_chunk;
+        const unsigned char* slot = ring + (k % kStreamStages) * kStreamChunkMax;
+        size_t r;
         float acc = -0.0f;  // the blocks of the row, added in order
-        for (int j = 0; j < nb; ++j) acc = __fadd_rn(acc, __shfl_sync(0xffffffffu, v, base + j));
-        if (r < n_out && b == 0 && rloc < rows_per_chunk) {
+        bool mine;
+        if (q6_cols) {  // warp = block column, lane = row (32 rows per chunk)
+            r = c0 + lane;
+            if (gw < nb && r < n_out)
+                s_v[grp][lane * 9 + gw] = q6k_block_realigned(slot + (size_t)lane * rb + (size_t)gw * 210,
+                                                               s_q + gw * kQStride, s_sc[gw], s_sum16 + gw * 16);
+            group_sync();
+            mine = gw == 0 && r < n_out;
+            if (mine)
+                for (int j = 0; j < nb; ++j) acc = __fadd_rn(acc, s_v[grp][lane * 9 + j]);
+        } else {
+            r = c0 + rloc;
+            const unsigned char* row = slot + (size_t)rloc * rb;
+            float v = 0.f;
+            if (r < n_out && b < nb && rloc < rows_per_chunk)
+                v = dtype == kGgmlQ4K
+                        ? lane_block_q4k(row + (size_t)b * bbytes, s_q + b * kQStride, s_sc[b], s_sum + b * 8)
+                        : lane_block_q6k(row + (size_t)b * bbytes, s_q + b * kQStride, s_sc[b], s_sum16 + b * 16);
+            for (int j = 0; j < nb; ++j) acc = __fadd_rn(acc, __shfl_sync(0xffffffffu, v, base + j));
+            mine = r < n_out && b == 0 && rloc < rows_per_chunk;
+        }
+        if (mine) {
             y[r] = acc;
             if constexpr (kHead)
                 if (acc > -CUDART_INF_F && (best_i == 0xffffffffu || acc > best_v)) best_v = acc, best_i = (uint32_t)r;
         }
-        __syncthreads();  // the slot is consumed
-        if (tid == 0) issue(k + kStreamStages);
+        group_sync();  // the slot is consumed
+        if (gtid == 0) issue(k + kStreamStages);
     }
-    if (tid == 0 && s_fail) {
+    if (gtid == 0 && s_fail[grp]) {
         *reinterpret_cast<volatile int*>(err) = kErrWaitTimeout;
-        for (size_t i = k; i < issued; ++i)  // copies still in flight must land before the CTA exits
-            stream_wait(bar0 + 8 * (uint32_t)(i % kStreamStages), (unsigned)((i / kStreamStages) & 1));
+        // copies still in flight must land before the CTA exits: of the chunks this group may
+        // have left unconsumed (k, and the refill k + 1 it issued), those that were issued
+        for (size_t i = k; i < k + 2; ++i)
+            if (blockIdx.x + i * gridDim.x < n_chunks &&
+                reinterpret_cast<volatile long long*>(s_issued)[i % kStreamStages] == (long long)i)
+                stream_wait(bar0 + 8 * (uint32_t)(i % kStreamStages), (unsigned)((i / kStreamStages) & 1));
     }
-    (void)chunk_bytes;
+    __syncthreads();
     if constexpr (kHead) {
         // a CTA whose wait gave up still takes part (with what it has), so the counter is
         // re-armed; the error word marks the result invalid
@@ -888,7 +981,7 @@ __global__ void __launch_bounds__(256, 1) qmv_stream_kernel(int dtype, const uin
         if (lane == 0) s_bv[warp] = best_v, s_bi[warp] = best_i;
         __syncthreads();
         if (tid == 0) {
-            for (int i = 1; i < 8; ++i) better_of(s_bv[0], s_bi[0], s_bv[i], s_bi[i]);
+            for (int i = 1; i < kStreamThreads / 32; ++i) better_of(s_bv[0], s_bi[0], s_bv[i], s_bi[i]);
             ha.cand_v[blockIdx.x] = s_bv[0];
             ha.cand_i[blockIdx.x] = s_bi[0];
             __threadfence();
@@ -1061,9 +1154,9 @@ static cudaError_t qmv_stream_impl(int dtype, const uint8_t* w, size_t n_out, co
     const size_t n_chunks = (n_out + rows_per_chunk - 1) / rows_per_chunk;
     const unsigned grid = (unsigned)std::min<size_t>(n_chunks, (size_t)n_sm[dev]);
     if (head)
-        qmv_stream_kernel<true><<<grid, 256, dyn, s>>>(dtype, w, rb, n_out, x, n_in, rows_per_chunk, y, err, *head);
+        qmv_stream_kernel<true><<<grid, kStreamThreads, dyn, s>>>(dtype, w, rb, n_out, x, n_in, rows_per_chunk, y, err, *head);
     else
-        qmv_stream_kernel<false><<<grid, 256, dyn, s>>>(dtype, w, rb, n_out, x, n_in, rows_per_chunk, y, err, HeadArgs{});
+        qmv_stream_kernel<false><<<grid, kStreamThreads, dyn, s>>>(dtype, w, rb, n_out, x, n_in, rows_per_chunk, y, err, HeadArgs{});
     return cudaGetLastError();
 }
 

@@ -495,7 +495,7 @@ def bench_logits_head(bb, torch, dev, stream, hbm_peak, peak_kind, vocab=128000,
     wbytes = vocab * nb * 210
     gbs = wbytes / (ms * 1e-3) / 1e9
     return {"workload": f"logits head per decode token: RMSNorm + Q6_K token_embd [{vocab}][{HID}] matvec + argmax, "
-                        "device in/out (3 launches)",
+                        "device in/out, one launch (norm, matvec and argmax fused)",
             "ms_per_token": round(ms, 4), "weight_gbs": round(gbs, 1),
             "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": hbm_peak, "unit": "GB/s",
                          "frac": round(gbs / hbm_peak, 4), "peak_kind": peak_kind}}

@@ -59,10 +59,11 @@ def test_argmax_edge_cases_match_the_oracle():
 
 @pytest.mark.parametrize("dtype,gen,vocab", [(bb.GGML_Q6_K, random_q6k, 3000), (bb.GGML_Q4_K, random_q4k, 3000),
                                              (bb.GGML_F16, None, 3000), (bb.GGML_Q6_K, random_q6k, 20000),
-                                             (bb.GGML_Q4_K, random_q4k, 12345)])
+                                             (bb.GGML_Q4_K, random_q4k, 12345), (bb.GGML_Q6_K, random_q6k, 128000)])
 def test_logits_head_matches_the_oracle(dtype, gen, vocab):
     """Small vocabularies take the lane kernel; from 8192 rows K-quants stream through shared
-    memory (ragged last chunk at 12345 rows)."""
+    memory (ragged last chunk at 12345 rows; at the model's 128000 rows each CTA streams ~27
+    chunks, alternating between its two warp groups)."""
     hidden = 2048
     if gen is None:
         w = (np.random.default_rng(3).standard_normal((vocab, hidden)) * 0.02).astype(np.float16).view(np.uint8)
