@@ -9,6 +9,8 @@
 #include <cstring>
 #include <mutex>
 #include <string>
+#include <unordered_map>
+#include <initializer_list>
 #include <vector>
 
 #include "../../include/bebelm_attn.h"
@@ -428,6 +430,35 @@ struct FusedStep {
     float eps;
 };
 
+// The output range of the last decode launch on each stream. Only decode grids launch as
+// programmatic dependents, so a decode grid can overlap nothing but the previous decode grid on
+// its stream, and that grid passed its own griddepcontrol.wait (everything before it complete)
+// before it let this one start: inputs outside its output were complete when this grid began.
+struct OutRange {
+    const char* p = nullptr;
+    size_t n = 0;  // SIZE_MAX: unknown (e.g. stores to peers), overlaps everything
+};
+std::mutex g_last_out_mu;
+std::unordered_map<cudaStream_t, OutRange> g_last_out;
+
+void record_decode_out(cudaStream_t s, const void* out, size_t bytes) {
+    std::lock_guard<std::mutex> lk(g_last_out_mu);
+    g_last_out[s] = OutRange{static_cast<const char*>(out), bytes};
+}
+
+bool inputs_clear_of_last_out(cudaStream_t s, std::initializer_list<std::pair<const void*, size_t>> ins) {
+    std::lock_guard<std::mutex> lk(g_last_out_mu);
+    auto it = g_last_out.find(s);
+    if (it == g_last_out.end()) return true;  // no decode grid before this one on the stream
+    const OutRange r = it->second;
+    if (r.n == SIZE_MAX) return false;
+    for (const auto& in : ins) {
+        const char* p = static_cast<const char*>(in.first);
+        if (p && p < r.p + r.n && r.p < p + in.second) return false;
+    }
+    return true;
+}
+
 void pick_heads_per_cta(int group, int* hpc, int* n_sub) {
     int h = group % 4 == 0 ? 4 : group % 3 == 0 ? 3 : group % 2 == 0 ? 2 : 1;
     *hpc = h;
@@ -506,6 +537,10 @@ int run_decode(bebelm_kv_pool* P, const std::vector<Window>& wins, int layer, in
         a.k_gain = fused->k_gain;
         a.theta_scale = fused->theta_scale;
         a.eps = fused->eps;
+        const size_t nq = (size_t)n * n_heads * kHeadDim * 4, nkv = (size_t)n * P->n_kv * kHeadDim * 4;
+        a.early_inputs = !peer && inputs_clear_of_last_out(s, {{fused->q_raw, nq}, {fused->k_new, nkv},
+                                                               {fused->v_new, nkv}, {fused->q_gain, 4 * kHeadDim},
+                                                               {fused->k_gain, 4 * kHeadDim}});
     }
     a.out = d_out;
     a.part_acc = P->part.as<float>();
@@ -529,6 +564,7 @@ int run_decode(bebelm_kv_pool* P, const std::vector<Window>& wins, int layer, in
         a.peer_off = peer->off;
     }
     CUDA_TRY(launch_decode(a, s));
+    record_decode_out(s, d_out, peer ? SIZE_MAX : (size_t)n * n_heads * kHeadDim * 4);
     P->last_plan = nullptr;
     P->last_writes.clear();
     if (fused)
@@ -1293,6 +1329,7 @@ extern "C" int bebelm_attn_decode_cached_noalloc(const bebelm_kv* kv, int layer,
     a.scale_log2 = 0.125f * 1.4426950408889634f;
     a.pdl = 1;
     CUDA_TRY(launch_decode(a, s));
+    record_decode_out(s, out, (size_t)n_heads * kHeadDim * 4);
     return 0;
 }
 
@@ -1607,6 +1644,7 @@ int bebelm_step_plan_launch(bebelm_step_plan* pl, const float* q, const float* k
     if (cs != cudaStreamCaptureStatusActive) cap_id = 0;
     a.step_prewait = P->last_plan != nullptr && P->last_plan != pl && P->last_capture == cap_id;
     CUDA_TRY(launch_decode(a, as_stream(stream)));
+    record_decode_out(as_stream(stream), a.out, (size_t)pl->n_heads * kHeadDim * 4);
     P->last_plan = pl;
     P->last_capture = cap_id;
     return 0;

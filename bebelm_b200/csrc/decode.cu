@@ -187,6 +187,25 @@ __device__ __forceinline__ void warp_norm_rope64(const float* x, const float* ga
     y1 = __fadd_rn(__fmul_rn(a, sn), __fmul_rn(b, cs));
 }
 
+// Per-CTA timeline for a timing build (-DBEBELM_DECODE_TRACE): %globaltimer at entry, after
+// griddepcontrol.wait, first stage landed, streaming done, exit. Compiled out otherwise.
+#ifdef BEBELM_DECODE_TRACE
+__device__ long long g_dtrace[4][1024 * 8];  // by the first sequence's position mod 4
+#define DTRACE(slot)                                                                          \
+    do {                                                                                      \
+        const unsigned cta_ = blockIdx.y * gridDim.x + blockIdx.x;                             \
+        if (threadIdx.x == 0 && cta_ < 1024) {                                                 \
+            long long t_;                                                                     \
+            asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_));                            \
+            g_dtrace[a.one.pos & 3][cta_ * 8 + (slot)] = t_;                                  \
+        }                                                                                     \
+    } while (0)
+#else
+#define DTRACE(slot) \
+    do {             \
+    } while (0)
+#endif
+
 template <int HPC, bool BF>
 __global__ void __launch_bounds__(kThreads, 2) decode_kernel(DecodeArgs a) {
     // BF: the cache holds bf16 (half the bytes per page row, twice the stages in the same ring)
@@ -214,6 +233,7 @@ __global__ void __launch_bounds__(kThreads, 2) decode_kernel(DecodeArgs a) {
 
     // which sequence owns this split
     const int gsplit = blockIdx.x;
+    DTRACE(0);
     int lo = 0, hi = a.n_seqs - 1;
     while (lo < hi) {
         int mid = (lo + hi + 1) >> 1;
@@ -278,61 +298,69 @@ __global__ void __launch_bounds__(kThreads, 2) decode_kernel(DecodeArgs a) {
         for (int i = NST; i < NST + kPrefetch && i < n_early; ++i) prefetch(i);
     }
 
-    // ---- everything below may read what the predecessor wrote --------------
-    grid_dep_wait();
-    if (tid == 0)
-        for (int i = n_early; i < n_first; ++i) issue(i);
-
-    // this CTA's query heads, normed + roped here for a fused step
-    if (warp < HPC) {
-        const int h = h0 + warp;
-        if (a.q_raw) {
-            float y0, y1;
-            warp_norm_rope64(a.q_raw + ((size_t)seq * a.n_heads + h) * kHeadDim, a.q_gain, S.pos, a.theta_scale,
-                             a.eps, lane, y0, y1);
-            s_q[warp][lane] = y0;
-            s_q[warp][lane + 32] = y1;
-        } else {
-            const float* qs = a.q + ((size_t)seq * a.n_heads + h) * kHeadDim;
-            s_q[warp][lane] = qs[lane];
-            s_q[warp][lane + 32] = qs[lane + 32];
-        }
-    }
-    // the appended token, if its slot is in our pages: norm+rope k, store k and v
+    // this CTA's query heads, normed + roped here for a fused step, and the appended token's
+    // k (normed + roped) and v if its slot is in our pages: computed before griddepcontrol.wait
+    // when the host saw that the inputs were complete before the predecessor began (early_inputs)
     const bool has_new = S.new_slot >= 0 && (S.new_slot >> 6) >= p0 && (S.new_slot >> 6) < p1 && sub == 0;
     const bool own_new = S.new_slot >= 0 && (S.new_slot >> 6) >= p0 && (S.new_slot >> 6) < p1;
-    if (own_new && warp == HPC % 4) {
-        const float* kr = a.k_new + ((size_t)seq * a.n_kv + kvh) * kHeadDim;
-        const float* vr = a.v_new + ((size_t)seq * a.n_kv + kvh) * kHeadDim;
-        float y0, y1;
-        warp_norm_rope64(kr, a.k_gain, S.pos, a.theta_scale, a.eps, lane, y0, y1);
-        float w0 = vr[lane], w1 = vr[lane + 32];
-        if (BF) {  // this step uses exactly what the cache will hold
-            y0 = __bfloat162float(__float2bfloat16_rn(y0));
-            y1 = __bfloat162float(__float2bfloat16_rn(y1));
-            w0 = __bfloat162float(__float2bfloat16_rn(w0));
-            w1 = __bfloat162float(__float2bfloat16_rn(w1));
-        }
-        s_knew[lane] = y0;
-        s_knew[lane + 32] = y1;
-        s_vnew[lane] = w0;
-        s_vnew[lane + 32] = w1;
-        if (has_new) {  // one CTA per kv head writes the cache
-            const int i = (int)((S.new_slot >> 6) - p0);
-            char* kd = a.pv.base + (size_t)s_phys[i] * a.pv.page_bytes + a.pv.layer_off + (size_t)kvh * ROWB +
-                       (size_t)(S.new_slot & 63) * kHeadDim * ES;
-            char* vd = kd + a.pv.block_bytes;
-            if (BF) {
-                reinterpret_cast<__nv_bfloat16*>(kd)[lane] = __float2bfloat16_rn(y0);
-                reinterpret_cast<__nv_bfloat16*>(kd)[lane + 32] = __float2bfloat16_rn(y1);
-                reinterpret_cast<__nv_bfloat16*>(vd)[lane] = __float2bfloat16_rn(w0);
-                reinterpret_cast<__nv_bfloat16*>(vd)[lane + 32] = __float2bfloat16_rn(w1);
+    auto read_inputs = [&]() {
+        if (warp < HPC) {
+            const int h = h0 + warp;
+            if (a.q_raw) {
+                float y0, y1;
+                warp_norm_rope64(a.q_raw + ((size_t)seq * a.n_heads + h) * kHeadDim, a.q_gain, S.pos,
+                                 a.theta_scale, a.eps, lane, y0, y1);
+                s_q[warp][lane] = y0;
+                s_q[warp][lane + 32] = y1;
             } else {
-                reinterpret_cast<float*>(kd)[lane] = y0;
-                reinterpret_cast<float*>(kd)[lane + 32] = y1;
-                reinterpret_cast<float*>(vd)[lane] = w0;
-                reinterpret_cast<float*>(vd)[lane + 32] = w1;
+                const float* qs = a.q + ((size_t)seq * a.n_heads + h) * kHeadDim;
+                s_q[warp][lane] = qs[lane];
+                s_q[warp][lane + 32] = qs[lane + 32];
             }
+        }
+        if (own_new && warp == HPC % 4) {
+            const float* kr = a.k_new + ((size_t)seq * a.n_kv + kvh) * kHeadDim;
+            const float* vr = a.v_new + ((size_t)seq * a.n_kv + kvh) * kHeadDim;
+            float y0, y1;
+            warp_norm_rope64(kr, a.k_gain, S.pos, a.theta_scale, a.eps, lane, y0, y1);
+            float w0 = vr[lane], w1 = vr[lane + 32];
+            if (BF) {  // this step uses exactly what the cache will hold
+                y0 = __bfloat162float(__float2bfloat16_rn(y0));
+                y1 = __bfloat162float(__float2bfloat16_rn(y1));
+                w0 = __bfloat162float(__float2bfloat16_rn(w0));
+                w1 = __bfloat162float(__float2bfloat16_rn(w1));
+            }
+            s_knew[lane] = y0;
+            s_knew[lane + 32] = y1;
+            s_vnew[lane] = w0;
+            s_vnew[lane + 32] = w1;
+        }
+    };
+    const bool early = a.early_inputs && !a.step;
+    if (early) read_inputs();
+
+    // ---- everything below may read what the predecessor wrote --------------
+    grid_dep_wait();
+    DTRACE(1);
+    if (tid == 0)
+        for (int i = n_early; i < n_first; ++i) issue(i);
+    if (!early) read_inputs();
+    if (has_new && warp == HPC % 4) {  // one CTA per kv head writes the cache (the warp that computed it)
+        const int i = (int)((S.new_slot >> 6) - p0);
+        char* kd = a.pv.base + (size_t)s_phys[i] * a.pv.page_bytes + a.pv.layer_off + (size_t)kvh * ROWB +
+                   (size_t)(S.new_slot & 63) * kHeadDim * ES;
+        char* vd = kd + a.pv.block_bytes;
+        const float y0 = s_knew[lane], y1 = s_knew[lane + 32], w0 = s_vnew[lane], w1 = s_vnew[lane + 32];
+        if (BF) {
+            reinterpret_cast<__nv_bfloat16*>(kd)[lane] = __float2bfloat16_rn(y0);
+            reinterpret_cast<__nv_bfloat16*>(kd)[lane + 32] = __float2bfloat16_rn(y1);
+            reinterpret_cast<__nv_bfloat16*>(vd)[lane] = __float2bfloat16_rn(w0);
+            reinterpret_cast<__nv_bfloat16*>(vd)[lane + 32] = __float2bfloat16_rn(w1);
+        } else {
+            reinterpret_cast<float*>(kd)[lane] = y0;
+            reinterpret_cast<float*>(kd)[lane + 32] = y1;
+            reinterpret_cast<float*>(vd)[lane] = w0;
+            reinterpret_cast<float*>(vd)[lane + 32] = w1;
         }
     }
     __syncthreads();
@@ -363,6 +391,7 @@ __global__ void __launch_bounds__(kThreads, 2) decode_kernel(DecodeArgs a) {
     for (int i = 0; i < np; ++i) {
         const int st = i % NST;
         const bool ok = __all_sync(0xffffffffu, mbar_wait_bounded(&full[st], (unsigned)((i / NST) & 1)));
+        if (i == 0) DTRACE(2);
         if (!ok) {
             if (lane == 0) {
                 *reinterpret_cast<volatile int*>(a.err) = kErrWaitTimeout;
@@ -477,6 +506,7 @@ __global__ void __launch_bounds__(kThreads, 2) decode_kernel(DecodeArgs a) {
         }
     }
     // the next launch may start its prologue now (it writes nothing before its own wait)
+    DTRACE(3);
     grid_dep_launch();
     __syncthreads();
     if (s_failed) {
@@ -545,10 +575,12 @@ __global__ void __launch_bounds__(kThreads, 2) decode_kernel(DecodeArgs a) {
     if (single) {
         signal_peers(a);
         step_done(a);
+        DTRACE(4);
         return;
     }
 
     // ---- last CTA of this (sequence, kv head) merges the splits ----------
+    DTRACE(5);
     __syncthreads();  // every partial of this CTA is stored before thread 0 releases it
     if (tid == 0) {
         unsigned* ctr = a.counters + (size_t)seq * NY + y;
@@ -557,7 +589,9 @@ __global__ void __launch_bounds__(kThreads, 2) decode_kernel(DecodeArgs a) {
         if (s_last) *ctr = 0u;  // ready for the next launch
     }
     __syncthreads();
+    DTRACE(6);
     if (!s_last) {
+        DTRACE(4);
         step_done(a);
         return;
     }
@@ -586,16 +620,22 @@ __global__ void __launch_bounds__(kThreads, 2) decode_kernel(DecodeArgs a) {
         sm_l[t] = __ldcg(a.part_ml + pi * 2 + 1);
     }
     __syncthreads();
-    if (tid < HPC) {
+    DTRACE(7);
+    if (warp < HPC) {  // warp h: the splits' maximum and rescaled sum of head h, lanes over splits
+        const int h = warp;
         float M = -INFINITY;
-        for (int k = 0; k < ns; ++k) M = fmaxf(M, sm_m[k * HPC + tid]);
+        for (int k = lane; k < ns; k += 32) M = fmaxf(M, sm_m[k * HPC + h]);
+#pragma unroll
+        for (int o2 = 16; o2 > 0; o2 >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o2));
         float L = 0.f;
-        for (int k = 0; k < ns; ++k) {
-            const float fk = M == -INFINITY ? 0.f : fast_exp2(sm_m[k * HPC + tid] - M);
-            sm_m[k * HPC + tid] = fk;  // now the rescale factor of split k
-            L = fmaf(fk, sm_l[k * HPC + tid], L);
+        for (int k = lane; k < ns; k += 32) {
+            const float fk = M == -INFINITY ? 0.f : fast_exp2(sm_m[k * HPC + h] - M);
+            sm_m[k * HPC + h] = fk;  // now the rescale factor of split k
+            L = fmaf(fk, sm_l[k * HPC + h], L);
         }
-        s_L[tid] = L;
+#pragma unroll
+        for (int o2 = 16; o2 > 0; o2 >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o2);
+        if (lane == 0) s_L[h] = L;
     }
     __syncthreads();
     if (active) {
@@ -629,6 +669,7 @@ __global__ void __launch_bounds__(kThreads, 2) decode_kernel(DecodeArgs a) {
     }
     signal_peers(a);
     step_done(a);
+    DTRACE(4);
 }
 
 template <int HPC, bool BF>
@@ -703,3 +744,10 @@ cudaError_t launch_decode(const DecodeArgs& a, cudaStream_t s) {
 }
 
 }  // namespace bebelm
+
+#ifdef BEBELM_DECODE_TRACE
+// timing build only: the last launch's per-CTA timeline (5 stamps per CTA, ns)
+extern "C" __attribute__((visibility("default"))) int bebelm_debug_decode_trace(long long* out, int n_ctas) {
+    return (int)cudaMemcpyFromSymbol(out, bebelm::g_dtrace, sizeof(long long) * 4 * 1024 * 8);
+}
+#endif

@@ -176,6 +176,10 @@ struct DecodeArgs {
     // dependents only after its own griddepcontrol.wait), so the counter and every page may
     // be read before the wait
     int step_prewait;
+    // the raw q/k/v and the gains were complete before the PDL predecessor passed its own wait
+    // (they do not overlap the previous decode launch's output), so a CTA norms and ropes them
+    // before griddepcontrol.wait; only the cache store of the new token waits
+    int early_inputs;
 };
 // Waits (bounded) until flags[r] >= expected for every source rank r, then copies n floats of
 // the gathered landing buffer to dst. On timeout it records kErrWaitTimeout and copies nothing.
