@@ -54,6 +54,13 @@ constexpr int kThreads = 128;
 constexpr int kRingBytes = kStages * 2 * kPageRowFloats * 4;  // the shared-memory ring: 3 fp32 pages of K + V
 constexpr long long kWaitLimit = 1ll << 22;          // try_wait polls before giving up
 constexpr int kPrefetch = BEBELM_DECODE_PREFETCH;     // pages prefetched into L2 beyond the ring
+#ifndef BEBELM_DECODE_EARLY_PREFETCH
+#define BEBELM_DECODE_EARLY_PREFETCH 2
+#endif
+// pages beyond the ring prefetched into L2 before griddepcontrol.wait: they load while the
+// previous step's grid finishes its merge (more of them slow that merge down: 2, 5, 8 and 11
+// gave 27.4, 28.6, 29.9 and 30.9 us per config-3 step, 0 and 1 gave 29.9 and 29.4)
+constexpr int kEarlyPrefetch = BEBELM_DECODE_EARLY_PREFETCH;
 constexpr int kMaxPagesPerSplit = kDecodeMaxPagesPerSplit;
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -295,7 +302,7 @@ __global__ void __launch_bounds__(kThreads, 2) decode_kernel(DecodeArgs a) {
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         for (int i = 0; i < n_first && i < n_early; ++i) issue(i);
-        for (int i = NST; i < NST + kPrefetch && i < n_early; ++i) prefetch(i);
+        for (int i = NST; i < NST + kEarlyPrefetch && i < n_early; ++i) prefetch(i);
     }
 
     // this CTA's query heads, normed + roped here for a fused step, and the appended token's
@@ -384,7 +391,7 @@ __global__ void __launch_bounds__(kThreads, 2) decode_kernel(DecodeArgs a) {
         for (int e = 0; e < 16; ++e) acc[h][e] = 0.f;
     }
     if (tid == 0)
-        for (int i = max(n_early, NST); i < NST + kPrefetch && i < np; ++i) prefetch(i);
+        for (int i = max(n_early, NST); i < NST + kEarlyPrefetch && i < np; ++i) prefetch(i);
 
     const long long win_lo = S.base, win_hi = S.base + S.len;
     const long long new_slot = own_new ? S.new_slot : -1;
