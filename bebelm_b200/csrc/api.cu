@@ -208,6 +208,10 @@ struct bebelm_kv_pool {
     ErrWord err;
     PinBuf pin;
     UploadRing uploads;
+    // a second stream for work that may run beside the caller's (forked and joined with events
+    // inside one call, so the call stays stream-ordered and capturable)
+    cudaStream_t side = nullptr;
+    cudaEvent_t ev_fork = nullptr, ev_join = nullptr;
     const void* last_plan = nullptr;  // the step plan of the last decode launch, if it was one
     unsigned long long last_capture = 0;  // the stream capture that launch was recorded in (0: none)
     std::vector<DecodeSeq> h_desc;
@@ -368,6 +372,11 @@ void pool_free(bebelm_kv_pool* P) {
     DeviceGuard g(P->device);
     cudaDeviceSynchronize();
     P->uploads.release();
+    if (P->side) cudaStreamDestroy(P->side);
+    if (P->ev_fork) cudaEventDestroy(P->ev_fork);
+    if (P->ev_join) cudaEventDestroy(P->ev_join);
+    P->side = nullptr;
+    P->ev_fork = P->ev_join = nullptr;
     cudaFree(P->mem);
     P->io.release();
     P->qn.release();
@@ -1844,9 +1853,21 @@ int project_qkv(bebelm_kv_pool* P, const bebelm_attn_weights* W, const float* dx
     Q8View q8;
     if (is_kquant(W->dt[0]) || is_kquant(W->dt[1]) || is_kquant(W->dt[2]))
         TRY(quantize_into_scratch(P, dx, W->hidden, t, &q8, s));
+    // the k and v projections (n_kv*64 rows: too few CTAs to fill the GPU) run on the pool's
+    // side stream beside the q projection, forked after the quantization and joined before
+    // anything reads them
+    if (!P->side) {
+        CUDA_TRY(cudaStreamCreateWithFlags(&P->side, cudaStreamNonBlocking));
+        CUDA_TRY(cudaEventCreateWithFlags(&P->ev_fork, cudaEventDisableTiming));
+        CUDA_TRY(cudaEventCreateWithFlags(&P->ev_join, cudaEventDisableTiming));
+    }
+    CUDA_TRY(cudaEventRecord(P->ev_fork, s));
+    CUDA_TRY(cudaStreamWaitEvent(P->side, P->ev_fork, 0));
+    TRY(project(W, 1, W->hidden, nkv, dx, t, q8, *k, P->err.d, P->side));
+    TRY(project(W, 2, W->hidden, nkv, dx, t, q8, *v, P->err.d, P->side));
+    CUDA_TRY(cudaEventRecord(P->ev_join, P->side));
     TRY(project(W, 0, W->hidden, nq, dx, t, q8, *q, P->err.d, s));
-    TRY(project(W, 1, W->hidden, nkv, dx, t, q8, *k, P->err.d, s));
-    TRY(project(W, 2, W->hidden, nkv, dx, t, q8, *v, P->err.d, s));
+    CUDA_TRY(cudaStreamWaitEvent(s, P->ev_join, 0));
     return 0;
 }
 

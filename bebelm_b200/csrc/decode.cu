@@ -614,10 +614,12 @@ __global__ void __launch_bounds__(kThreads, 2) decode_kernel(DecodeArgs a) {
     const int hh = (f * 4) / kHeadDim;
     const float4* src = reinterpret_cast<const float4*>(a.part_acc) + ((size_t)S.split0 * NY + y) * kVec + f;
     const size_t stride = (size_t)NY * kVec;
-    // one round of loads: split maxima/sums and this thread's first 16 partial vectors
-    float4 x[16];
+    // one round of loads: split maxima/sums and this thread's first kRound partial vectors
+    // (kRound * G splits: 40 with 128 threads and 4 heads, enough for a 32k window's 37 splits)
+    constexpr int kRound = 20;
+    float4 x[kRound];
 #pragma unroll
-    for (int u = 0; u < 16; ++u) {
+    for (int u = 0; u < kRound; ++u) {
         const int k = g0 + u * G;
         x[u] = active && k < ns ? __ldcg(src + (size_t)k * stride) : make_float4(0.f, 0.f, 0.f, 0.f);
     }
@@ -647,16 +649,16 @@ __global__ void __launch_bounds__(kThreads, 2) decode_kernel(DecodeArgs a) {
     __syncthreads();
     if (active) {
         float4 A = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (int k0 = g0; k0 < ns; k0 += 16 * G) {
+        for (int k0 = g0; k0 < ns; k0 += kRound * G) {
             if (k0 != g0) {  // more splits than one round holds
 #pragma unroll
-                for (int u = 0; u < 16; ++u) {
+                for (int u = 0; u < kRound; ++u) {
                     const int k = k0 + u * G;
                     x[u] = k < ns ? __ldcg(src + (size_t)k * stride) : make_float4(0.f, 0.f, 0.f, 0.f);
                 }
             }
 #pragma unroll
-            for (int u = 0; u < 16; ++u) {
+            for (int u = 0; u < kRound; ++u) {
                 const int k = k0 + u * G;
                 const float fk = k < ns ? sm_m[k * HPC + hh] : 0.f;
                 A.x = fmaf(fk, x[u].x, A.x);
