@@ -227,7 +227,8 @@ cudaError_t launch_qmatmul(int dtype, const uint8_t* w, size_t n_in, size_t n_ou
 // launch_qmatmul. A bounded wait that gives up stores kErrWaitTimeout to *err.
 // cudaErrorNotSupported (nothing launched) when the buffers cannot be described to TMA.
 cudaError_t launch_kquant_tc(int dtype, const uint8_t* w, size_t n_in, size_t n_out, size_t n_tokens,
-                             const int8_t* q8, const float* q8_scales, float* y, int* err, cudaStream_t s);
+                             const int8_t* q8, const float* q8_scales, const int* q8_sums, float* y, int* err,
+                             cudaStream_t s);
 // whether launch_qmatmul sends K-quant batches to launch_kquant_tc (on unless BEBELM_QMM_TC=0)
 bool kquant_tc_enabled();
 cudaError_t launch_dequantize(int dtype, const uint8_t* data, size_t n, float* out, cudaStream_t s);

@@ -1072,7 +1072,7 @@ cudaError_t launch_qmatmul(int dtype, const uint8_t* w, size_t n_in, size_t n_ou
     if (n_out == 0 || n_tokens == 0) return cudaSuccess;
     const size_t rb = ggml_row_bytes(dtype, n_in);
     if ((dtype == kGgmlQ4K || dtype == kGgmlQ6K) && n_tokens >= kTcMinTokens && err && kquant_tc_enabled()) {
-        const cudaError_t e = launch_kquant_tc(dtype, w, n_in, n_out, n_tokens, q8, q8_scales, y, err, s);
+        const cudaError_t e = launch_kquant_tc(dtype, w, n_in, n_out, n_tokens, q8, q8_scales, q8_sums, y, err, s);
         if (e != cudaErrorNotSupported) return e;  // else: no tensor maps for these buffers; dp4a below
     }
     if ((dtype == kGgmlQ4K || dtype == kGgmlQ6K) && n_tokens >= kTiledMinTokens) {

@@ -83,6 +83,8 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t addr) {  // 128B swizzle,
 }
 // kind::i8: D s32 (2 at bit 4), A and B signed 8-bit (1 at bits 7 and 10), both K-major, N, M
 constexpr uint32_t kIdesc = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kN >> 3) << 17) | ((uint32_t)(kM >> 4) << 24);
+// kind::f16: D f32 (1 at bit 4), A and B f16 (0 at bits 7 and 10), both K-major, N, M
+constexpr uint32_t kIdescF16 = (1u << 4) | ((uint32_t)(kN >> 3) << 17) | ((uint32_t)(kM >> 4) << 24);
 
 // byte offset of (row, k) in a K-major A tile of two 128-byte-swizzled atoms (K 0..127, 128..255):
 // inside an atom, 8-row groups of 1024 bytes, the 16-byte chunk index XORed with the row in its group
@@ -161,7 +163,7 @@ __device__ __forceinline__ void load_realigned(const unsigned char* row16, int s
 template <bool Q6>
 __global__ void __launch_bounds__(kThreads, 1)
     kquant_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_q, size_t n_in,
-                  size_t n_out, size_t n_tokens, const float* q8_scales, float* y, int* err) {
+                  size_t n_out, size_t n_tokens, const float* q8_scales, const int* q8_sums, float* y, int* err) {
     using L = Lay<Q6>;
     extern __shared__ unsigned char smem_raw[];
     unsigned char* sm = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -221,7 +223,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 tc_after();
                 const uint32_t bB = sb + kOffB + (uint32_t)(b & 1) * kTileB;
 #pragma unroll
-                for (int a = 0; a < 3; ++a) {
+                for (int a = 0; a < (Q6 ? 3 : 2); ++a) {
 #pragma unroll
                     for (int kk = 0; kk < 8; ++kk) {  // K step: atom kk / 4, 32 bytes at (kk % 4) * 32
                         const uint32_t koff = (uint32_t)(kk & 3) * 32;
@@ -233,6 +235,15 @@ __global__ void __launch_bounds__(kThreads, 1)
                             "l"(ad), "l"(bd), "r"(kIdesc), "r"(kk)
                             : "memory");
                     }
+                }
+                if constexpr (!Q6) {  // sm: one f16 MMA, K = 16, into the third accumulator (f32)
+                    const uint64_t ad = smem_desc(sb + kOffA + 2 * kTileA);
+                    const uint64_t bd = smem_desc(sb + kOffA + 2 * kTileA + kAtomA);
+                    asm volatile(
+                        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+                        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem + 2 * kN),
+                        "l"(ad), "l"(bd), "r"(kIdescF16), "r"(0)
+                        : "memory");
                 }
                 asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
                                  mma_done)
@@ -259,6 +270,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         const float* sx_src = q8_scales + (t0 + tid) * nb;
         const bool sx_ok = tid < kN && t0 + tid < n_tokens;
         float sx_next = sx_ok && nb ? sx_src[0] : 0.f;
+        // Q4_K: the token's 32-wide sub-block sums S_j of the next block (8 ints), for B'
+        const int4* sum_src = reinterpret_cast<const int4*>(q8_sums + (t0 + tid) * nb * 8);
+        int4 sum_next[2] = {make_int4(0, 0, 0, 0), make_int4(0, 0, 0, 0)};
+        if (!Q6 && sx_ok && nb) sum_next[0] = sum_src[0], sum_next[1] = sum_src[1];
         float d = 0.f, dmin = 0.f;  // of the block whose accumulators are read next
         float acc[32];
 #pragma unroll
@@ -295,7 +310,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         } else {  // sd = lo + 8 hi, sm = min; sx * (d * sd - dmin * sm)
                             const int sd = a0[i] + 8 * a1[i];
                             v = __fmul_rn(sx[16 * h + i], __fsub_rn(__fmul_rn(d, __int2float_rn(sd)),
-                                                                    __fmul_rn(dmin, __int2float_rn(a2[i]))));
+                                                                    __fmul_rn(dmin, __int_as_float(a2[i]))));
                         }
                         acc[16 * h + i] = __fadd_rn(acc[16 * h + i], v);
                     }
@@ -386,12 +401,47 @@ __global__ void __launch_bounds__(kThreads, 1)
                             lo[e] = nib * (sc[h] & 7);  // bytewise: 15 * 7 < 256, no carries
                             hi[e] = nib * (sc[h] >> 3);
                         }
-                        const uint32_t m4 = mn[h] * 0x01010101u;
                         const uint32_t off = swz_a(row, (2 * quarter + h) * 32 + p);
                         *reinterpret_cast<uint4*>(sm + kOffA + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
                         *reinterpret_cast<uint4*>(sm + kOffA + kTileA + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-                        *reinterpret_cast<uint4*>(sm + kOffA + 2 * kTileA + off) = make_uint4(m4, m4, m4, m4);
                     }
+                }
+                // sm = Σ_j m_j S_j as one f16 MMA (K = 16): A' row = the 8 mins twice, B' token =
+                // 64 a_j then b_j with S_j = 64 a_j + b_j, b_j in [0, 63]. Every operand is an
+                // exact f16 and every partial sum an integer below 2^24, so the f32 result is exact.
+                if (quarter == 0) {
+                    uint32_t mw[4];
+#pragma unroll
+                    for (int jj = 0; jj < 8; jj += 2) {
+                        uint32_t m2[2];
+#pragma unroll
+                        for (int u = 0; u < 2; ++u) {
+                            const int j = jj + u;
+                            m2[u] = j < 4 ? (s1 >> (8 * j)) & 63
+                                          : (((s2 >> (8 * (j - 4))) & 0xff) >> 4) | (((s1 >> (8 * (j - 4) + 6)) & 3) << 4);
+                        }
+                        const __half2 hv = __floats2half2_rn((float)m2[0], (float)m2[1]);
+                        mw[jj / 2] = *reinterpret_cast<const uint32_t*>(&hv);
+                    }
+                    const uint4 mv = make_uint4(mw[0], mw[1], mw[2], mw[3]);
+                    *reinterpret_cast<uint4*>(sm + kOffA + 2 * kTileA + swz_a(row, 0)) = mv;
+                    *reinterpret_cast<uint4*>(sm + kOffA + 2 * kTileA + swz_a(row, 16)) = mv;
+                }
+                if (tid < kN) {
+                    const int sv[8] = {sum_next[0].x, sum_next[0].y, sum_next[0].z, sum_next[0].w,
+                                       sum_next[1].x, sum_next[1].y, sum_next[1].z, sum_next[1].w};
+                    uint32_t aw[4], bw[4];
+#pragma unroll
+                    for (int jj = 0; jj < 8; jj += 2) {
+                        const __half2 ha = __floats2half2_rn((float)((sv[jj] >> 6) * 64), (float)((sv[jj + 1] >> 6) * 64));
+                        const __half2 hb = __floats2half2_rn((float)(sv[jj] & 63), (float)(sv[jj + 1] & 63));
+                        aw[jj / 2] = *reinterpret_cast<const uint32_t*>(&ha);
+                        bw[jj / 2] = *reinterpret_cast<const uint32_t*>(&hb);
+                    }
+                    unsigned char* bp = sm + kOffA + 2 * kTileA + kAtomA;
+                    *reinterpret_cast<uint4*>(bp + swz_a(tid, 0)) = make_uint4(aw[0], aw[1], aw[2], aw[3]);
+                    *reinterpret_cast<uint4*>(bp + swz_a(tid, 16)) = make_uint4(bw[0], bw[1], bw[2], bw[3]);
+                    if (sx_ok && b + 1 < nb) sum_next[0] = sum_src[2 * (b + 1)], sum_next[1] = sum_src[2 * (b + 1) + 1];
                 }
             }
             if (tid < kN) {  // this block's token scales for the epilogue; the next block's from memory
@@ -451,12 +501,13 @@ bool byte_map(CUtensorMap* m, const void* base, size_t row_bytes, size_t rows, u
 namespace {
 template <bool Q6>
 cudaError_t launch_tc(const uint8_t* w, size_t n_in, size_t n_out, size_t n_tokens, const int8_t* q8,
-                      const float* q8_scales, float* y, int* err, cudaStream_t s) {
+                      const float* q8_scales, const int* q8_sums, float* y, int* err, cudaStream_t s) {
     using L = Lay<Q6>;
     const size_t row_bytes = n_in / kQK * L::kBlockBytes;
     // TMA wants 16-byte aligned bases and row strides; rows and tokens must fit the 32-bit
     // coordinates
     if ((reinterpret_cast<uintptr_t>(w) & 15) || (reinterpret_cast<uintptr_t>(q8) & 15) || (row_bytes & 15) ||
+        (reinterpret_cast<uintptr_t>(q8_sums) & 15) ||
         n_out >= (1u << 31) || n_tokens >= (1u << 31) || row_bytes >= (1u << 31))
         return cudaErrorNotSupported;
     CUtensorMap tw, tq;
@@ -473,15 +524,17 @@ cudaError_t launch_tc(const uint8_t* w, size_t n_in, size_t n_out, size_t n_toke
         if (dev >= 0 && dev < 64) attr_set[dev] = true;
     }
     const dim3 grid((unsigned)((n_out + kM - 1) / kM), (unsigned)((n_tokens + kN - 1) / kN));
-    kquant_tc_kernel<Q6><<<grid, kThreads, L::kSmemBytes, s>>>(tw, tq, n_in, n_out, n_tokens, q8_scales, y, err);
+    kquant_tc_kernel<Q6><<<grid, kThreads, L::kSmemBytes, s>>>(tw, tq, n_in, n_out, n_tokens, q8_scales, q8_sums, y,
+                                                                err);
     return cudaGetLastError();
 }
 }  // namespace
 
 cudaError_t launch_kquant_tc(int dtype, const uint8_t* w, size_t n_in, size_t n_out, size_t n_tokens,
-                             const int8_t* q8, const float* q8_scales, float* y, int* err, cudaStream_t s) {
-    if (dtype == kGgmlQ4K) return launch_tc<false>(w, n_in, n_out, n_tokens, q8, q8_scales, y, err, s);
-    if (dtype == kGgmlQ6K) return launch_tc<true>(w, n_in, n_out, n_tokens, q8, q8_scales, y, err, s);
+                             const int8_t* q8, const float* q8_scales, const int* q8_sums, float* y, int* err,
+                             cudaStream_t s) {
+    if (dtype == kGgmlQ4K) return launch_tc<false>(w, n_in, n_out, n_tokens, q8, q8_scales, q8_sums, y, err, s);
+    if (dtype == kGgmlQ6K) return launch_tc<true>(w, n_in, n_out, n_tokens, q8, q8_scales, q8_sums, y, err, s);
     return cudaErrorNotSupported;
 }
 
