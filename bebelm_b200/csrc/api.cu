@@ -468,6 +468,11 @@ bool inputs_clear_of_last_out(cudaStream_t s, std::initializer_list<std::pair<co
     return true;
 }
 
+#ifndef BEBELM_BATCH_PAGES_PER_SPLIT
+#define BEBELM_BATCH_PAGES_PER_SPLIT 32
+#endif
+constexpr long long kBatchMaxPagesPerSplit = BEBELM_BATCH_PAGES_PER_SPLIT;
+
 void pick_heads_per_cta(int group, int* hpc, int* n_sub) {
     int h = group % 4 == 0 ? 4 : group % 3 == 0 ? 3 : group % 2 == 0 ? 2 : 1;
     *hpc = h;
@@ -508,7 +513,7 @@ int run_decode(bebelm_kv_pool* P, const std::vector<Window>& wins, int layer, in
     }
     const long long target = (long long)P->num_sms * 2;  // two resident CTAs per SM
     long long per = std::max<long long>(1, (total_units + target - 1) / target);
-    if (n > 1) per = std::min<long long>(per, 8);  // uneven sequences: more, smaller splits
+    if (n > 1) per = std::min<long long>(per, kBatchMaxPagesPerSplit);  // uneven sequences: more, smaller splits
     per = std::min<long long>(per, kDecodeMaxPagesPerSplit);
     P->h_desc.resize(n);
     int total_splits = 0;

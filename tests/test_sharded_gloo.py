@@ -83,12 +83,19 @@ def test_kv_head_sharding_matches_unsharded(world):
     ctx = mp.get_context("fork")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
+    # daemon ranks, ended on the way out: a rank that hangs (e.g. forked from a process that
+    # had initialised CUDA) must not keep the interpreter from exiting
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q), daemon=True) for r in range(world)]
     for p in procs:
         p.start()
-    res = [q.get(timeout=180) for _ in range(world)]
-    for p in procs:
-        p.join(timeout=60)
+    try:
+        res = [q.get(timeout=180) for _ in range(world)]
+        for p in procs:
+            p.join(timeout=60)
+    finally:
+        for p in procs:
+            if p.is_alive():
+                p.terminate()
     for r in res:
         assert not isinstance(r[1], str), r[1]
     # unsharded reference
