@@ -469,7 +469,7 @@ bool inputs_clear_of_last_out(cudaStream_t s, std::initializer_list<std::pair<co
 }
 
 #ifndef BEBELM_BATCH_PAGES_PER_SPLIT
-#define BEBELM_BATCH_PAGES_PER_SPLIT 32
+#define BEBELM_BATCH_PAGES_PER_SPLIT 8
 #endif
 constexpr long long kBatchMaxPagesPerSplit = BEBELM_BATCH_PAGES_PER_SPLIT;
 
