@@ -209,7 +209,7 @@ struct bebelm_kv_pool {
     PinBuf pin;
     UploadRing uploads;
     // a second stream for work that may run beside the caller's (forked and joined with events
-    // inside one call, so the call stays stream-ordered and capturable)
+    // inside one call, so the call stays ordered on the caller's stream)
     cudaStream_t side = nullptr;
     cudaEvent_t ev_fork = nullptr, ev_join = nullptr;
     const void* last_plan = nullptr;  // the step plan of the last decode launch, if it was one
