@@ -125,5 +125,7 @@ def test_kquant_tensor_core_matmul_bit_exact(dtype, gen, n_out, n_in, t):
     xs = oracle.normal(120 + t, (t, n_in))
     xs[5] = 0.0
     xs[t - 1] = np.where(np.arange(n_in) % 3, 1e3, -1e3)  # every quant at +-127
+    xs[t - 2] = 1e3   # sub-block sums at +4064: the Q4_K min term's split 64 * 63 + 32
+    xs[t - 3] = -1e3  # and at -4064: 64 * (-64) + 32
     np.testing.assert_array_equal(bb.matmul(dtype, w, n_in, n_out, xs, t),
                                   oracle.matmul(dtype, w, n_in, n_out, xs, t))
