@@ -272,39 +272,6 @@ __global__ void __launch_bounds__(kThreads, 2) decode_kernel(DecodeArgs a) {
     const long long dep_page = S.dep_slot >> 6;
     const int n_early = dep_page <= p0 ? 0 : (int)min((long long)np, dep_page - p0);
 
-    // page-table slice (written by the host, never by a kernel)
-    for (int i = tid; i < np; i += kThreads) s_phys[i] = S.table[(int)((p0 + i) % S.cap)];
-    __syncthreads();
-    auto page_src = [&](int i) -> const char* {
-        return a.pv.base + (size_t)s_phys[i] * a.pv.page_bytes + a.pv.layer_off + (size_t)kvh * ROWB;
-    };
-    auto issue = [&](int i) {
-        const int st = i % NST;
-        const char* kp = page_src(i);
-        unsigned char* dk = stages + (size_t)st * SB;
-        mbar_expect_tx(&full[st], SB);
-        bulk_g2s(dk, kp, ROWB, &full[st]);
-        bulk_g2s(dk + ROWB, kp + a.pv.block_bytes, ROWB, &full[st]);
-    };
-    auto prefetch = [&](int i) {
-        const char* kp = page_src(i);
-        bulk_prefetch_l2(kp, ROWB);
-        bulk_prefetch_l2(kp + a.pv.block_bytes, ROWB);
-    };
-
-    const int n_first = min(NST, np);
-    if (tid == 0) {
-        for (int s = 0; s < NST; ++s) {
-            mbar_init(&full[s], 1);
-            s_release[s] = 0;
-        }
-        s_failed = 0;
-        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        for (int i = 0; i < n_first && i < n_early; ++i) issue(i);
-        for (int i = NST; i < NST + kEarlyPrefetch && i < n_early; ++i) prefetch(i);
-    }
-
     // this CTA's query heads, normed + roped here for a fused step, and the appended token's
     // k (normed + roped) and v if its slot is in our pages: computed before griddepcontrol.wait
     // when the host saw that the inputs were complete before the predecessor began (early_inputs)
@@ -344,7 +311,51 @@ __global__ void __launch_bounds__(kThreads, 2) decode_kernel(DecodeArgs a) {
         }
     };
     const bool early = a.early_inputs && !a.step;
+
+    // page-table slice (written by the host, never by a kernel): its loads are started first, so
+    // that with early inputs their latency overlaps the norm and RoPE of the step's inputs
+    static_assert(kMaxPagesPerSplit <= 2 * kThreads, "page-table slice: two entries per thread");
+    int ph[2];
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+        const int i = tid + u * kThreads;
+        ph[u] = i < np ? S.table[(int)((p0 + i) % S.cap)] : 0;
+    }
     if (early) read_inputs();
+#pragma unroll
+    for (int u = 0; u < 2; ++u)
+        if (tid + u * kThreads < np) s_phys[tid + u * kThreads] = ph[u];
+    __syncthreads();
+    auto page_src = [&](int i) -> const char* {
+        return a.pv.base + (size_t)s_phys[i] * a.pv.page_bytes + a.pv.layer_off + (size_t)kvh * ROWB;
+    };
+    auto issue = [&](int i) {
+        const int st = i % NST;
+        const char* kp = page_src(i);
+        unsigned char* dk = stages + (size_t)st * SB;
+        mbar_expect_tx(&full[st], SB);
+        bulk_g2s(dk, kp, ROWB, &full[st]);
+        bulk_g2s(dk + ROWB, kp + a.pv.block_bytes, ROWB, &full[st]);
+    };
+    auto prefetch = [&](int i) {
+        const char* kp = page_src(i);
+        bulk_prefetch_l2(kp, ROWB);
+        bulk_prefetch_l2(kp + a.pv.block_bytes, ROWB);
+    };
+
+    const int n_first = min(NST, np);
+    if (tid == 0) {
+        for (int s = 0; s < NST; ++s) {
+            mbar_init(&full[s], 1);
+            s_release[s] = 0;
+        }
+        s_failed = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        for (int i = 0; i < n_first && i < n_early; ++i) issue(i);
+        for (int i = NST; i < NST + kEarlyPrefetch && i < n_early; ++i) prefetch(i);
+    }
+
 
     // ---- everything below may read what the predecessor wrote --------------
     grid_dep_wait();
