@@ -27,6 +27,7 @@ LIB_PATH = os.path.join(_HERE, "libbebelm_attn.so")
 OK, ERR_INVALID, ERR_CUDA, ERR_OOM, ERR_CAPACITY, ERR_UNSUPPORTED, ERR_TIMEOUT, ERR_NO_DEVICE = 0, -1, -2, -3, -4, -5, -7, -8
 MEM_HOST, MEM_DEVICE = 0, 1
 F32, BF16 = 0, 1
+F32_TENSOR = 2  # prefill in_dtype: fp32 inputs, tensor-core attention
 
 # reference constants (src/config.rs:14-32)
 N_HEADS, N_KV_HEADS, HEAD_DIM, KV_DIM, HIDDEN = 32, 8, 64, 512, 2048
@@ -380,13 +381,15 @@ class Cache:
         return out
 
     def attn_prefill(self, layer: int, q, k, v, q_gain, k_gain, pos0: int, theta: float = ROPE_THETA,
-                     eps: float = RMS_EPS, out=None, stream=None, n_heads: int = N_HEADS):
+                     eps: float = RMS_EPS, out=None, stream=None, n_heads: int = N_HEADS,
+                     tensor_cores: bool = False):
         """src/model.rs:232-254 for t tokens. q [t, n_heads*64], k/v [t, n_kv*64] (float32 or bf16
-        tensors). Returns out [t, n_heads*64] float32."""
+        tensors). Returns out [t, n_heads*64] float32. bf16 inputs always take the tensor cores;
+        float32 inputs take them when ``tensor_cores`` is set (else the reference's fp32 arithmetic)."""
         is_dev = _is_torch(q) and q.is_cuda
         if is_dev:
             import torch
-            in_dtype = BF16 if q.dtype == torch.bfloat16 else F32
+            in_dtype = BF16 if q.dtype == torch.bfloat16 else (F32_TENSOR if tensor_cores else F32)
             t = q.numel() // (n_heads * self.head_dim)
             if out is None:
                 out = torch.empty((t, n_heads * self.head_dim), dtype=torch.float32, device=q.device)
@@ -395,7 +398,7 @@ class Cache:
             keep = (q, k, v, q_gain, k_gain, out)
         else:
             q = np.ascontiguousarray(q)
-            in_dtype = F32
+            in_dtype = F32_TENSOR if tensor_cores else F32
             if q.dtype != np.float32:
                 q = q.astype(np.float32)
             k = np.ascontiguousarray(k, np.float32)

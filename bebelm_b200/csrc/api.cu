@@ -84,13 +84,17 @@ struct DevBuf {
     size_t bytes = 0;
     int ensure(size_t need, bool zero = false, cudaStream_t s = 0) {
         if (need <= bytes) return 0;
+        // a buffer that has to grow gets half as much again on top: scratch that follows a
+        // growing window (split partials of a decode step whose sequences lengthen) then grows
+        // a few times per run, not every few steps — each regrowth waits for the stream
+        size_t n = std::max<size_t>(need, 256);
         if (p) {
+            n = std::max(n, bytes + bytes / 2);
             cudaStreamSynchronize(s);
             cudaFree(p);
             p = nullptr;
             bytes = 0;
         }
-        size_t n = std::max<size_t>(need, 256);
         CUDA_TRY(cudaMalloc(&p, n));
         bytes = n;
         if (zero) CUDA_TRY(cudaMemsetAsync(p, 0, n, s));
@@ -621,6 +625,10 @@ int stage_in(bebelm_kv_pool* P, Stage* st, int n, size_t out_bytes, void** d_out
     return 0;
 }
 
+// Zeroes the split counters of the no-allocation decode on `dev` (if that path was ever set up
+// there): a decode CTA that gave up on a wait left its counter short.
+void clear_noalloc_counters(int dev, cudaStream_t s);
+
 // Waits for the call's work, surfaces a device-side timeout recorded by a kernel, and
 // delivers the output to the caller's host memory (from the pinned buffer, after copying
 // it there unless the kernel stored it there directly).
@@ -632,6 +640,7 @@ int stage_out(bebelm_kv_pool* P, const void* d_src, void* h_dst, size_t bytes, c
     if (derr) {
         P->err.clear();
         if (P->counters.p) cudaMemsetAsync(P->counters.p, 0, P->counters.bytes, s);
+        clear_noalloc_counters(P->device, s);
         cudaStreamSynchronize(s);
         return fail(BEBELM_ERR_TIMEOUT, "a device-side wait timed out (code %d); outputs are invalid", derr);
     }
@@ -1182,14 +1191,14 @@ int bebelm_attn_prefill(bebelm_kv* kv, int layer, int n_heads, const void* q, co
     TRY(check_mem(mem));
     bebelm_kv_pool* P = kv->pool;
     TRY(check_geometry(n_heads, P->n_kv));
-    if (in_dtype != BEBELM_F32 && in_dtype != BEBELM_BF16)
-        return fail(BEBELM_ERR_UNSUPPORTED, "in_dtype must be BEBELM_F32 or BEBELM_BF16");
+    if (in_dtype != BEBELM_F32 && in_dtype != BEBELM_BF16 && in_dtype != BEBELM_F32_TENSOR)
+        return fail(BEBELM_ERR_UNSUPPORTED, "in_dtype must be BEBELM_F32, BEBELM_BF16 or BEBELM_F32_TENSOR");
     if (t == 0) return 0;
     if (!q || !k || !v || !q_gain || !k_gain || !out) return fail(BEBELM_ERR_INVALID, "null buffer");
     if (t > (size_t)INT32_MAX / (size_t)n_heads) return fail(BEBELM_ERR_INVALID, "t too large");
     DeviceGuard g(P->device);
     cudaStream_t s = as_stream(stream);
-    const size_t esz = in_dtype == BEBELM_F32 ? 4 : 2;
+    const size_t esz = in_dtype == BEBELM_BF16 ? 2 : 4;
     const size_t qn = (size_t)n_heads * kHeadDim * t, kvn = (size_t)P->n_kv * kHeadDim * t;
     const void *dq = q, *dk = k, *dv = v;
     const float *dqg = q_gain, *dkg = k_gain;
@@ -1201,8 +1210,8 @@ int bebelm_attn_prefill(bebelm_kv* kv, int layer, int n_heads, const void* q, co
         dq = a0; dk = a1; dv = a2;
         dqg = (const float*)a3; dkg = (const float*)a4; dout = (float*)o;
     }
-    const bool bf = in_dtype == BEBELM_BF16;
-    TRY(prefill_device(kv, layer, n_heads, dq, dk, dv, bf, bf, t, pos0, dqg, dkg, theta, eps, dout, s));
+    const bool bf = in_dtype == BEBELM_BF16, tc = in_dtype != BEBELM_F32;
+    TRY(prefill_device(kv, layer, n_heads, dq, dk, dv, bf, tc, t, pos0, dqg, dkg, theta, eps, dout, s));
     if (mem == BEBELM_MEM_HOST) return stage_out(P, dout, out, 4 * qn, s);
     return 0;
 }
@@ -1282,6 +1291,16 @@ int noalloc_scratch(int dev, cudaStream_t s, float** out) {
     return 0;
 }
 
+void clear_noalloc_counters(int dev, cudaStream_t s) {
+    if (dev < 0 || dev >= 64) return;
+    float* ptr = nullptr;
+    {
+        std::lock_guard<std::mutex> lk(g_noalloc_mu);
+        ptr = g_noalloc_addr[dev];
+    }
+    if (ptr) cudaMemsetAsync(ptr + kNoAllocPartialFloats, 0, sizeof(unsigned) * kNoAllocCounterWords, s);
+}
+
 }  // namespace
 
 extern "C" int bebelm_attn_decode_cached_noalloc(const bebelm_kv* kv, int layer, int n_heads, const float* q,
@@ -1310,7 +1329,11 @@ extern "C" int bebelm_attn_decode_cached_noalloc(const bebelm_kv* kv, int layer,
     per = std::min<long long>(per, kDecodeMaxPagesPerSplit);
     const long long n_splits = (npages + per - 1) / per;
     const size_t need = (size_t)n_splits * NY * hpc * (kHeadDim + 2);
-    if (need > kNoAllocPartialFloats || (size_t)NY > kNoAllocCounterWords)
+    if ((size_t)NY > kNoAllocCounterWords)
+        return fail(BEBELM_ERR_INVALID,
+                    "%d kv heads x %d head groups need %d split counters; the no-allocation path holds at most %zu",
+                    P->n_kv, n_sub, NY, kNoAllocCounterWords);
+    if (need > kNoAllocPartialFloats)
         return fail(BEBELM_ERR_INVALID,
                     "window of %lld positions needs %zu scratch floats (%lld splits x %d heads); the no-allocation "
                     "path holds at most %zu",
@@ -1332,7 +1355,7 @@ extern "C" int bebelm_attn_decode_cached_noalloc(const bebelm_kv* kv, int layer,
     a.part_acc = scratch;
     a.part_ml = scratch + (size_t)n_splits * NY * hpc * kHeadDim;
     a.counters = reinterpret_cast<unsigned*>(scratch + kNoAllocPartialFloats);
-    a.err = reinterpret_cast<int*>(scratch + kNoAllocPartialFloats + kNoAllocCounterWords);
+    a.err = P->err.d;  // the pool's mapped error word (allocated with the pool): bebelm_kv_check reads it
     a.n_heads = n_heads;
     a.n_kv = P->n_kv;
     a.group = group;
@@ -1387,6 +1410,7 @@ int bebelm_kv_check(const bebelm_kv* kv, void* stream) {
     if (derr) {
         P->err.clear();
         if (P->counters.p) cudaMemsetAsync(P->counters.p, 0, P->counters.bytes, s);
+        clear_noalloc_counters(P->device, s);
         cudaStreamSynchronize(s);
         return fail(BEBELM_ERR_TIMEOUT, "a device-side wait timed out (code %d); outputs are invalid", derr);
     }

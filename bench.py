@@ -34,6 +34,14 @@ THETA, EPS = 1e6, 1e-5
 METRIC = "decode-attn KV-read GB/s @32k ctx (1 layer, 32q/8kv, d=64, fp32 KV)"
 
 
+def workload_config(world: int) -> dict:
+    """The workload, identical in both arms' JSON lines."""
+    return {"workload": "config3: 1 seq per GPU, 32768-position window, append+evict per step",
+            "n_ctx": CTX, "heads": "32q/8kv", "head_dim": D, "theta": THETA, "kv_dtype": "f32",
+            "parallelism": f"per-sequence x{world}",
+            "l2": "no flush: the 134 MB window exceeds the 126 MB L2"}
+
+
 def bytes_per_step(n_ctx: int) -> int:
     return 2 * n_ctx * KVD * 4
 
@@ -166,8 +174,7 @@ def run_reference(args):
         "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(sec * 1e3, 3), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded N(0,1))",
-        "config": {"workload": "config3: 1 seq, 32768-position window, append+evict per step", "n_ctx": CTX,
-                   "heads": "32q/8kv", "head_dim": D, "theta": THETA},
+        "config": workload_config(world),
         "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": threads, "kind": "port",
                          "sample": f"{done} of {args.steps} decode steps at 32768 positions (oracle C restatement of "
                                    f"src/kernels/attention.rs, heads over {threads} threads)"},
@@ -250,7 +257,7 @@ def run_ours(args):
     # there (PDL-chained) is the timed time per step
     achieved = bytes_per_step(CTX + 1) / (ms / args.steps * 1e-3) / 1e9
     isolated = bytes_per_step(CTX) / (kern_ms * 1e-3) / 1e9
-    traffic = load_profile_traffic()
+    traffic, traffic_src = load_profile_traffic()
 
     # -- end to end through the C-ABI with host buffers: the call a Rust caller makes per step
     #    (bebelm_attn_step with mem = HOST: inputs copied in and the output back inside the
@@ -296,7 +303,7 @@ def run_ours(args):
     hbm_peak_, bf16_peak_, _ = peaks()
     cfg5 = None if args.no_cfg5 else bench_config5(bb, torch, dev, stream, world, rank, bf16_peak_)
 
-    cpu = None
+    cpu = cpu1 = None
     if rank == 0 and world == 1 and not args.no_cpu:
         import oracle
         threads = oracle.max_threads()
@@ -304,17 +311,19 @@ def run_ours(args):
         cpu = {"value": round(bytes_per_step(CTX + 1) / sec / 1e9, 3), "unit": "GB/s", "cores": threads,
                "kind": "port",
                "sample": f"{done} decode steps at 32768 positions on {threads} threads (C restatement of the "
-                         f"reference arithmetic; the reference itself runs attention on 1 core)"}
+                         f"reference arithmetic, heads spread over threads by the harness; the reference itself "
+                         f"runs attention on 1 core)"}
+        sec1, done1 = cpu_decode_sample(1, 10.0, 16)
+        cpu1 = {"value": round(bytes_per_step(CTX + 1) / sec1 / 1e9, 4), "unit": "GB/s", "cores": 1, "kind": "port",
+                "sample": f"{done1} decode steps at 32768 positions on 1 thread (serial, as the reference's "
+                          f"attention_decode runs)"}
 
     if rank == 0:
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 5), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded N(0,1))",
-            "config": {"workload": "config3: 1 seq per GPU, 32768-position window, append+evict per step",
-                       "n_ctx": CTX, "heads": "32q/8kv", "head_dim": D, "theta": THETA, "kv_dtype": "f32",
-                       "parallelism": f"per-sequence x{world}",
-                       "l2": "no flush: the 134 MB window exceeds the 126 MB L2"},
+            "config": workload_config(world),
             "tok_per_s": round(args.steps * world / (ms * 1e-3), 1),
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
                          "frac": round(achieved / hbm_peak, 4), "peak_kind": peak_kind,
@@ -322,12 +331,13 @@ def run_ours(args):
                          "kernel_us": round(ms / args.steps * 1e3, 2),
                          "isolated_launch": {"us": round(kern_ms * 1e3, 2), "gbs": round(isolated, 1),
                                              "note": "one launch between events, no PDL overlap"},
-                         "traffic": traffic},
+                         "traffic": traffic, "traffic_source": traffic_src},
             "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": 4 * (HID + 2 * KVD + 2 * D),
                     "d2h_bytes_per_step": 4 * HID, "steps": e2e_steps},
             "gpu_launches": args.steps,
             "clocks": clk,
             "cpu_baseline": cpu,
+            "cpu_baseline_1core": cpu1,
             "prefill": prefill,
             "config3_bf16_kv": c3bf,
             "logits_head": head,
@@ -340,16 +350,21 @@ def run_ours(args):
 
 
 def load_profile_traffic():
-    """DRAM bytes per decode launch from the committed ncu summary, if present."""
+    """DRAM bytes per decode launch and where they come from: the committed ncu summary of the
+    decode kernel (an ncu capture cannot run inside this timed process). The summary names the
+    commit of the kernel source it captured; the line carries that label so a stale figure shows."""
     p = os.path.join(ROOT, "profiles", "decode_kernel_config3.md")
+    val, src = None, None
     try:
         with open(p) as f:
             for line in f:
                 if line.startswith("| dram_bytes_per_launch |"):
-                    return int(line.split("|")[2])
+                    val = int(line.split("|")[2])
+                elif line.startswith("| kernel_source_commit |"):
+                    src = line.split("|")[2].strip()
     except Exception:
         pass
-    return None
+    return val, f"ncu capture in profiles/decode_kernel_config3.md (decode kernel source of commit {src})"
 
 
 def bench_prefill(bb, torch, dev, stream, bf16_peak, peak_kind, T=2048, reps=6):

@@ -55,6 +55,9 @@ enum {
 
 enum { BEBELM_MEM_HOST = 0, BEBELM_MEM_DEVICE = 1 };
 enum { BEBELM_F32 = 0, BEBELM_BF16 = 1 };
+/* bebelm_attn_prefill only: fp32 inputs (as the reference's attn_batch passes them), attention
+ * on the tensor cores. */
+enum { BEBELM_F32_TENSOR = 2 };
 
 typedef struct bebelm_kv_pool bebelm_kv_pool; /* device page pool + scratch */
 typedef struct bebelm_kv bebelm_kv;           /* one sequence's KV window */
@@ -161,7 +164,10 @@ BEBELM_API int bebelm_attn_decode_cached(const bebelm_kv* kv, int layer, int n_h
  * The first call on a device looks up the array's address and clears its
  * counters (do that call before any stream capture). A window too large for
  * the array is rejected with BEBELM_ERR_INVALID. All calls share the array:
- * calls that overlap on the GPU (different streams, or another thread) race. */
+ * calls that overlap on the GPU (different streams, or another thread) race.
+ * A bounded device-side wait that gives up is recorded in kv's pool error word,
+ * like every other call on the pool: bebelm_kv_check reports it and then also
+ * clears the array's split counters, so the next call starts clean. */
 BEBELM_API int bebelm_attn_decode_cached_noalloc(const bebelm_kv* kv, int layer, int n_heads, const float* q,
                                                  float* out, void* stream);
 
@@ -172,7 +178,11 @@ BEBELM_API int bebelm_attn_decode_cached_noalloc(const bebelm_kv* kv, int layer,
  * always stores the fp32 normed/roped k and raw v. BEBELM_BF16 inputs run the
  * attention on the tensor cores (tcgen05, bf16 operands, fp32 accumulation,
  * within 2e-2 relative of the reference); BEBELM_F32 inputs keep the reference's
- * fp32 arithmetic on the CUDA cores (within 1e-3 absolute). */
+ * fp32 arithmetic on the CUDA cores (within 1e-3 absolute). BEBELM_F32_TENSOR takes
+ * fp32 inputs like BEBELM_F32, norms and ropes them in fp32 (the cache gets the
+ * same fp32 k as with BEBELM_F32) and rounds the normed q, k and the v to bf16 for
+ * the tensor-core attention: the BEBELM_BF16 speed for an fp32 caller, within the
+ * same 2e-2 relative. */
 BEBELM_API int bebelm_attn_prefill(bebelm_kv* kv, int layer, int n_heads, const void* q, const void* k,
                         const void* v, int in_dtype, size_t t, size_t pos0,
                         const float* q_gain, const float* k_gain, float theta, float eps,

@@ -342,6 +342,22 @@ def test_tensor_core_prefill_matches_oracle(t):
     assert np.abs(kd - ck).max() <= ROPE_ATOL and np.array_equal(vd, v)
 
 
+@pytest.mark.parametrize("t", [300, 2048])
+def test_f32_inputs_on_tensor_cores_match_oracle(t):
+    """BEBELM_F32_TENSOR: the fp32 inputs a Rust attn_batch passes (host memory, not
+    bf16-rounded), normed and roped in fp32, attention on the tensor cores."""
+    qg, kg = gains(63)
+    q, k, v = oracle.normal(31, (t, HID)), oracle.normal(32, (t, KVD)), oracle.normal(33, (t, KVD))
+    dev = bb.Cache(n_layers=1, max_context=4096)
+    got = dev.attn_prefill(0, q, k, v, qg, kg, 0, theta=1e6, tensor_cores=True)
+    want, ck, cv, _, _ = oracle.attn_batch(q, k, v, 0, qg, kg, 1e6, 1e-5, H, KVH, D, n_threads=oracle.max_threads())
+    rel = np.abs(got - want).max() / np.abs(want).max()
+    assert rel <= PREFILL_REL, rel
+    # the cache holds exactly what the fp32 path stores
+    kd, vd = dev.read(0)
+    assert np.abs(kd - ck).max() <= ROPE_ATOL and np.array_equal(vd, v)
+
+
 def test_tensor_core_prefill_on_a_cached_prefix():
     """A chunk after 333 cached positions (not a multiple of the 128-key tile), after eviction."""
     qg, kg = gains(71)

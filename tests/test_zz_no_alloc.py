@@ -43,6 +43,9 @@ def test_noalloc_decode_matches_cached_decode_twice():
         torch.cuda.synchronize()
         err = (got - want).abs().max().item()
         assert err <= DECODE_ATOL, (call, err)
+        # the call left no timeout behind, and the pool's check (which also covers this
+        # path's waits) reports a clean run
+        assert L.bebelm_kv_check(cache._h, stream) == 0, bb.last_error()
     # and both agree with the reference arithmetic
     kw, vw = cache.read(1)
     ref = oracle.attention_decode(q.cpu().numpy(), kw, vw, kw.shape[0], H, KVH, D)
@@ -63,5 +66,36 @@ def test_noalloc_rejects_oversized_window():
     rc = L.bebelm_attn_decode_cached_noalloc(cache._h, 0, n_kv, C.c_void_p(q.data_ptr()), C.c_void_p(out.data_ptr()),
                                              C.c_void_p(torch.cuda.current_stream().cuda_stream))
     assert rc == bb.ERR_INVALID
-    assert "no-allocation" in bb.last_error()
+    assert "split counters" in bb.last_error() and "no-allocation" in bb.last_error()
     cache.close()
+
+
+def test_noalloc_rejects_window_beyond_partial_region():
+    torch = pytest.importorskip("torch")
+    L = bb.load_library()
+    # 1024 kv heads (one split counter each, within the limit) over a 500-page window: the split
+    # plan caps a split at 256 pages, so 2 splits x 1024 heads x 4 query heads x 66 floats of
+    # partial results, more than the array's partial region. bf16 pages keep the pool at ~8.4 GB.
+    n_kv, n_pos = 1024, 500 * 64
+    cache = bb.Cache(n_layers=1, n_kv_heads=n_kv, max_context=n_pos, kv_dtype=bb.BF16)
+    rows = torch.zeros((2048, n_kv * D), device="cuda")
+    for _ in range(n_pos // 2048):
+        cache.append(0, rows, rows)
+    cache.append(0, rows[: n_pos % 2048], rows[: n_pos % 2048])
+    assert cache.layer_len(0) == n_pos
+    del rows
+    q = torch.zeros(4 * n_kv * D, device="cuda")
+    out = torch.zeros(4 * n_kv * D, device="cuda")
+    stream = C.c_void_p(torch.cuda.current_stream().cuda_stream)
+    rc = L.bebelm_attn_decode_cached_noalloc(cache._h, 0, 4 * n_kv, C.c_void_p(q.data_ptr()),
+                                             C.c_void_p(out.data_ptr()), stream)
+    assert rc == bb.ERR_INVALID
+    msg = bb.last_error()
+    assert "scratch floats" in msg and "no-allocation" in msg, msg
+    # the regular entry point serves the same window (it grows its scratch)
+    rc = L.bebelm_attn_decode_cached(cache._h, 0, 4 * n_kv, C.c_void_p(q.data_ptr()), C.c_void_p(out.data_ptr()),
+                                     bb.MEM_DEVICE, stream)
+    assert rc == 0, bb.last_error()
+    assert L.bebelm_kv_check(cache._h, stream) == 0
+    cache.close()
+    torch.cuda.empty_cache()
