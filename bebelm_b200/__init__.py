@@ -25,6 +25,7 @@ _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_HERE, "libbebelm_attn.so")
 
 OK, ERR_INVALID, ERR_CUDA, ERR_OOM, ERR_CAPACITY, ERR_UNSUPPORTED, ERR_TIMEOUT, ERR_NO_DEVICE = 0, -1, -2, -3, -4, -5, -7, -8
+ERR_FORMAT, ERR_NOT_FOUND, ERR_IO = -9, -10, -11
 MEM_HOST, MEM_DEVICE = 0, 1
 F32, BF16 = 0, 1
 F32_TENSOR = 2  # prefill in_dtype: fp32 inputs, tensor-core attention
@@ -45,10 +46,21 @@ EXPORTS = [
     "bebelm_step_plan_finish", "bebelm_matvec", "bebelm_matmul", "bebelm_dequantize",
     "bebelm_attn_weights_create", "bebelm_attn_weights_destroy", "bebelm_attn_layer_step", "bebelm_attn_layer_batch",
     "bebelm_step_plan_create_layer", "bebelm_step_plan_launch_layer", "bebelm_head_create", "bebelm_head_destroy",
-    "bebelm_head_logits", "bebelm_sample_greedy",
+    "bebelm_head_logits", "bebelm_sample_greedy", "bebelm_gguf_open", "bebelm_gguf_from_bytes", "bebelm_gguf_close",
+    "bebelm_gguf_header", "bebelm_gguf_tensor_at", "bebelm_gguf_find_tensor", "bebelm_gguf_key_at",
+    "bebelm_gguf_get_u32", "bebelm_gguf_get_f32", "bebelm_gguf_get_str", "bebelm_gguf_get_u32_array",
+    "bebelm_gguf_array_len", "bebelm_gguf_get_str_at", "bebelm_gguf_validate", "bebelm_attn_weights_from_gguf",
+    "bebelm_head_from_gguf",
 ]
 GGML_F32, GGML_F16, GGML_Q4_K, GGML_Q6_K = 0, 1, 12, 14
 IPC_HANDLE_BYTES = 64
+
+
+class GgufTensor(C.Structure):
+    """bebelm_gguf_tensor: one entry of the tensor table (TensorInfo, src/gguf.rs:120-139)."""
+    _fields_ = [("name", C.c_void_p), ("name_len", C.c_size_t), ("n_dims", C.c_uint32), ("dims", C.c_uint64 * 8),
+                ("n_elements", C.c_uint64), ("ggml_type", C.c_int), ("offset", C.c_uint64),
+                ("data_start", C.c_uint64), ("data_len", C.c_uint64), ("data", C.c_void_p)]
 
 
 class BebelmError(RuntimeError):
@@ -118,6 +130,23 @@ def load_library(path: str = LIB_PATH):
         "bebelm_head_destroy": ([vp], i),
         "bebelm_head_logits": ([vp, vp, f, vp, vp, i, vp], i),
         "bebelm_sample_greedy": ([vp, sz, vp, sz, f, vp, i, vp], i),
+        "bebelm_gguf_open": ([C.c_char_p, C.POINTER(vp)], i),
+        "bebelm_gguf_from_bytes": ([vp, sz, C.POINTER(vp)], i),
+        "bebelm_gguf_close": ([vp], i),
+        "bebelm_gguf_header": ([vp, C.POINTER(C.c_uint32), C.POINTER(C.c_uint64), C.POINTER(C.c_uint64),
+                                C.POINTER(sz), C.POINTER(sz)], i),
+        "bebelm_gguf_tensor_at": ([vp, sz, C.POINTER(GgufTensor)], i),
+        "bebelm_gguf_find_tensor": ([vp, C.c_char_p, C.POINTER(GgufTensor)], i),
+        "bebelm_gguf_key_at": ([vp, sz, C.POINTER(C.c_void_p), C.POINTER(sz), C.POINTER(i)], i),
+        "bebelm_gguf_get_u32": ([vp, C.c_char_p, C.POINTER(C.c_uint32)], i),
+        "bebelm_gguf_get_f32": ([vp, C.c_char_p, C.POINTER(f)], i),
+        "bebelm_gguf_get_str": ([vp, C.c_char_p, C.c_char_p, sz, C.POINTER(sz)], i),
+        "bebelm_gguf_get_u32_array": ([vp, C.c_char_p, C.POINTER(C.c_uint32), sz, C.POINTER(sz)], i),
+        "bebelm_gguf_array_len": ([vp, C.c_char_p, C.POINTER(i), C.POINTER(sz)], i),
+        "bebelm_gguf_get_str_at": ([vp, C.c_char_p, sz, C.POINTER(C.c_void_p), C.POINTER(sz)], i),
+        "bebelm_gguf_validate": ([vp], i),
+        "bebelm_attn_weights_from_gguf": ([vp, i, i, C.POINTER(vp)], i),
+        "bebelm_head_from_gguf": ([vp, i, C.POINTER(vp)], i),
     }
     for name, (args, res) in sig.items():
         fn = getattr(L, name)
@@ -679,3 +708,149 @@ def attn_decode_batched(caches, layer: int, q, k, v, q_gain, k_gain, pos, theta:
     _check(load_library().bebelm_attn_decode_batched(arr, n, layer, n_heads, qb[0], kb[0], vb[0], qg[0], kg[0], theta,
                                                      eps, posa, ob, mem, _stream_ptr(stream, mem)))
     return out
+
+
+# ------------------------------------------------------------------ GGUF --
+class Gguf:
+    """``GgufFile`` (src/gguf.rs:157-298) over the library's native reader: ``Gguf(path)``
+    memory-maps a file (GgufFile::open), ``Gguf(data=bytes)`` parses a copy of a buffer
+    (GgufFile::from_bytes). Raises :class:`BebelmError` (ERR_FORMAT with the reference's
+    wording) on a malformed file."""
+
+    def __init__(self, path: str | None = None, data: bytes | None = None):
+        L = load_library()
+        self._h = C.c_void_p()
+        if path is not None:
+            _check(L.bebelm_gguf_open(os.fsencode(path), C.byref(self._h)))
+        else:
+            buf = C.create_string_buffer(bytes(data), len(data)) if data else None
+            _check(L.bebelm_gguf_from_bytes(buf, len(data or b""), C.byref(self._h)))
+        ver, al, off = C.c_uint32(), C.c_uint64(), C.c_uint64()
+        nt, nk = C.c_size_t(), C.c_size_t()
+        _check(L.bebelm_gguf_header(self._h, C.byref(ver), C.byref(al), C.byref(off), C.byref(nt), C.byref(nk)))
+        self.version, self.alignment, self.data_offset = ver.value, al.value, off.value
+        self.n_tensors, self.n_kv = nt.value, nk.value
+
+    @staticmethod
+    def _info(t: GgufTensor) -> dict:
+        return {"name": C.string_at(t.name, t.name_len).decode(), "dims": [t.dims[d] for d in range(min(t.n_dims, 8))],
+                "n_dims": t.n_dims, "ggml_type": t.ggml_type, "n_elements": t.n_elements, "offset": t.offset,
+                "data_start": t.data_start, "data_len": t.data_len, "data_ptr": t.data}
+
+    @property
+    def tensors(self) -> list:
+        out = []
+        for i in range(self.n_tensors):
+            t = GgufTensor()
+            _check(load_library().bebelm_gguf_tensor_at(self._h, i, C.byref(t)))
+            out.append(self._info(t))
+        return out
+
+    def tensor(self, name: str) -> dict | None:
+        t = GgufTensor()
+        rc = load_library().bebelm_gguf_find_tensor(self._h, name.encode(), C.byref(t))
+        if rc == ERR_NOT_FOUND:
+            return None
+        _check(rc)
+        return self._info(t)
+
+    def tensor_data(self, name: str) -> bytes:
+        t = self.tensor(name)
+        return C.string_at(t["data_ptr"], t["data_len"])
+
+    def keys(self) -> list:
+        """[(key, value type)] in file order."""
+        out = []
+        for i in range(self.n_kv):
+            k, n, vt = C.c_void_p(), C.c_size_t(), C.c_int()
+            _check(load_library().bebelm_gguf_key_at(self._h, i, C.byref(k), C.byref(n), C.byref(vt)))
+            out.append((C.string_at(k, n.value).decode(), vt.value))
+        return out
+
+    def get_u32(self, key: str):
+        v = C.c_uint32()
+        rc = load_library().bebelm_gguf_get_u32(self._h, key.encode(), C.byref(v))
+        if rc == ERR_NOT_FOUND:
+            return None
+        _check(rc)
+        return v.value
+
+    def get_f32(self, key: str):
+        v = C.c_float()
+        rc = load_library().bebelm_gguf_get_f32(self._h, key.encode(), C.byref(v))
+        if rc == ERR_NOT_FOUND:
+            return None
+        _check(rc)
+        return v.value
+
+    def get_str(self, key: str):
+        n = C.c_size_t()
+        L = load_library()
+        rc = L.bebelm_gguf_get_str(self._h, key.encode(), None, 0, C.byref(n))
+        if rc == ERR_NOT_FOUND:
+            return None
+        _check(rc)
+        buf = C.create_string_buffer(n.value + 1)
+        _check(L.bebelm_gguf_get_str(self._h, key.encode(), buf, n.value + 1, C.byref(n)))
+        return buf.raw[: n.value].decode()
+
+    def get_u32_array(self, key: str):
+        n = C.c_size_t()
+        L = load_library()
+        rc = L.bebelm_gguf_get_u32_array(self._h, key.encode(), None, 0, C.byref(n))
+        if rc == ERR_NOT_FOUND:
+            return None
+        _check(rc)
+        out = (C.c_uint32 * max(n.value, 1))()
+        _check(L.bebelm_gguf_get_u32_array(self._h, key.encode(), out, n.value, C.byref(n)))
+        return list(out[: n.value])
+
+    def get_str_array(self, key: str):
+        et, n = C.c_int(), C.c_size_t()
+        L = load_library()
+        rc = L.bebelm_gguf_array_len(self._h, key.encode(), C.byref(et), C.byref(n))
+        if rc == ERR_NOT_FOUND or et.value != 8:
+            return None
+        _check(rc)
+        out = []
+        for i in range(n.value):
+            p, ln = C.c_void_p(), C.c_size_t()
+            _check(L.bebelm_gguf_get_str_at(self._h, key.encode(), i, C.byref(p), C.byref(ln)))
+            out.append(C.string_at(p, ln.value).decode())
+        return out
+
+    def architecture(self):
+        return self.get_str("general.architecture")
+
+    def validate(self) -> None:
+        """config::validate (src/config.rs:50-96)."""
+        _check(load_library().bebelm_gguf_validate(self._h))
+
+    def attn_weights(self, block: int, device: int = 0) -> "AttnWeights":
+        """The attention weights of model block ``block`` (blk.N.attn_*), uploaded to ``device``."""
+        w = AttnWeights.__new__(AttnWeights)
+        w._h = C.c_void_p()
+        _check(load_library().bebelm_attn_weights_from_gguf(self._h, block, device, C.byref(w._h)))
+        q, k = self.tensor(f"blk.{block}.attn_q.weight"), self.tensor(f"blk.{block}.attn_k.weight")
+        w.hidden, w.n_heads, w.n_kv = q["dims"][0], q["dims"][1] // HEAD_DIM, k["dims"][1] // HEAD_DIM
+        return w
+
+    def head(self, device: int = 0) -> "Head":
+        """The logits head (token_embd + token_embd_norm), uploaded to ``device``."""
+        h = Head.__new__(Head)
+        h._h = C.c_void_p()
+        _check(load_library().bebelm_head_from_gguf(self._h, device, C.byref(h._h)))
+        t = self.tensor("token_embd.weight")
+        h.hidden, h.vocab = t["dims"][0], t["dims"][1]
+        return h
+
+    def close(self):
+        if self._h:
+            load_library().bebelm_gguf_close(self._h)
+            self._h = C.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

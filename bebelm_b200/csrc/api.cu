@@ -31,6 +31,11 @@ static int fail(int code, const char* fmt, ...) {
     return code;
 }
 
+int bebelm::set_last_error(int code, const char* msg) {
+    g_err = msg;
+    return code;
+}
+
 #define CUDA_TRY(x)                                                                          \
     do {                                                                                     \
         cudaError_t e_ = (x);                                                                \

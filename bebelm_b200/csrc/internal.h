@@ -9,6 +9,9 @@
 
 namespace bebelm {
 
+// Records `msg` as the calling thread's last error (bebelm_last_error) and returns code.
+int set_last_error(int code, const char* msg);
+
 constexpr int kHeadDim = 64;     // LFM2.5 head_dim (src/config.rs:20)
 constexpr int kPageTokens = 64;  // positions per KV page
 constexpr int kPageRowFloats = kPageTokens * kHeadDim;  // one kv head of one page: 4096 floats

@@ -50,7 +50,10 @@ enum {
     BEBELM_ERR_CAPACITY = -4,    /* the window would exceed the cache's capacity */
     BEBELM_ERR_UNSUPPORTED = -5, /* geometry/dtype this build does not implement */
     BEBELM_ERR_TIMEOUT = -7,     /* a bounded device-side wait gave up */
-    BEBELM_ERR_NO_DEVICE = -8    /* no CUDA device, or the device is not sm_100 */
+    BEBELM_ERR_NO_DEVICE = -8,   /* no CUDA device, or the device is not sm_100 */
+    BEBELM_ERR_FORMAT = -9,      /* malformed GGUF file, or metadata that does not match the model */
+    BEBELM_ERR_NOT_FOUND = -10,  /* no such GGUF tensor or metadata key (of the asked type) */
+    BEBELM_ERR_IO = -11          /* a file could not be opened, read or mapped */
 };
 
 enum { BEBELM_MEM_HOST = 0, BEBELM_MEM_DEVICE = 1 };
@@ -338,6 +341,67 @@ BEBELM_API int bebelm_head_logits(bebelm_head* head, const float* h, float eps, 
  * history ids >= n are ignored. */
 BEBELM_API int bebelm_sample_greedy(float* logits, size_t n, const uint32_t* history, size_t n_history,
                                     float repeat_penalty, uint32_t* token, int mem, void* stream);
+
+/* ------------------------------------------------------------- GGUF weights ---
+ * The reference's GGUF reader (src/gguf.rs): GgufFile::open memory-maps a file and
+ * GgufFile::from_bytes parses a buffer (here: a copy of it); both parse the header,
+ * the metadata key/values and the tensor table, and check that each tensor's bytes lie
+ * inside the file. Failures return BEBELM_ERR_FORMAT with the reference's GgufError
+ * wording (bad magic, unsupported version, unexpected end of file, unknown metadata
+ * value type, invalid UTF-8, unmodeled ggml type, data range outside the file), or
+ * BEBELM_ERR_IO. A handle is immutable after parsing: it may be read from any thread.
+ * Pointers it hands out (names, strings, tensor data) live until bebelm_gguf_close. */
+typedef struct bebelm_gguf bebelm_gguf;
+#define BEBELM_GGUF_MAX_DIMS 8
+/* TensorInfo (src/gguf.rs:120-139). dims fastest-varying first; offset is relative to
+ * the data section, data_start absolute in the file; data points at the bytes. */
+typedef struct {
+    const char* name;
+    size_t name_len; /* bytes of name (a name may hold a NUL byte) */
+    uint32_t n_dims; /* may exceed BEBELM_GGUF_MAX_DIMS; only the first ones are in dims */
+    uint64_t dims[BEBELM_GGUF_MAX_DIMS];
+    uint64_t n_elements;
+    int ggml_type;
+    uint64_t offset, data_start, data_len;
+    const void* data;
+} bebelm_gguf_tensor;
+BEBELM_API int bebelm_gguf_open(const char* path, bebelm_gguf** out);
+BEBELM_API int bebelm_gguf_from_bytes(const void* data, size_t n, bebelm_gguf** out);
+BEBELM_API int bebelm_gguf_close(bebelm_gguf* g);
+/* GgufFile's version, alignment (general.alignment, default 32), data_offset, and counts. */
+BEBELM_API int bebelm_gguf_header(const bebelm_gguf* g, uint32_t* version, uint64_t* alignment,
+                                  uint64_t* data_offset, size_t* n_tensors, size_t* n_kv);
+/* GgufFile::tensors[i], and Model::tensor by name (src/model.rs:79-81; BEBELM_ERR_NOT_FOUND). */
+BEBELM_API int bebelm_gguf_tensor_at(const bebelm_gguf* g, size_t i, bebelm_gguf_tensor* out);
+BEBELM_API int bebelm_gguf_find_tensor(const bebelm_gguf* g, const char* name, bebelm_gguf_tensor* out);
+/* The i-th distinct metadata key in file order, its byte length (a key may hold a NUL byte;
+ * the lookups below take NUL-terminated keys) and its value type (the GGUF discriminant). */
+BEBELM_API int bebelm_gguf_key_at(const bebelm_gguf* g, size_t i, const char** key, size_t* key_len,
+                                  int* value_type);
+/* The typed accessors of src/gguf.rs:196-283: get_u32 widens any integer type, get_f32
+ * takes F32 or F64, get_u32_array any integer array (copies up to cap, *len = its length),
+ * get_str copies up to cap-1 bytes and a NUL (*len = its byte length). A missing key or
+ * another type gives BEBELM_ERR_NOT_FOUND, as the reference's None. */
+BEBELM_API int bebelm_gguf_get_u32(const bebelm_gguf* g, const char* key, uint32_t* out);
+BEBELM_API int bebelm_gguf_get_f32(const bebelm_gguf* g, const char* key, float* out);
+BEBELM_API int bebelm_gguf_get_str(const bebelm_gguf* g, const char* key, char* buf, size_t cap, size_t* len);
+BEBELM_API int bebelm_gguf_get_u32_array(const bebelm_gguf* g, const char* key, uint32_t* out, size_t cap,
+                                         size_t* len);
+/* An array's element type and length, and its i-th string (get_str_array, src/gguf.rs:248-262). */
+BEBELM_API int bebelm_gguf_array_len(const bebelm_gguf* g, const char* key, int* elem_type, size_t* len);
+BEBELM_API int bebelm_gguf_get_str_at(const bebelm_gguf* g, const char* key, size_t i, const char** s,
+                                      size_t* len);
+/* config::validate (src/config.rs:50-96): BEBELM_ERR_FORMAT unless the metadata is
+ * LFM2.5-8B-A1B's (architecture, sizes, rope base, eps, the kv-head schedule). */
+BEBELM_API int bebelm_gguf_validate(const bebelm_gguf* g);
+/* The attention weights of block `block` (0..23; attention blocks 2, 6, 10, 14, 18, 21)
+ * by their GGUF names blk.N.attn_{q,k,v,output}.weight and blk.N.attn_{q,k}_norm.weight
+ * (src/model.rs:228-233, 434-439, 454), uploaded by bebelm_attn_weights_create. */
+BEBELM_API int bebelm_attn_weights_from_gguf(const bebelm_gguf* g, int block, int device,
+                                             bebelm_attn_weights** out);
+/* The logits head from token_embd.weight and token_embd_norm.weight (src/model.rs:379-388),
+ * uploaded by bebelm_head_create. */
+BEBELM_API int bebelm_head_from_gguf(const bebelm_gguf* g, int device, bebelm_head** out);
 
 #ifdef __cplusplus
 }
