@@ -50,7 +50,7 @@ EXPORTS = [
     "bebelm_gguf_header", "bebelm_gguf_tensor_at", "bebelm_gguf_find_tensor", "bebelm_gguf_key_at",
     "bebelm_gguf_get_u32", "bebelm_gguf_get_f32", "bebelm_gguf_get_str", "bebelm_gguf_get_u32_array",
     "bebelm_gguf_array_len", "bebelm_gguf_get_str_at", "bebelm_gguf_validate", "bebelm_attn_weights_from_gguf",
-    "bebelm_head_from_gguf",
+    "bebelm_head_from_gguf", "bebelm_step_plan_launch_allgather",
 ]
 GGML_F32, GGML_F16, GGML_Q4_K, GGML_Q6_K = 0, 1, 12, 14
 IPC_HANDLE_BYTES = 64
@@ -115,6 +115,7 @@ def load_library(path: str = LIB_PATH):
         "bebelm_attn_step_allgather": ([vp, vp, i, i, vp, vp, vp, vp, vp, f, f, sz, vp, i, vp], i),
         "bebelm_step_plan_create": ([vp, i, i, sz, C.POINTER(vp)], i),
         "bebelm_step_plan_launch": ([vp, vp, vp, vp, vp, vp, f, f, vp, vp], i),
+        "bebelm_step_plan_launch_allgather": ([vp, vp, vp, vp, vp, vp, vp, f, f, vp, vp], i),
         "bebelm_step_plan_steps": ([vp, C.POINTER(C.c_ulonglong), vp], i),
         "bebelm_step_plan_finish": ([vp, vp], i),
         "bebelm_matvec": ([i, vp, sz, sz, vp, vp, i, vp], i),
@@ -653,6 +654,18 @@ class StepPlan:
         _check(load_library().bebelm_step_plan_launch(self._h, q.data_ptr(), k.data_ptr(), v.data_ptr(),
                                                       q_gain.data_ptr(), k_gain.data_ptr(), theta, eps,
                                                       out.data_ptr(), _stream_ptr(stream)))
+        return out
+
+    def launch_allgather(self, group: "PeerGroup", q, k, v, q_gain, k_gain, out, theta: float = ROPE_THETA,
+                         eps: float = RMS_EPS, stream=None):
+        """:meth:`launch` on this rank's heads, gathered over ``group`` into out [world*n_heads*64];
+        capturable in a CUDA graph on every rank."""
+        for x in (q, k, v, q_gain, k_gain, out):
+            if not (_is_torch(x) and x.is_cuda and x.is_contiguous()):
+                raise ValueError("step plans take contiguous CUDA tensors")
+        _check(load_library().bebelm_step_plan_launch_allgather(
+            self._h, group._h, q.data_ptr(), k.data_ptr(), v.data_ptr(), q_gain.data_ptr(), k_gain.data_ptr(), theta,
+            eps, out.data_ptr(), _stream_ptr(stream)))
         return out
 
     def steps(self, stream=None) -> int:

@@ -477,8 +477,11 @@ bool inputs_clear_of_last_out(cudaStream_t s, std::initializer_list<std::pair<co
     return true;
 }
 
+// Split size cap of batched decode (pages per CTA). Config 4 (64 sequences, 1k-16k positions):
+// 8, 32 and 64 pages gave 0.545, 0.436 and 0.434 ms per step; small caps make thousands of
+// short CTAs, each paying its prologue and its share of the merge.
 #ifndef BEBELM_BATCH_PAGES_PER_SPLIT
-#define BEBELM_BATCH_PAGES_PER_SPLIT 8
+#define BEBELM_BATCH_PAGES_PER_SPLIT 32
 #endif
 constexpr long long kBatchMaxPagesPerSplit = BEBELM_BATCH_PAGES_PER_SPLIT;
 
@@ -503,6 +506,7 @@ struct PeerTarget {
     unsigned long long* const* flags;
     int world, rank;
     size_t off;
+    const unsigned long long* epoch;  // the group's device epoch word (then `off` is unused)
 };
 
 int run_decode(bebelm_kv_pool* P, const std::vector<Window>& wins, int layer, int n_heads, const float* d_q,
@@ -539,7 +543,10 @@ int run_decode(bebelm_kv_pool* P, const std::vector<Window>& wins, int layer, in
         d.dep_slot = dep_slot_for(P, wins[i].kv, layer);
         total_splits += d.n_splits;
     }
-    TRY(P->part.ensure(sizeof(float) * (size_t)total_splits * NY * hpc * (kHeadDim + 2), false, s));
+    // room for one more split per sequence: a growing window then crosses into a new split (and
+    // a regrowth, which waits for the stream) only once per `per` pages of steps
+    const size_t part_splits = (size_t)total_splits + (n > 1 ? (size_t)n : 0);
+    TRY(P->part.ensure(sizeof(float) * part_splits * NY * hpc * (kHeadDim + 2), false, s));
     TRY(P->counters.ensure(sizeof(unsigned) * (size_t)n * NY, true, s));
     DecodeArgs a{};
     if (n == 1) {
@@ -585,6 +592,7 @@ int run_decode(bebelm_kv_pool* P, const std::vector<Window>& wins, int layer, in
         a.peer_world = peer->world;
         a.peer_rank = peer->rank;
         a.peer_off = peer->off;
+        a.peer_epoch = peer->epoch;
     }
     CUDA_TRY(launch_decode(a, s));
     record_decode_out(s, d_out, peer ? SIZE_MAX : (size_t)n * n_heads * kHeadDim * 4);
@@ -1393,15 +1401,37 @@ struct bebelm_peer_group {
     size_t slice = 0;  // floats per rank per parity
     char* zone = nullptr;
     char* peer_base[kMaxPeers] = {};  // opened IPC mappings (own entry: zone)
-    DevBuf tables;                    // float* bufs[world], then u64* flags[world]
-    unsigned long long epoch = 0;
+    DevBuf tables;                    // float* bufs[world], u64* flags[world], then the epoch word
     bool connected = false;
     size_t zone_bytes() const { return 256 + 2 * (size_t)world * slice * sizeof(float); }
     float* const* d_bufs() const { return tables.as<float* const>(); }
     unsigned long long* const* d_flags() const {
         return reinterpret_cast<unsigned long long* const*>(tables.as<char>() + sizeof(void*) * world);
     }
+    // Steps completed on this rank, in device memory: a decode step is epoch + 1; its wait kernel
+    // stores that back once the gathered output is copied out. Keeping it on the device lets a
+    // captured graph of steps replay without any launch argument changing.
+    unsigned long long* d_epoch() const {
+        return reinterpret_cast<unsigned long long*>(tables.as<char>() + 2 * sizeof(void*) * world);
+    }
 };
+
+namespace {
+
+// The wait kernel that follows a decode step whose CTAs store into the landing zones: it
+// waits for every rank's writers of this step and copies the gathered [world][slice] out.
+int peer_gather_out(const bebelm_peer_group* g, bebelm_kv_pool* P, int n_heads, float* dout, cudaStream_t s) {
+    // output-writing CTAs per rank: one per (kv head, head subgroup); every rank has the same shape
+    int hpc, n_sub;
+    pick_heads_per_cta(n_heads / P->n_kv, &hpc, &n_sub);
+    const unsigned long long writers = (unsigned long long)P->n_kv * n_sub;
+    const float* land = reinterpret_cast<const float*>(g->zone + 256);
+    CUDA_TRY(launch_peer_wait(reinterpret_cast<const unsigned long long*>(g->zone), g->world, 0, land, dout,
+                              (size_t)g->world * g->slice, P->err.d, g->d_epoch(), writers, s));
+    return 0;
+}
+
+}  // namespace
 
 extern "C" {
 
@@ -1473,8 +1503,9 @@ int bebelm_peer_group_connect(bebelm_peer_group* g, const void* handles) {
         tab[r] = g->peer_base[r] + 256;
         tab[g->world + r] = g->peer_base[r];
     }
-    TRY(g->tables.ensure(sizeof(void*) * tab.size()));
+    TRY(g->tables.ensure(sizeof(void*) * tab.size() + sizeof(unsigned long long), true));
     CUDA_TRY(cudaMemcpy(g->tables.p, tab.data(), sizeof(void*) * tab.size(), cudaMemcpyHostToDevice));
+    CUDA_TRY(cudaDeviceSynchronize());  // the zeroed epoch word too
     g->connected = true;
     return 0;
 }
@@ -1520,18 +1551,9 @@ int bebelm_attn_step_allgather(bebelm_kv* kv, bebelm_peer_group* g, int layer, i
     TRY(reserve(kv, layer, 1, &slot0, s));
     const FusedStep fs{dq, dk, dv, dqg, dkg, theta_scale_of(theta, kHeadDim), eps};
     std::vector<Window> w{{kv, kv->base[layer], kv->len[layer], slot0, (long long)pos}};
-    const unsigned long long e = g->epoch + 1;
-    const size_t par_off = (size_t)(e & 1) * g->world * g->slice;
-    const PeerTarget pt{g->d_bufs(), g->d_flags(), g->world, g->rank, par_off};
+    const PeerTarget pt{g->d_bufs(), g->d_flags(), g->world, g->rank, 0, g->d_epoch()};
     TRY(run_decode(P, w, layer, n_heads, nullptr, dout, 0.125f, &fs, s, &pt));
-    g->epoch = e;
-    // output-writing CTAs per rank: one per (kv head, head subgroup); every rank has the same shape
-    int hpc, n_sub;
-    pick_heads_per_cta(n_heads / P->n_kv, &hpc, &n_sub);
-    const unsigned long long writers = (unsigned long long)P->n_kv * n_sub;
-    const float* land = reinterpret_cast<const float*>(g->zone + 256) + par_off;
-    CUDA_TRY(launch_peer_wait(reinterpret_cast<const unsigned long long*>(g->zone), g->world, e * writers, land, dout,
-                              full, P->err.d, s));
+    TRY(peer_gather_out(g, P, n_heads, dout, s));
     if (mem == BEBELM_MEM_HOST) return stage_out(P, dout, out, 4 * full, s);
     return 0;
 }
@@ -1635,13 +1657,25 @@ int bebelm_step_plan_create(bebelm_kv* kv, int layer, int n_heads, size_t window
     return 0;
 }
 
-int bebelm_step_plan_launch(bebelm_step_plan* pl, const float* q, const float* k, const float* v,
-                            const float* q_gain, const float* k_gain, float theta, float eps, float* out,
-                            void* stream) {
+}  // extern "C"
+
+namespace {
+
+// One step of a plan; with a peer group the outputs go to every rank's landing zone and a wait
+// kernel gathers them into `out` ([world][n_heads*64]).
+int plan_launch(bebelm_step_plan* pl, const bebelm_peer_group* grp, const float* q, const float* k, const float* v,
+                const float* q_gain, const float* k_gain, float theta, float eps, float* out, void* stream) {
     if (!pl || !pl->kv) return fail(BEBELM_ERR_INVALID, "null step plan");
     if (!q || !k || !v || !q_gain || !k_gain || !out) return fail(BEBELM_ERR_INVALID, "null buffer");
     bebelm_kv* kv = pl->kv;
     bebelm_kv_pool* P = kv->pool;
+    if (grp) {
+        if (!grp->connected) return fail(BEBELM_ERR_INVALID, "peer group not connected");
+        if (grp->device != P->device) return fail(BEBELM_ERR_INVALID, "cache and peer group are on different devices");
+        if ((size_t)pl->n_heads * kHeadDim != grp->slice)
+            return fail(BEBELM_ERR_INVALID, "n_heads*64 (%d) differs from the group's slice (%zu)", pl->n_heads * 64,
+                        grp->slice);
+    }
     DeviceGuard g(P->device);
     const int NY = P->n_kv * pl->n_sub;
     DecodeArgs a{};
@@ -1686,11 +1720,38 @@ int bebelm_step_plan_launch(bebelm_step_plan* pl, const float* q, const float* k
     CUDA_TRY(cudaStreamGetCaptureInfo(as_stream(stream), &cs, &cap_id));
     if (cs != cudaStreamCaptureStatusActive) cap_id = 0;
     a.step_prewait = P->last_plan != nullptr && P->last_plan != pl && P->last_capture == cap_id;
+    if (grp) {
+        a.peer_bufs = grp->d_bufs();
+        a.peer_flags = grp->d_flags();
+        a.peer_world = grp->world;
+        a.peer_rank = grp->rank;
+        a.peer_epoch = grp->d_epoch();
+        // the wait kernel between two such steps is not a decode grid: nothing is read early
+        a.step_prewait = 0;
+    }
     CUDA_TRY(launch_decode(a, as_stream(stream)));
-    record_decode_out(as_stream(stream), a.out, (size_t)pl->n_heads * kHeadDim * 4);
-    P->last_plan = pl;
+    record_decode_out(as_stream(stream), a.out, grp ? SIZE_MAX : (size_t)pl->n_heads * kHeadDim * 4);
+    P->last_plan = grp ? nullptr : pl;
     P->last_capture = cap_id;
+    if (grp) TRY(peer_gather_out(grp, P, pl->n_heads, out, as_stream(stream)));
     return 0;
+}
+
+}  // namespace
+
+extern "C" {
+
+int bebelm_step_plan_launch(bebelm_step_plan* pl, const float* q, const float* k, const float* v,
+                            const float* q_gain, const float* k_gain, float theta, float eps, float* out,
+                            void* stream) {
+    return plan_launch(pl, nullptr, q, k, v, q_gain, k_gain, theta, eps, out, stream);
+}
+
+int bebelm_step_plan_launch_allgather(bebelm_step_plan* pl, bebelm_peer_group* g, const float* q, const float* k,
+                                      const float* v, const float* q_gain, const float* k_gain, float theta,
+                                      float eps, float* out, void* stream) {
+    if (!g) return fail(BEBELM_ERR_INVALID, "null peer group");
+    return plan_launch(pl, g, q, k, v, q_gain, k_gain, theta, eps, out, stream);
 }
 
 int bebelm_step_plan_steps(const bebelm_step_plan* pl, unsigned long long* n, void* stream) {

@@ -139,9 +139,18 @@ __device__ __forceinline__ void fma2(float& c0, float& c1, float a0, float a1, f
 
 // Final output element `idx` (head*64 + d) of sequence `seq`: to `out`, or, for the fused
 // all-gather, to this rank's slice of every rank's landing zone (NVLink stores to peers).
-__device__ __forceinline__ void emit_out(const DecodeArgs& a, int seq, size_t idx, float v) {
+// The landing-zone parity offset of this step: from the device epoch word when the group keeps
+// one (read after griddepcontrol.wait: the previous step's wait kernel advanced it), else the
+// launch argument.
+__device__ __forceinline__ size_t peer_offset(const DecodeArgs& a) {
+    if (!a.peer_epoch) return a.peer_off;
+    const unsigned long long e = *reinterpret_cast<const volatile unsigned long long*>(a.peer_epoch) + 1ull;
+    return (size_t)(e & 1ull) * a.peer_world * a.n_heads * kHeadDim;
+}
+
+__device__ __forceinline__ void emit_out(const DecodeArgs& a, int seq, size_t idx, float v, size_t poff) {
     if (a.peer_world > 0) {
-        const size_t off = a.peer_off + (size_t)a.peer_rank * a.n_heads * kHeadDim + idx;
+        const size_t off = poff + (size_t)a.peer_rank * a.n_heads * kHeadDim + idx;
         for (int w = 0; w < a.peer_world; ++w) a.peer_bufs[w][off] = v;
     } else {
         a.out[(size_t)seq * a.n_heads * kHeadDim + idx] = v;
@@ -360,6 +369,7 @@ __global__ void __launch_bounds__(kThreads, 2) decode_kernel(DecodeArgs a) {
     // ---- everything below may read what the predecessor wrote --------------
     grid_dep_wait();
     DTRACE(1);
+    const size_t poff = a.peer_world > 0 ? peer_offset(a) : 0;
     if (tid == 0)
         for (int i = n_early; i < n_first; ++i) issue(i);
     if (!early) read_inputs();
@@ -580,7 +590,7 @@ __global__ void __launch_bounds__(kThreads, 2) decode_kernel(DecodeArgs a) {
             }
         }
         if (single) {
-            emit_out(a, seq, (size_t)(h0 + h) * kHeadDim + d, L > 0.f ? A / L : 0.f);
+            emit_out(a, seq, (size_t)(h0 + h) * kHeadDim + d, L > 0.f ? A / L : 0.f, poff);
         } else {
             const size_t pi = ((size_t)gsplit * NY + y) * HPC + h;
             a.part_acc[pi * kHeadDim + d] = A;
@@ -685,7 +695,7 @@ __global__ void __launch_bounds__(kThreads, 2) decode_kernel(DecodeArgs a) {
         float A = 0.f;
         for (int g = 0; g < G; ++g) A += sm_acc[g * HPC * kHeadDim + o];
         const float L = s_L[o / kHeadDim];
-        emit_out(a, seq, (size_t)h0 * kHeadDim + o, L > 0.f ? A / L : 0.f);
+        emit_out(a, seq, (size_t)h0 * kHeadDim + o, L > 0.f ? A / L : 0.f, poff);
     }
     signal_peers(a);
     step_done(a);
@@ -717,10 +727,19 @@ cudaError_t launch_hpc(const DecodeArgs& a, cudaStream_t s) {
 }
 
 __global__ void peer_wait_kernel(const unsigned long long* flags, int world, unsigned long long expected,
-                                 const float* src, float* dst, size_t n, int* err) {
+                                 const float* src, float* dst, size_t n, int* err, unsigned long long* epoch,
+                                 unsigned long long writers) {
     __shared__ int s_ok;
-    if (threadIdx.x == 0) s_ok = 1;
+    __shared__ unsigned long long s_e;
+    if (threadIdx.x == 0) {
+        s_ok = 1;
+        s_e = epoch ? *reinterpret_cast<volatile unsigned long long*>(epoch) + 1ull : 0ull;
+    }
     __syncthreads();
+    if (epoch) {  // this step's epoch from the device word: the expected count and the parity
+        expected = s_e * writers;
+        src += (size_t)(s_e & 1ull) * n;
+    }
     if ((int)threadIdx.x < world) {
         bool ok = false;
         for (long long it = 0; it < kWaitLimit; ++it) {
@@ -738,15 +757,21 @@ __global__ void peer_wait_kernel(const unsigned long long* flags, int world, uns
         }
     }
     __syncthreads();
-    if (!s_ok) return;
-    for (size_t i = threadIdx.x; i < n; i += blockDim.x) dst[i] = __ldcv(src + i);  // written by peers
+    if (s_ok)
+        for (size_t i = threadIdx.x; i < n; i += blockDim.x) dst[i] = __ldcv(src + i);  // written by peers
+    // the step is over on this rank (copied out, or failed and reported): the next one may begin
+    if (epoch) {
+        __syncthreads();
+        if (threadIdx.x == 0) *reinterpret_cast<volatile unsigned long long*>(epoch) = s_e;
+    }
 }
 
 }  // namespace
 
 cudaError_t launch_peer_wait(const unsigned long long* flags, int world, unsigned long long expected, const float* src,
-                             float* dst, size_t n, int* err, cudaStream_t s) {
-    peer_wait_kernel<<<1, 256, 0, s>>>(flags, world, expected, src, dst, n, err);
+                             float* dst, size_t n, int* err, unsigned long long* epoch, unsigned long long writers,
+                             cudaStream_t s) {
+    peer_wait_kernel<<<1, 256, 0, s>>>(flags, world, expected, src, dst, n, err, epoch, writers);
     return cudaGetLastError();
 }
 

@@ -171,6 +171,8 @@ struct DecodeArgs {
     unsigned long long* const* peer_flags;
     int peer_world, peer_rank;
     size_t peer_off;
+    // device epoch word of the group (non-null: the parity offset follows it, peer_off unused)
+    const unsigned long long* peer_epoch;
     // step plan (one sequence): non-null step makes the window of `one` follow the counter
     StepState* step;
     long long step_slot0, step_pos0, step_len0, step_window;
@@ -186,8 +188,12 @@ struct DecodeArgs {
 };
 // Waits (bounded) until flags[r] >= expected for every source rank r, then copies n floats of
 // the gathered landing buffer to dst. On timeout it records kErrWaitTimeout and copies nothing.
+// With `epoch` (the group's device epoch word) the step is e = *epoch + 1: expected becomes
+// e * writers, src the parity (e & 1) buffer that follows src, and the kernel stores e back
+// when done, so a replayed graph of steps advances on its own.
 cudaError_t launch_peer_wait(const unsigned long long* flags, int world, unsigned long long expected, const float* src,
-                             float* dst, size_t n, int* err, cudaStream_t s);
+                             float* dst, size_t n, int* err, unsigned long long* epoch, unsigned long long writers,
+                             cudaStream_t s);
 cudaError_t launch_decode(const DecodeArgs& a, cudaStream_t s);
 size_t decode_smem_bytes();
 constexpr int kDecodeMaxPagesPerSplit = 256;

@@ -45,12 +45,13 @@ class KVHeadSharded:
     """One rank's share of a KV-head-sharded attention stack."""
 
     def __init__(self, n_layers: int, max_context: int, n_heads: int = N_HEADS, n_kv_heads: int = N_KV_HEADS,
-                 group=None, cache_factory=None, fused_gather: bool | None = None):
+                 group=None, cache_factory=None, fused_gather: bool | None = None, local: bool = False):
         """fused_gather: gather decode outputs inside the decode kernel over peer memory
-        (default: on for the CUDA cache with more than one rank); off uses NCCL."""
+        (default: on for the CUDA cache with more than one rank); off uses NCCL. local: this
+        process alone holds every head (world 1), whatever the process group."""
         self.group = group
-        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
-        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        self.world = dist.get_world_size(group) if dist.is_initialized() and not local else 1
+        self.rank = dist.get_rank(group) if dist.is_initialized() and not local else 0
         if n_kv_heads % self.world or n_heads % n_kv_heads:
             raise ValueError(f"{n_kv_heads} kv heads cannot be split over {self.world} ranks")
         self.n_heads, self.n_kv = n_heads, n_kv_heads
@@ -112,6 +113,24 @@ class KVHeadSharded:
         if self.world == 1:
             return full
         return full.permute(1, 0, 2).reshape(t, -1)
+
+    def step_plans(self, window: int = 0) -> list:
+        """One device-driven step plan per layer of this rank's cache (see
+        :class:`bebelm_b200.StepPlan`), for decode steps captured in a CUDA graph."""
+        return [self.cache.step_plan(layer, n_heads=self.h_per, window=window)
+                for layer in range(self.cache.n_layers)]
+
+    def plan_step(self, plan, q, k, v, q_gain, k_gain, out, theta: float = ROPE_THETA, eps: float = RMS_EPS):
+        """One step of ``plan`` (a :meth:`step_plans` entry): q [n_heads*64], k/v [n_kv*64]
+        replicated -> out [n_heads*64], gathered inside the step (fused) with no host work, so
+        the call can be captured in a CUDA graph on every rank."""
+        q, k, v = (self._heads(x, per, first).contiguous() for x, per, first in
+                   ((q, self.h_per, self.h0), (k, self.kv_per, self.kv0), (v, self.kv_per, self.kv0)))
+        if self.peers is None:
+            if self.world > 1:
+                raise RuntimeError("plan steps on several ranks need the fused gather")
+            return plan.launch(q, k, v, q_gain, k_gain, out, theta=theta, eps=eps)
+        return plan.launch_allgather(self.peers, q, k, v, q_gain, k_gain, out, theta=theta, eps=eps)
 
     def evict_front(self, n: int):
         self.cache.evict_front(n)

@@ -607,8 +607,11 @@ def bench_config4(bb, torch, dev, stream, world, rank, steps=128):
 def bench_config5(bb, torch, dev, stream, world, rank, bf16_peak, T=8192, steps=512):
     """Config 5: the 6 attention layers of the stack, KV heads sharded over the ranks: causal
     prefill of T bf16 tokens (NCCL all-gather of head outputs), then `steps` decode steps whose
-    all-gather is fused into the decode kernel (peer stores over NVLink). With more than one
-    rank the decode is also timed with an NCCL all-gather instead, for comparison."""
+    all-gather is fused into the decode kernel (peer stores over NVLink). Decode is timed
+    host-driven and as one CUDA graph of step plans (all steps x 6 layers). With more than one
+    rank, rank 0 also runs the same workload unsharded on its own GPU (the others wait), so the
+    line carries the 1 -> N speed-up and efficiency of this run; the host-driven decode is also
+    timed with an NCCL all-gather instead of the fused one, for comparison."""
     from bebelm_b200.sharded import KVHeadSharded
     L = 6
     g = torch.Generator(device=dev)
@@ -622,76 +625,104 @@ def bench_config5(bb, torch, dev, stream, world, rank, bf16_peak, T=8192, steps=
     Kd = torch.randn((steps, KVD), generator=g, device=dev)
     Vd = torch.randn((steps, KVD), generator=g, device=dev)
 
-    def run(fused):
-        sh = KVHeadSharded(n_layers=L, max_context=T + steps + 64, fused_gather=fused)
-        # untimed warm-up of every call and collective the timed region makes
-        for layer in range(L):
+    def ev():
+        return torch.cuda.Event(enable_timing=True)
+
+    def run(sh, sync):
+        """prefill ms, host-driven decode ms, graph decode ms (per whole run, this rank)."""
+        for layer in range(L):  # untimed warm-up of every call and collective the timed region makes
             sh.attn_prefill(layer, q, k, v, qg, kg, 0, theta=THETA)
-            for s in range(3):
-                sh.attn_step(layer, Qd[s], Kd[s], Vd[s], qg, kg, pos=T + s, theta=THETA)
+            for s_ in range(3):
+                sh.attn_step(layer, Qd[s_], Kd[s_], Vd[s_], qg, kg, pos=T + s_, theta=THETA)
         sh.clear()
-        barrier(world)
-        torch.cuda.synchronize()
-        e = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+        sync()
+        e = [ev() for _ in range(3)]
         e[0].record(stream)
         for layer in range(L):
             sh.attn_prefill(layer, q, k, v, qg, kg, 0, theta=THETA)
         e[1].record(stream)
-        for s in range(steps):
+        for s_ in range(steps):
             for layer in range(L):
-                sh.attn_step(layer, Qd[s], Kd[s], Vd[s], qg, kg, pos=T + s, theta=THETA)
+                sh.attn_step(layer, Qd[s_], Kd[s_], Vd[s_], qg, kg, pos=T + s_, theta=THETA)
         e[2].record(stream)
         torch.cuda.synchronize()
-        barrier(world)
-        pre = max_over_ranks(e[0].elapsed_time(e[1]), world, dev)
-        dec = max_over_ranks(e[1].elapsed_time(e[2]), world, dev)
-        sh.close()
-        sh.cache.close()
-        return pre, dec
-
-    pre_ms, dec_ms = run(None)
-    flops = L * 4096.0 * T * (T + 1)
-    tf = flops / (pre_ms * 1e-3) / 1e12
-    out = {"workload": f"config5: 6 GQA layers, causal prefill of {T} bf16 tokens then {steps} decode steps",
-           "prefill_ms": round(pre_ms, 3), "prefill_tflops": round(tf, 1),
-           "prefill_frac_of_bf16_peak_per_gpu": round(tf / world / bf16_peak, 4),
-           "decode_ms_per_step": round(dec_ms / steps, 4), "decode_tok_per_s": round(steps / (dec_ms * 1e-3), 1),
-           "parallelism": (f"kv heads / {world} per GPU; prefill: NCCL all-gather of head outputs; decode: "
-                           "all-gather fused into the decode kernel (NVLink peer stores + flags)") if world > 1
-           else "one GPU, all heads"}
-    if world > 1:
-        _, dec_nccl = run(False)
-        out["decode_ms_per_step_nccl_gather"] = round(dec_nccl / steps, 4)
-    else:
-        # the same decode as one CUDA graph: step plans (device-driven window state) for the 6
-        # layers, all `steps` steps x 6 layers captured once (each node reads its own step's
-        # inputs) and replayed, so no host work sits between the kernels
-        from bebelm_b200 import Cache
-        c = Cache(n_layers=L, max_context=T + steps + 64)
+        sync()
+        pre, dec = e[0].elapsed_time(e[1]), e[1].elapsed_time(e[2])
+        if getattr(sh, "peers", 1) is None and sh.world > 1:
+            return pre, dec, None
+        # decode as one CUDA graph: a step plan per layer, all `steps` x 6 layers captured once
+        # (each node reads its own step's inputs) and replayed twice (warm-up, timed)
+        sh.clear()
         for layer in range(L):
-            c.attn_prefill(layer, q, k, v, qg, kg, 0, theta=THETA)
-        c.pos = T
-        plans = [c.step_plan(layer) for layer in range(L)]
+            sh.attn_prefill(layer, q, k, v, qg, kg, 0, theta=THETA)
+        sh.cache.pos = T
+        plans = sh.step_plans()
         o = torch.empty((steps, L, HID), device=dev)
         graph, cap = torch.cuda.CUDAGraph(), torch.cuda.Stream()
         torch.cuda.synchronize()
         with torch.cuda.graph(graph, stream=cap):
             for s_ in range(steps):
                 for layer in range(L):
-                    plans[layer].launch(Qd[s_], Kd[s_], Vd[s_], qg, kg, o[s_, layer], theta=THETA)
-        graph.replay()  # warm-up: steps tokens
+                    sh.plan_step(plans[layer], Qd[s_], Kd[s_], Vd[s_], qg, kg, o[s_, layer], theta=THETA)
+        sync()
+        graph.replay()
         torch.cuda.synchronize()
-        e = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+        sync()
+        e = [ev() for _ in range(2)]
         e[0].record(stream)
-        graph.replay()  # the next steps tokens
+        graph.replay()
         e[1].record(stream)
         torch.cuda.synchronize()
-        g_ms = e[0].elapsed_time(e[1])
+        sync()
         for p_ in plans:
             p_.finish()
-        c.close()
-        out["decode_graph"] = {"ms_per_step": round(g_ms / steps, 4), "tok_per_s": round(steps / (g_ms * 1e-3), 1),
-                               "how": "step plans, one CUDA graph of all steps x 6 layers"}
+        sh.cache.check()
+        return pre, dec, e[0].elapsed_time(e[1])
+
+    flops = L * 4096.0 * T * (T + 1)
+
+    def line(pre, dec, gms, n):
+        tf = flops / (pre * 1e-3) / 1e12
+        out = {"prefill_ms": round(pre, 3), "prefill_tflops": round(tf, 1),
+               "prefill_frac_of_bf16_peak_per_gpu": round(tf / n / bf16_peak, 4),
+               "decode_ms_per_step": round(dec / steps, 4), "decode_tok_per_s": round(steps / (dec * 1e-3), 1)}
+        if gms is not None:
+            out["decode_graph"] = {"ms_per_step": round(gms / steps, 4), "tok_per_s": round(steps / (gms * 1e-3), 1),
+                                   "how": "step plans, one CUDA graph of all steps x 6 layers"}
+        return out
+
+    sync = (lambda: barrier(world))
+    sh = KVHeadSharded(n_layers=L, max_context=T + 2 * steps + 64)
+    pre, dec, gms = run(sh, sync)
+    sh.close()
+    sh.cache.close()
+    pre = max_over_ranks(pre, world, dev)
+    dec = max_over_ranks(dec, world, dev)
+    gms = max_over_ranks(gms, world, dev)
+    out = {"workload": f"config5: 6 GQA layers, causal prefill of {T} bf16 tokens then {steps} decode steps",
+           **line(pre, dec, gms, world),
+           "parallelism": (f"kv heads / {world} per GPU; prefill: NCCL all-gather of head outputs; decode: "
+                           "all-gather fused into the decode kernel (NVLink peer stores + flags)") if world > 1
+           else "one GPU, all heads"}
+    if world > 1:
+        shn = KVHeadSharded(n_layers=L, max_context=T + 2 * steps + 64, fused_gather=False)
+        _, dec_nccl, _ = run(shn, sync)
+        shn.close()
+        shn.cache.close()
+        out["decode_ms_per_step_nccl_gather"] = round(max_over_ranks(dec_nccl, world, dev) / steps, 4)
+        # the same workload unsharded on rank 0's GPU (one process, no collective) in this run
+        base = None
+        if rank == 0:
+            one = KVHeadSharded(n_layers=L, max_context=T + 2 * steps + 64, local=True)
+            b_pre, b_dec, b_g = run(one, lambda: None)
+            one.cache.close()
+            base = line(b_pre, b_dec, b_g, 1)
+            out["one_gpu_same_run"] = base
+            out["speedup_vs_1gpu"] = {
+                "prefill": round(b_pre / pre, 3), "decode_graph": round(b_g / gms, 3),
+                "decode_host_driven": round(b_dec / dec, 3)}
+            out["efficiency_vs_1gpu"] = {k_: round(v_ / world, 3) for k_, v_ in out["speedup_vs_1gpu"].items()}
+        barrier(world)
     return out
 
 

@@ -320,6 +320,15 @@ BEBELM_API int bebelm_attn_step_allgather(bebelm_kv* kv, bebelm_peer_group* g, i
                                           const float* q, const float* k, const float* v,
                                           const float* q_gain, const float* k_gain, float theta,
                                           float eps, size_t pos, float* out, int mem, void* stream);
+/* A step plan's step (bebelm_step_plan_launch, device memory) on this rank's heads, gathered
+ * the same way: out [world*n_heads*64]. The group counts its steps in device memory (the
+ * epoch that picks the landing buffer and the flag count to wait for), so a CUDA graph of
+ * these steps, captured once on every rank, replays with no host work. Every rank's plans
+ * must step in the same order, and replays must be launched on all ranks. */
+BEBELM_API int bebelm_step_plan_launch_allgather(bebelm_step_plan* plan, bebelm_peer_group* g,
+                                                 const float* q, const float* k, const float* v,
+                                                 const float* q_gain, const float* k_gain, float theta,
+                                                 float eps, float* out, void* stream);
 
 /* ---- logits head and greedy token choice (next after the projections) ----
  * Replaces Model::logits_from_hidden (src/model.rs:379-388: final RMSNorm with

@@ -1,10 +1,13 @@
 """Fused decode + all-gather over peer memory (KV-head sharding), through the C-ABI.
 
 * world 1 (any GPU box): the landing-zone path — output CTAs store into the zone and raise
-  the flag, the wait kernel copies the zone out — must give exactly the plain fused step.
+  the flag, the wait kernel copies the zone out — must give exactly the plain fused step, also
+  as step-plan steps captured in a CUDA graph and replayed (the group's epoch lives on the
+  device).
 * world 2 (needs 2 GPUs, one process each): every rank's gathered output must match the
   unsharded oracle (src/model.rs:440-451 over all 32 heads) within the decode tolerance,
-  and be identical on both ranks. Then rank 1 skips a step between steps (no kernel in
+  and be identical on both ranks, for host-driven steps and for step-plan steps captured in a
+  CUDA graph on both ranks and replayed. Then rank 1 skips a step between steps (no kernel in
   flight) and rank 0's bounded wait must report BEBELM_ERR_TIMEOUT instead of hanging.
 """
 import multiprocessing as mp
@@ -54,6 +57,42 @@ def test_world1_zone_path_equals_fused_step():
         g.close()
 
 
+def test_world1_graph_of_plan_steps_through_the_zone():
+    """Eight plan steps through the zone, captured once and replayed twice, against the same
+    steps of a plain plan on a copy of the cache (bit for bit): the second replay must land in
+    the other parity and wait for the next epoch's count, which only the device epoch knows."""
+    qq, kk, vv, qg, kg = [x.cuda() for x in _inputs(12, 1208)]
+    a = bb.Cache(n_layers=2, max_context=2048)
+    a.attn_prefill(1, qq[:1200], kk[:1200], vv[:1200], qg, kg, 0, theta=THETA)
+    a.pos = 1200
+    b = a.clone()
+    g = bb.PeerGroup(1, 0, H * D, device=0)
+    g.connect([g.handle])
+    pa, pb = a.step_plan(1), b.step_plan(1)
+    want = torch.empty((2, 8, H * D), device="cuda")
+    got = torch.full((8, H * D), float("nan"), device="cuda")
+    try:
+        for r in range(2):  # the plain plan, twice over the same eight inputs
+            for i in range(8):
+                pa.launch(qq[1200 + i], kk[1200 + i], vv[1200 + i], qg, kg, want[r, i], theta=THETA)
+        graph, cap = torch.cuda.CUDAGraph(), torch.cuda.Stream()
+        torch.cuda.synchronize()
+        with torch.cuda.graph(graph, stream=cap):
+            for i in range(8):  # each node reads its own step's inputs
+                pb.launch_allgather(g, qq[1200 + i], kk[1200 + i], vv[1200 + i], qg, kg, got[i], theta=THETA)
+        for r in range(2):
+            graph.replay()
+            torch.cuda.synchronize()
+            b.check()
+            torch.testing.assert_close(got, want[r], rtol=0, atol=0)
+        assert pb.steps() == 16
+    finally:
+        torch.cuda.synchronize()
+        pa.finish()
+        pb.finish()
+        g.close()
+
+
 def _free_port():
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
@@ -69,20 +108,36 @@ def _worker(rank, world, port, q):
         from bebelm_b200.sharded import KVHeadSharded
         sh = KVHeadSharded(n_layers=2, max_context=4096)
         assert sh.peers is not None
-        qq, kk, vv, qg, kg = [x.cuda() for x in _inputs(7, 3000 + 10)]
+        qq, kk, vv, qg, kg = [x.cuda() for x in _inputs(7, 3000 + 16)]
         sh.attn_prefill(1, qq[:3000], kk[:3000], vv[:3000], qg, kg, 0)
         outs = []
         for i in range(10):
             p = 3000 + i
             outs.append(sh.attn_step(1, qq[p], kk[p], vv[p], qg, kg, pos=p).cpu().numpy())
         sh.cache.check()
+        # six more steps from step plans, captured in one CUDA graph on each rank and replayed
+        sh.cache.pos = 3010
+        plan = sh.cache.step_plan(1, n_heads=sh.h_per)
+        gout = torch.empty((6, H * D), device="cuda")
+        graph, cap = torch.cuda.CUDAGraph(), torch.cuda.Stream()
+        torch.cuda.synchronize()
+        with torch.cuda.graph(graph, stream=cap):
+            for i in range(6):
+                p = 3010 + i
+                sh.plan_step(plan, qq[p], kk[p], vv[p], qg, kg, gout[i])
+        torch.distributed.barrier()
+        graph.replay()
+        torch.cuda.synchronize()
+        plan.finish()
+        sh.cache.check()
+        outs += list(gout.cpu().numpy())
         # rank 1 leaves between steps; rank 0's next step must time out, not hang
         status = None
         if rank == 0:
             h = [x.cpu().numpy() for x in (qq[0], kk[0], vv[0])]
             try:
                 sh.cache.attn_step_allgather(sh.peers, 1, h[0][:H // world * D], h[1][:KVH // world * D],
-                                             h[2][:KVH // world * D], qg.cpu().numpy(), kg.cpu().numpy(), pos=3010)
+                                             h[2][:KVH // world * D], qg.cpu().numpy(), kg.cpu().numpy(), pos=3016)
                 status = 0
             except bb.BebelmError as e:
                 status = e.code
@@ -112,11 +167,11 @@ def test_world2_fused_gather_matches_oracle_and_times_out_cleanly():
     for r in range(world):
         assert not isinstance(res[r][0], str), res[r][0]
 
-    qq, kk, vv, qg, kg = [x.numpy() for x in _inputs(7, 3010)]
+    qq, kk, vv, qg, kg = [x.numpy() for x in _inputs(7, 3016)]
     ref = oracle.Cache(2, KVH * D)
     _, ref.k[1], ref.v[1], _, _ = oracle.attn_batch(qq[:3000], kk[:3000], vv[:3000], 0, qg, kg, THETA, EPS, H, KVH, D,
                                                     None, None, n_threads=oracle.max_threads())
-    for i in range(10):
+    for i in range(16):
         p = 3000 + i
         want = ref.attn_step(1, qq[p], kk[p], vv[p], qg, kg, THETA, EPS, H, KVH, D, pos=p)
         np.testing.assert_allclose(res[0][0][i], want, atol=1e-3, rtol=0)
