@@ -29,6 +29,7 @@ ERR_FORMAT, ERR_NOT_FOUND, ERR_IO = -9, -10, -11
 MEM_HOST, MEM_DEVICE = 0, 1
 F32, BF16 = 0, 1
 F32_TENSOR = 2  # prefill in_dtype: fp32 inputs, tensor-core attention
+FP8 = 3  # cache dtype: K/V as fp8 e4m3
 
 # reference constants (src/config.rs:14-32)
 N_HEADS, N_KV_HEADS, HEAD_DIM, KV_DIM, HIDDEN = 32, 8, 64, 512, 2048

@@ -239,7 +239,7 @@ struct bebelm_kv_pool {
         v.page_bytes = page_bytes;
         v.layer_off = (size_t)layer * 2 * block_bytes;
         v.block_bytes = block_bytes;
-        v.bf16 = dtype == BEBELM_BF16;
+        v.kind = dtype == BEBELM_BF16 ? kElemBF16 : dtype == BEBELM_FP8_E4M3 ? kElemFP8 : kElemF32;
         return v;
     }
 };
@@ -334,8 +334,8 @@ int pool_create(int n_layers, int n_kv_heads, int head_dim, size_t n_pages, int 
     if (head_dim != kHeadDim) return fail(BEBELM_ERR_UNSUPPORTED, "cache head_dim must be 64 (got %d)", head_dim);
     if (page_tokens != kPageTokens)
         return fail(BEBELM_ERR_UNSUPPORTED, "page_tokens must be 64 (got %d)", page_tokens);
-    if (dtype != BEBELM_F32 && dtype != BEBELM_BF16)
-        return fail(BEBELM_ERR_UNSUPPORTED, "cache dtype must be BEBELM_F32 or BEBELM_BF16");
+    if (dtype != BEBELM_F32 && dtype != BEBELM_BF16 && dtype != BEBELM_FP8_E4M3)
+        return fail(BEBELM_ERR_UNSUPPORTED, "cache dtype must be BEBELM_F32, BEBELM_BF16 or BEBELM_FP8_E4M3");
     if (n_pages > (size_t)INT32_MAX) return fail(BEBELM_ERR_INVALID, "too many pages");
     TRY(check_device(device));
     DeviceGuard g(device);
@@ -345,7 +345,7 @@ int pool_create(int n_layers, int n_kv_heads, int head_dim, size_t n_pages, int 
     P->n_kv = n_kv_heads;
     P->n_pages = n_pages;
     P->dtype = dtype;
-    P->block_bytes = (size_t)n_kv_heads * kPageRowFloats * (dtype == BEBELM_BF16 ? 2 : 4);
+    P->block_bytes = (size_t)n_kv_heads * kPageRowFloats * (dtype == BEBELM_F32 ? 4 : dtype == BEBELM_BF16 ? 2 : 1);
     P->page_bytes = (size_t)n_layers * 2 * P->block_bytes;
     cudaDeviceGetAttribute(&P->num_sms, cudaDevAttrMultiProcessorCount, device);
     const size_t bytes = n_pages * P->page_bytes;

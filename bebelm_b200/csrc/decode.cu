@@ -222,10 +222,13 @@ __device__ long long g_dtrace[4][1024 * 8];  // by the first sequence's position
     } while (0)
 #endif
 
-template <int HPC, bool BF>
+template <int HPC, int KT>
 __global__ void __launch_bounds__(kThreads, 2) decode_kernel(DecodeArgs a) {
-    // BF: the cache holds bf16 (half the bytes per page row, twice the stages in the same ring)
-    constexpr int ES = BF ? 2 : 4;
+    // KT: the cache's element type. bf16 and fp8 (e4m3) rows take a half and a quarter of the
+    // bytes, so the same ring holds two and four times the stages; BF: a narrow type, whose
+    // loop is short of issue slots rather than of bytes (packed FMAs)
+    constexpr bool BF = KT != kElemF32;
+    constexpr int ES = KT == kElemF32 ? 4 : KT == kElemBF16 ? 2 : 1;
     constexpr int ROWB = kPageRowFloats * ES;  // one kv head of one page
     constexpr int SB = 2 * ROWB;               // a stage: its K rows and V rows
     constexpr int NST = kRingBytes / SB;
@@ -308,10 +311,10 @@ __global__ void __launch_bounds__(kThreads, 2) decode_kernel(DecodeArgs a) {
             warp_norm_rope64(kr, a.k_gain, S.pos, a.theta_scale, a.eps, lane, y0, y1);
             float w0 = vr[lane], w1 = vr[lane + 32];
             if (BF) {  // this step uses exactly what the cache will hold
-                y0 = __bfloat162float(__float2bfloat16_rn(y0));
-                y1 = __bfloat162float(__float2bfloat16_rn(y1));
-                w0 = __bfloat162float(__float2bfloat16_rn(w0));
-                w1 = __bfloat162float(__float2bfloat16_rn(w1));
+                y0 = round_to_kind(y0, KT);
+                y1 = round_to_kind(y1, KT);
+                w0 = round_to_kind(w0, KT);
+                w1 = round_to_kind(w1, KT);
             }
             s_knew[lane] = y0;
             s_knew[lane + 32] = y1;
@@ -379,11 +382,16 @@ __global__ void __launch_bounds__(kThreads, 2) decode_kernel(DecodeArgs a) {
                    (size_t)(S.new_slot & 63) * kHeadDim * ES;
         char* vd = kd + a.pv.block_bytes;
         const float y0 = s_knew[lane], y1 = s_knew[lane + 32], w0 = s_vnew[lane], w1 = s_vnew[lane + 32];
-        if (BF) {
+        if (KT == kElemBF16) {
             reinterpret_cast<__nv_bfloat16*>(kd)[lane] = __float2bfloat16_rn(y0);
             reinterpret_cast<__nv_bfloat16*>(kd)[lane + 32] = __float2bfloat16_rn(y1);
             reinterpret_cast<__nv_bfloat16*>(vd)[lane] = __float2bfloat16_rn(w0);
             reinterpret_cast<__nv_bfloat16*>(vd)[lane + 32] = __float2bfloat16_rn(w1);
+        } else if (KT == kElemFP8) {  // the values are e4m3-exact already
+            reinterpret_cast<unsigned char*>(kd)[lane] = float_to_fp8(y0);
+            reinterpret_cast<unsigned char*>(kd)[lane + 32] = float_to_fp8(y1);
+            reinterpret_cast<unsigned char*>(vd)[lane] = float_to_fp8(w0);
+            reinterpret_cast<unsigned char*>(vd)[lane + 32] = float_to_fp8(w1);
         } else {
             reinterpret_cast<float*>(kd)[lane] = y0;
             reinterpret_cast<float*>(kd)[lane + 32] = y1;
@@ -427,11 +435,12 @@ __global__ void __launch_bounds__(kThreads, 2) decode_kernel(DecodeArgs a) {
             }
             break;
         }
-        // 4 elements of chunk c of row r, as floats (16 B of fp32 or 8 B of bf16)
+        // 4 elements of chunk c of row r, as floats (16 B of fp32, 8 B of bf16, 4 B of fp8)
         const unsigned char* Kst = stages + (size_t)st * SB;
         const unsigned char* Vst = Kst + ROWB;
         auto ld4 = [&](const unsigned char* base, int idx) -> float4 {
-            if (BF) {
+            if (KT == kElemFP8) return fp8x4_to_float4(reinterpret_cast<const uint32_t*>(base)[idx]);
+            if (KT == kElemBF16) {
                 const uint2 u = reinterpret_cast<const uint2*>(base)[idx];
                 return make_float4(__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xffff0000u),
                                    __uint_as_float(u.y << 16), __uint_as_float(u.y & 0xffff0000u));
@@ -702,14 +711,14 @@ __global__ void __launch_bounds__(kThreads, 2) decode_kernel(DecodeArgs a) {
     DTRACE(4);
 }
 
-template <int HPC, bool BF>
+template <int HPC, int KT>
 cudaError_t launch_hpc(const DecodeArgs& a, cudaStream_t s) {
     static bool attr_set[64] = {};  // the attribute is per device
     const int smem = (int)decode_smem_bytes();
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 0 || dev >= 64 || !attr_set[dev]) {
-        cudaError_t e = cudaFuncSetAttribute(decode_kernel<HPC, BF>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        cudaError_t e = cudaFuncSetAttribute(decode_kernel<HPC, KT>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
         if (e != cudaSuccess) return e;
         if (dev >= 0 && dev < 64) attr_set[dev] = true;
     }
@@ -723,7 +732,7 @@ cudaError_t launch_hpc(const DecodeArgs& a, cudaStream_t s) {
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = a.pdl ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, decode_kernel<HPC, BF>, a);
+    return cudaLaunchKernelEx(&cfg, decode_kernel<HPC, KT>, a);
 }
 
 __global__ void peer_wait_kernel(const unsigned long long* flags, int world, unsigned long long expected,
@@ -775,15 +784,25 @@ cudaError_t launch_peer_wait(const unsigned long long* flags, int world, unsigne
     return cudaGetLastError();
 }
 
-size_t decode_smem_bytes() { return (size_t)kRingBytes + 2 * kStages * sizeof(uint64_t); }
+// the ring, then one mbarrier per stage (fp8 rows: four times kStages stages)
+size_t decode_smem_bytes() { return (size_t)kRingBytes + 4 * kStages * sizeof(uint64_t); }
+
+template <int HPC>
+cudaError_t launch_kt(const DecodeArgs& a, cudaStream_t s) {
+    switch (a.pv.kind) {
+        case kElemBF16: return launch_hpc<HPC, kElemBF16>(a, s);
+        case kElemFP8: return launch_hpc<HPC, kElemFP8>(a, s);
+        default: return launch_hpc<HPC, kElemF32>(a, s);
+    }
+}
 
 cudaError_t launch_decode(const DecodeArgs& a, cudaStream_t s) {
     if (a.total_splits <= 0) return cudaSuccess;
     switch (a.hpc) {
-        case 1: return a.pv.bf16 ? launch_hpc<1, true>(a, s) : launch_hpc<1, false>(a, s);
-        case 2: return a.pv.bf16 ? launch_hpc<2, true>(a, s) : launch_hpc<2, false>(a, s);
-        case 3: return a.pv.bf16 ? launch_hpc<3, true>(a, s) : launch_hpc<3, false>(a, s);
-        case 4: return a.pv.bf16 ? launch_hpc<4, true>(a, s) : launch_hpc<4, false>(a, s);
+        case 1: return launch_kt<1>(a, s);
+        case 2: return launch_kt<2>(a, s);
+        case 3: return launch_kt<3>(a, s);
+        case 4: return launch_kt<4>(a, s);
         default: return cudaErrorInvalidValue;
     }
 }

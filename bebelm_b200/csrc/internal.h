@@ -3,6 +3,7 @@
 #pragma once
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
+#include <cuda_fp8.h>
 #include <cuda_fp16.h>
 #include <stddef.h>
 #include <stdint.h>
@@ -17,14 +18,15 @@ constexpr int kPageTokens = 64;  // positions per KV page
 constexpr int kPageRowFloats = kPageTokens * kHeadDim;  // one kv head of one page: 4096 floats
 
 // Device-side view of the page pool for one layer. A physical page p holds, for every
-// layer l: K[l] then V[l], each a "block" [n_kv][64 tokens][64] of fp32 or bf16 elements.
+// layer l: K[l] then V[l], each a "block" [n_kv][64 tokens][64] of fp32, bf16 or fp8 (e4m3)
+// elements.
 // All offsets are in bytes.
 struct PoolView {
     char* base;           // pool memory
     size_t page_bytes;    // one physical page (all layers, K and V)
     size_t layer_off;     // page start to this layer's K block
     size_t block_bytes;   // one K (or V) block = n_kv rows of a page
-    int bf16;             // elements are bf16 (else fp32)
+    int kind;             // element type: kElemF32, kElemBF16 or kElemFP8 (e4m3)
 };
 
 // A sequence's window for one layer: logical slots [base, base+len) live in
@@ -37,7 +39,9 @@ struct SeqWindow {
 };
 
 // Bytes of one kv head of one page (64 tokens x 64 elements).
-__host__ __device__ inline size_t row_bytes(const PoolView& pv) { return (size_t)kPageRowFloats * (pv.bf16 ? 2 : 4); }
+constexpr int kElemF32 = 0, kElemBF16 = 1, kElemFP8 = 2;
+__host__ __device__ inline int elem_bytes(int kind) { return kind == kElemF32 ? 4 : kind == kElemBF16 ? 2 : 1; }
+__host__ __device__ inline size_t row_bytes(const PoolView& pv) { return (size_t)kPageRowFloats * elem_bytes(pv.kind); }
 
 // Byte offset of (slot, kv head, K or V) in the pool.
 __host__ __device__ inline size_t slot_offset(const PoolView& pv, const int* table, int cap, long long slot, int kvh,
@@ -45,27 +49,53 @@ __host__ __device__ inline size_t slot_offset(const PoolView& pv, const int* tab
     const long long lp = slot >> 6;
     const int phys = table[(int)(lp % cap)];
     return (size_t)phys * pv.page_bytes + pv.layer_off + (size_t)kind * pv.block_bytes + (size_t)kvh * row_bytes(pv) +
-           (size_t)(slot & 63) * kHeadDim * (pv.bf16 ? 2 : 4);
+           (size_t)(slot & 63) * kHeadDim * elem_bytes(pv.kind);
 }
 
 #ifdef __CUDACC__
+// Two e4m3 values (the low byte first) as floats; the conversion is exact.
+__device__ __forceinline__ float2 fp8x2_to_float2(unsigned short v) {
+    const __half2_raw h = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)v, __NV_E4M3);
+    return __half22float2(*reinterpret_cast<const __half2*>(&h));
+}
+// Four e4m3 values packed in a word (element 0 in the low byte) as floats.
+__device__ __forceinline__ float4 fp8x4_to_float4(uint32_t u) {
+    const float2 a = fp8x2_to_float2((unsigned short)(u & 0xffffu)), b = fp8x2_to_float2((unsigned short)(u >> 16));
+    return make_float4(a.x, a.y, b.x, b.y);
+}
+// x rounded to nearest e4m3 (saturating at +-448), returned as its byte.
+__device__ __forceinline__ unsigned char float_to_fp8(float x) {
+    return (unsigned char)__nv_cvt_float_to_fp8(x, __NV_SATFINITE, __NV_E4M3);
+}
+// x as the cache of element type `kind` holds it.
+__device__ __forceinline__ float round_to_kind(float x, int kind) {
+    if (kind == kElemBF16) return __bfloat162float(__float2bfloat16_rn(x));
+    if (kind == kElemFP8) return fp8x2_to_float2((unsigned short)float_to_fp8(x)).x;
+    return x;
+}
 // Four consecutive elements (e..e+3) of the row at byte offset `off`, as floats.
 __device__ __forceinline__ float4 kv_load4(const PoolView& pv, size_t off, int e) {
-    if (pv.bf16) {
+    if (pv.kind == kElemBF16) {
         const uint2 u = *reinterpret_cast<const uint2*>(pv.base + off + 2 * (size_t)e);
         return make_float4(__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xffff0000u), __uint_as_float(u.y << 16),
                            __uint_as_float(u.y & 0xffff0000u));
     }
+    if (pv.kind == kElemFP8) return fp8x4_to_float4(*reinterpret_cast<const uint32_t*>(pv.base + off + (size_t)e));
     return *reinterpret_cast<const float4*>(pv.base + off + 4 * (size_t)e);
 }
-// Stores four floats at elements e..e+3 (rounded to nearest-even bf16 in a bf16 pool).
+// Stores four floats at elements e..e+3 (rounded to nearest-even bf16, or to nearest e4m3 with
+// saturation, in a narrower pool).
 __device__ __forceinline__ void kv_store4(const PoolView& pv, size_t off, int e, float4 v) {
-    if (pv.bf16) {
+    if (pv.kind == kElemBF16) {
         __nv_bfloat162 a = __floats2bfloat162_rn(v.x, v.y), b = __floats2bfloat162_rn(v.z, v.w);
         uint2 u;
         u.x = *reinterpret_cast<uint32_t*>(&a);
         u.y = *reinterpret_cast<uint32_t*>(&b);
         *reinterpret_cast<uint2*>(pv.base + off + 2 * (size_t)e) = u;
+    } else if (pv.kind == kElemFP8) {
+        const uint32_t u = (uint32_t)float_to_fp8(v.x) | ((uint32_t)float_to_fp8(v.y) << 8) |
+                           ((uint32_t)float_to_fp8(v.z) << 16) | ((uint32_t)float_to_fp8(v.w) << 24);
+        *reinterpret_cast<uint32_t*>(pv.base + off + (size_t)e) = u;
     } else {
         *reinterpret_cast<float4*>(pv.base + off + 4 * (size_t)e) = v;
     }

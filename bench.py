@@ -298,7 +298,8 @@ def run_ours(args):
                    "config5_8192_one_layer": bench_prefill(bb, torch, dev, stream, bf16_peak, peak_kind, 8192, 2)}
 
     head = bench_logits_head(bb, torch, dev, stream, hbm_peak, peak_kind) if rank == 0 and not args.no_prefill else None
-    c3bf = bench_config3_bf16(bb, torch, dev, stream, world, args.steps)
+    c3bf = bench_config3_narrow(bb, torch, dev, stream, world, args.steps, bb.BF16)
+    c3f8 = bench_config3_narrow(bb, torch, dev, stream, world, args.steps, bb.FP8)
     cfg4 = None if args.no_cfg4 else bench_config4(bb, torch, dev, stream, world, rank)
     hbm_peak_, bf16_peak_, _ = peaks()
     cfg5 = None if args.no_cfg5 else bench_config5(bb, torch, dev, stream, world, rank, bf16_peak_)
@@ -340,6 +341,7 @@ def run_ours(args):
             "cpu_baseline_1core": cpu1,
             "prefill": prefill,
             "config3_bf16_kv": c3bf,
+            "config3_fp8_kv": c3f8,
             "logits_head": head,
             "config4": cfg4,
             "config5": cfg5,
@@ -516,9 +518,10 @@ def bench_logits_head(bb, torch, dev, stream, hbm_peak, peak_kind, vocab=128000,
                          "frac": round(gbs / hbm_peak, 4), "peak_kind": peak_kind}}
 
 
-def bench_config3_bf16(bb, torch, dev, stream, world, steps):
-    """Config 3 with the bf16 KV cache: same step, half the bytes per position."""
-    cache = bb.Cache(n_layers=1, max_context=CTX, device=dev.index, kv_dtype=bb.BF16)
+def bench_config3_narrow(bb, torch, dev, stream, world, steps, kv_dtype):
+    """Config 3 with a bf16 or fp8 (e4m3) KV cache: same step, a half or a quarter of the bytes
+    per position."""
+    cache = bb.Cache(n_layers=1, max_context=CTX, device=dev.index, kv_dtype=kv_dtype)
     g = torch.Generator(device=dev)
     g.manual_seed(31)
     for c0 in range(0, CTX, 4096):
@@ -545,9 +548,10 @@ def bench_config3_bf16(bb, torch, dev, stream, world, steps):
     barrier(world)
     ms = max_over_ranks(a.elapsed_time(b), world, dev)
     cache.close()
-    per_step = 2 * (CTX + 1) * KVD * 2
-    return {"workload": "config3 with a bf16 KV cache (K/V rounded to bf16 on append, attention in fp32)",
-            "value": round(per_step * steps * world / (ms * 1e-3) / 1e9, 1), "unit": "GB/s (bf16 bytes)",
+    es, name = (2, "bf16") if kv_dtype == bb.BF16 else (1, "fp8 e4m3")
+    per_step = 2 * (CTX + 1) * KVD * es
+    return {"workload": f"config3 with a {name} KV cache (K/V rounded on append, attention in fp32)",
+            "value": round(per_step * steps * world / (ms * 1e-3) / 1e9, 1), "unit": f"GB/s ({name} bytes)",
             "tok_per_s": round(steps * world / (ms * 1e-3), 1), "ms_per_step": round(ms / steps, 5)}
 
 

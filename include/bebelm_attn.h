@@ -58,6 +58,8 @@ enum {
 
 enum { BEBELM_MEM_HOST = 0, BEBELM_MEM_DEVICE = 1 };
 enum { BEBELM_F32 = 0, BEBELM_BF16 = 1 };
+/* cache dtype only: K and V stored as fp8 e4m3 (one byte each) */
+enum { BEBELM_FP8_E4M3 = 3 };
 /* bebelm_attn_prefill only: fp32 inputs (as the reference's attn_batch passes them), attention
  * on the tensor cores. */
 enum { BEBELM_F32_TENSOR = 2 };
@@ -97,7 +99,10 @@ BEBELM_API int bebelm_norm_rope_heads(float* buf, size_t n_tokens, int n_heads, 
  * every attention layer, laid out [layer][K|V][kv_head][token][64]. dtype
  * BEBELM_F32 keeps the reference's fp32 history; BEBELM_BF16 stores K and V
  * rounded to bf16 (nearest even) when appended, halving the bytes each decode
- * step reads, with attention still computed in fp32.
+ * step reads, with attention still computed in fp32. BEBELM_FP8_E4M3 stores them
+ * as e4m3 (nearest, saturating at +-448): a quarter of the fp32 bytes; e4m3 keeps
+ * 3 mantissa bits, so each stored value carries up to 2^-4 relative rounding
+ * (the reference's planned reduced-precision cache, design.md:451).
  * A sequence's window is a ring of pages, so evict_front (the sliding window
  * of src/agent.rs:471-476) moves an offset and recycles whole pages instead of
  * moving memory. The ring has ceil(max_context/64) + 2 pages: a window always

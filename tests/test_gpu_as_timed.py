@@ -7,7 +7,7 @@ before the previous grid has finished. These tests run exactly that (every step'
 row of its own) and only then compare every row with the oracle's sequence of
 ``attn_step`` calls (src/model.rs:440-451), plus the cache read back at the end:
 
-* config 3: a full 32768-position window (fp32 and bf16 caches), 64 steps, each followed by
+* config 3: a full 32768-position window (fp32, bf16 and fp8 caches), 64 steps, each followed by
   evict_front(1);
 * config 4 at its full shape: 64 sequences with lengths U[1024, 16384] (seed 4), 8 batched
   steps with the default split plan;
@@ -36,20 +36,21 @@ def _gains(seed):
     return oracle.normal(seed, (D,), 1.0, 0.02), oracle.normal(seed + 1, (D,), 1.0, 0.02)
 
 
-@pytest.mark.parametrize("kv_dtype", [bb.F32, bb.BF16])
+@pytest.mark.parametrize("kv_dtype", [bb.F32, bb.BF16, bb.FP8])
 def test_config3_pdl_chained_steps_match_oracle(kv_dtype):
     torch = pytest.importorskip("torch")
     n, steps = 32768, 64
     dev = bb.Cache(n_layers=1, max_context=n, kv_dtype=kv_dtype)
     ref = oracle.Cache(1, KVD)
-    rnd = (lambda x: torch.from_numpy(x).to(torch.bfloat16).float().numpy()) if kv_dtype == bb.BF16 else (lambda x: x)
+    narrow = {bb.BF16: torch.bfloat16, bb.FP8: torch.float8_e4m3fn}.get(kv_dtype)
+    rnd = (lambda x: torch.from_numpy(x).to(narrow).float().numpy()) if narrow else (lambda x: x)
     for c0 in range(0, n, 8192):
         k, v = rnd(oracle.normal(3000 + c0, (8192, KVD))), rnd(oracle.normal(3001 + c0, (8192, KVD)))
         dev.append(0, k, v)
         ref.append(0, k, v)
     qg, kg = _gains(310)
     Qh, Kh, Vh = oracle.normal(41, (steps, HID)), oracle.normal(42, (steps, KVD)), oracle.normal(43, (steps, KVD))
-    if kv_dtype == bb.BF16:
+    if narrow:
         Vh = rnd(Vh)
     Q, K, V = (torch.from_numpy(x).cuda() for x in (Qh, Kh, Vh))
     tqg, tkg = torch.from_numpy(qg).cuda(), torch.from_numpy(kg).cuda()
@@ -65,8 +66,8 @@ def test_config3_pdl_chained_steps_match_oracle(kv_dtype):
     threads = oracle.max_threads()
     kd, vd = dev.read(0)
     for i in range(steps):
-        if kv_dtype == bb.BF16:
-            # the oracle step appends exactly the k the cache holds (its bf16 rounding)
+        if narrow:
+            # the oracle step appends exactly the k the cache holds (its bf16 / e4m3 rounding)
             kn = kd[n - steps + i]
             qn = oracle.norm_rope_heads(Qh[i], H, D, qg, n + i, THETA, EPS)
             ref.append(0, kn, Vh[i])

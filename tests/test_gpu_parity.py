@@ -456,3 +456,102 @@ def test_bf16_cache_tensor_core_prefill():
     want = oracle.attn_batch(q, k, v, 300, qg, kg, 1e6, 1e-5, H, KVH, D, pk, pv, n_threads=oracle.max_threads())[0]
     rel = np.abs(got - want).max() / np.abs(want).max()
     assert rel <= PREFILL_REL, rel
+
+
+# ------------------------------------------------------------- fp8 KV cache --
+def _fp8(x):
+    """x rounded to e4m3 (nearest even; these N(0,1) values are far from the +-448 limit)."""
+    torch = pytest.importorskip("torch")
+    return torch.from_numpy(np.ascontiguousarray(x, np.float32)).to(torch.float8_e4m3fn).float().numpy()
+
+
+def test_fp8_cache_decode_matches_oracle_on_the_same_values():
+    """Over e4m3-exact K/V the fp8 cache must give what the fp32 reference arithmetic gives."""
+    n = 3000
+    dev = bb.Cache(n_layers=2, max_context=4096, kv_dtype=bb.FP8)
+    k, v = _fp8(oracle.normal(1, (n, KVD))), _fp8(oracle.normal(2, (n, KVD)))
+    dev.append(1, k, v)
+    dev.evict_front(129)
+    kd, vd = dev.read(1)
+    assert np.array_equal(kd, k[129:]) and np.array_equal(vd, v[129:])
+    torch = pytest.importorskip("torch")
+    q = oracle.normal(3, (HID,))
+    got = dev.decode(1, torch.from_numpy(q).cuda()).cpu().numpy()
+    want = oracle.attention_decode(q, k[129:], v[129:], n - 129, H, KVH, D)
+    assert np.abs(got - want).max() <= 1e-5
+
+
+FP8_VS_FP32_ATOL = 5e-2  # fp8 cache against the fp32 reference on unrounded N(0,1) K/V
+
+
+def test_fp8_cache_accuracy_against_fp32_reference():
+    """The stated cost of the fp8 cache: on N(0,1) data (4096 positions) the decode output stays
+    within FP8_VS_FP32_ATOL of the fp32 reference on the unrounded values."""
+    torch = pytest.importorskip("torch")
+    n = 4096
+    dev = bb.Cache(n_layers=1, max_context=n, kv_dtype=bb.FP8)
+    k, v = oracle.normal(61, (n, KVD)), oracle.normal(62, (n, KVD))
+    dev.append(0, k, v)
+    q = oracle.normal(63, (HID,))
+    got = dev.decode(0, torch.from_numpy(q).cuda()).cpu().numpy()
+    want = oracle.attention_decode(q, k, v, n, H, KVH, D)
+    err = np.abs(got - want).max()
+    print(f"fp8 cache vs fp32 reference: max |err| {err:.3e} (outputs up to {np.abs(want).max():.3f})")
+    assert err <= FP8_VS_FP32_ATOL, err
+
+
+def test_fp8_cache_fused_step_and_batched():
+    """The fused step and batched decode on an fp8 cache. The oracle step appends the k the
+    cache holds (read back: the device's RoPE may round one element to the next e4m3 value)."""
+    torch = pytest.importorskip("torch")
+    qg, kg = gains(93)
+    dev = bb.Cache(n_layers=1, max_context=2048, kv_dtype=bb.FP8)
+    ref = oracle.Cache(1, KVD)
+    k0, v0 = _fp8(oracle.normal(4, (700, KVD))), _fp8(oracle.normal(5, (700, KVD)))
+    dev.append(0, k0, v0)
+    ref.append(0, k0, v0)
+    for step in range(3):
+        q, k, v = oracle.normal(10 + step, (HID,)), oracle.normal(20 + step, (KVD,)), oracle.normal(30 + step, (KVD,))
+        got = dev.attn_step(0, q, k, v, qg, kg, pos=700 + step, theta=1e6)
+        kd, vd = dev.read(0)
+        kn = oracle.norm_rope_heads(k, KVH, D, kg, 700 + step, 1e6, 1e-5)
+        # the stored k is the e4m3 rounding of the normed, roped k (one step apart at most)
+        assert np.abs(kd[-1] - kn).max() <= 0.07 * np.abs(kn).max() + 1e-6
+        assert np.array_equal(vd[-1], _fp8(v))
+        ref.append(0, kd[-1], vd[-1])
+        qn = oracle.norm_rope_heads(q, H, D, qg, 700 + step, 1e6, 1e-5)
+        want = oracle.attention_decode(qn, ref.k[0], ref.v[0], ref.k[0].shape[0], H, KVH, D)
+        assert np.abs(got - want).max() <= 1e-4, step
+    pool = bb.Pool(n_layers=1, n_pages=100, kv_dtype=bb.FP8)
+    lens = [5, 130, 1000]
+    devs = [bb.Cache(max_context=2048, pool=pool, kv_dtype=bb.FP8) for _ in lens]
+    refs = [oracle.Cache(1, KVD) for _ in lens]
+    for i, n in enumerate(lens):
+        kk, vv = _fp8(oracle.normal(40 + i, (n, KVD))), _fp8(oracle.normal(50 + i, (n, KVD)))
+        devs[i].append(0, kk, vv)
+        refs[i].append(0, kk, vv)
+    q, k, v = oracle.normal(6, (3, HID)), oracle.normal(7, (3, KVD)), oracle.normal(8, (3, KVD))
+    got = bb.attn_decode_batched(devs, 0, q, k, v, qg, kg, [n for n in lens], theta=1e6)
+    for i in range(3):
+        kd, vd = devs[i].read(0)
+        refs[i].append(0, kd[-1], vd[-1])
+        qn = oracle.norm_rope_heads(q[i], H, D, qg, lens[i], 1e6, 1e-5)
+        want = oracle.attention_decode(qn, refs[i].k[0], refs[i].v[0], refs[i].k[0].shape[0], H, KVH, D)
+        assert np.abs(got[i] - want).max() <= 1e-4, i
+
+
+def test_fp8_cache_tensor_core_prefill():
+    """A bf16 chunk on top of an fp8 prefix: the prefix enters the tensor cores as the cache
+    holds it; the chunk's own keys as bf16 (the cache stores their e4m3 rounding)."""
+    qg, kg = gains(97)
+    dev = bb.Cache(n_layers=1, max_context=4096, kv_dtype=bb.FP8)
+    pk, pv = _fp8(oracle.normal(5, (300, KVD))), _fp8(oracle.normal(6, (300, KVD)))
+    dev.append(0, pk, pv)
+    t = 400
+    q, k, v = (_bf16_round(oracle.normal(s, shp)) for s, shp in ((7, (t, HID)), (8, (t, KVD)), (9, (t, KVD))))
+    got = _prefill_bf16(dev, q, k, v, qg, kg, 300, 1e6)
+    want = oracle.attn_batch(q, k, v, 300, qg, kg, 1e6, 1e-5, H, KVH, D, pk, pv, n_threads=oracle.max_threads())[0]
+    rel = np.abs(got - want).max() / np.abs(want).max()
+    assert rel <= PREFILL_REL, rel
+    kd, vd = dev.read(0)
+    assert np.array_equal(vd[300:], _fp8(v))
