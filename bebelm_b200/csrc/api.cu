@@ -464,6 +464,9 @@ void record_decode_out(cudaStream_t s, const void* out, size_t bytes) {
     g_last_out[s] = OutRange{static_cast<const char*>(out), bytes};
 }
 
+// the running host call's inputs are copied to the device by a kernel (see stage_in)
+thread_local bool g_inputs_staged = false;
+
 bool inputs_clear_of_last_out(cudaStream_t s, std::initializer_list<std::pair<const void*, size_t>> ins) {
     std::lock_guard<std::mutex> lk(g_last_out_mu);
     auto it = g_last_out.find(s);
@@ -568,7 +571,8 @@ int run_decode(bebelm_kv_pool* P, const std::vector<Window>& wins, int layer, in
         a.theta_scale = fused->theta_scale;
         a.eps = fused->eps;
         const size_t nq = (size_t)n * n_heads * kHeadDim * 4, nkv = (size_t)n * P->n_kv * kHeadDim * 4;
-        a.early_inputs = !peer && inputs_clear_of_last_out(s, {{fused->q_raw, nq}, {fused->k_new, nkv},
+        // inputs staged from host memory by a copy kernel are complete only after the wait
+        a.early_inputs = !g_inputs_staged && !peer && inputs_clear_of_last_out(s, {{fused->q_raw, nq}, {fused->k_new, nkv},
                                                                {fused->v_new, nkv}, {fused->q_gain, 4 * kHeadDim},
                                                                {fused->k_gain, 4 * kHeadDim}});
     }
@@ -612,6 +616,10 @@ struct Stage {
 };
 
 thread_local size_t g_pin_out_off = 0;   // set by stage_in, read by stage_out (calls are host-synchronous)
+// Host inputs up to this size reach the device through a copy kernel rather than a DMA copy:
+// the decode grid launched behind it overlaps its prologue with the copy (programmatic
+// dependent launch), where a cudaMemcpyAsync before it would finish first.
+constexpr size_t kKernelStageBytes = 64 * 1024;
 thread_local bool g_pin_out_direct = false;  // the output was stored straight into the pinned buffer
 
 // Outputs up to this size are stored by the kernel straight into the mapped pinned buffer
@@ -631,7 +639,11 @@ int stage_in(bebelm_kv_pool* P, Stage* st, int n, size_t out_bytes, void** d_out
         *st[i].dev = st[i].src ? P->io.as<char>() + off : nullptr;
         off += (st[i].bytes + 255) & ~size_t(255);
     }
-    if (out_off) CUDA_TRY(cudaMemcpyAsync(P->io.p, P->pin.p, out_off, cudaMemcpyHostToDevice, s));
+    g_inputs_staged = out_off > 0 && out_off <= kKernelStageBytes;
+    if (g_inputs_staged)
+        CUDA_TRY(launch_stage_copy(P->io.p, P->pin.d, out_off, s));
+    else if (out_off)
+        CUDA_TRY(cudaMemcpyAsync(P->io.p, P->pin.p, out_off, cudaMemcpyHostToDevice, s));
     g_pin_out_direct = out_bytes <= kDirectOutBytes;
     if (d_out) *d_out = (g_pin_out_direct ? static_cast<char*>(P->pin.d) : P->io.as<char>()) + out_off;
     g_pin_out_off = out_off;
@@ -646,6 +658,7 @@ void clear_noalloc_counters(int dev, cudaStream_t s);
 // delivers the output to the caller's host memory (from the pinned buffer, after copying
 // it there unless the kernel stored it there directly).
 int stage_out(bebelm_kv_pool* P, const void* d_src, void* h_dst, size_t bytes, cudaStream_t s) {
+    g_inputs_staged = false;
     char* pin = P->pin.as<char>() + g_pin_out_off;
     if (bytes && !g_pin_out_direct) CUDA_TRY(cudaMemcpyAsync(pin, d_src, bytes, cudaMemcpyDeviceToHost, s));
     CUDA_TRY(cudaStreamSynchronize(s));

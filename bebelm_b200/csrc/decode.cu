@@ -38,6 +38,8 @@
 // every float4 shared-memory read conflict-free and lets each lane keep its q
 // slice in registers; the 4 lanes of a row reduce the dot with two xor
 // shuffles (identical result on all 4 lanes).
+#include <algorithm>
+
 #include "internal.h"
 
 namespace bebelm {
@@ -775,7 +777,25 @@ __global__ void peer_wait_kernel(const unsigned long long* flags, int world, uns
     }
 }
 
+// Copies a host call's staged inputs (mapped pinned memory) into device memory. It lets its
+// dependents launch at once, so the decode grid that follows (a programmatic dependent) runs its
+// prologue and first page copies while the inputs cross the host link; that grid reads them
+// only after griddepcontrol.wait.
+__global__ void stage_copy_kernel(const uint4* __restrict__ src, uint4* __restrict__ dst, size_t n16) {
+    grid_dep_launch();
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n16; i += (size_t)gridDim.x * blockDim.x)
+        dst[i] = src[i];
+}
+
 }  // namespace
+
+cudaError_t launch_stage_copy(void* dst, const void* src_mapped, size_t bytes, cudaStream_t s) {
+    const size_t n16 = bytes / 16;
+    if (!n16) return cudaSuccess;
+    const unsigned blocks = (unsigned)std::min<size_t>(16, (n16 + 255) / 256);
+    stage_copy_kernel<<<blocks, 256, 0, s>>>(static_cast<const uint4*>(src_mapped), static_cast<uint4*>(dst), n16);
+    return cudaGetLastError();
+}
 
 cudaError_t launch_peer_wait(const unsigned long long* flags, int world, unsigned long long expected, const float* src,
                              float* dst, size_t n, int* err, unsigned long long* epoch, unsigned long long writers,

@@ -225,6 +225,9 @@ cudaError_t launch_peer_wait(const unsigned long long* flags, int world, unsigne
                              float* dst, size_t n, int* err, unsigned long long* epoch, unsigned long long writers,
                              cudaStream_t s);
 cudaError_t launch_decode(const DecodeArgs& a, cudaStream_t s);
+// Copies `bytes` (a multiple of 16) from mapped pinned memory to device memory on s, letting
+// the next kernel launch as a programmatic dependent right away.
+cudaError_t launch_stage_copy(void* dst, const void* src_mapped, size_t bytes, cudaStream_t s);
 size_t decode_smem_bytes();
 constexpr int kDecodeMaxPagesPerSplit = 256;
 

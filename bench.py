@@ -730,6 +730,68 @@ def bench_config5(bb, torch, dev, stream, world, rank, bf16_peak, T=8192, steps=
     return out
 
 
+def profile_workload(name: str):
+    """Small cases for ncu captures of one kernel each (inputs above L2 where it matters, a few
+    GB at most): `norm_rope` (config-2 prefill: kernel 1 then the tensor-core prefill), `batched`
+    (batched decode over 16 sequences of U[1024,16384] positions, ~560 MB of fp32 K/V),
+    `qmv` (one-token attention operator steps: the qmv_lane_kernel projections)."""
+    import numpy as np
+    import torch
+    import bebelm_b200 as bb
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev)
+    g.manual_seed(5)
+    qg = torch.ones(D, device=dev)
+    if name == "norm_rope":
+        T = 2048
+        q = torch.randn((T, HID), generator=g, device=dev).to(torch.bfloat16)
+        k = torch.randn((T, KVD), generator=g, device=dev).to(torch.bfloat16)
+        v = torch.randn((T, KVD), generator=g, device=dev).to(torch.bfloat16)
+        for _ in range(3):
+            c = bb.Cache(n_layers=1, max_context=T)
+            c.attn_prefill(0, q, k, v, qg, qg, 0, theta=THETA)
+            torch.cuda.synchronize()
+            c.close()
+    elif name == "batched":
+        lengths = np.random.default_rng(4).integers(1024, 16385, size=16)
+        pool = bb.Pool(n_layers=1, n_pages=sum(int(l) // 64 + 4 for l in lengths))
+        cs = [bb.Cache(max_context=int(l) + 64, pool=pool) for l in lengths]
+        for c, l in zip(cs, lengths):
+            c.append(0, torch.randn((int(l), KVD), generator=g, device=dev),
+                     torch.randn((int(l), KVD), generator=g, device=dev))
+        Q = torch.randn((16, HID), generator=g, device=dev)
+        K = torch.randn((16, KVD), generator=g, device=dev)
+        for s_ in range(3):
+            bb.attn_decode_batched(cs, 0, Q, K, K, qg, qg, [int(l) + s_ for l in lengths], theta=THETA)
+        torch.cuda.synchronize()
+        for c in cs:
+            c.close()
+        pool.close()
+    elif name == "qmv":
+        rng = np.random.default_rng(3)
+
+        def kq(rows, n_in, six=False):
+            nb = 210 if six else 144
+            w = rng.integers(0, 256, size=(rows, n_in // 256, nb), dtype=np.uint8)
+            d = (rng.standard_normal((rows, n_in // 256)) * (0.002 if six else 0.01)).astype(np.float16)
+            w[:, :, (208 if six else 0):(210 if six else 2)] = d.view(np.uint8).reshape(rows, -1, 2)
+            return w.reshape(-1)
+
+        W = bb.AttnWeights((bb.GGML_Q4_K, kq(HID, HID)), (bb.GGML_Q4_K, kq(KVD, HID)),
+                           (bb.GGML_Q6_K, kq(KVD, HID, True)), (bb.GGML_Q4_K, kq(HID, HID)),
+                           np.ones(D, np.float32), np.ones(D, np.float32))
+        c = bb.Cache(n_layers=1, max_context=4096)
+        c.append(0, torch.randn((2000, KVD), generator=g, device=dev), torch.randn((2000, KVD), generator=g, device=dev))
+        x = torch.randn((8, HID), generator=g, device=dev)
+        o = torch.empty(HID, device=dev)
+        for i in range(8):
+            bb.attn_layer_step(c, 0, W, x[i], 2000 + i, theta=THETA, out=o)
+        torch.cuda.synchronize()
+    else:
+        raise SystemExit(f"unknown profile workload {name}")
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -740,9 +802,13 @@ def main():
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--no-cfg4", action="store_true")
     ap.add_argument("--no-cfg5", action="store_true")
+    ap.add_argument("--profile-workload", default=None, choices=["norm_rope", "batched", "qmv"],
+                    help="run one small case for an ncu capture and exit")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    if args.profile_workload:
+        return profile_workload(args.profile_workload)
     if args.impl == "reference":
         return run_reference(args)
     return run_ours(args)
