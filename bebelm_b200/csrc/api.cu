@@ -1734,17 +1734,19 @@ int plan_launch(bebelm_step_plan* pl, const bebelm_peer_group* grp, const float*
     if (cs != cudaStreamCaptureStatusActive) cap_id = 0;
     a.step_prewait = P->last_plan != nullptr && P->last_plan != pl && P->last_capture == cap_id;
     if (grp) {
+        // Between two gathered steps sits the previous step's wait kernel, an ordinary launch:
+        // it starts once that decode grid has completed, and lets this grid start at once. So,
+        // as between two plain plans, this plan's own previous step is complete when this grid
+        // starts, and step_prewait (decided above) holds as it stands.
         a.peer_bufs = grp->d_bufs();
         a.peer_flags = grp->d_flags();
         a.peer_world = grp->world;
         a.peer_rank = grp->rank;
         a.peer_epoch = grp->d_epoch();
-        // the wait kernel between two such steps is not a decode grid: nothing is read early
-        a.step_prewait = 0;
     }
     CUDA_TRY(launch_decode(a, as_stream(stream)));
     record_decode_out(as_stream(stream), a.out, grp ? SIZE_MAX : (size_t)pl->n_heads * kHeadDim * 4);
-    P->last_plan = grp ? nullptr : pl;
+    P->last_plan = pl;
     P->last_capture = cap_id;
     if (grp) TRY(peer_gather_out(grp, P, pl->n_heads, out, as_stream(stream)));
     return 0;

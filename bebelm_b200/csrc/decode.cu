@@ -742,6 +742,10 @@ __global__ void peer_wait_kernel(const unsigned long long* flags, int world, uns
                                  unsigned long long writers) {
     __shared__ int s_ok;
     __shared__ unsigned long long s_e;
+    // the next decode grid (a programmatic dependent) may start its prologue — page-table loads,
+    // its first page copies — while this one waits for the peers; it reads this grid's output
+    // only after its own griddepcontrol.wait
+    grid_dep_launch();
     if (threadIdx.x == 0) {
         s_ok = 1;
         s_e = epoch ? *reinterpret_cast<volatile unsigned long long*>(epoch) + 1ull : 0ull;

@@ -295,7 +295,8 @@ def run_ours(args):
     if rank == 0 and not args.no_prefill:
         prefill = {"attn_layer": bench_attn_layer(bb, torch, dev, stream),
                    "config2_2048": bench_prefill(bb, torch, dev, stream, bf16_peak, peak_kind, 2048, 6),
-                   "config5_8192_one_layer": bench_prefill(bb, torch, dev, stream, bf16_peak, peak_kind, 8192, 2)}
+                   "config5_8192_one_layer": bench_prefill(bb, torch, dev, stream, bf16_peak, peak_kind, 8192, 2),
+                   "f32_host_inputs": bench_prefill_f32_host(bb, torch, bf16_peak, peak_kind)}
 
     head = bench_logits_head(bb, torch, dev, stream, hbm_peak, peak_kind) if rank == 0 and not args.no_prefill else None
     c3bf = bench_config3_narrow(bb, torch, dev, stream, world, args.steps, bb.BF16)
@@ -404,6 +405,38 @@ def bench_prefill(bb, torch, dev, stream, bf16_peak, peak_kind, T=2048, reps=6):
             "ms": round(ms, 4), "value": round(tf, 3), "unit": "TFLOP/s",
             "roofline": {"bound": "tensor", "achieved": round(tf, 3), "peak": bf16_peak, "unit": "TFLOP/s",
                          "frac": round(tf / bf16_peak, 4), "peak_kind": peak_kind}}
+
+
+def bench_prefill_f32_host(bb, torch, bf16_peak, peak_kind):
+    """The drop-in prefill a Rust attn_batch makes (src/model.rs:232-254): fp32 q/k/v in host
+    memory through bebelm_attn_prefill with mem = HOST, output back in host memory, the copies
+    inside the timed region. BEBELM_F32_TENSOR (tensor cores) at 2048 and 8192 tokens, and the
+    reference-arithmetic fp32 path (one causal split-K decode per token) at 2048."""
+    import numpy as np
+    rng = np.random.default_rng(78)
+    out = {}
+    for T, tc in ((2048, True), (8192, True), (2048, False)):
+        q = rng.standard_normal((T, HID), dtype=np.float32)
+        k = rng.standard_normal((T, KVD), dtype=np.float32)
+        v = rng.standard_normal((T, KVD), dtype=np.float32)
+        qg = (1 + 0.02 * rng.standard_normal(D)).astype(np.float32)
+        kg = (1 + 0.02 * rng.standard_normal(D)).astype(np.float32)
+        c = bb.Cache(n_layers=1, max_context=T)
+        times = []
+        for it in range(3):
+            c.clear()
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            c.attn_prefill(0, q, k, v, qg, kg, 0, theta=THETA, tensor_cores=tc)  # returns once out is on the host
+            times.append(time.perf_counter() - t0)
+        c.close()
+        ms = statistics.median(times[1:]) * 1e3
+        tf = 4096.0 * T * (T + 1) / (ms * 1e-3) / 1e12
+        name = f"{'tensor_cores' if tc else 'fp32_reference_arithmetic'}_{T}"
+        out[name] = {"ms": round(ms, 3), "tflops": round(tf, 2), "frac_of_bf16_peak": round(tf / bf16_peak, 4),
+                     "h2d_bytes": int(4 * (q.size + k.size + v.size + 2 * D)), "d2h_bytes": int(4 * T * HID)}
+    out["how"] = "host fp32 buffers through the C-ABI, wall clock per call (copies in and out included)"
+    return out
 
 
 def bench_attn_layer(bb, torch, dev, stream, T=2048, steps=64):
@@ -664,7 +697,7 @@ def bench_config5(bb, torch, dev, stream, world, rank, bf16_peak, T=8192, steps=
         o = torch.empty((steps, L, HID), device=dev)
         graph, cap = torch.cuda.CUDAGraph(), torch.cuda.Stream()
         torch.cuda.synchronize()
-        with torch.cuda.graph(graph, stream=cap):
+        with torch.cuda.graph(graph, stream=cap, capture_error_mode="thread_local"):  # NCCL watchdog threads run meanwhile
             for s_ in range(steps):
                 for layer in range(L):
                     sh.plan_step(plans[layer], Qd[s_], Kd[s_], Vd[s_], qg, kg, o[s_, layer], theta=THETA)

@@ -121,7 +121,7 @@ def _worker(rank, world, port, q):
         gout = torch.empty((6, H * D), device="cuda")
         graph, cap = torch.cuda.CUDAGraph(), torch.cuda.Stream()
         torch.cuda.synchronize()
-        with torch.cuda.graph(graph, stream=cap):
+        with torch.cuda.graph(graph, stream=cap, capture_error_mode="thread_local"):
             for i in range(6):
                 p = 3010 + i
                 sh.plan_step(plan, qq[p], kk[p], vv[p], qg, kg, gout[i])
