@@ -51,7 +51,7 @@ EXPORTS = [
     "bebelm_gguf_header", "bebelm_gguf_tensor_at", "bebelm_gguf_find_tensor", "bebelm_gguf_key_at",
     "bebelm_gguf_get_u32", "bebelm_gguf_get_f32", "bebelm_gguf_get_str", "bebelm_gguf_get_u32_array",
     "bebelm_gguf_array_len", "bebelm_gguf_get_str_at", "bebelm_gguf_validate", "bebelm_attn_weights_from_gguf",
-    "bebelm_head_from_gguf", "bebelm_step_plan_launch_allgather",
+    "bebelm_head_from_gguf", "bebelm_step_plan_launch_allgather", "bebelm_attn_prefill_allgather",
 ]
 GGML_F32, GGML_F16, GGML_Q4_K, GGML_Q6_K = 0, 1, 12, 14
 IPC_HANDLE_BYTES = 64
@@ -117,6 +117,7 @@ def load_library(path: str = LIB_PATH):
         "bebelm_step_plan_create": ([vp, i, i, sz, C.POINTER(vp)], i),
         "bebelm_step_plan_launch": ([vp, vp, vp, vp, vp, vp, f, f, vp, vp], i),
         "bebelm_step_plan_launch_allgather": ([vp, vp, vp, vp, vp, vp, vp, f, f, vp, vp], i),
+        "bebelm_attn_prefill_allgather": ([vp, vp, i, i, vp, vp, vp, i, sz, sz, vp, vp, f, f, vp, vp], i),
         "bebelm_step_plan_steps": ([vp, C.POINTER(C.c_ulonglong), vp], i),
         "bebelm_step_plan_finish": ([vp, vp], i),
         "bebelm_matvec": ([i, vp, sz, sz, vp, vp, i, vp], i),
@@ -390,6 +391,25 @@ class Cache:
         ob, _, _ = _buf(out)
         _check(load_library().bebelm_attn_step_allgather(self._h, group._h, layer, n_heads, qb[0], kb[0], vb[0], qg[0],
                                                          kg[0], theta, eps, pos, ob, mem, _stream_ptr(stream, mem)))
+        return out
+
+    def attn_prefill_allgather(self, group: "PeerGroup", layer: int, q, k, v, q_gain, k_gain, pos0: int,
+                               theta: float = ROPE_THETA, eps: float = RMS_EPS, out=None, stream=None,
+                               n_heads: int | None = None):
+        """:meth:`attn_prefill` on this rank's heads of the full rows q [t, world*n_heads*64],
+        k/v [t, world*n_kv*64] (CUDA tensors, bf16, or float32 for the tensor cores), gathered
+        over ``group``: returns out [t, world*n_heads*64] float32."""
+        import torch
+        world = group.world
+        if n_heads is None:
+            n_heads = q.shape[-1] // (self.head_dim * world)
+        t = q.numel() // (world * n_heads * self.head_dim)
+        in_dtype = BF16 if q.dtype == torch.bfloat16 else F32_TENSOR
+        if out is None:
+            out = torch.empty((t, world * n_heads * self.head_dim), dtype=torch.float32, device=q.device)
+        _check(load_library().bebelm_attn_prefill_allgather(
+            self._h, group._h, layer, n_heads, q.data_ptr(), k.data_ptr(), v.data_ptr(), in_dtype, t, pos0,
+            q_gain.data_ptr(), k_gain.data_ptr(), theta, eps, out.data_ptr(), _stream_ptr(stream)))
         return out
 
     def check(self, stream=None) -> None:

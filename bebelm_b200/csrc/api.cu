@@ -1143,9 +1143,20 @@ namespace {
 // window. tc: the tensor-core kernel (bf16 operands; the inputs are rounded to bf16 by the
 // norm kernel when they are fp32), else the exact fp32 split-K path with one causal window
 // per token. dout [t][n_heads*64] fp32 on the device.
+// A rank's share of a KV-head-sharded prefill: which heads of the replicated full input rows
+// are this call's, and where the gathered output goes (the landing zones of a peer group).
+struct PrefillShard {
+    int q_row_heads, q_head0, kv_row_heads, kv_head0;
+    float* const* bufs;
+    unsigned long long* const* flags;
+    const unsigned long long* epoch;
+    int world, rank;
+    size_t slice;
+};
+
 int prefill_device(bebelm_kv* kv, int layer, int n_heads, const void* dq, const void* dk, const void* dv, bool in_bf16,
                    bool tc, size_t t, size_t pos0, const float* dqg, const float* dkg, float theta, float eps,
-                   float* dout, cudaStream_t s) {
+                   float* dout, cudaStream_t s, const PrefillShard* shard = nullptr) {
     bebelm_kv_pool* P = kv->pool;
     const size_t qn = (size_t)n_heads * kHeadDim * t;
     long long slot0 = 0;
@@ -1165,6 +1176,14 @@ int prefill_device(bebelm_kv* kv, int layer, int n_heads, const void* dq, const 
         pa.t = (int)t; pa.len_before = (int)len_before; pa.n_heads = n_heads; pa.n_kv = P->n_kv;
         pa.scale_log2 = 0.125f * 1.4426950408889634f;
         pa.err = P->err.d;
+        if (shard) {
+            pa.peer_bufs = shard->bufs;
+            pa.peer_flags = shard->flags;
+            pa.peer_epoch = shard->epoch;
+            pa.peer_world = shard->world;
+            pa.peer_rank = shard->rank;
+            pa.peer_slice = shard->slice;
+        }
         PrefillMaps maps;
         if (!prefill_make_maps(pa, &maps)) return fail(BEBELM_ERR_CUDA, "building the TMA tensor maps for prefill failed");
         if (len_before > 0)
@@ -1180,6 +1199,12 @@ int prefill_device(bebelm_kv* kv, int layer, int n_heads, const void* dq, const 
         a.q_bf16 = qb; a.k_bf16 = kb + (size_t)len_before * kvrow; a.v_bf16 = vb + (size_t)len_before * kvrow;
         a.append = 1; a.pv = P->view(layer); a.table = kv->d_table; a.cap = kv->cap; a.slot0 = slot0;
         a.in_bf16 = in_bf16 ? 1 : 0;  // norm + RoPE read the inputs in their own type
+        if (shard) {
+            a.q_row_heads = shard->q_row_heads;
+            a.q_head0 = shard->q_head0;
+            a.kv_row_heads = shard->kv_row_heads;
+            a.kv_head0 = shard->kv_head0;
+        }
         CUDA_TRY(launch_norm_rope(a, s));
         P->last_writes.assign(1, {kv, layer, slot0});
         CUDA_TRY(launch_prefill(pa, maps, s));
@@ -1187,6 +1212,7 @@ int prefill_device(bebelm_kv* kv, int layer, int n_heads, const void* dq, const 
         return 0;
     }
     if (in_bf16) return fail(BEBELM_ERR_UNSUPPORTED, "bf16 inputs take the tensor-core path");
+    if (shard) return fail(BEBELM_ERR_UNSUPPORTED, "a gathered prefill takes the tensor-core path");
     TRY(P->qn.ensure(4 * qn, false, s));
     NormRopeArgs a{};
     a.q = (const float*)dq; a.k = (const float*)dk; a.v = (const float*)dv; a.q_gain = dqg; a.k_gain = dkg;
@@ -1568,6 +1594,38 @@ int bebelm_attn_step_allgather(bebelm_kv* kv, bebelm_peer_group* g, int layer, i
     TRY(run_decode(P, w, layer, n_heads, nullptr, dout, 0.125f, &fs, s, &pt));
     TRY(peer_gather_out(g, P, n_heads, dout, s));
     if (mem == BEBELM_MEM_HOST) return stage_out(P, dout, out, 4 * full, s);
+    return 0;
+}
+
+int bebelm_attn_prefill_allgather(bebelm_kv* kv, bebelm_peer_group* g, int layer, int n_heads, const void* q,
+                                  const void* k, const void* v, int in_dtype, size_t t, size_t pos0,
+                                  const float* q_gain, const float* k_gain, float theta, float eps, float* out,
+                                  void* stream) {
+    TRY(validate_layer(kv, layer));
+    if (!g || !g->connected) return fail(BEBELM_ERR_INVALID, "peer group missing or not connected");
+    bebelm_kv_pool* P = kv->pool;
+    TRY(check_geometry(n_heads, P->n_kv));
+    if (P->device != g->device) return fail(BEBELM_ERR_INVALID, "cache and peer group are on different devices");
+    if (in_dtype != BEBELM_BF16 && in_dtype != BEBELM_F32_TENSOR)
+        return fail(BEBELM_ERR_UNSUPPORTED, "a gathered prefill takes BEBELM_BF16 or BEBELM_F32_TENSOR inputs");
+    if (t == 0) return 0;
+    if (!q || !k || !v || !q_gain || !k_gain || !out) return fail(BEBELM_ERR_INVALID, "null buffer");
+    const size_t row = (size_t)n_heads * kHeadDim;
+    if (t * row > g->slice)
+        return fail(BEBELM_ERR_CAPACITY, "%zu tokens x %d heads exceed the group's landing zone (%zu floats a rank)", t,
+                    n_heads, g->slice);
+    DeviceGuard dg(P->device);
+    cudaStream_t s = as_stream(stream);
+    const PrefillShard sh{n_heads * g->world, n_heads * g->rank, P->n_kv * g->world, P->n_kv * g->rank,
+                          g->d_bufs(), g->d_flags(), g->d_epoch(), g->world, g->rank, g->slice};
+    TRY(prefill_device(kv, layer, n_heads, q, k, v, in_dtype == BEBELM_BF16, true, t, pos0, q_gain, k_gain, theta,
+                       eps, nullptr, s, &sh));
+    // every rank's prefill grid has the same shape: its CTAs are the writers of each rank
+    const unsigned long long writers = (unsigned long long)n_heads * ((((t + 127) / 128) + 1) / 2);
+    CUDA_TRY(launch_peer_wait(reinterpret_cast<const unsigned long long*>(g->zone), g->world, 0, nullptr, nullptr, 0,
+                              P->err.d, g->d_epoch(), writers, s));
+    CUDA_TRY(launch_gather_rows(reinterpret_cast<const float*>(g->zone + 256), g->d_epoch(), g->world, g->slice, t,
+                                row, out, s));
     return 0;
 }
 

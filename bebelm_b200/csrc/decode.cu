@@ -791,7 +791,28 @@ __global__ void stage_copy_kernel(const uint4* __restrict__ src, uint4* __restri
         dst[i] = src[i];
 }
 
+__global__ void gather_rows_kernel(const float* __restrict__ zone, const unsigned long long* epoch, int world,
+                                   size_t slice, size_t rows, size_t row_floats, float* __restrict__ dst) {
+    const unsigned long long e = *reinterpret_cast<const volatile unsigned long long*>(epoch);
+    const float4* src = reinterpret_cast<const float4*>(zone + (size_t)(e & 1ull) * world * slice);
+    const size_t rq = row_floats / 4, total = (size_t)world * rows * rq;
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+        const size_t w = i / (rows * rq), rem = i % (rows * rq), r = rem / rq, c = rem % rq;
+        reinterpret_cast<float4*>(dst)[(r * world + w) * rq + c] =
+            __ldcv(reinterpret_cast<const float4*>(reinterpret_cast<const float*>(src) + w * slice) + r * rq + c);
+    }
+}
+
 }  // namespace
+
+cudaError_t launch_gather_rows(const float* zone, const unsigned long long* epoch, int world, size_t slice,
+                               size_t rows, size_t row_floats, float* dst, cudaStream_t s) {
+    const size_t total = (size_t)world * rows * (row_floats / 4);
+    if (!total) return cudaSuccess;
+    const unsigned blocks = (unsigned)std::min<size_t>((total + 255) / 256, 148 * 8);
+    gather_rows_kernel<<<blocks, 256, 0, s>>>(zone, epoch, world, slice, rows, row_floats, dst);
+    return cudaGetLastError();
+}
 
 cudaError_t launch_stage_copy(void* dst, const void* src_mapped, size_t bytes, cudaStream_t s) {
     const size_t n16 = bytes / 16;

@@ -139,6 +139,10 @@ struct NormRopeArgs {
     long long slot0;  // logical slot of token 0
     const AppendTarget* targets;  // non-null: per-token table/slot/pos instead of the above
     int in_bf16;                  // q, k, v hold bf16 (head_dim 64 only)
+    // input rows wider than this call's heads (a rank's heads of replicated full rows): a q row
+    // holds q_row_heads heads of which this call's start at q_head0; likewise k/v (0: exactly
+    // n_heads / n_kv, from 0)
+    int q_row_heads, q_head0, kv_row_heads, kv_head0;
 };
 cudaError_t launch_norm_rope(const NormRopeArgs& a, cudaStream_t s);
 
@@ -228,6 +232,10 @@ cudaError_t launch_decode(const DecodeArgs& a, cudaStream_t s);
 // Copies `bytes` (a multiple of 16) from mapped pinned memory to device memory on s, letting
 // the next kernel launch as a programmatic dependent right away.
 cudaError_t launch_stage_copy(void* dst, const void* src_mapped, size_t bytes, cudaStream_t s);
+// After a gathered prefill's wait: copies the landing zone's parity (*epoch & 1), laid out
+// [world][rows][row_floats], into dst [rows][world * row_floats] (rank = column block).
+cudaError_t launch_gather_rows(const float* zone, const unsigned long long* epoch, int world, size_t slice,
+                               size_t rows, size_t row_floats, float* dst, cudaStream_t s);
 size_t decode_smem_bytes();
 constexpr int kDecodeMaxPagesPerSplit = 256;
 
@@ -240,6 +248,15 @@ struct PrefillArgs {
     int t, len_before, n_heads, n_kv;
     float scale_log2;        // score scale times log2(e)
     int* err;
+    // fused all-gather (KV-head sharding): with peer_world > 0 the output rows go to every
+    // rank's landing zone instead of `out`: [parity e&1][peer_rank][t][n_heads][64] floats, parity
+    // from the group's device epoch (e = *peer_epoch + 1), peer_slice floats per rank; each CTA
+    // then bumps peer_flags[w][peer_rank] on every rank w
+    float* const* peer_bufs;
+    unsigned long long* const* peer_flags;
+    const unsigned long long* peer_epoch;
+    int peer_world, peer_rank;
+    size_t peer_slice;
 };
 // TMA descriptors of q, k, v (opaque 128-byte CUtensorMap objects).
 struct alignas(64) PrefillMaps {

@@ -50,7 +50,9 @@ __global__ void __launch_bounds__(256) norm_rope_kernel(NormRopeArgs a) {
     const int hh = (int)(item % nh_all);
     const bool is_q = hh < a.n_heads;
     const int head = is_q ? hh : hh - a.n_heads;
-    const size_t src_elem = is_q ? ((size_t)tok * a.n_heads + head) * hd : ((size_t)tok * a.n_kv + head) * hd;
+    const int q_row = a.q_row_heads ? a.q_row_heads : a.n_heads, kv_row = a.kv_row_heads ? a.kv_row_heads : a.n_kv;
+    const size_t src_elem = is_q ? ((size_t)tok * q_row + a.q_head0 + head) * hd
+                                 : ((size_t)tok * kv_row + a.kv_head0 + head) * hd;
     const float* src = a.in_bf16 ? reinterpret_cast<const float*>(
                                        reinterpret_cast<const __nv_bfloat16*>(is_q ? a.q : a.k) + src_elem)
                                  : (is_q ? a.q : a.k) + src_elem;
@@ -77,7 +79,7 @@ __global__ void __launch_bounds__(256) norm_rope_kernel(NormRopeArgs a) {
     }
 
     // V row of the same kv head passes through unchanged (loaded now, stored at the end)
-    const size_t v_elem = ((size_t)tok * a.n_kv + head) * 64;
+    const size_t v_elem = ((size_t)tok * kv_row + a.kv_head0 + head) * 64;
     const float* vsrc = !HD64 || is_q || !a.v ? nullptr
                         : a.in_bf16 ? reinterpret_cast<const float*>(reinterpret_cast<const __nv_bfloat16*>(a.v) + v_elem)
                                     : a.v + v_elem;

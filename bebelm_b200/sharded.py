@@ -45,8 +45,10 @@ class KVHeadSharded:
     """One rank's share of a KV-head-sharded attention stack."""
 
     def __init__(self, n_layers: int, max_context: int, n_heads: int = N_HEADS, n_kv_heads: int = N_KV_HEADS,
-                 group=None, cache_factory=None, fused_gather: bool | None = None, local: bool = False):
-        """fused_gather: gather decode outputs inside the decode kernel over peer memory
+                 group=None, cache_factory=None, fused_gather: bool | None = None, local: bool = False,
+                 max_prefill_tokens: int = 8192):
+        """fused_gather: gather decode outputs inside the decode kernel over peer memory, and
+        tensor-core prefill outputs (chunks up to max_prefill_tokens) inside the prefill kernel
         (default: on for the CUDA cache with more than one rank); off uses NCCL. local: this
         process alone holds every head (world 1), whatever the process group."""
         self.group = group
@@ -65,12 +67,16 @@ class KVHeadSharded:
             self.cache = cache_factory(n_layers, self.kv_per, max_context)
         if fused_gather is None:
             fused_gather = cache_factory is None and self.world > 1
-        self.peers = None
+        self.peers = self.prefill_peers = None
+        self.max_prefill_tokens = max_prefill_tokens
         if fused_gather:
-            self.peers = PeerGroup(self.world, self.rank, self.h_per * HEAD_DIM, device=torch.cuda.current_device())
-            handles = [None] * self.world
-            dist.all_gather_object(handles, self.peers.handle, group=self.group)
-            self.peers.connect(handles)
+            dev = torch.cuda.current_device()
+            self.peers = PeerGroup(self.world, self.rank, self.h_per * HEAD_DIM, device=dev)
+            self.prefill_peers = PeerGroup(self.world, self.rank, max_prefill_tokens * self.h_per * HEAD_DIM, device=dev)
+            for g in (self.peers, self.prefill_peers):
+                handles = [None] * self.world
+                dist.all_gather_object(handles, g.handle, group=self.group)
+                g.connect(handles)
             dist.barrier(group=self.group)
 
     # -- slicing ---------------------------------------------------------------
@@ -106,6 +112,11 @@ class KVHeadSharded:
                      eps: float = RMS_EPS):
         """q [t, n_heads*64], k/v [t, n_kv*64] -> full out [t, n_heads*64]."""
         t = q.shape[0]
+        if self.prefill_peers is not None and t <= self.max_prefill_tokens and q.dtype == torch.bfloat16:
+            # the tensor-core prefill stores every rank's rows into every landing zone itself
+            return self.cache.attn_prefill_allgather(self.prefill_peers, layer, q.contiguous(), k.contiguous(),
+                                                     v.contiguous(), q_gain, k_gain, pos0, theta=theta, eps=eps,
+                                                     n_heads=self.h_per)
         out = self.cache.attn_prefill(layer, self._heads(q, self.h_per, self.h0, t),
                                       self._heads(k, self.kv_per, self.kv0, t), self._heads(v, self.kv_per, self.kv0, t),
                                       q_gain, k_gain, pos0, theta=theta, eps=eps, n_heads=self.h_per)
@@ -147,4 +158,5 @@ class KVHeadSharded:
             torch.cuda.synchronize()
             dist.barrier(group=self.group)
             self.peers.close()
-            self.peers = None
+            self.prefill_peers.close()
+            self.peers = self.prefill_peers = None

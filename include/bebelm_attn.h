@@ -325,6 +325,18 @@ BEBELM_API int bebelm_attn_step_allgather(bebelm_kv* kv, bebelm_peer_group* g, i
                                           const float* q, const float* k, const float* v,
                                           const float* q_gain, const float* k_gain, float theta,
                                           float eps, size_t pos, float* out, int mem, void* stream);
+/* bebelm_attn_prefill on this rank's heads, gathered (device memory): q [t][world*n_heads*64]
+ * and k/v [t][world*n_kv_heads*64] are the full, replicated input rows (the call takes its
+ * rank's heads from them); out [t][world*n_heads*64] receives every rank's heads. The
+ * tensor-core prefill stores its output rows straight into every rank's landing zone (NVLink
+ * stores from the kernel's epilogue, then one flag per CTA); a wait kernel and a copy into
+ * `out` follow. in_dtype BEBELM_BF16 or BEBELM_F32_TENSOR. The group's slice_floats must hold
+ * t*n_heads*64 (BEBELM_ERR_CAPACITY otherwise): make a separate group for prefill, sized for
+ * the largest chunk. */
+BEBELM_API int bebelm_attn_prefill_allgather(bebelm_kv* kv, bebelm_peer_group* g, int layer, int n_heads,
+                                             const void* q, const void* k, const void* v, int in_dtype, size_t t,
+                                             size_t pos0, const float* q_gain, const float* k_gain, float theta,
+                                             float eps, float* out, void* stream);
 /* A step plan's step (bebelm_step_plan_launch, device memory) on this rank's heads, gathered
  * the same way: out [world*n_heads*64]. The group counts its steps in device memory (the
  * epoch that picks the landing buffer and the flag count to wait for), so a CUDA graph of

@@ -1,13 +1,15 @@
-"""Fused decode + all-gather over peer memory (KV-head sharding), through the C-ABI.
+"""Fused decode / prefill + all-gather over peer memory (KV-head sharding), through the C-ABI.
 
 * world 1 (any GPU box): the landing-zone path — output CTAs store into the zone and raise
   the flag, the wait kernel copies the zone out — must give exactly the plain fused step, also
   as step-plan steps captured in a CUDA graph and replayed (the group's epoch lives on the
-  device).
+  device); the gathered tensor-core prefill must give exactly the plain prefill.
 * world 2 (needs 2 GPUs, one process each): every rank's gathered output must match the
   unsharded oracle (src/model.rs:440-451 over all 32 heads) within the decode tolerance,
   and be identical on both ranks, for host-driven steps and for step-plan steps captured in a
-  CUDA graph on both ranks and replayed. Then rank 1 skips a step between steps (no kernel in
+  CUDA graph on both ranks and replayed; a bf16 prefill gathered inside the prefill kernel
+  must be identical on both ranks and match the oracle within 2e-2. Then rank 1 skips a step
+  between steps (no kernel in
   flight) and rank 0's bounded wait must report BEBELM_ERR_TIMEOUT instead of hanging.
 """
 import multiprocessing as mp
@@ -93,6 +95,38 @@ def test_world1_graph_of_plan_steps_through_the_zone():
         g.close()
 
 
+def test_world1_gathered_prefill_equals_plain_prefill():
+    """The tensor-core prefill storing its rows into the landing zone (then the wait and the
+    copy-out) gives exactly what the plain call writes, twice in a row (both parities)."""
+    t = 700
+    qq, kk, vv, qg, kg = [x.cuda() for x in _inputs(13, t)]
+    qb, kb, vb = (x.to(torch.bfloat16) for x in (qq, kk, vv))
+    g = bb.PeerGroup(1, 0, 1024 * H * D, device=0)
+    g.connect([g.handle])
+    try:
+        for rep in range(2):
+            a = bb.Cache(n_layers=1, max_context=2048)
+            b = bb.Cache(n_layers=1, max_context=2048)
+            want = a.attn_prefill(0, qb, kb, vb, qg, kg, 0, theta=THETA)
+            got = b.attn_prefill_allgather(g, 0, qb, kb, vb, qg, kg, 0, theta=THETA)
+            b.check()
+            torch.testing.assert_close(got, want, rtol=0, atol=0)
+            ka, va = a.read(0)
+            kb_, vb_ = b.read(0)
+            assert np.array_equal(ka, kb_) and np.array_equal(va, vb_)
+            a.close()
+            b.close()
+        with pytest.raises(bb.BebelmError) as e:  # more rows than the zone holds
+            c = bb.Cache(n_layers=1, max_context=4096)
+            big = torch.zeros((1100, H * D), device="cuda", dtype=torch.bfloat16)
+            kvz = torch.zeros((1100, KVH * D), device="cuda", dtype=torch.bfloat16)
+            c.attn_prefill_allgather(g, 0, big, kvz, kvz, qg, kg, 0)
+        assert e.value.code == bb.ERR_CAPACITY
+    finally:
+        torch.cuda.synchronize()
+        g.close()
+
+
 def _free_port():
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
@@ -106,8 +140,13 @@ def _worker(rank, world, port, q):
         torch.distributed.init_process_group("nccl", rank=rank, world_size=world,
                                              device_id=torch.device("cuda", rank))
         from bebelm_b200.sharded import KVHeadSharded
-        sh = KVHeadSharded(n_layers=2, max_context=4096)
+        sh = KVHeadSharded(n_layers=2, max_context=4096, max_prefill_tokens=1024)
         assert sh.peers is not None
+        # layer 0: a bf16 prefill gathered inside the prefill kernel (peer stores from its epilogue)
+        pq, pk, pv, pqg, pkg = [x.cuda() for x in _inputs(17, 600)]
+        pre = sh.attn_prefill(0, pq.to(torch.bfloat16), pk.to(torch.bfloat16), pv.to(torch.bfloat16), pqg, pkg, 0)
+        sh.cache.check()
+        pre = pre.cpu().numpy()
         qq, kk, vv, qg, kg = [x.cuda() for x in _inputs(7, 3000 + 16)]
         sh.attn_prefill(1, qq[:3000], kk[:3000], vv[:3000], qg, kg, 0)
         outs = []
@@ -142,7 +181,7 @@ def _worker(rank, world, port, q):
             except bb.BebelmError as e:
                 status = e.code
         sh.close()
-        q.put((rank, np.stack(outs), status))
+        q.put((rank, (np.stack(outs), pre), status))
         torch.distributed.destroy_process_group()
     except Exception as e:  # surface the failure to the parent
         import traceback
@@ -166,6 +205,16 @@ def test_world2_fused_gather_matches_oracle_and_times_out_cleanly():
         p.join(timeout=120)
     for r in range(world):
         assert not isinstance(res[r][0], str), res[r][0]
+    pre = {r: res[r][0][1] for r in range(world)}
+    res = {r: (res[r][0][0], res[r][1]) for r in range(world)}
+    # the gathered bf16 prefill: identical on both ranks, and the reference arithmetic on the
+    # bf16-rounded inputs within the tensor-core tolerance
+    np.testing.assert_array_equal(pre[0], pre[1])
+    pq, pk, pv, pqg, pkg = _inputs(17, 600)
+    rb = [x.to(torch.bfloat16).float().numpy() for x in (pq, pk, pv)]
+    want_pre = oracle.attn_batch(rb[0], rb[1], rb[2], 0, pqg.numpy(), pkg.numpy(), THETA, EPS, H, KVH, D,
+                                 n_threads=oracle.max_threads())[0]
+    assert np.abs(pre[0] - want_pre).max() / np.abs(want_pre).max() <= 2e-2
 
     qq, kk, vv, qg, kg = [x.numpy() for x in _inputs(7, 3016)]
     ref = oracle.Cache(2, KVH * D)
