@@ -505,11 +505,9 @@ long long dep_slot_for(const bebelm_kv_pool* P, const bebelm_kv* kv, int layer) 
 // query is d_q (normed+roped, [n][n_heads][64]) or, for a fused step, fused->q_raw.
 // Where a fused all-gather sends the final outputs (one window only): every rank's landing zone.
 struct PeerTarget {
-    float* const* bufs;
-    unsigned long long* const* flags;
+    unsigned long long* const* bufs;  // every rank's landing zone (tagged words)
     int world, rank;
-    size_t off;
-    const unsigned long long* epoch;  // the group's device epoch word (then `off` is unused)
+    const unsigned long long* epoch;  // the group's device epoch word
 };
 
 int run_decode(bebelm_kv_pool* P, const std::vector<Window>& wins, int layer, int n_heads, const float* d_q,
@@ -592,10 +590,8 @@ int run_decode(bebelm_kv_pool* P, const std::vector<Window>& wins, int layer, in
     a.pdl = 1;
     if (peer) {
         a.peer_bufs = peer->bufs;
-        a.peer_flags = peer->flags;
         a.peer_world = peer->world;
         a.peer_rank = peer->rank;
-        a.peer_off = peer->off;
         a.peer_epoch = peer->epoch;
     }
     CUDA_TRY(launch_decode(a, s));
@@ -1147,8 +1143,7 @@ namespace {
 // are this call's, and where the gathered output goes (the landing zones of a peer group).
 struct PrefillShard {
     int q_row_heads, q_head0, kv_row_heads, kv_head0;
-    float* const* bufs;
-    unsigned long long* const* flags;
+    unsigned long long* const* bufs;
     const unsigned long long* epoch;
     int world, rank;
     size_t slice;
@@ -1178,7 +1173,6 @@ int prefill_device(bebelm_kv* kv, int layer, int n_heads, const void* dq, const 
         pa.err = P->err.d;
         if (shard) {
             pa.peer_bufs = shard->bufs;
-            pa.peer_flags = shard->flags;
             pa.peer_epoch = shard->epoch;
             pa.peer_world = shard->world;
             pa.peer_rank = shard->rank;
@@ -1423,15 +1417,16 @@ extern "C" int bebelm_attn_decode_cached_noalloc(const bebelm_kv* kv, int layer,
 }
 
 // ---------------------------------------------------------------------------
-// Fused KV-head-sharded step: decode + all-gather over peer memory (NVLink stores).
+// Fused KV-head-sharded steps: decode (or prefill) + all-gather over peer memory (NVLink stores).
 //
 // Each rank owns a landing zone allocated with cudaMalloc and exported by CUDA IPC:
-//   [flags: world x u64, padded to 256 B][parity 0: world x slice floats][parity 1: ...]
-// flags[r] counts the output-writing CTAs of source rank r over all steps; step e (1-based)
-// is complete on this rank once every flags[r] >= e * writers. Parity e&1 alternates so a
-// rank may run one step ahead of a peer that is still copying out the previous step: a
-// writer of step e+2 has already waited for every rank's step e+1 signals, which each rank
-// issues only after (stream order) its own copy-out of step e.
+//   [256-byte header, unused][parity 0: world x slice words][parity 1: world x slice words]
+// A word is 8 bytes: the step's tag (low 32 bits of its epoch) above a float's bits. Step e
+// writes parity e&1 of every rank's zone with plain stores; a rank's gather kernel polls its own
+// zone until every word carries tag e, copies the floats out and advances the epoch (a device
+// word, so a captured graph of steps replays unchanged). A rank may run one step ahead of a peer
+// that is still copying out: a writer of step e+2 has seen every rank's step e+1 words, which a
+// rank writes only after (stream order) its own copy-out of step e.
 // ---------------------------------------------------------------------------
 constexpr int kMaxPeers = 32;  // flags fit the 256-byte header
 
@@ -1440,33 +1435,27 @@ struct bebelm_peer_group {
     size_t slice = 0;  // floats per rank per parity
     char* zone = nullptr;
     char* peer_base[kMaxPeers] = {};  // opened IPC mappings (own entry: zone)
-    DevBuf tables;                    // float* bufs[world], u64* flags[world], then the epoch word
+    DevBuf tables;                    // u64* bufs[world], the epoch word, the gather's done counter
     bool connected = false;
-    size_t zone_bytes() const { return 256 + 2 * (size_t)world * slice * sizeof(float); }
-    float* const* d_bufs() const { return tables.as<float* const>(); }
-    unsigned long long* const* d_flags() const {
-        return reinterpret_cast<unsigned long long* const*>(tables.as<char>() + sizeof(void*) * world);
-    }
-    // Steps completed on this rank, in device memory: a decode step is epoch + 1; its wait kernel
+    size_t zone_bytes() const { return 256 + 2 * (size_t)world * slice * sizeof(unsigned long long); }
+    unsigned long long* const* d_bufs() const { return tables.as<unsigned long long* const>(); }
+    // Steps completed on this rank, in device memory: a step is epoch + 1; its gather kernel
     // stores that back once the gathered output is copied out. Keeping it on the device lets a
     // captured graph of steps replay without any launch argument changing.
     unsigned long long* d_epoch() const {
-        return reinterpret_cast<unsigned long long*>(tables.as<char>() + 2 * sizeof(void*) * world);
+        return reinterpret_cast<unsigned long long*>(tables.as<char>() + sizeof(void*) * world);
     }
+    unsigned* d_done() const { return reinterpret_cast<unsigned*>(d_epoch() + 1); }
+    const unsigned long long* local_zone() const { return reinterpret_cast<const unsigned long long*>(zone + 256); }
 };
 
 namespace {
 
-// The wait kernel that follows a decode step whose CTAs store into the landing zones: it
-// waits for every rank's writers of this step and copies the gathered [world][slice] out.
-int peer_gather_out(const bebelm_peer_group* g, bebelm_kv_pool* P, int n_heads, float* dout, cudaStream_t s) {
-    // output-writing CTAs per rank: one per (kv head, head subgroup); every rank has the same shape
-    int hpc, n_sub;
-    pick_heads_per_cta(n_heads / P->n_kv, &hpc, &n_sub);
-    const unsigned long long writers = (unsigned long long)P->n_kv * n_sub;
-    const float* land = reinterpret_cast<const float*>(g->zone + 256);
-    CUDA_TRY(launch_peer_wait(reinterpret_cast<const unsigned long long*>(g->zone), g->world, 0, land, dout,
-                              (size_t)g->world * g->slice, P->err.d, g->d_epoch(), writers, s));
+// The gather kernel that follows a decode step whose CTAs store into the landing zones: it
+// waits for every rank's words of this step and copies the gathered [world][slice] out.
+int peer_gather_out(const bebelm_peer_group* g, bebelm_kv_pool* P, float* dout, cudaStream_t s) {
+    CUDA_TRY(launch_gather_ll(g->local_zone(), g->d_epoch(), g->d_done(), g->world, g->slice, 1, g->slice, dout,
+                              P->err.d, s));
     return 0;
 }
 
@@ -1537,12 +1526,9 @@ int bebelm_peer_group_connect(bebelm_peer_group* g, const void* handles) {
         }
         g->peer_base[r] = static_cast<char*>(p);
     }
-    std::vector<void*> tab(2 * (size_t)g->world);
-    for (int r = 0; r < g->world; ++r) {
-        tab[r] = g->peer_base[r] + 256;
-        tab[g->world + r] = g->peer_base[r];
-    }
-    TRY(g->tables.ensure(sizeof(void*) * tab.size() + sizeof(unsigned long long), true));
+    std::vector<void*> tab((size_t)g->world);
+    for (int r = 0; r < g->world; ++r) tab[r] = g->peer_base[r] + 256;
+    TRY(g->tables.ensure(sizeof(void*) * tab.size() + 2 * sizeof(unsigned long long), true));
     CUDA_TRY(cudaMemcpy(g->tables.p, tab.data(), sizeof(void*) * tab.size(), cudaMemcpyHostToDevice));
     CUDA_TRY(cudaDeviceSynchronize());  // the zeroed epoch word too
     g->connected = true;
@@ -1590,9 +1576,9 @@ int bebelm_attn_step_allgather(bebelm_kv* kv, bebelm_peer_group* g, int layer, i
     TRY(reserve(kv, layer, 1, &slot0, s));
     const FusedStep fs{dq, dk, dv, dqg, dkg, theta_scale_of(theta, kHeadDim), eps};
     std::vector<Window> w{{kv, kv->base[layer], kv->len[layer], slot0, (long long)pos}};
-    const PeerTarget pt{g->d_bufs(), g->d_flags(), g->world, g->rank, 0, g->d_epoch()};
+    const PeerTarget pt{g->d_bufs(), g->world, g->rank, g->d_epoch()};
     TRY(run_decode(P, w, layer, n_heads, nullptr, dout, 0.125f, &fs, s, &pt));
-    TRY(peer_gather_out(g, P, n_heads, dout, s));
+    TRY(peer_gather_out(g, P, dout, s));
     if (mem == BEBELM_MEM_HOST) return stage_out(P, dout, out, 4 * full, s);
     return 0;
 }
@@ -1617,15 +1603,11 @@ int bebelm_attn_prefill_allgather(bebelm_kv* kv, bebelm_peer_group* g, int layer
     DeviceGuard dg(P->device);
     cudaStream_t s = as_stream(stream);
     const PrefillShard sh{n_heads * g->world, n_heads * g->rank, P->n_kv * g->world, P->n_kv * g->rank,
-                          g->d_bufs(), g->d_flags(), g->d_epoch(), g->world, g->rank, g->slice};
+                          g->d_bufs(), g->d_epoch(), g->world, g->rank, g->slice};
     TRY(prefill_device(kv, layer, n_heads, q, k, v, in_dtype == BEBELM_BF16, true, t, pos0, q_gain, k_gain, theta,
                        eps, nullptr, s, &sh));
-    // every rank's prefill grid has the same shape: its CTAs are the writers of each rank
-    const unsigned long long writers = (unsigned long long)n_heads * ((((t + 127) / 128) + 1) / 2);
-    CUDA_TRY(launch_peer_wait(reinterpret_cast<const unsigned long long*>(g->zone), g->world, 0, nullptr, nullptr, 0,
-                              P->err.d, g->d_epoch(), writers, s));
-    CUDA_TRY(launch_gather_rows(reinterpret_cast<const float*>(g->zone + 256), g->d_epoch(), g->world, g->slice, t,
-                                row, out, s));
+    CUDA_TRY(launch_gather_ll(g->local_zone(), g->d_epoch(), g->d_done(), g->world, g->slice, t, row, out, P->err.d,
+                              s));
     return 0;
 }
 
@@ -1797,7 +1779,6 @@ int plan_launch(bebelm_step_plan* pl, const bebelm_peer_group* grp, const float*
         // as between two plain plans, this plan's own previous step is complete when this grid
         // starts, and step_prewait (decided above) holds as it stands.
         a.peer_bufs = grp->d_bufs();
-        a.peer_flags = grp->d_flags();
         a.peer_world = grp->world;
         a.peer_rank = grp->rank;
         a.peer_epoch = grp->d_epoch();
@@ -1806,7 +1787,7 @@ int plan_launch(bebelm_step_plan* pl, const bebelm_peer_group* grp, const float*
     record_decode_out(as_stream(stream), a.out, grp ? SIZE_MAX : (size_t)pl->n_heads * kHeadDim * 4);
     P->last_plan = pl;
     P->last_capture = cap_id;
-    if (grp) TRY(peer_gather_out(grp, P, pl->n_heads, out, as_stream(stream)));
+    if (grp) TRY(peer_gather_out(grp, P, out, as_stream(stream)));
     return 0;
 }
 

@@ -139,37 +139,25 @@ __device__ __forceinline__ void fma2(float& c0, float& c1, float a0, float a1, f
     }
 }
 
-// Final output element `idx` (head*64 + d) of sequence `seq`: to `out`, or, for the fused
-// all-gather, to this rank's slice of every rank's landing zone (NVLink stores to peers).
-// The landing-zone parity offset of this step: from the device epoch word when the group keeps
-// one (read after griddepcontrol.wait: the previous step's wait kernel advanced it), else the
-// launch argument.
-__device__ __forceinline__ size_t peer_offset(const DecodeArgs& a) {
-    if (!a.peer_epoch) return a.peer_off;
-    const unsigned long long e = *reinterpret_cast<const volatile unsigned long long*>(a.peer_epoch) + 1ull;
-    return (size_t)(e & 1ull) * a.peer_world * a.n_heads * kHeadDim;
+// This step's epoch for the fused all-gather: one more than the group's device word (read after
+// griddepcontrol.wait: the previous step's gather kernel advanced it). Its parity picks the
+// landing buffer; its low 32 bits tag every element written there.
+__device__ __forceinline__ unsigned long long peer_step(const DecodeArgs& a) {
+    return *reinterpret_cast<const volatile unsigned long long*>(a.peer_epoch) + 1ull;
 }
 
-__device__ __forceinline__ void emit_out(const DecodeArgs& a, int seq, size_t idx, float v, size_t poff) {
+// Final output element `idx` (head*64 + d) of sequence `seq`: to `out`, or, for the fused
+// all-gather, into this rank's slice of every rank's landing zone as one 8-byte word (the
+// step's tag above the float's bits), stored over NVLink: a reader knows the value has arrived
+// when it sees the tag, so no fence or flag follows the stores.
+__device__ __forceinline__ void emit_out(const DecodeArgs& a, int seq, size_t idx, float v, unsigned long long pe) {
     if (a.peer_world > 0) {
-        const size_t off = poff + (size_t)a.peer_rank * a.n_heads * kHeadDim + idx;
-        for (int w = 0; w < a.peer_world; ++w) a.peer_bufs[w][off] = v;
+        const size_t off = ((size_t)(pe & 1ull) * a.peer_world + a.peer_rank) * a.n_heads * kHeadDim + idx;
+        const unsigned long long word = (pe << 32) | __float_as_uint(v);
+        for (int w = 0; w < a.peer_world; ++w)
+            asm volatile("st.volatile.global.u64 [%0], %1;" ::"l"(a.peer_bufs[w] + off), "l"(word) : "memory");
     } else {
         a.out[(size_t)seq * a.n_heads * kHeadDim + idx] = v;
-    }
-}
-
-// After a CTA has emitted its outputs to the landing zones: make them visible system-wide,
-// then count this CTA once on every rank's flag for this source rank (release, system scope).
-__device__ __forceinline__ void signal_peers(const DecodeArgs& a) {
-    if (a.peer_world <= 0) return;
-    __threadfence_system();
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        for (int w = 0; w < a.peer_world; ++w) {
-            unsigned long long* f = a.peer_flags[w] + a.peer_rank;
-            asm volatile("red.release.sys.global.add.u64 [%0], %1;" ::"l"(f), "l"(1ull) : "memory");
-        }
     }
 }
 
@@ -374,7 +362,7 @@ __global__ void __launch_bounds__(kThreads, 2) decode_kernel(DecodeArgs a) {
     // ---- everything below may read what the predecessor wrote --------------
     grid_dep_wait();
     DTRACE(1);
-    const size_t poff = a.peer_world > 0 ? peer_offset(a) : 0;
+    const unsigned long long pe = a.peer_world > 0 ? peer_step(a) : 0ull;
     if (tid == 0)
         for (int i = n_early; i < n_first; ++i) issue(i);
     if (!early) read_inputs();
@@ -450,19 +438,6 @@ __global__ void __launch_bounds__(kThreads, 2) decode_kernel(DecodeArgs a) {
             return reinterpret_cast<const float4*>(base)[idx];
         };
         const long long slot0 = (p0 + i) << 6;
-#ifdef BEBELM_DECODE_NOCOMPUTE
-        __syncwarp();
-        if (lane == 0 && atomicAdd(&s_release[st], 1) == 3) {
-            s_release[st] = 0;
-            if (i + NST < np) {
-                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-                issue(i + NST);
-                if (i + NST + kPrefetch < np) prefetch(i + NST + kPrefetch);
-            }
-        }
-        acc[0][0] += ld4(Kst, lane).x;
-        continue;
-#endif
         // both rows of K and V into registers, then hand the stage back at once
         float4 kk[2][4], vv[2][4];
 #pragma unroll
@@ -601,7 +576,7 @@ __global__ void __launch_bounds__(kThreads, 2) decode_kernel(DecodeArgs a) {
             }
         }
         if (single) {
-            emit_out(a, seq, (size_t)(h0 + h) * kHeadDim + d, L > 0.f ? A / L : 0.f, poff);
+            emit_out(a, seq, (size_t)(h0 + h) * kHeadDim + d, L > 0.f ? A / L : 0.f, pe);
         } else {
             const size_t pi = ((size_t)gsplit * NY + y) * HPC + h;
             a.part_acc[pi * kHeadDim + d] = A;
@@ -612,7 +587,6 @@ __global__ void __launch_bounds__(kThreads, 2) decode_kernel(DecodeArgs a) {
         }
     }
     if (single) {
-        signal_peers(a);
         step_done(a);
         DTRACE(4);
         return;
@@ -706,9 +680,8 @@ __global__ void __launch_bounds__(kThreads, 2) decode_kernel(DecodeArgs a) {
         float A = 0.f;
         for (int g = 0; g < G; ++g) A += sm_acc[g * HPC * kHeadDim + o];
         const float L = s_L[o / kHeadDim];
-        emit_out(a, seq, (size_t)h0 * kHeadDim + o, L > 0.f ? A / L : 0.f, poff);
+        emit_out(a, seq, (size_t)h0 * kHeadDim + o, L > 0.f ? A / L : 0.f, pe);
     }
-    signal_peers(a);
     step_done(a);
     DTRACE(4);
 }
@@ -737,47 +710,50 @@ cudaError_t launch_hpc(const DecodeArgs& a, cudaStream_t s) {
     return cudaLaunchKernelEx(&cfg, decode_kernel<HPC, KT>, a);
 }
 
-__global__ void peer_wait_kernel(const unsigned long long* flags, int world, unsigned long long expected,
-                                 const float* src, float* dst, size_t n, int* err, unsigned long long* epoch,
-                                 unsigned long long writers) {
-    __shared__ int s_ok;
+// The gather of a fused all-gather step: every element of the landing buffer of this step's
+// parity, [world][rows][row_elems] tagged words, copied into dst [rows][world * row_elems] once
+// its tag is this step's (bounded polling: a value that does not arrive records kErrWaitTimeout
+// and the rest is skipped). The last CTA to finish advances the group's epoch. It lets its
+// dependents launch at once: the next decode grid (a programmatic dependent) starts its prologue
+// and first page copies meanwhile, and reads this grid's output only after its own wait.
+__global__ void gather_ll_kernel(const unsigned long long* __restrict__ zone, unsigned long long* epoch,
+                                 unsigned* done, int world, size_t slice, size_t rows, size_t row_elems,
+                                 float* __restrict__ dst, int* err) {
     __shared__ unsigned long long s_e;
-    // the next decode grid (a programmatic dependent) may start its prologue — page-table loads,
-    // its first page copies — while this one waits for the peers; it reads this grid's output
-    // only after its own griddepcontrol.wait
     grid_dep_launch();
-    if (threadIdx.x == 0) {
-        s_ok = 1;
-        s_e = epoch ? *reinterpret_cast<volatile unsigned long long*>(epoch) + 1ull : 0ull;
-    }
+    if (threadIdx.x == 0) s_e = *reinterpret_cast<volatile unsigned long long*>(epoch) + 1ull;
     __syncthreads();
-    if (epoch) {  // this step's epoch from the device word: the expected count and the parity
-        expected = s_e * writers;
-        src += (size_t)(s_e & 1ull) * n;
-    }
-    if ((int)threadIdx.x < world) {
-        bool ok = false;
-        for (long long it = 0; it < kWaitLimit; ++it) {
-            unsigned long long v;
-            asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(flags + threadIdx.x) : "memory");
-            if (v >= expected) {
-                ok = true;
+    const unsigned long long e = s_e;
+    const unsigned tag = (unsigned)e;
+    const unsigned long long* base = zone + (size_t)(e & 1ull) * world * slice;
+    const size_t rp = row_elems / 2, per_w = rows * rp, pairs = (size_t)world * per_w;
+    long long budget = kWaitLimit;
+    bool bad = false;
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < pairs && !bad;
+         i += (size_t)gridDim.x * blockDim.x) {
+        const size_t w = i / per_w, rem = i % per_w, r = rem / rp, c = rem % rp;
+        const unsigned long long* src = base + w * slice + r * row_elems + 2 * c;
+        unsigned long long v0, v1;
+        for (;;) {
+            asm volatile("ld.volatile.global.v2.u64 {%0, %1}, [%2];" : "=l"(v0), "=l"(v1) : "l"(src) : "memory");
+            if ((unsigned)(v0 >> 32) == tag && (unsigned)(v1 >> 32) == tag) break;
+            if (--budget <= 0) {
+                bad = true;
                 break;
             }
-            __nanosleep(128);
         }
-        if (!ok) {
-            atomicExch(&s_ok, 0);
-            *reinterpret_cast<volatile int*>(err) = kErrWaitTimeout;
-        }
+        if (!bad)
+            reinterpret_cast<float2*>(dst)[(r * world + w) * rp + c] =
+                make_float2(__uint_as_float((unsigned)v0), __uint_as_float((unsigned)v1));
     }
+    if (bad) *reinterpret_cast<volatile int*>(err) = kErrWaitTimeout;
     __syncthreads();
-    if (s_ok)
-        for (size_t i = threadIdx.x; i < n; i += blockDim.x) dst[i] = __ldcv(src + i);  // written by peers
-    // the step is over on this rank (copied out, or failed and reported): the next one may begin
-    if (epoch) {
-        __syncthreads();
-        if (threadIdx.x == 0) *reinterpret_cast<volatile unsigned long long*>(epoch) = s_e;
+    if (threadIdx.x == 0) {  // the step is over on this rank once every CTA is: the next may begin
+        __threadfence();
+        if (atomicAdd(done, 1u) == gridDim.x - 1) {
+            *done = 0u;
+            *reinterpret_cast<volatile unsigned long long*>(epoch) = e;
+        }
     }
 }
 
@@ -791,26 +767,13 @@ __global__ void stage_copy_kernel(const uint4* __restrict__ src, uint4* __restri
         dst[i] = src[i];
 }
 
-__global__ void gather_rows_kernel(const float* __restrict__ zone, const unsigned long long* epoch, int world,
-                                   size_t slice, size_t rows, size_t row_floats, float* __restrict__ dst) {
-    const unsigned long long e = *reinterpret_cast<const volatile unsigned long long*>(epoch);
-    const float4* src = reinterpret_cast<const float4*>(zone + (size_t)(e & 1ull) * world * slice);
-    const size_t rq = row_floats / 4, total = (size_t)world * rows * rq;
-    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
-        const size_t w = i / (rows * rq), rem = i % (rows * rq), r = rem / rq, c = rem % rq;
-        reinterpret_cast<float4*>(dst)[(r * world + w) * rq + c] =
-            __ldcv(reinterpret_cast<const float4*>(reinterpret_cast<const float*>(src) + w * slice) + r * rq + c);
-    }
-}
-
 }  // namespace
 
-cudaError_t launch_gather_rows(const float* zone, const unsigned long long* epoch, int world, size_t slice,
-                               size_t rows, size_t row_floats, float* dst, cudaStream_t s) {
-    const size_t total = (size_t)world * rows * (row_floats / 4);
-    if (!total) return cudaSuccess;
-    const unsigned blocks = (unsigned)std::min<size_t>((total + 255) / 256, 148 * 8);
-    gather_rows_kernel<<<blocks, 256, 0, s>>>(zone, epoch, world, slice, rows, row_floats, dst);
+cudaError_t launch_gather_ll(const unsigned long long* zone, unsigned long long* epoch, unsigned* done, int world,
+                             size_t slice, size_t rows, size_t row_elems, float* dst, int* err, cudaStream_t s) {
+    const size_t pairs = (size_t)world * rows * (row_elems / 2);
+    const unsigned blocks = (unsigned)std::max<size_t>(1, std::min<size_t>((pairs + 1023) / 1024, 148 * 4));
+    gather_ll_kernel<<<blocks, 256, 0, s>>>(zone, epoch, done, world, slice, rows, row_elems, dst, err);
     return cudaGetLastError();
 }
 
@@ -819,13 +782,6 @@ cudaError_t launch_stage_copy(void* dst, const void* src_mapped, size_t bytes, c
     if (!n16) return cudaSuccess;
     const unsigned blocks = (unsigned)std::min<size_t>(16, (n16 + 255) / 256);
     stage_copy_kernel<<<blocks, 256, 0, s>>>(static_cast<const uint4*>(src_mapped), static_cast<uint4*>(dst), n16);
-    return cudaGetLastError();
-}
-
-cudaError_t launch_peer_wait(const unsigned long long* flags, int world, unsigned long long expected, const float* src,
-                             float* dst, size_t n, int* err, unsigned long long* epoch, unsigned long long writers,
-                             cudaStream_t s) {
-    peer_wait_kernel<<<1, 256, 0, s>>>(flags, world, expected, src, dst, n, err, epoch, writers);
     return cudaGetLastError();
 }
 

@@ -199,13 +199,11 @@ struct DecodeArgs {
     float scale_log2;       // score scale (1/sqrt(head_dim)) times log2(e)
     int pdl;                // launched as a programmatic dependent of the previous kernel
     // fused all-gather (KV-head sharding): when peer_world > 0 the final output of sequence 0
-    // goes to every rank's landing zone instead of `out`, at [peer_off + peer_rank*n_heads*64 +
-    // head*64 + d], and each writing CTA then bumps peer_flags[w][peer_rank] on every rank w
-    float* const* peer_bufs;
-    unsigned long long* const* peer_flags;
+    // goes to every rank's landing zone instead of `out`, as tagged words (tag = the step's
+    // epoch, see peer_epoch) at [(parity * peer_world + peer_rank) * n_heads*64 + head*64 + d]
+    unsigned long long* const* peer_bufs;
     int peer_world, peer_rank;
-    size_t peer_off;
-    // device epoch word of the group (non-null: the parity offset follows it, peer_off unused)
+    // device epoch word of the group: this step is *peer_epoch + 1
     const unsigned long long* peer_epoch;
     // step plan (one sequence): non-null step makes the window of `one` follow the counter
     StepState* step;
@@ -220,22 +218,16 @@ struct DecodeArgs {
     // before griddepcontrol.wait; only the cache store of the new token waits
     int early_inputs;
 };
-// Waits (bounded) until flags[r] >= expected for every source rank r, then copies n floats of
-// the gathered landing buffer to dst. On timeout it records kErrWaitTimeout and copies nothing.
-// With `epoch` (the group's device epoch word) the step is e = *epoch + 1: expected becomes
-// e * writers, src the parity (e & 1) buffer that follows src, and the kernel stores e back
-// when done, so a replayed graph of steps advances on its own.
-cudaError_t launch_peer_wait(const unsigned long long* flags, int world, unsigned long long expected, const float* src,
-                             float* dst, size_t n, int* err, unsigned long long* epoch, unsigned long long writers,
-                             cudaStream_t s);
+// The gather of a fused all-gather step (a landing zone of tagged words, see DecodeArgs): waits
+// (bounded) for every element of this step's parity to carry this step's tag, copies them into
+// dst [rows][world * row_elems], and advances *epoch (the last CTA; `done` counts them).
+cudaError_t launch_gather_ll(const unsigned long long* zone, unsigned long long* epoch, unsigned* done, int world,
+                             size_t slice, size_t rows, size_t row_elems, float* dst, int* err, cudaStream_t s);
 cudaError_t launch_decode(const DecodeArgs& a, cudaStream_t s);
 // Copies `bytes` (a multiple of 16) from mapped pinned memory to device memory on s, letting
 // the next kernel launch as a programmatic dependent right away.
 cudaError_t launch_stage_copy(void* dst, const void* src_mapped, size_t bytes, cudaStream_t s);
-// After a gathered prefill's wait: copies the landing zone's parity (*epoch & 1), laid out
-// [world][rows][row_floats], into dst [rows][world * row_floats] (rank = column block).
-cudaError_t launch_gather_rows(const float* zone, const unsigned long long* epoch, int world, size_t slice,
-                               size_t rows, size_t row_floats, float* dst, cudaStream_t s);
+
 size_t decode_smem_bytes();
 constexpr int kDecodeMaxPagesPerSplit = 256;
 
@@ -249,11 +241,9 @@ struct PrefillArgs {
     float scale_log2;        // score scale times log2(e)
     int* err;
     // fused all-gather (KV-head sharding): with peer_world > 0 the output rows go to every
-    // rank's landing zone instead of `out`: [parity e&1][peer_rank][t][n_heads][64] floats, parity
-    // from the group's device epoch (e = *peer_epoch + 1), peer_slice floats per rank; each CTA
-    // then bumps peer_flags[w][peer_rank] on every rank w
-    float* const* peer_bufs;
-    unsigned long long* const* peer_flags;
+    // rank's landing zone instead of `out`, as tagged words (see DecodeArgs):
+    // [parity e&1][peer_rank][t][n_heads][64], e = *peer_epoch + 1, peer_slice words per rank
+    unsigned long long* const* peer_bufs;
     const unsigned long long* peer_epoch;
     int peer_world, peer_rank;
     size_t peer_slice;

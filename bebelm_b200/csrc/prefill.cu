@@ -571,15 +571,21 @@ __global__ void __launch_bounds__(kCtaThreads, 1)
             if (qi < a.t) {
                 const float inv = l > 0.f ? 1.f / l : 0.f;
                 const size_t row = ((size_t)qi * a.n_heads + h) * kHeadDim;
-                if (a.peer_world > 0) {  // this rank's rows into every rank's landing zone (NVLink stores)
+                if (a.peer_world > 0) {
+                    // this rank's rows into every rank's landing zone over NVLink, each value in an
+                    // 8-byte word tagged with the step's epoch: a reader polls the words themselves
                     const unsigned long long e =
                         *reinterpret_cast<const volatile unsigned long long*>(a.peer_epoch) + 1ull;
                     const size_t off = ((size_t)(e & 1ull) * a.peer_world + a.peer_rank) * a.peer_slice + row;
+                    const unsigned long long tag = e << 32;
                     for (int w = 0; w < a.peer_world; ++w) {
-                        float4* dst = reinterpret_cast<float4*>(a.peer_bufs[w] + off);
+                        unsigned long long* dst = a.peer_bufs[w] + off;
 #pragma unroll
-                        for (int d = 0; d < kHeadDim; d += 4)
-                            dst[d / 4] = make_float4(o[d] * inv, o[d + 1] * inv, o[d + 2] * inv, o[d + 3] * inv);
+                        for (int d = 0; d < kHeadDim; d += 2)
+                            asm volatile("st.volatile.global.v2.u64 [%0], {%1, %2};" ::"l"(dst + d),
+                                         "l"(tag | __float_as_uint(o[d] * inv)),
+                                         "l"(tag | __float_as_uint(o[d + 1] * inv))
+                                         : "memory");
                     }
                 } else {
                     float4* dst = reinterpret_cast<float4*>(a.out + row);
@@ -592,12 +598,7 @@ __global__ void __launch_bounds__(kCtaThreads, 1)
     }
 
     tc_fence_before();
-    if (a.peer_world > 0) __threadfence_system();  // the zone stores are visible before the flags move
     __syncthreads();
-    if (a.peer_world > 0 && !s_fail && tid == 0)  // this CTA's rows are in every zone
-        for (int w = 0; w < a.peer_world; ++w)
-            asm volatile("red.release.sys.global.add.u64 [%0], %1;" ::"l"(a.peer_flags[w] + a.peer_rank), "l"(1ull)
-                         : "memory");
     if (s_fail && tid == 0) {
         *reinterpret_cast<volatile int*>(a.err) = kErrWaitTimeout;
         // let copies and MMAs this CTA started land (bounded) before its memory goes away

@@ -3,13 +3,13 @@
 * :class:`KVHeadSharded` — KV-head sharding. Rank r of N owns kv heads
   [8r/N, 8(r+1)/N) and their query heads [32r/N, 32(r+1)/N) for every attention
   layer; its cache holds only those heads, so each rank reads 1/N of the KV bytes.
-  After the local prefill the head outputs are all-gathered over NCCL; a decode
-  step instead gathers inside its kernel (``fused_gather``): the CTAs that finish
-  each head store it into every rank's landing zone over NVLink and raise a flag
-  there (:class:`bebelm_b200.PeerGroup`). Rank order is head order, so the
-  gathered buffer is the full
-  [n_heads*64] (or [t, n_heads*64]) output of ``attn_step`` / ``attn_batch``
-  (src/model.rs:440-451, 232-254).
+  The head outputs are gathered inside the kernels (``fused_gather``): the CTAs
+  that finish a head (decode) or a tile of query rows (tensor-core prefill) store
+  it into every rank's landing zone over NVLink as words tagged with the step's
+  number, which the receiving rank polls (:class:`bebelm_b200.PeerGroup`); other
+  prefills all-gather over NCCL. Rank order is head order, so the gathered buffer
+  is the full [n_heads*64] (or [t, n_heads*64]) output of ``attn_step`` /
+  ``attn_batch`` (src/model.rs:440-451, 232-254).
 * :func:`assign_sequences` — per-sequence sharding for independent Agent
   sequences: longest-processing-time assignment of sequences to ranks by KV
   length. No collective is needed; each rank runs batched decode on its share.

@@ -300,8 +300,10 @@ BEBELM_API int bebelm_step_plan_launch_layer(bebelm_step_plan* plan, const float
  * query heads, and the full [world * n_heads * 64] output of the step lands
  * on every rank without a separate collective: the kernel's output-writing
  * CTAs store their heads straight into every rank's landing zone (peer
- * stores over NVLink) and raise a per-source flag there; a one-block kernel
- * then waits (bounded) for all ranks' flags and copies the zone out.
+ * stores over NVLink), each value in an 8-byte word tagged with the step's
+ * number; a one-block kernel then polls its own zone (bounded) until every
+ * word carries this step's tag and copies the values out. No fence or flag
+ * sits between the stores and the reader.
  *
  * Setup is collective: every rank calls bebelm_peer_group_create (which
  * allocates its zone and writes a BEBELM_IPC_HANDLE_BYTES handle), the caller
@@ -329,8 +331,8 @@ BEBELM_API int bebelm_attn_step_allgather(bebelm_kv* kv, bebelm_peer_group* g, i
  * and k/v [t][world*n_kv_heads*64] are the full, replicated input rows (the call takes its
  * rank's heads from them); out [t][world*n_heads*64] receives every rank's heads. The
  * tensor-core prefill stores its output rows straight into every rank's landing zone (NVLink
- * stores from the kernel's epilogue, then one flag per CTA); a wait kernel and a copy into
- * `out` follow. in_dtype BEBELM_BF16 or BEBELM_F32_TENSOR. The group's slice_floats must hold
+ * stores of tagged words from the kernel's epilogue); a gather kernel polls the tags and
+ * copies the rows into `out`. in_dtype BEBELM_BF16 or BEBELM_F32_TENSOR. The group's slice_floats must hold
  * t*n_heads*64 (BEBELM_ERR_CAPACITY otherwise): make a separate group for prefill, sized for
  * the largest chunk. */
 BEBELM_API int bebelm_attn_prefill_allgather(bebelm_kv* kv, bebelm_peer_group* g, int layer, int n_heads,
@@ -339,7 +341,7 @@ BEBELM_API int bebelm_attn_prefill_allgather(bebelm_kv* kv, bebelm_peer_group* g
                                              float eps, float* out, void* stream);
 /* A step plan's step (bebelm_step_plan_launch, device memory) on this rank's heads, gathered
  * the same way: out [world*n_heads*64]. The group counts its steps in device memory (the
- * epoch that picks the landing buffer and the flag count to wait for), so a CUDA graph of
+ * epoch that picks the landing buffer and tags the words), so a CUDA graph of
  * these steps, captured once on every rank, replays with no host work. Every rank's plans
  * must step in the same order, and replays must be launched on all ranks. */
 BEBELM_API int bebelm_step_plan_launch_allgather(bebelm_step_plan* plan, bebelm_peer_group* g,

@@ -142,11 +142,6 @@ def _worker(rank, world, port, q):
         from bebelm_b200.sharded import KVHeadSharded
         sh = KVHeadSharded(n_layers=2, max_context=4096, max_prefill_tokens=1024)
         assert sh.peers is not None
-        # layer 0: a bf16 prefill gathered inside the prefill kernel (peer stores from its epilogue)
-        pq, pk, pv, pqg, pkg = [x.cuda() for x in _inputs(17, 600)]
-        pre = sh.attn_prefill(0, pq.to(torch.bfloat16), pk.to(torch.bfloat16), pv.to(torch.bfloat16), pqg, pkg, 0)
-        sh.cache.check()
-        pre = pre.cpu().numpy()
         qq, kk, vv, qg, kg = [x.cuda() for x in _inputs(7, 3000 + 16)]
         sh.attn_prefill(1, qq[:3000], kk[:3000], vv[:3000], qg, kg, 0)
         outs = []
@@ -170,6 +165,11 @@ def _worker(rank, world, port, q):
         plan.finish()
         sh.cache.check()
         outs += list(gout.cpu().numpy())
+        # layer 0: a bf16 prefill gathered inside the prefill kernel (peer stores from its epilogue)
+        pq, pk, pv, pqg, pkg = [x.cuda() for x in _inputs(17, 600)]
+        pre = sh.attn_prefill(0, pq.to(torch.bfloat16), pk.to(torch.bfloat16), pv.to(torch.bfloat16), pqg, pkg, 0)
+        sh.cache.check()
+        pre = pre.cpu().numpy()
         # rank 1 leaves between steps; rank 0's next step must time out, not hang
         status = None
         if rank == 0:
