@@ -45,9 +45,10 @@ __global__ void __launch_bounds__(256) norm_rope_kernel(NormRopeArgs a) {
 
     const int hd = HD64 ? 64 : a.head_dim;
     const int half = hd >> 1;
-    const int tok = (int)(item / nh_all);
+    // 32-bit division (a launch holds fewer than 2^31 head items; 64-bit division is emulated)
+    const int tok = (int)((unsigned)item / (unsigned)nh_all);
 
-    const int hh = (int)(item % nh_all);
+    const int hh = (int)((unsigned)item - (unsigned)tok * (unsigned)nh_all);
     const bool is_q = hh < a.n_heads;
     const int head = is_q ? hh : hh - a.n_heads;
     const int q_row = a.q_row_heads ? a.q_row_heads : a.n_heads, kv_row = a.kv_row_heads ? a.kv_row_heads : a.n_kv;
@@ -101,12 +102,12 @@ __global__ void __launch_bounds__(256) norm_rope_kernel(NormRopeArgs a) {
     // It does so after issuing its loads, so their latency overlaps the table.
     __shared__ float s_cos[32][32], s_sin[32][32];
     const long long item0 = (long long)blockIdx.x * (blockDim.x >> 3);
-    const int tok0 = (int)(item0 / nh_all);
+    const int tok0 = (int)((unsigned)item0 / (unsigned)nh_all);
     if (a.norm_q || a.norm_k) {
         const long long item_last = min(total - 1, item0 + (blockDim.x >> 3) - 1);
-        const int ntok = (int)(item_last / nh_all) - tok0 + 1;
+        const int ntok = (int)((unsigned)item_last / (unsigned)nh_all) - tok0 + 1;
         for (int idx = threadIdx.x; idx < ntok * half; idx += blockDim.x) {
-            const int t = idx / half, i = idx % half;
+            const int t = HD64 ? idx >> 5 : idx / half, i = HD64 ? idx & 31 : idx % half;
             const long long pos = a.targets ? a.targets[tok0 + t].pos : a.pos0 + tok0 + t;
             float theta = __ll2float_rn(pos);
             for (int r = 0; r < i; ++r) theta = __fmul_rn(theta, a.theta_scale);
@@ -269,6 +270,7 @@ cudaError_t launch_kv_gather_bf16(const PoolView& pv, const int* table, int cap,
 cudaError_t launch_norm_rope(const NormRopeArgs& a, cudaStream_t s) {
     const long long items = (long long)a.T * (a.n_heads + a.n_kv);
     if (items <= 0) return cudaSuccess;
+    if (items >= (1ll << 31)) return cudaErrorInvalidValue;  // the kernel indexes items in 32 bits
     const int heads_per_block = 256 / 8;
     const long long blocks = (items + heads_per_block - 1) / heads_per_block;
     if (a.head_dim == 64)
