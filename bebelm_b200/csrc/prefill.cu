@@ -561,38 +561,56 @@ __global__ void __launch_bounds__(kCtaThreads, 1)
         }
         // epilogue: wait for the last PV, normalise, store
         if (ok && nkt[X] > 0) ok = __all_sync(0xffffffffu, mbar_wait_bounded(bar(kBarO + X), (nkt[X] - 1) & 1));
-        if (!ok) {
-            s_fail = 1;
-        } else if (nkt[X] > 0) {
+        if (!ok) s_fail = 1;
+        if (nkt[X] > 0 && a.peer_world > 0) {
+            // Fused all-gather: the tile's rows go into every rank's landing zone over NVLink as
+            // 8-byte words tagged with the step's epoch. A thread holds one row; to make each store
+            // instruction cover whole rows (32 lanes x 8 B, one 256-byte run), the rows pass
+            // through shared memory half a row at a time (Q_X: its last MMA has completed). Every
+            // thread of the group takes part in both barriers, also after a failed wait.
+            float o[kHeadDim];
+            if (ok) {
+                tc_fence_after();
+                tmem_ld32(t_o, o);
+                tmem_ld32(t_o + 32, o + 32);
+            } else {
+#pragma unroll
+                for (int d = 0; d < kHeadDim; ++d) o[d] = 0.f;
+            }
+            const float inv = ok && l > 0.f ? 1.f / l : 0.f;
+            const unsigned long long e = *reinterpret_cast<const volatile unsigned long long*>(a.peer_epoch) + 1ull;
+            const unsigned long long tag = e << 32;
+            float* tile = reinterpret_cast<float*>(smem + kOff2Q + X * kTileBytes);  // [128 rows][32], rotated
+            const int wq = warp & 3, q0 = (2 * pair + X) * kTileQ;
+            const size_t zone0 = ((size_t)(e & 1ull) * a.peer_world + a.peer_rank) * a.peer_slice;
+#pragma unroll
+            for (int hf = 0; hf < 2; ++hf) {
+#pragma unroll
+                for (int c = 0; c < 32; ++c) tile[row * 32 + ((c + row) & 31)] = o[hf * 32 + c] * inv;
+                asm volatile("bar.sync %0, 128;" ::"r"(1 + X) : "memory");
+                for (int r = 0; r < 32; ++r) {
+                    const int rr = wq * 32 + r;
+                    if (q0 + rr < a.t) {
+                        const unsigned long long word = tag | __float_as_uint(tile[rr * 32 + ((lane + rr) & 31)]);
+                        const size_t off = zone0 + ((size_t)(q0 + rr) * a.n_heads + h) * kHeadDim + hf * 32 + lane;
+                        for (int w = 0; w < a.peer_world; ++w)
+                            asm volatile("st.volatile.global.u64 [%0], %1;" ::"l"(a.peer_bufs[w] + off), "l"(word)
+                                         : "memory");
+                    }
+                }
+                asm volatile("bar.sync %0, 128;" ::"r"(1 + X) : "memory");
+            }
+        } else if (ok && nkt[X] > 0) {
             tc_fence_after();
             float o[kHeadDim];
             tmem_ld32(t_o, o);
             tmem_ld32(t_o + 32, o + 32);
             if (qi < a.t) {
                 const float inv = l > 0.f ? 1.f / l : 0.f;
-                const size_t row = ((size_t)qi * a.n_heads + h) * kHeadDim;
-                if (a.peer_world > 0) {
-                    // this rank's rows into every rank's landing zone over NVLink, each value in an
-                    // 8-byte word tagged with the step's epoch: a reader polls the words themselves
-                    const unsigned long long e =
-                        *reinterpret_cast<const volatile unsigned long long*>(a.peer_epoch) + 1ull;
-                    const size_t off = ((size_t)(e & 1ull) * a.peer_world + a.peer_rank) * a.peer_slice + row;
-                    const unsigned long long tag = e << 32;
-                    for (int w = 0; w < a.peer_world; ++w) {
-                        unsigned long long* dst = a.peer_bufs[w] + off;
+                float4* dst = reinterpret_cast<float4*>(a.out + ((size_t)qi * a.n_heads + h) * kHeadDim);
 #pragma unroll
-                        for (int d = 0; d < kHeadDim; d += 2)
-                            asm volatile("st.volatile.global.v2.u64 [%0], {%1, %2};" ::"l"(dst + d),
-                                         "l"(tag | __float_as_uint(o[d] * inv)),
-                                         "l"(tag | __float_as_uint(o[d + 1] * inv))
-                                         : "memory");
-                    }
-                } else {
-                    float4* dst = reinterpret_cast<float4*>(a.out + row);
-#pragma unroll
-                    for (int d = 0; d < kHeadDim; d += 4)
-                        dst[d / 4] = make_float4(o[d] * inv, o[d + 1] * inv, o[d + 2] * inv, o[d + 3] * inv);
-                }
+                for (int d = 0; d < kHeadDim; d += 4)
+                    dst[d / 4] = make_float4(o[d] * inv, o[d + 1] * inv, o[d + 2] * inv, o[d + 3] * inv);
             }
         }
     }
