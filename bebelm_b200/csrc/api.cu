@@ -511,8 +511,7 @@ struct PeerTarget {
 };
 
 int run_decode(bebelm_kv_pool* P, const std::vector<Window>& wins, int layer, int n_heads, const float* d_q,
-               float* d_out, float scale, const FusedStep* fused, cudaStream_t s, const PeerTarget* peer = nullptr,
-               const InlineStep* inl = nullptr) {
+               float* d_out, float scale, const FusedStep* fused, cudaStream_t s, const PeerTarget* peer = nullptr) {
     const int n = (int)wins.size();
     if (n == 0) return 0;
     const int group = n_heads / P->n_kv;
@@ -595,7 +594,7 @@ int run_decode(bebelm_kv_pool* P, const std::vector<Window>& wins, int layer, in
         a.peer_rank = peer->rank;
         a.peer_epoch = peer->epoch;
     }
-    CUDA_TRY(launch_decode(a, s, inl));
+    CUDA_TRY(launch_decode(a, s));
     record_decode_out(s, d_out, peer ? SIZE_MAX : (size_t)n * n_heads * kHeadDim * 4);
     P->last_plan = nullptr;
     P->last_writes.clear();
@@ -1069,21 +1068,7 @@ int bebelm_attn_step(bebelm_kv* kv, int layer, int n_heads, const float* q, cons
     const size_t qn = (size_t)n_heads * kHeadDim, kvn = (size_t)P->n_kv * kHeadDim;
     const float *dq = q, *dk = k, *dv = v, *dqg = q_gain, *dkg = k_gain;
     float* dout = out;
-    // a host call of the model's size carries its inputs in the launch (no copy before the grid)
-    InlineStep* inl = nullptr;
-    thread_local InlineStep g_inline;
-    if (mem == BEBELM_MEM_HOST && qn <= (size_t)kInlineQ && kvn <= (size_t)kInlineKV) {
-        inl = &g_inline;
-        std::memcpy(inl->q, q, 4 * qn);
-        std::memcpy(inl->k, k, 4 * kvn);
-        std::memcpy(inl->v, v, 4 * kvn);
-        std::memcpy(inl->q_gain, q_gain, 4 * kHeadDim);
-        std::memcpy(inl->k_gain, k_gain, 4 * kHeadDim);
-        void* o;
-        TRY(stage_in(P, nullptr, 0, 4 * qn, &o, s));  // the output only
-        dq = inl->q; dk = inl->k; dv = inl->v; dqg = inl->q_gain; dkg = inl->k_gain;  // read from the launch
-        dout = (float*)o;
-    } else if (mem == BEBELM_MEM_HOST) {
+    if (mem == BEBELM_MEM_HOST) {
         void *a0, *a1, *a2, *a3, *a4, *o;
         Stage st[5] = {{q, 4 * qn, &a0}, {k, 4 * kvn, &a1}, {v, 4 * kvn, &a2}, {q_gain, 4 * 64, &a3}, {k_gain, 4 * 64, &a4}};
         TRY(stage_in(P, st, 5, 4 * qn, &o, s));
@@ -1094,7 +1079,7 @@ int bebelm_attn_step(bebelm_kv* kv, int layer, int n_heads, const float* q, cons
     TRY(reserve(kv, layer, 1, &slot0, s));
     const FusedStep fs{dq, dk, dv, dqg, dkg, theta_scale_of(theta, kHeadDim), eps};
     std::vector<Window> w{{kv, kv->base[layer], kv->len[layer], slot0, (long long)pos}};
-    TRY(run_decode(P, w, layer, n_heads, nullptr, dout, 0.125f, &fs, s, nullptr, inl));
+    TRY(run_decode(P, w, layer, n_heads, nullptr, dout, 0.125f, &fs, s));
     if (mem == BEBELM_MEM_HOST) return stage_out(P, dout, out, 4 * qn, s);
     return 0;
 }

@@ -691,34 +691,16 @@ __global__ void __launch_bounds__(kThreads, 2) decode_kernel(DecodeArgs a) {
     decode_body<HPC, KT>(a);
 }
 
-// The fused step of a host-memory call: the step's inputs travel inside the launch (kernel
-// parameter space, up to 32 KB on sm_100), so no copy to device memory precedes the grid and
-// every CTA reads them at once (they are complete when the grid starts).
 template <int HPC, int KT>
-__global__ void __launch_bounds__(kThreads, 2) decode_kernel_inline(DecodeArgs a, const __grid_constant__ InlineStep in) {
-    a.q_raw = in.q;
-    a.k_new = in.k;
-    a.v_new = in.v;
-    a.q_gain = in.q_gain;
-    a.k_gain = in.k_gain;
-    a.early_inputs = 1;
-    decode_body<HPC, KT>(a);
-}
-
-template <int HPC, int KT>
-cudaError_t launch_hpc(const DecodeArgs& a, cudaStream_t s, const InlineStep* in = nullptr) {
-    static bool attr_set[2][64] = {};  // the attribute is per device and kernel
+cudaError_t launch_hpc(const DecodeArgs& a, cudaStream_t s) {
+    static bool attr_set[64] = {};  // the attribute is per device
     const int smem = (int)decode_smem_bytes();
     int dev = 0;
     cudaGetDevice(&dev);
-    const int which = in ? 1 : 0;
-    if (dev < 0 || dev >= 64 || !attr_set[which][dev]) {
-        cudaError_t e = in ? cudaFuncSetAttribute(decode_kernel_inline<HPC, KT>,
-                                                  cudaFuncAttributeMaxDynamicSharedMemorySize, smem)
-                           : cudaFuncSetAttribute(decode_kernel<HPC, KT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                  smem);
+    if (dev < 0 || dev >= 64 || !attr_set[dev]) {
+        cudaError_t e = cudaFuncSetAttribute(decode_kernel<HPC, KT>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
         if (e != cudaSuccess) return e;
-        if (dev >= 0 && dev < 64) attr_set[which][dev] = true;
+        if (dev >= 0 && dev < 64) attr_set[dev] = true;
     }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)a.total_splits, (unsigned)(a.n_kv * a.n_sub));
@@ -730,7 +712,6 @@ cudaError_t launch_hpc(const DecodeArgs& a, cudaStream_t s, const InlineStep* in
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = a.pdl ? 1 : 0;
-    if (in) return cudaLaunchKernelEx(&cfg, decode_kernel_inline<HPC, KT>, a, *in);
     return cudaLaunchKernelEx(&cfg, decode_kernel<HPC, KT>, a);
 }
 
@@ -813,21 +794,21 @@ cudaError_t launch_stage_copy(void* dst, const void* src_mapped, size_t bytes, c
 size_t decode_smem_bytes() { return (size_t)kRingBytes + 4 * kStages * sizeof(uint64_t); }
 
 template <int HPC>
-cudaError_t launch_kt(const DecodeArgs& a, cudaStream_t s, const InlineStep* in) {
+cudaError_t launch_kt(const DecodeArgs& a, cudaStream_t s) {
     switch (a.pv.kind) {
-        case kElemBF16: return launch_hpc<HPC, kElemBF16>(a, s, in);
-        case kElemFP8: return launch_hpc<HPC, kElemFP8>(a, s, in);
-        default: return launch_hpc<HPC, kElemF32>(a, s, in);
+        case kElemBF16: return launch_hpc<HPC, kElemBF16>(a, s);
+        case kElemFP8: return launch_hpc<HPC, kElemFP8>(a, s);
+        default: return launch_hpc<HPC, kElemF32>(a, s);
     }
 }
 
-cudaError_t launch_decode(const DecodeArgs& a, cudaStream_t s, const InlineStep* in) {
+cudaError_t launch_decode(const DecodeArgs& a, cudaStream_t s) {
     if (a.total_splits <= 0) return cudaSuccess;
     switch (a.hpc) {
-        case 1: return launch_kt<1>(a, s, in);
-        case 2: return launch_kt<2>(a, s, in);
-        case 3: return launch_kt<3>(a, s, in);
-        case 4: return launch_kt<4>(a, s, in);
+        case 1: return launch_kt<1>(a, s);
+        case 2: return launch_kt<2>(a, s);
+        case 3: return launch_kt<3>(a, s);
+        case 4: return launch_kt<4>(a, s);
         default: return cudaErrorInvalidValue;
     }
 }

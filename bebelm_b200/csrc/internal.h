@@ -223,19 +223,7 @@ struct DecodeArgs {
 // dst [rows][world * row_elems], and advances *epoch (the last CTA; `done` counts them).
 cudaError_t launch_gather_ll(const unsigned long long* zone, unsigned long long* epoch, unsigned* done, int world,
                              size_t slice, size_t rows, size_t row_elems, float* dst, int* err, cudaStream_t s);
-// A fused step's inputs carried in the launch itself (kernel parameters): q of up to 32 heads,
-// k and v of up to 8 kv heads, the two gains. 12.8 KB, within sm_100's 32 KB of parameters.
-constexpr int kInlineQ = 32 * kHeadDim, kInlineKV = 8 * kHeadDim;
-struct InlineStep {
-    float q[kInlineQ];
-    float k[kInlineKV];
-    float v[kInlineKV];
-    float q_gain[kHeadDim];
-    float k_gain[kHeadDim];
-};
-// With `in`, the fused step reads its q/k/v/gains from the launch parameters instead of the
-// pointers in `a` (one window, host-memory calls).
-cudaError_t launch_decode(const DecodeArgs& a, cudaStream_t s, const InlineStep* in = nullptr);
+cudaError_t launch_decode(const DecodeArgs& a, cudaStream_t s);
 // Copies `bytes` (a multiple of 16) from mapped pinned memory to device memory on s, letting
 // the next kernel launch as a programmatic dependent right away.
 cudaError_t launch_stage_copy(void* dst, const void* src_mapped, size_t bytes, cudaStream_t s);
