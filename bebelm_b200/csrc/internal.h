@@ -46,8 +46,9 @@ __host__ __device__ inline size_t row_bytes(const PoolView& pv) { return (size_t
 // Byte offset of (slot, kv head, K or V) in the pool.
 __host__ __device__ inline size_t slot_offset(const PoolView& pv, const int* table, int cap, long long slot, int kvh,
                                               int kind) {
-    const long long lp = slot >> 6;
-    const int phys = table[(int)(lp % cap)];
+    // logical pages stay below 2^32 (2^38 positions), so the ring index is a 32-bit modulo
+    const unsigned lp = (unsigned)(slot >> 6);
+    const int phys = table[lp % (unsigned)cap];
     return (size_t)phys * pv.page_bytes + pv.layer_off + (size_t)kind * pv.block_bytes + (size_t)kvh * row_bytes(pv) +
            (size_t)(slot & 63) * kHeadDim * elem_bytes(pv.kind);
 }

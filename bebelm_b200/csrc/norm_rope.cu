@@ -201,7 +201,7 @@ __global__ void __launch_bounds__(256) norm_rope_kernel(NormRopeArgs a) {
         const int cap = a.targets ? a.targets[tok].cap : a.cap;
         const long long slot = a.targets ? a.targets[tok].slot : a.slot0 + tok;
         const size_t kd = slot_offset(a.pv, table, cap, slot, head, 0);
-        const size_t vd = slot_offset(a.pv, table, cap, slot, head, 1);
+        const size_t vd = kd + a.pv.block_bytes;  // the V row of the same slot and head
         kv_store4(a.pv, kd, 4 * sub, make_float4(x0[0], x0[1], x0[2], x0[3]));
         kv_store4(a.pv, kd, 32 + 4 * sub, make_float4(x1[0], x1[1], x1[2], x1[3]));
         kv_store4(a.pv, vd, 4 * sub, v0);
@@ -235,8 +235,9 @@ __global__ void kv_gather_bf16_kernel(PoolView pv, const int* table, int cap, lo
         const int e = (int)(i & 15) * 4;
         const long long t = row / n_kv;
         const int h = (int)(row % n_kv);
-        const float4 kf = kv_load4(pv, slot_offset(pv, table, cap, base + t, h, 0), e);
-        const float4 vf = kv_load4(pv, slot_offset(pv, table, cap, base + t, h, 1), e);
+        const size_t ko = slot_offset(pv, table, cap, base + t, h, 0);
+        const float4 kf = kv_load4(pv, ko, e);
+        const float4 vf = kv_load4(pv, ko + pv.block_bytes, e);
         __nv_bfloat162 k0 = __floats2bfloat162_rn(kf.x, kf.y), k1 = __floats2bfloat162_rn(kf.z, kf.w);
         __nv_bfloat162 v0 = __floats2bfloat162_rn(vf.x, vf.y), v1 = __floats2bfloat162_rn(vf.z, vf.w);
         uint2 kw, vw;

@@ -699,6 +699,8 @@ __global__ void __launch_bounds__(256) qmv_lane_kernel(QmvSegs segs, const float
     __shared__ int s_sum16[kMvMaxIn / 16];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int nb = (int)(n_in / kQK);
+    q8_into_smem(x, nb, s_q, s_sc, s_sum, s_sum16);
+    __syncthreads();
     int L = 1;
     while (L < nb) L <<= 1;
     const int b = lane & (L - 1);
@@ -713,24 +715,15 @@ __global__ void __launch_bounds__(256) qmv_lane_kernel(QmvSegs segs, const float
         sg = 2;
         r -= segs.n_out[0] + segs.n_out[1];
     }
-    const bool live = sg >= 0 && b < nb;
-    const int dt = sg <= 0 ? segs.dtype[0] : sg == 1 ? segs.dtype[1] : segs.dtype[2];
-    const uint8_t* blk = nullptr;
-    if (live) {
+    float v = 0.f;
+    if (sg >= 0 && b < nb) {
+        const int dt = sg == 0 ? segs.dtype[0] : sg == 1 ? segs.dtype[1] : segs.dtype[2];
         const uint8_t* wb = sg == 0 ? segs.w[0] : sg == 1 ? segs.w[1] : segs.w[2];
         const size_t rb = sg == 0 ? segs.row_bytes[0] : sg == 1 ? segs.row_bytes[1] : segs.row_bytes[2];
-        blk = wb + r * rb + (size_t)b * (dt == kGgmlQ4K ? 144 : 210);
-        // the block's bytes start towards L2 now, while the CTA quantizes x
-        asm volatile("prefetch.global.L2 [%0];" ::"l"(blk));
-        asm volatile("prefetch.global.L2 [%0];" ::"l"(blk + 128));
-        if (dt != kGgmlQ4K) asm volatile("prefetch.global.L2 [%0];" ::"l"(blk + 209));
+        const uint8_t* row = wb + r * rb;
+        v = dt == kGgmlQ4K ? lane_block_q4k(row + (size_t)b * 144, s_q + b * kQStride, s_sc[b], s_sum + b * 8)
+                           : lane_block_q6k(row + (size_t)b * 210, s_q + b * kQStride, s_sc[b], s_sum16 + b * 16);
     }
-    q8_into_smem(x, nb, s_q, s_sc, s_sum, s_sum16);
-    __syncthreads();
-    float v = 0.f;
-    if (live)
-        v = dt == kGgmlQ4K ? lane_block_q4k(blk, s_q + b * kQStride, s_sc[b], s_sum + b * 8)
-                           : lane_block_q6k(blk, s_q + b * kQStride, s_sc[b], s_sum16 + b * 16);
     const int base = lane & ~(L - 1);
     float acc = -0.0f;  // the blocks of the row, added in order
     for (int j = 0; j < nb; ++j) acc = __fadd_rn(acc, __shfl_sync(0xffffffffu, v, base + j));
