@@ -488,11 +488,8 @@ bool inputs_clear_of_last_out(cudaStream_t s, std::initializer_list<std::pair<co
 #endif
 constexpr long long kBatchMaxPagesPerSplit = BEBELM_BATCH_PAGES_PER_SPLIT;
 
-// Query heads a decode CTA serves (all of a kv head's group where possible, so each K/V byte is
-// read once). A narrow cache (bf16, fp8) takes two: its loop is bound by arithmetic latency, and
-// two-head CTAs fit three to an SM (the second CTA of a kv head reads the pages from L2).
-void pick_heads_per_cta(int group, int* hpc, int* n_sub, bool narrow = false) {
-    int h = narrow && group % 2 == 0 ? 2 : group % 4 == 0 ? 4 : group % 3 == 0 ? 3 : group % 2 == 0 ? 2 : 1;
+void pick_heads_per_cta(int group, int* hpc, int* n_sub) {
+    int h = group % 4 == 0 ? 4 : group % 3 == 0 ? 3 : group % 2 == 0 ? 2 : 1;
     *hpc = h;
     *n_sub = group / h;
 }
@@ -519,7 +516,7 @@ int run_decode(bebelm_kv_pool* P, const std::vector<Window>& wins, int layer, in
     if (n == 0) return 0;
     const int group = n_heads / P->n_kv;
     int hpc, n_sub;
-    pick_heads_per_cta(group, &hpc, &n_sub, P->dtype != BEBELM_F32);
+    pick_heads_per_cta(group, &hpc, &n_sub);
     const int NY = P->n_kv * n_sub;
     long long total_units = 0;
     std::vector<long long> npages(n);
@@ -1370,7 +1367,7 @@ extern "C" int bebelm_attn_decode_cached_noalloc(const bebelm_kv* kv, int layer,
     // the same split plan as run_decode for one window
     const int group = n_heads / P->n_kv;
     int hpc, n_sub;
-    pick_heads_per_cta(group, &hpc, &n_sub, P->dtype != BEBELM_F32);
+    pick_heads_per_cta(group, &hpc, &n_sub);
     const int NY = P->n_kv * n_sub;
     const long long npages = (base + len - 1) / kPageTokens - base / kPageTokens + 1;
     const long long target = (long long)P->num_sms * 2;
@@ -1689,7 +1686,7 @@ int bebelm_step_plan_create(bebelm_kv* kv, int layer, int n_heads, size_t window
     pl->window = (long long)window;
     // split plan for the largest window: the pages [base, base + window) can span
     const int group = n_heads / P->n_kv;
-    pick_heads_per_cta(group, &pl->hpc, &pl->n_sub, P->dtype != BEBELM_F32);
+    pick_heads_per_cta(group, &pl->hpc, &pl->n_sub);
     const int NY = P->n_kv * pl->n_sub;
     const long long max_pages = (pl->window + kPageTokens - 1) / kPageTokens + 1;
     const long long target = (long long)P->num_sms * 2;  // two resident CTAs per SM, as run_decode

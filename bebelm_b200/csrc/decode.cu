@@ -212,15 +212,6 @@ __device__ long long g_dtrace[4][1024 * 8];  // by the first sequence's position
     } while (0)
 #endif
 
-// Narrow caches with two query heads a CTA (the host picks that split for bf16 and fp8): their
-// loop is bound by its dependent arithmetic, not by bytes, so a CTA holds fewer registers and a
-// 64 KB ring, and three CTAs share an SM instead of two (more warps to hide the latency).
-template <int HPC, int KT> constexpr bool three_per_sm() { return KT != kElemF32 && HPC <= 2; }
-template <int HPC, int KT> constexpr int ring_bytes() { return three_per_sm<HPC, KT>() ? 64 * 1024 : kRingBytes; }
-template <int HPC, int KT> constexpr size_t smem_bytes() {
-    return (size_t)ring_bytes<HPC, KT>() + 4 * kStages * sizeof(uint64_t);
-}
-
 template <int HPC, int KT>
 __device__ __forceinline__ void decode_body(DecodeArgs a) {
     // KT: the cache's element type. bf16 and fp8 (e4m3) rows take a half and a quarter of the
@@ -230,12 +221,10 @@ __device__ __forceinline__ void decode_body(DecodeArgs a) {
     constexpr int ES = KT == kElemF32 ? 4 : KT == kElemBF16 ? 2 : 1;
     constexpr int ROWB = kPageRowFloats * ES;  // one kv head of one page
     constexpr int SB = 2 * ROWB;               // a stage: its K rows and V rows
-    constexpr int RB = ring_bytes<HPC, KT>();
-    constexpr int NST = RB / SB;
-    static_assert(NST <= 4 * kStages, "one mbarrier per stage after the ring");
+    constexpr int NST = kRingBytes / SB;
     extern __shared__ __align__(128) unsigned char smem[];
     unsigned char* stages = smem;
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + RB);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + kRingBytes);
     __shared__ float s_m[4][HPC], s_l[4][HPC];
     __shared__ int s_release[NST];
     __shared__ int s_failed, s_last;
@@ -698,14 +687,14 @@ __device__ __forceinline__ void decode_body(DecodeArgs a) {
 }
 
 template <int HPC, int KT>
-__global__ void __launch_bounds__(kThreads, three_per_sm<HPC, KT>() ? 3 : 2) decode_kernel(DecodeArgs a) {
+__global__ void __launch_bounds__(kThreads, 2) decode_kernel(DecodeArgs a) {
     decode_body<HPC, KT>(a);
 }
 
 template <int HPC, int KT>
 cudaError_t launch_hpc(const DecodeArgs& a, cudaStream_t s) {
     static bool attr_set[64] = {};  // the attribute is per device
-    const int smem = (int)smem_bytes<HPC, KT>();
+    const int smem = (int)decode_smem_bytes();
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 0 || dev >= 64 || !attr_set[dev]) {
@@ -801,6 +790,8 @@ cudaError_t launch_stage_copy(void* dst, const void* src_mapped, size_t bytes, c
     return cudaGetLastError();
 }
 
+// the ring, then one mbarrier per stage (fp8 rows: four times kStages stages)
+size_t decode_smem_bytes() { return (size_t)kRingBytes + 4 * kStages * sizeof(uint64_t); }
 
 template <int HPC>
 cudaError_t launch_kt(const DecodeArgs& a, cudaStream_t s) {

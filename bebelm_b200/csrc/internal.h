@@ -229,6 +229,7 @@ cudaError_t launch_decode(const DecodeArgs& a, cudaStream_t s);
 // the next kernel launch as a programmatic dependent right away.
 cudaError_t launch_stage_copy(void* dst, const void* src_mapped, size_t bytes, cudaStream_t s);
 
+size_t decode_smem_bytes();
 constexpr int kDecodeMaxPagesPerSplit = 256;
 
 // ---- kernel 2: causal prefill on the tensor cores ---------------------------
