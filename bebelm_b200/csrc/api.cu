@@ -1199,6 +1199,7 @@ int prefill_device(bebelm_kv* kv, int layer, int n_heads, const void* dq, const 
             a.kv_row_heads = shard->kv_row_heads;
             a.kv_head0 = shard->kv_head0;
         }
+        a.trigger_dependents = 1;  // the prefill kernel sets up while this one runs, then waits for it
         CUDA_TRY(launch_norm_rope(a, s));
         P->last_writes.assign(1, {kv, layer, slot0});
         CUDA_TRY(launch_prefill(pa, maps, s));

@@ -144,6 +144,9 @@ struct NormRopeArgs {
     // holds q_row_heads heads of which this call's start at q_head0; likewise k/v (0: exactly
     // n_heads / n_kv, from 0)
     int q_row_heads, q_head0, kv_row_heads, kv_head0;
+    // let the next kernel launch as a programmatic dependent at once (it must wait with
+    // griddepcontrol.wait before reading anything this kernel writes: the tensor-core prefill)
+    int trigger_dependents;
 };
 cudaError_t launch_norm_rope(const NormRopeArgs& a, cudaStream_t s);
 

@@ -35,6 +35,7 @@ __device__ __forceinline__ void load_bf16x4(const __nv_bfloat16* p, float* out) 
 
 template <bool HD64>
 __global__ void __launch_bounds__(256) norm_rope_kernel(NormRopeArgs a) {
+    if (a.trigger_dependents) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const int lane = threadIdx.x & 31;
     const int sub = lane & 7;
     const int nh_all = a.n_heads + a.n_kv;

@@ -278,6 +278,26 @@ __device__ long long g_trace[16 * 2 * 64];  // [event][tile][j] = clock64, CTA (
     } while (0)
 #endif
 
+// Per-CTA timeline for a timing build (-DBEBELM_PREFILL_CTA_TRACE): %globaltimer at entry, after
+// set-up, when tile A's softmax first sees S, at the end of its loop, after its stores, and at
+// exit, plus the SM. Compiled out otherwise.
+#ifdef BEBELM_PREFILL_CTA_TRACE
+__device__ long long g_ctat[2048][8];
+#define CTAT(slot)                                                                    \
+    do {                                                                              \
+        const unsigned cta_ = blockIdx.y * gridDim.x + blockIdx.x;                    \
+        if (cta_ < 2048) {                                                            \
+            long long t_;                                                             \
+            asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_));                    \
+            g_ctat[cta_][slot] = t_;                                                  \
+        }                                                                             \
+    } while (0)
+#else
+#define CTAT(slot) \
+    do {           \
+    } while (0)
+#endif
+
 // ---- roles: warps 0 / 10 MMA for tile A / B, 1 TMA, 2-5 softmax for tile A, 6-9 for tile B ----
 constexpr int kWarpMmaB = 10;  // issuer of the second query tile (the first is warp 0)
 #ifdef BEBELM_PREFILL_TRACE
@@ -330,6 +350,15 @@ __global__ void __launch_bounds__(kCtaThreads, 1)
     };
     const int nkt[2] = {n_kt_of(0), n_kt_of(1)};
     const int nkt_max = max(nkt[0], nkt[1]);
+#ifdef BEBELM_PREFILL_CTA_TRACE
+    if (tid == 0) {
+        CTAT(0);
+        unsigned smid;
+        asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
+        g_ctat[blockIdx.y * gridDim.x + blockIdx.x][6] = smid;
+        g_ctat[blockIdx.y * gridDim.x + blockIdx.x][7] = nkt_max;
+    }
+#endif
 
     if (warp == 0) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&s_tmem)),
@@ -348,6 +377,10 @@ __global__ void __launch_bounds__(kCtaThreads, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = s_tmem;
+    // launched as a programmatic dependent: the set-up above overlaps the kernel before (which
+    // writes q, k and v); nothing it wrote is read, and nothing is written, before this wait
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    if (tid == 0) CTAT(1);
 
     if (warp == 1) {
         // ---------------- TMA producer ----------------
@@ -447,6 +480,7 @@ __global__ void __launch_bounds__(kCtaThreads, 1)
             ok = __all_sync(0xffffffffu, mbar_wait_bounded(bar(kBarS + X), j & 1));
             if (!ok) break;
             if ((warp & 3) == 0 && lane == 0) TRACE(3, j, X);
+            if (warp == 2 && lane == 0 && j == 0) CTAT(2);
             tc_fence_after();
             const long long k0 = (long long)j * kTileK;
             const bool diag = k0 + kTileK - 1 > (long long)a.len_before + (2 * pair + X) * kTileQ;
@@ -559,6 +593,7 @@ __global__ void __launch_bounds__(kCtaThreads, 1)
             asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar(kBarP + X)) : "memory");
             if ((warp & 3) == 0 && lane == 0) TRACE(4, j, X);
         }
+        if (warp == 2 && lane == 0) CTAT(3);
         // epilogue: wait for the last PV, normalise, store
         if (ok && nkt[X] > 0) ok = __all_sync(0xffffffffu, mbar_wait_bounded(bar(kBarO + X), (nkt[X] - 1) & 1));
         if (!ok) s_fail = 1;
@@ -613,6 +648,7 @@ __global__ void __launch_bounds__(kCtaThreads, 1)
                     dst[d / 4] = make_float4(o[d] * inv, o[d + 1] * inv, o[d + 2] * inv, o[d + 3] * inv);
             }
         }
+        if (warp == 2 && lane == 0) CTAT(4);
     }
 
     tc_fence_before();
@@ -629,6 +665,7 @@ __global__ void __launch_bounds__(kCtaThreads, 1)
     if (warp == 0) {
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmem2Cols));
+        if (lane == 0) CTAT(5);
     }
 }
 
@@ -679,11 +716,18 @@ cudaError_t launch_prefill(const PrefillArgs& a, const PrefillMaps& m, cudaStrea
         if (dev >= 0 && dev < 64) attr_set[dev] = true;
     }
     const int n_qt = (a.t + kTileQ - 1) / kTileQ;
-    dim3 grid((unsigned)a.n_heads, (unsigned)((n_qt + 1) / 2));
-    prefill_kernel<<<grid, kCtaThreads, kSmem2Bytes, s>>>(*reinterpret_cast<const CUtensorMap*>(m.q),
-                                                           *reinterpret_cast<const CUtensorMap*>(m.k),
-                                                           *reinterpret_cast<const CUtensorMap*>(m.v), a);
-    return cudaGetLastError();
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)a.n_heads, (unsigned)((n_qt + 1) / 2));
+    cfg.blockDim = dim3(kCtaThreads);
+    cfg.dynamicSmemBytes = (size_t)kSmem2Bytes;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, prefill_kernel, *reinterpret_cast<const CUtensorMap*>(m.q),
+                              *reinterpret_cast<const CUtensorMap*>(m.k), *reinterpret_cast<const CUtensorMap*>(m.v), a);
 }
 
 }  // namespace bebelm
