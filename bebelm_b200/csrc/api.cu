@@ -2,13 +2,16 @@
 // sequence-window bookkeeping (the device replacement of src/cache.rs), host /
 // device staging, and the launch sequences of the fused calls.
 #include <algorithm>
+#include <atomic>
 #include <climits>
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <condition_variable>
 #include <mutex>
 #include <string>
+#include <thread>
 #include <unordered_map>
 #include <initializer_list>
 #include <vector>
@@ -165,6 +168,91 @@ struct ErrWord {
 
 }  // namespace
 
+// Large copies between caller memory and the pinned staging buffer run on a few host threads:
+// one thread's memcpy is slower than the host link, and a prefill of thousands of tokens moves
+// tens of MB each way. The calling thread takes a share; `copy` returns once all are done.
+struct HostCopier {
+    static constexpr size_t kMinParallel = 1 << 20;
+    std::vector<std::thread> th;
+    std::mutex mu, run;
+    std::condition_variable cv, cv_done;
+    char* dst = nullptr;
+    const char* src = nullptr;
+    size_t n = 0;
+    int parts = 0;
+    std::atomic<int> next{0}, done{0};
+    unsigned long long gen = 0;
+    bool stop = false;
+
+    static HostCopier& get() {
+        static HostCopier c;
+        return c;
+    }
+    HostCopier() {
+        const unsigned hc = std::thread::hardware_concurrency();
+        const int k = (int)std::min(7u, hc > 2 ? hc / 2 : 0u);
+        for (int i = 0; i < k; ++i) th.emplace_back([this] { loop(); });
+    }
+    ~HostCopier() {
+        {
+            std::lock_guard<std::mutex> lk(mu);
+            stop = true;
+        }
+        cv.notify_all();
+        for (auto& t : th) t.join();
+    }
+    void work() {
+        for (;;) {
+            const int i = next.fetch_add(1);
+            if (i >= parts) return;
+            const size_t a = n * (size_t)i / (size_t)parts, b = n * (size_t)(i + 1) / (size_t)parts;
+            std::memcpy(dst + a, src + a, b - a);
+            if (done.fetch_add(1) + 1 == parts) {
+                std::lock_guard<std::mutex> lk(mu);
+                cv_done.notify_all();
+            }
+        }
+    }
+    void loop() {
+        unsigned long long seen = 0;
+        for (;;) {
+            {
+                std::unique_lock<std::mutex> lk(mu);
+                cv.wait(lk, [&] { return stop || gen != seen; });
+                if (stop) return;
+                seen = gen;
+            }
+            work();
+        }
+    }
+    void copy(void* d, const void* sp, size_t bytes) {
+        if (bytes < kMinParallel || th.empty()) {
+            std::memcpy(d, sp, bytes);
+            return;
+        }
+        std::lock_guard<std::mutex> one(run);  // one parallel copy at a time
+        {
+            std::lock_guard<std::mutex> lk(mu);
+            dst = static_cast<char*>(d);
+            src = static_cast<const char*>(sp);
+            n = bytes;
+            parts = 2 * ((int)th.size() + 1);
+            done = 0;
+            next = 0;
+            ++gen;
+        }
+        cv.notify_all();
+        work();
+        std::unique_lock<std::mutex> lk(mu);
+        cv_done.wait(lk, [&] { return done.load() >= parts; });
+    }
+};
+
+// Host-link transfers of a large staged call go in chunks of this size: the copy of chunk i
+// between caller memory and the pinned buffer overlaps the DMA of its neighbour.
+constexpr size_t kStageChunk = 4u << 20;
+constexpr int kStageEvents = 8;
+
 // Small host-to-device uploads (page-table entries, sequence descriptors) go through a
 // ring of pinned slots: a copy from pinned memory is truly asynchronous, whereas one from
 // pageable memory is staged by the runtime and can hold the host to the GPU's pace. A slot
@@ -216,6 +304,7 @@ struct bebelm_kv_pool {
     DevBuf io, qn, part, counters, seqdesc, pf, q8, proj, sample;
     ErrWord err;
     PinBuf pin;
+    cudaEvent_t out_ev[kStageEvents] = {};  // chunks of a large output copied back
     UploadRing uploads;
     // a second stream for work that may run beside the caller's (forked and joined with events
     // inside one call, so the call stays ordered on the caller's stream)
@@ -398,6 +487,8 @@ void pool_free(bebelm_kv_pool* P) {
     P->sample.release();
     P->err.release();
     P->pin.release();
+    for (cudaEvent_t& e : P->out_ev)
+        if (e) cudaEventDestroy(e);
     delete P;
 }
 
@@ -629,17 +720,25 @@ int stage_in(bebelm_kv_pool* P, Stage* st, int n, size_t out_bytes, void** d_out
     total += ((out_bytes + 255) & ~size_t(255)) + 256;
     TRY(P->io.ensure(total, false, s));
     TRY(P->pin.ensure(total));
+    g_inputs_staged = out_off > 0 && out_off <= kKernelStageBytes;
     size_t off = 0;
     for (int i = 0; i < n; ++i) {
-        if (st[i].src && st[i].bytes) std::memcpy(P->pin.as<char>() + off, st[i].src, st[i].bytes);
         *st[i].dev = st[i].src ? P->io.as<char>() + off : nullptr;
+        if (st[i].src && st[i].bytes) {
+            char* pin = P->pin.as<char>() + off;
+            if (g_inputs_staged) {
+                std::memcpy(pin, st[i].src, st[i].bytes);
+            } else {  // large: chunk by chunk, each DMA overlapping the next chunk's host copy
+                for (size_t c = 0; c < st[i].bytes; c += kStageChunk) {
+                    const size_t len = std::min(kStageChunk, st[i].bytes - c);
+                    HostCopier::get().copy(pin + c, static_cast<const char*>(st[i].src) + c, len);
+                    CUDA_TRY(cudaMemcpyAsync(P->io.as<char>() + off + c, pin + c, len, cudaMemcpyHostToDevice, s));
+                }
+            }
+        }
         off += (st[i].bytes + 255) & ~size_t(255);
     }
-    g_inputs_staged = out_off > 0 && out_off <= kKernelStageBytes;
-    if (g_inputs_staged)
-        CUDA_TRY(launch_stage_copy(P->io.p, P->pin.d, out_off, s));
-    else if (out_off)
-        CUDA_TRY(cudaMemcpyAsync(P->io.p, P->pin.p, out_off, cudaMemcpyHostToDevice, s));
+    if (g_inputs_staged) CUDA_TRY(launch_stage_copy(P->io.p, P->pin.d, out_off, s));
     g_pin_out_direct = out_bytes <= kDirectOutBytes;
     if (d_out) *d_out = (g_pin_out_direct ? static_cast<char*>(P->pin.d) : P->io.as<char>()) + out_off;
     g_pin_out_off = out_off;
@@ -656,7 +755,28 @@ void clear_noalloc_counters(int dev, cudaStream_t s);
 int stage_out(bebelm_kv_pool* P, const void* d_src, void* h_dst, size_t bytes, cudaStream_t s) {
     g_inputs_staged = false;
     char* pin = P->pin.as<char>() + g_pin_out_off;
-    if (bytes && !g_pin_out_direct) CUDA_TRY(cudaMemcpyAsync(pin, d_src, bytes, cudaMemcpyDeviceToHost, s));
+    if (bytes > kStageChunk && !g_pin_out_direct) {
+        // large: chunks copied back behind events, each delivered while the next one crosses
+        const size_t chunk = std::max(kStageChunk, (bytes + kStageEvents - 1) / kStageEvents);
+        const int nc = (int)((bytes + chunk - 1) / chunk);
+        for (int i = 0; i < nc; ++i) {
+            if (!P->out_ev[i]) CUDA_TRY(cudaEventCreateWithFlags(&P->out_ev[i], cudaEventDisableTiming));
+            const size_t c = (size_t)i * chunk, len = std::min(chunk, bytes - c);
+            CUDA_TRY(cudaMemcpyAsync(pin + c, static_cast<const char*>(d_src) + c, len, cudaMemcpyDeviceToHost, s));
+            CUDA_TRY(cudaEventRecord(P->out_ev[i], s));
+        }
+        CUDA_TRY(cudaEventSynchronize(P->out_ev[0]));  // every kernel of the call has completed
+        if (P->err.read() == 0) {
+            for (int i = 0; i < nc; ++i) {
+                const size_t c = (size_t)i * chunk, len = std::min(chunk, bytes - c);
+                if (i) CUDA_TRY(cudaEventSynchronize(P->out_ev[i]));
+                HostCopier::get().copy(static_cast<char*>(h_dst) + c, pin + c, len);
+            }
+            bytes = 0;  // delivered
+        }
+    } else if (bytes && !g_pin_out_direct) {
+        CUDA_TRY(cudaMemcpyAsync(pin, d_src, bytes, cudaMemcpyDeviceToHost, s));
+    }
     CUDA_TRY(cudaStreamSynchronize(s));
     const int derr = P->err.read();
     if (derr) {
