@@ -457,7 +457,11 @@ class Cache:
             qg = np.ascontiguousarray(q_gain, np.float32)
             kg = np.ascontiguousarray(k_gain, np.float32)
             t = q.size // (n_heads * self.head_dim)
-            out = np.zeros((t, n_heads * self.head_dim), np.float32)
+            if out is None:
+                out = np.zeros((t, n_heads * self.head_dim), np.float32)
+            elif not (isinstance(out, np.ndarray) and out.dtype == np.float32 and out.flags.c_contiguous
+                      and out.size == t * n_heads * self.head_dim):
+                raise ValueError("out must be a C-contiguous float32 array of t * n_heads * 64 elements")
             keep = (q, k, v, qg, kg, out)
             ptrs = [C.c_void_p(x.ctypes.data) for x in keep]
             mem = MEM_HOST

