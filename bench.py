@@ -644,8 +644,9 @@ def bench_config4(bb, torch, dev, stream, world, rank, steps=128):
 
 def bench_config5(bb, torch, dev, stream, world, rank, bf16_peak, T=8192, steps=512):
     """Config 5: the 6 attention layers of the stack, KV heads sharded over the ranks: causal
-    prefill of T bf16 tokens (NCCL all-gather of head outputs), then `steps` decode steps whose
-    all-gather is fused into the decode kernel (peer stores over NVLink). Decode is timed
+    prefill of T bf16 tokens whose all-gather of head outputs is fused into the prefill kernel's
+    epilogue, then `steps` decode steps whose all-gather is fused into the decode kernel (both:
+    tagged 8-byte words stored over NVLink into every rank's landing zone). Decode is timed
     host-driven and as one CUDA graph of step plans (all steps x 6 layers). With more than one
     rank, rank 0 also runs the same workload unsharded on its own GPU (the others wait), so the
     line carries the 1 -> N speed-up and efficiency of this run; the host-driven decode is also
@@ -739,8 +740,8 @@ def bench_config5(bb, torch, dev, stream, world, rank, bf16_peak, T=8192, steps=
     gms = max_over_ranks(gms, world, dev)
     out = {"workload": f"config5: 6 GQA layers, causal prefill of {T} bf16 tokens then {steps} decode steps",
            **line(pre, dec, gms, world),
-           "parallelism": (f"kv heads / {world} per GPU; prefill: NCCL all-gather of head outputs; decode: "
-                           "all-gather fused into the decode kernel (NVLink peer stores + flags)") if world > 1
+           "parallelism": (f"kv heads / {world} per GPU; all-gather of head outputs fused into the prefill "
+                           "and decode kernels (tagged words stored over NVLink)") if world > 1
            else "one GPU, all heads"}
     if world > 1:
         shn = KVHeadSharded(n_layers=L, max_context=T + 2 * steps + 64, fused_gather=False)
