@@ -42,7 +42,7 @@ EXPORTS = [
     "bebelm_kv_create", "bebelm_kv_create_in_pool", "bebelm_kv_destroy", "bebelm_kv_clone", "bebelm_kv_clear",
     "bebelm_kv_len", "bebelm_kv_layer_len", "bebelm_kv_pos", "bebelm_kv_set_pos", "bebelm_kv_evict_front",
     "bebelm_kv_append", "bebelm_kv_read", "bebelm_attn_step", "bebelm_attn_decode_cached", "bebelm_attn_decode_cached_noalloc", "bebelm_attn_prefill", "bebelm_attn_decode_batched",
-    "bebelm_kv_check", "bebelm_peer_group_create", "bebelm_peer_group_connect", "bebelm_peer_group_destroy",
+    "bebelm_kv_check", "bebelm_debug_expire_next_wait", "bebelm_peer_group_create", "bebelm_peer_group_connect", "bebelm_peer_group_destroy",
     "bebelm_attn_step_allgather", "bebelm_step_plan_create", "bebelm_step_plan_launch", "bebelm_step_plan_steps",
     "bebelm_step_plan_finish", "bebelm_matvec", "bebelm_matmul", "bebelm_dequantize",
     "bebelm_attn_weights_create", "bebelm_attn_weights_destroy", "bebelm_attn_layer_step", "bebelm_attn_layer_batch",
@@ -110,6 +110,7 @@ def load_library(path: str = LIB_PATH):
         "bebelm_attn_prefill": ([vp, i, i, vp, vp, vp, i, sz, sz, vp, vp, f, f, vp, i, vp], i),
         "bebelm_attn_decode_batched": ([vp, i, i, i, vp, vp, vp, vp, vp, f, f, vp, vp, i, vp], i),
         "bebelm_kv_check": ([vp, vp], i),
+        "bebelm_debug_expire_next_wait": ([i], i),
         "bebelm_peer_group_create": ([i, i, i, sz, vp, C.POINTER(vp)], i),
         "bebelm_peer_group_connect": ([vp, vp], i),
         "bebelm_peer_group_destroy": ([vp], i),

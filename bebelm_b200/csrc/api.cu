@@ -679,6 +679,10 @@ int run_decode(bebelm_kv_pool* P, const std::vector<Window>& wins, int layer, in
     a.total_splits = total_splits;
     a.scale_log2 = scale * 1.4426950408889634f;
     a.pdl = 1;
+    if (g_expire_waits > 0) {  // test hook (bebelm_debug_expire_next_wait)
+        a.expire_wait = 1;
+        --g_expire_waits;
+    }
     if (peer) {
         a.peer_bufs = peer->bufs;
         a.peer_world = peer->world;
@@ -1470,6 +1474,16 @@ void clear_noalloc_counters(int dev, cudaStream_t s) {
 
 }  // namespace
 
+namespace bebelm {
+int g_expire_waits = 0;
+}
+
+extern "C" int bebelm_debug_expire_next_wait(int n_launches) {
+    if (n_launches < 0) return fail(BEBELM_ERR_INVALID, "n_launches < 0");
+    g_expire_waits = n_launches;
+    return 0;
+}
+
 extern "C" int bebelm_attn_decode_cached_noalloc(const bebelm_kv* kv, int layer, int n_heads, const float* q,
                                                  float* out, void* stream) {
     TRY(validate_layer(kv, layer));
@@ -1532,6 +1546,10 @@ extern "C" int bebelm_attn_decode_cached_noalloc(const bebelm_kv* kv, int layer,
     a.total_splits = (int)n_splits;
     a.scale_log2 = 0.125f * 1.4426950408889634f;
     a.pdl = 1;
+    if (g_expire_waits > 0) {  // test hook (bebelm_debug_expire_next_wait)
+        a.expire_wait = 1;
+        --g_expire_waits;
+    }
     CUDA_TRY(launch_decode(a, s));
     record_decode_out(s, out, (size_t)n_heads * kHeadDim * 4);
     return 0;
@@ -1881,6 +1899,10 @@ int plan_launch(bebelm_step_plan* pl, const bebelm_peer_group* grp, const float*
     a.total_splits = pl->n_splits;
     a.scale_log2 = 0.125f * 1.4426950408889634f;
     a.pdl = 1;
+    if (g_expire_waits > 0) {  // test hook (bebelm_debug_expire_next_wait)
+        a.expire_wait = 1;
+        --g_expire_waits;
+    }
     a.step = pl->state.as<StepState>();
     a.step_slot0 = pl->slot0;
     a.step_pos0 = pl->pos0;

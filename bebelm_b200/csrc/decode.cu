@@ -90,8 +90,8 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, unsigned parity) {
     return ok != 0;
 }
 
-__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, unsigned parity) {
-    for (long long it = 0; it < kWaitLimit; ++it)
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, unsigned parity, long long limit = kWaitLimit) {
+    for (long long it = 0; it < limit; ++it)
         if (mbar_try_wait(bar, parity)) return true;
     return false;
 }
@@ -228,6 +228,8 @@ __device__ __forceinline__ void decode_body(DecodeArgs a) {
     __shared__ float s_m[4][HPC], s_l[4][HPC];
     __shared__ int s_release[NST];
     __shared__ int s_failed, s_last;
+    __shared__ int s_issued;  // pages whose copies have been issued (the stream's cleanup waits for these)
+    __shared__ uint64_t s_never;  // test hook: a barrier that nothing arrives on
     __shared__ int s_phys[kMaxPagesPerSplit];
     __shared__ __align__(16) float s_q[HPC][kHeadDim];
     __shared__ __align__(16) float s_knew[kHeadDim], s_vnew[kHeadDim];
@@ -352,9 +354,12 @@ __device__ __forceinline__ void decode_body(DecodeArgs a) {
             s_release[s] = 0;
         }
         s_failed = 0;
+        s_issued = 0;
+        mbar_init(&s_never, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         for (int i = 0; i < n_first && i < n_early; ++i) issue(i);
+        s_issued = max(0, min(n_first, n_early));
         for (int i = NST; i < NST + kEarlyPrefetch && i < n_early; ++i) prefetch(i);
     }
 
@@ -365,6 +370,7 @@ __device__ __forceinline__ void decode_body(DecodeArgs a) {
     const unsigned long long pe = a.peer_world > 0 ? peer_step(a) : 0ull;
     if (tid == 0)
         for (int i = n_early; i < n_first; ++i) issue(i);
+    if (tid == 0) s_issued = n_first;
     if (!early) read_inputs();
     if (has_new && warp == HPC % 4) {  // one CTA per kv head writes the cache (the warp that computed it)
         const int i = (int)((S.new_slot >> 6) - p0);
@@ -416,7 +422,10 @@ __device__ __forceinline__ void decode_body(DecodeArgs a) {
     const long long new_slot = own_new ? S.new_slot : -1;
     for (int i = 0; i < np; ++i) {
         const int st = i % NST;
-        const bool ok = __all_sync(0xffffffffu, mbar_wait_bounded(&full[st], (unsigned)((i / NST) & 1)));
+        // (test hook: CTA (0, 0) first waits, with a short limit, on a barrier nothing completes)
+        const bool expire = a.expire_wait && i == 0 && blockIdx.x == 0 && blockIdx.y == 0;
+        const bool ok = __all_sync(0xffffffffu, expire ? mbar_wait_bounded(&s_never, 0u, kWaitLimit >> 8)
+                                                       : mbar_wait_bounded(&full[st], (unsigned)((i / NST) & 1)));
         if (i == 0) DTRACE(2);
         if (!ok) {
             if (lane == 0) {
@@ -464,6 +473,7 @@ __device__ __forceinline__ void decode_body(DecodeArgs a) {
                 if (i + NST < np) {
                     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
                     issue(i + NST);
+                    s_issued = i + NST + 1;
                     if (i + NST + kPrefetch < np) prefetch(i + NST + kPrefetch);
                 }
             }
@@ -526,8 +536,9 @@ __device__ __forceinline__ void decode_body(DecodeArgs a) {
     if (s_failed) {
         // a wait gave up: let our own copies still in flight land (bounded), then leave
         if (tid == 0) {
-            for (int k = 0; k < NST && k < np; ++k) {
-                const int last = ((np - 1 - k) / NST) * NST + k;
+            const int n_iss = s_issued;
+            for (int k = 0; k < NST && k < n_iss; ++k) {  // the last issued use of stage k
+                const int last = ((n_iss - 1 - k) / NST) * NST + k;
                 mbar_wait_bounded(&full[k], (unsigned)((last / NST) & 1));
             }
         }

@@ -221,7 +221,12 @@ struct DecodeArgs {
     // (they do not overlap the previous decode launch's output), so a CTA norms and ropes them
     // before griddepcontrol.wait; only the cache store of the new token waits
     int early_inputs;
+    // test hook (bebelm_debug_expire_next_wait): CTA (0, 0) waits on a phase of its first stage
+    // that nothing completes, with a short limit, so the launch takes the timeout path
+    int expire_wait;
 };
+// Launches of the decode kernel still to be given expire_wait (set through the C-ABI for tests).
+extern int g_expire_waits;
 // The gather of a fused all-gather step (a landing zone of tagged words, see DecodeArgs): waits
 // (bounded) for every element of this step's parity to carry this step's tag, copies them into
 // dst [rows][world * row_elems], and advances *epoch (the last CTA; `done` counts them).

@@ -210,6 +210,14 @@ BEBELM_API int bebelm_attn_decode_batched(bebelm_kv* const* seqs, int n_seqs, in
  * calls only enqueue work, so their callers check here. */
 BEBELM_API int bebelm_kv_check(const bebelm_kv* kv, void* stream);
 
+/* Testing only; no counterpart in the reference. Makes the next `n_launches`
+ * decode-kernel launches (any entry point that decodes) take their timeout path:
+ * the first CTA first waits, with a short limit, on a barrier nothing completes,
+ * records BEBELM_ERR_TIMEOUT in the pool's error word and leaves once its own
+ * copies have landed. No GPU fault is involved. Lets a test check that a wait
+ * that gives up is reported and that the next call is correct again. */
+BEBELM_API int bebelm_debug_expire_next_wait(int n_launches);
+
 /* ---------------------------------------------- quantized weights (GGML) --- */
 /* The projections that feed the path (src/model.rs:434-436, 454) multiply GGML-quantized
  * weights by f32 activations. Weight dtypes are ggml's type ids. W is [n_out rows][n_in],

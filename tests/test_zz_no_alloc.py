@@ -99,3 +99,51 @@ def test_noalloc_rejects_window_beyond_partial_region():
     assert L.bebelm_kv_check(cache._h, stream) == 0
     cache.close()
     torch.cuda.empty_cache()
+
+
+def test_expired_wait_is_reported_and_the_next_call_is_correct():
+    """A bounded device-side wait that gives up (forced through bebelm_debug_expire_next_wait:
+    the first CTA waits, with a short limit, on a barrier nothing completes; no GPU fault) is
+    reported, on the no-allocation path by bebelm_kv_check and on a host-memory call by the
+    call itself, and leaves nothing behind: the split counters are cleared and the next call
+    returns the same output as before the failure."""
+    torch = pytest.importorskip("torch")
+    L = bb.load_library()
+    n = 16384  # 7 pages a split: more than the 3-stage ring, so the timed-out CTA has copies to wait for
+    cache = bb.Cache(n_layers=1, max_context=n)
+    for c0 in range(0, n, 4096):
+        cache.append(0, oracle.normal(10 + c0, (4096, KVH * D)), oracle.normal(11 + c0, (4096, KVH * D)))
+    qh = oracle.normal(12, (H * D,))
+    q = torch.from_numpy(qh).cuda()
+    stream = C.c_void_p(torch.cuda.current_stream().cuda_stream)
+    outs = [torch.full((H * D,), float("nan"), device="cuda") for _ in range(3)]
+
+    def noalloc(o):
+        return L.bebelm_attn_decode_cached_noalloc(cache._h, 0, H, C.c_void_p(q.data_ptr()),
+                                                   C.c_void_p(o.data_ptr()), stream)
+
+    assert noalloc(outs[0]) == 0, bb.last_error()
+    assert L.bebelm_kv_check(cache._h, stream) == 0, bb.last_error()
+    assert L.bebelm_debug_expire_next_wait(1) == 0
+    assert noalloc(outs[1]) == 0, bb.last_error()  # device memory: the call only enqueues
+    assert L.bebelm_kv_check(cache._h, stream) == bb.ERR_TIMEOUT
+    assert "timed out" in bb.last_error()
+    assert noalloc(outs[2]) == 0, bb.last_error()
+    assert L.bebelm_kv_check(cache._h, stream) == 0, bb.last_error()
+    assert torch.equal(outs[2], outs[0])
+
+    # a host-memory call reports the timeout itself, and the next one is correct
+    oh = np.full(H * D, np.nan, np.float32)
+    assert L.bebelm_debug_expire_next_wait(1) == 0
+    rc = L.bebelm_attn_decode_cached(cache._h, 0, H, C.c_void_p(qh.ctypes.data), C.c_void_p(oh.ctypes.data),
+                                     bb.MEM_HOST, None)
+    assert rc == bb.ERR_TIMEOUT, bb.last_error()
+    rc = L.bebelm_attn_decode_cached(cache._h, 0, H, C.c_void_p(qh.ctypes.data), C.c_void_p(oh.ctypes.data),
+                                     bb.MEM_HOST, None)
+    assert rc == 0, bb.last_error()
+    assert np.abs(oh - outs[0].cpu().numpy()).max() <= 1e-6  # the same split plan as the no-allocation path
+    kw, vw = cache.read(0)
+    ref = oracle.attention_decode(qh, kw, vw, kw.shape[0], H, KVH, D)
+    assert np.abs(oh - ref).max() <= DECODE_ATOL
+    assert L.bebelm_debug_expire_next_wait(0) == 0
+    cache.close()
