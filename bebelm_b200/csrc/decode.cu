@@ -763,6 +763,10 @@ __global__ void gather_ll_kernel(const unsigned long long* __restrict__ zone, un
                 make_float2(__uint_as_float((unsigned)v0), __uint_as_float((unsigned)v1));
     }
     if (bad) *reinterpret_cast<volatile int*>(err) = kErrWaitTimeout;
+    // launched as a programmatic dependent of the kernel that stores this rank's words (its
+    // CTAs poll while that grid's tail runs): complete only after that grid has, so whatever
+    // follows this kernel also follows it
+    grid_dep_wait();
     __syncthreads();
     if (threadIdx.x == 0) {  // the step is over on this rank once every CTA is: the next may begin
         __threadfence();
@@ -789,8 +793,16 @@ cudaError_t launch_gather_ll(const unsigned long long* zone, unsigned long long*
                              size_t slice, size_t rows, size_t row_elems, float* dst, int* err, cudaStream_t s) {
     const size_t pairs = (size_t)world * rows * (row_elems / 2);
     const unsigned blocks = (unsigned)std::max<size_t>(1, std::min<size_t>((pairs + 1023) / 1024, 148 * 4));
-    gather_ll_kernel<<<blocks, 256, 0, s>>>(zone, epoch, done, world, slice, rows, row_elems, dst, err);
-    return cudaGetLastError();
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(blocks);
+    cfg.blockDim = dim3(256);
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, gather_ll_kernel, zone, epoch, done, world, slice, rows, row_elems, dst, err);
 }
 
 cudaError_t launch_stage_copy(void* dst, const void* src_mapped, size_t bytes, cudaStream_t s) {
