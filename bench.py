@@ -769,7 +769,11 @@ def profile_workload(name: str):
     """Small cases for ncu captures of one kernel each (inputs above L2 where it matters, a few
     GB at most): `norm_rope` (config-2 prefill: kernel 1 then the tensor-core prefill), `batched`
     (batched decode over 16 sequences of U[1024,16384] positions, ~560 MB of fp32 K/V),
-    `qmv` (one-token attention operator steps: the qmv_lane_kernel projections)."""
+    `qmv` (one-token attention operator steps: the qmv_lane_kernel projections), `aux` (the
+    small kernels around them: host-buffer decode steps on a 32768-position window, whose
+    inputs a stage_copy_kernel brings in; a 2048-token prefill chunk after 6144 cached positions,
+    whose prefix kv_gather_bf16_kernel gathers; fused all-gather steps through a one-rank peer
+    group, whose words gather_ll_kernel copies out)."""
     import numpy as np
     import torch
     import bebelm_b200 as bb
@@ -822,6 +826,38 @@ def profile_workload(name: str):
         for i in range(8):
             bb.attn_layer_step(c, 0, W, x[i], 2000 + i, theta=THETA, out=o)
         torch.cuda.synchronize()
+    elif name == "aux":
+        c = bb.Cache(n_layers=1, max_context=CTX)
+        for c0 in range(0, CTX, 4096):
+            c.append(0, torch.randn((4096, KVD), generator=g, device=dev), torch.randn((4096, KVD), generator=g, device=dev))
+        c.evict_front(1)
+        rng = np.random.default_rng(6)
+        qh, kh, vh = (rng.standard_normal(n, dtype=np.float32) for n in (HID, KVD, KVD))
+        gh = np.ones(D, np.float32)
+        for i in range(4):  # host buffers: the inputs come in through the staging copy kernel
+            c.attn_step(0, qh, kh, vh, gh, gh, pos=CTX + i, theta=THETA)
+            c.evict_front(1)
+        c.close()
+        T0, T1 = 6144, 2048
+        q = torch.randn((T0 + T1, HID), generator=g, device=dev).to(torch.bfloat16)
+        k = torch.randn((T0 + T1, KVD), generator=g, device=dev).to(torch.bfloat16)
+        c = bb.Cache(n_layers=1, max_context=T0 + T1)
+        c.attn_prefill(0, q[:T0], k[:T0], k[:T0], qg, qg, 0, theta=THETA)
+        c.attn_prefill(0, q[T0:], k[T0:], k[T0:], qg, qg, T0, theta=THETA)  # gathers the 6144 cached positions
+        torch.cuda.synchronize()
+        c.close()
+        c = bb.Cache(n_layers=1, max_context=4096)
+        c.append(0, torch.randn((4000, KVD), generator=g, device=dev), torch.randn((4000, KVD), generator=g, device=dev))
+        grp = bb.PeerGroup(1, 0, HID, device=0)
+        grp.connect([grp.handle])
+        x = torch.randn((3, HID), generator=g, device=dev)
+        kx = torch.randn((3, KVD), generator=g, device=dev)
+        for i in range(3):
+            c.attn_step_allgather(grp, 0, x[i], kx[i], kx[i], qg, qg, pos=4000 + i, theta=THETA)
+        torch.cuda.synchronize()
+        c.check()
+        grp.close()
+        c.close()
     else:
         raise SystemExit(f"unknown profile workload {name}")
     return 0
@@ -837,7 +873,7 @@ def main():
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--no-cfg4", action="store_true")
     ap.add_argument("--no-cfg5", action="store_true")
-    ap.add_argument("--profile-workload", default=None, choices=["norm_rope", "batched", "qmv"],
+    ap.add_argument("--profile-workload", default=None, choices=["norm_rope", "batched", "qmv", "aux"],
                     help="run one small case for an ncu capture and exit")
     args = ap.parse_args()
     if args.warmup < 3:
