@@ -792,7 +792,8 @@ __global__ void stage_copy_kernel(const uint4* __restrict__ src, uint4* __restri
 cudaError_t launch_gather_ll(const unsigned long long* zone, unsigned long long* epoch, unsigned* done, int world,
                              size_t slice, size_t rows, size_t row_elems, float* dst, int* err, cudaStream_t s) {
     const size_t pairs = (size_t)world * rows * (row_elems / 2);
-    const unsigned blocks = (unsigned)std::max<size_t>(1, std::min<size_t>((pairs + 1023) / 1024, 148 * 4));
+    // one 16-byte pair a thread while that fits in 4 CTAs an SM: every word is polled at once
+    const unsigned blocks = (unsigned)std::max<size_t>(1, std::min<size_t>((pairs + 255) / 256, 148 * 4));
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(blocks);
     cfg.blockDim = dim3(256);
