@@ -229,7 +229,9 @@ struct DecodeArgs {
 extern int g_expire_waits;
 // The gather of a fused all-gather step (a landing zone of tagged words, see DecodeArgs): waits
 // (bounded) for every element of this step's parity to carry this step's tag, copies them into
-// dst [rows][world * row_elems], and advances *epoch (the last CTA; `done` counts them).
+// dst [rows][world * row_elems], and advances *epoch (the last CTA; `done` counts them). It is
+// launched as a programmatic dependent of the kernel before it (the one storing this rank's
+// words): it polls during that grid's tail and completes only after that grid has.
 cudaError_t launch_gather_ll(const unsigned long long* zone, unsigned long long* epoch, unsigned* done, int world,
                              size_t slice, size_t rows, size_t row_elems, float* dst, int* err, cudaStream_t s);
 cudaError_t launch_decode(const DecodeArgs& a, cudaStream_t s);
