@@ -16,6 +16,8 @@
 #include <initializer_list>
 #include <vector>
 
+#include <unistd.h>
+
 #include "../../include/bebelm_attn.h"
 #include "internal.h"
 
@@ -182,24 +184,19 @@ struct HostCopier {
     int parts = 0;
     std::atomic<int> next{0}, done{0};
     unsigned long long gen = 0;
-    bool stop = false;
 
+    pid_t owner = 0;  // the process whose threads these are (a forked child has none of them)
+
+    // Created on first use and never destroyed: the idle workers end with the process, and no
+    // exit-time join can wait on threads that a forked child does not have.
     static HostCopier& get() {
-        static HostCopier c;
-        return c;
+        static HostCopier* c = new HostCopier();
+        return *c;
     }
-    HostCopier() {
+    HostCopier() : owner(getpid()) {
         const unsigned hc = std::thread::hardware_concurrency();
         const int k = (int)std::min(7u, hc > 2 ? hc / 2 : 0u);
         for (int i = 0; i < k; ++i) th.emplace_back([this] { loop(); });
-    }
-    ~HostCopier() {
-        {
-            std::lock_guard<std::mutex> lk(mu);
-            stop = true;
-        }
-        cv.notify_all();
-        for (auto& t : th) t.join();
     }
     void work() {
         for (;;) {
@@ -218,15 +215,14 @@ struct HostCopier {
         for (;;) {
             {
                 std::unique_lock<std::mutex> lk(mu);
-                cv.wait(lk, [&] { return stop || gen != seen; });
-                if (stop) return;
+                cv.wait(lk, [&] { return gen != seen; });
                 seen = gen;
             }
             work();
         }
     }
     void copy(void* d, const void* sp, size_t bytes) {
-        if (bytes < kMinParallel || th.empty()) {
+        if (bytes < kMinParallel || th.empty() || getpid() != owner) {
             std::memcpy(d, sp, bytes);
             return;
         }
