@@ -214,9 +214,20 @@ def run_ours(args):
     OUT = torch.empty((n_steps, HID), device=dev)
     pos = [CTX]
 
+    # the C-ABI called as a Rust caller would (device pointers computed once, no per-call
+    # wrapper work), so that the host's launch rate does not cap the device-timed step
+    lib = bb.load_library()
+    sp = stream.cuda_stream
+    qp0, kp0, vp0, op0 = Q.data_ptr(), K.data_ptr(), V.data_ptr(), OUT.data_ptr()
+    qgp, kgp = qg.data_ptr(), kg.data_ptr()
+
     def step(i):
-        cache.attn_step(0, Q[i], K[i], V[i], qg, kg, pos=pos[0], theta=THETA, eps=EPS, out=OUT[i], stream=stream)
-        cache.evict_front(1)
+        rc = lib.bebelm_attn_step(cache._h, 0, H, qp0 + 4 * HID * i, kp0 + 4 * KVD * i, vp0 + 4 * KVD * i, qgp, kgp,
+                                  THETA, EPS, pos[0], op0 + 4 * HID * i, bb.MEM_DEVICE, sp)
+        if rc == 0:
+            rc = lib.bebelm_kv_evict_front(cache._h, 1)
+        if rc != 0:
+            raise bb.BebelmError(rc, bb.last_error())
         pos[0] += 1
 
     for i in range(args.warmup):
